@@ -1,0 +1,98 @@
+// Entry points of the RW4 C ABI that are not tied to one kernel file: version, error reporting,
+// device queries and the rw4_linear dispatcher.
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "rw4_common.cuh"
+
+namespace rw4 {
+
+namespace {
+thread_local std::string g_last_error;
+}
+
+void set_error_message(const char* msg) { g_last_error = msg ? msg : ""; }
+
+int sm_count() {
+  static std::mutex mu;
+  static std::vector<int> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+  if (cache[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[dev] = n;
+  }
+  return cache[dev];
+}
+
+int gemv_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
+                const void* zr, int64_t N, void* y, cudaStream_t s);
+int gemm_tc_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
+                   const void* zr, int64_t N, void* y, cudaStream_t s);
+bool gemm_tc_supported(int64_t M, int64_t K, int64_t N);
+
+// Shape / pointer validation shared by every RW4 matmul entry point.
+int check_linear_args(const char* who, const void* x, int64_t M, int64_t K, const uint8_t* wq,
+                      const void* sc, const void* zr, int64_t N, int32_t group, const void* y) {
+  if (M < 0 || K <= 0 || N < 0)
+    return fail(RW4_EINVAL, "%s: bad shape M=%lld K=%lld N=%lld", who, (long long)M,
+                (long long)K, (long long)N);
+  if (group != 64) return fail(RW4_EINVAL, "%s: group %d unsupported (64 only)", who, group);
+  if (K % 64) return fail(RW4_EINVAL, "%s: K=%lld is not a multiple of 64", who, (long long)K);
+  if (K > (1ll << 30) || N > (1ll << 30) || M > (1ll << 30))
+    return fail(RW4_EINVAL, "%s: dimension beyond 2^30", who);
+  if (M == 0 || N == 0) return RW4_OK;
+  if (!x || !wq || !sc || !zr || !y) return fail(RW4_EINVAL, "%s: null pointer", who);
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(wq, 16) || !aligned(sc, 8) || !aligned(zr, 8))
+    return fail(RW4_EINVAL, "%s: x/y/packed must be 16-byte and scale/zero 8-byte aligned", who);
+  if ((N * 2) % 16)
+    return fail(RW4_EINVAL, "%s: N=%lld must be a multiple of 8 (16-byte output rows)", who,
+                (long long)N);
+  return RW4_OK;
+}
+
+}  // namespace rw4
+
+extern "C" int rw4_version(void) { return 100; }
+
+extern "C" int rw4_last_error(char* buf, size_t n) {
+  const std::string& e = rw4::g_last_error;
+  if (buf && n) {
+    const size_t c = e.size() < n - 1 ? e.size() : n - 1;
+    memcpy(buf, e.data(), c);
+    buf[c] = 0;
+  }
+  return (int)e.size();
+}
+
+extern "C" int rw4_linear_path(int64_t M, int64_t K, int64_t N) {
+  if (M < 0 || K <= 0 || N < 0 || K % 64) return RW4_EINVAL;
+  if (M <= 16) return 1;
+  if (rw4::gemm_tc_supported(M, K, N)) return 2;
+  return 3;
+}
+
+extern "C" int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                          const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
+                          void* y_bf16, void* stream) {
+  using namespace rw4;
+  int st = check_linear_args("rw4_linear", x_bf16, M, K, packed, scale_f16, zero_f16, N, group,
+                             y_bf16);
+  if (st != RW4_OK || M == 0 || N == 0) return st;
+  cudaStream_t s = as_stream(stream);
+  switch (rw4_linear_path(M, K, N)) {
+    case 1:
+    case 3:
+      return gemv_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s);
+    case 2:
+      return gemm_tc_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s);
+    default:
+      return fail(RW4_EINVAL, "rw4_linear: no path for M=%lld K=%lld N=%lld", (long long)M,
+                  (long long)K, (long long)N);
+  }
+}

@@ -1,0 +1,88 @@
+// Shared helpers for the RW4 CUDA library: status handling, argument checks, small device
+// utilities.  Every extern "C" entry point returns an int status and records a message for
+// rw4_last_error() on failure; no C++ exception crosses the ABI.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/rw4.h"
+
+namespace rw4 {
+
+// Thread-local last error message (defined in rw4_abi.cu).
+void set_error_message(const char* msg);
+
+inline int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  set_error_message(buf);
+  return code;
+}
+
+inline int cuda_status(cudaError_t err, const char* what) {
+  if (err == cudaSuccess) return RW4_OK;
+  return fail(RW4_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(err), cudaGetErrorName(err));
+}
+
+// Status of the launch just queued (configuration errors only; asynchronous faults surface on
+// the next synchronising call, as with any CUDA launch).
+inline int launch_status(const char* what) { return cuda_status(cudaGetLastError(), what); }
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+// Number of SMs of the current device, cached per device.
+int sm_count();
+
+}  // namespace rw4
+
+// ---------------------------------------------------------------------------------------------
+// device helpers
+// ---------------------------------------------------------------------------------------------
+
+// 8-byte streaming load through the non-coherent path, not kept in L1 (weights are read once).
+__device__ __forceinline__ uint2 ldg_stream_u2(const void* p) {
+  uint2 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
+               : "=r"(v.x), "=r"(v.y)
+               : "l"(p));
+  return v;
+}
+
+__device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Read-only cached loads (activations and scales are re-read by neighbouring warps).
+__device__ __forceinline__ uint4 ldg_u4(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+__device__ __forceinline__ uint2 ldg_u2(const void* p) {
+  return __ldg(reinterpret_cast<const uint2*>(p));
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + C, fp32 accumulate (warp-wide).
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1, const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%11,%12,%13};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
+        "f"(c[2]), "f"(c[3]));
+}

@@ -1,0 +1,101 @@
+"""Torch-tensor front end of the RW4 C ABI: device pointers and the current stream in, no copies.
+
+Each function validates that its tensors live on a CUDA device with the layout the C ABI expects
+and calls the matching ``rw4_*`` entry point on ``torch.cuda.current_stream()``.  Shapes follow
+RocketLLM's int4 codec (``rocketllm/quant/kv_cache.py:190-272``) applied to a Linear weight
+``W[N, K]``: ``packed`` uint8 ``[N, Kp/2]``, ``scale``/``zero`` fp16 ``[N, Kp/64]``.
+"""
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: _lib.RW4_F32, torch.bfloat16: _lib.RW4_BF16,
+               torch.float16: _lib.RW4_F16}
+
+
+def _stream():
+    return ctypes_stream(torch.cuda.current_stream())
+
+
+def ctypes_stream(stream):
+    return stream.cuda_stream
+
+
+def _require_cuda(*tensors):
+    for t in tensors:
+        if not t.is_cuda:
+            raise ValueError("RW4 kernels take CUDA tensors only (there is no CPU path); got a "
+                             f"{t.device} tensor of shape {tuple(t.shape)}")
+        if not t.is_contiguous():
+            raise ValueError(f"RW4 kernels need contiguous tensors; got strides {t.stride()}")
+
+
+def _check_weight(packed, scale, zero):
+    if packed.dtype != torch.uint8:
+        raise TypeError(f"packed must be uint8, not {packed.dtype}")
+    if scale.dtype != torch.float16 or zero.dtype != torch.float16:
+        raise TypeError("scale and zero must be float16")
+    if packed.dim() != 2 or scale.shape != zero.shape or scale.shape[0] != packed.shape[0]:
+        raise ValueError(f"inconsistent RW4 weight: packed {tuple(packed.shape)}, scale "
+                         f"{tuple(scale.shape)}, zero {tuple(zero.shape)}")
+
+
+def dequantize(packed, scale, zero, k=None, dtype=torch.bfloat16, out=None):
+    """Expand an RW4 weight to ``[N, k]`` in ``dtype``; bit-exact with the reference codec."""
+    _require_cuda(packed, scale, zero)
+    _check_weight(packed, scale, zero)
+    n = packed.shape[0]
+    kp = packed.shape[1] * 2
+    k = kp if k is None else int(k)
+    group = kp // scale.shape[1] if scale.shape[1] else 64
+    if out is None:
+        out = torch.empty((n, k), dtype=dtype, device=packed.device)
+    _require_cuda(out)
+    _lib.call("rw4_dequant", packed.data_ptr(), scale.data_ptr(), zero.data_ptr(), n, k, group,
+              out.data_ptr(), _DTYPE_CODE[out.dtype], _stream())
+    return out
+
+
+def quantize(w, group=64):
+    """Encode ``w[N, K]`` (fp32 or bf16, CUDA) as ``(packed, scale, zero, padding)``.
+
+    Bit-exact with the reference ``quantize(w, 1, group)``.
+    """
+    _require_cuda(w)
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        raise TypeError(f"quantize takes float32 or bfloat16, not {w.dtype}")
+    n, k = w.shape
+    g = min(group, k) if k else group
+    groups = (k + g - 1) // g if k else 0
+    packed = torch.empty((n, groups * g // 2), dtype=torch.uint8, device=w.device)
+    scale = torch.empty((n, groups), dtype=torch.float16, device=w.device)
+    zero = torch.empty((n, groups), dtype=torch.float16, device=w.device)
+    _lib.call("rw4_quantize", w.data_ptr(), _DTYPE_CODE[w.dtype], n, k, group, packed.data_ptr(),
+              scale.data_ptr(), zero.data_ptr(), _stream())
+    return packed, scale, zero, groups * g - k
+
+
+def linear(x, packed, scale, zero, out=None):
+    """``y = x . W^T`` with ``x`` bf16 ``[..., K]`` and W in RW4; returns bf16 ``[..., N]``."""
+    _require_cuda(x, packed, scale, zero)
+    _check_weight(packed, scale, zero)
+    if x.dtype != torch.bfloat16:
+        raise TypeError(f"rw4 linear takes bf16 activations, not {x.dtype}")
+    k = x.shape[-1]
+    n = packed.shape[0]
+    if packed.shape[1] * 2 != k:
+        raise ValueError(f"x has K={k} but the weight packs {packed.shape[1] * 2} values per row")
+    x2 = x.reshape(-1, k)
+    if not x2.is_contiguous():
+        x2 = x2.contiguous()
+    m = x2.shape[0]
+    if out is None:
+        out = torch.empty((*x.shape[:-1], n), dtype=torch.bfloat16, device=x.device)
+    _lib.call("rw4_linear", x2.data_ptr(), m, k, packed.data_ptr(), scale.data_ptr(),
+              zero.data_ptr(), n, 64, out.data_ptr(), _stream())
+    return out
+
+
+def linear_path(m, k, n):
+    """Which kernel :func:`linear` launches: 1 GEMV, 2 tcgen05 GEMM, 3 GEMV slices."""
+    return _lib.check(_lib.lib().rw4_linear_path(m, k, n), "rw4_linear_path")

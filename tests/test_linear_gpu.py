@@ -1,0 +1,80 @@
+"""GPU parity of rw4_linear (dequant-GEMV and GEMM paths) with the oracle, through the C ABI.
+
+Tolerance: the device output is bf16 of an fp32 accumulation, so each element may differ from the
+fp32 oracle by one bf16 rounding (2^-8 relative) plus accumulation-order noise; the bound used is
+|y - ref| <= ref_abs / 128 + 2e-3 * rms(ref).
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import rw4_oracle as o
+from rocketllm_b200 import kernels
+from rocketllm_b200.synthetic import make_activation, make_weight
+
+pytestmark = pytest.mark.gpu
+
+
+def check_close(y, ref):
+    y = y.float().cpu().numpy()
+    rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2))) + 1e-12
+    err = np.abs(y - ref)
+    bound = np.abs(ref) / 128 + 2e-3 * rms
+    assert np.all(err <= bound), f"max err {err.max():.4g}, worst excess {(err - bound).max():.4g}"
+
+
+def oracle_linear(x, packed, scale, zero, rows=None):
+    xb = x.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+    p, s, z = packed.cpu().numpy(), scale.cpu().numpy(), zero.cpu().numpy()
+    if rows is not None:
+        p, s, z = p[rows], s[rows], z[rows]
+    return o.linear(xb, p, s, z)
+
+
+@pytest.mark.parametrize("m", [1, 2, 3, 4, 7, 8, 9, 15, 16, 17, 33, 64])
+@pytest.mark.parametrize("k,n", [(4096, 512), (320, 136), (1024, 4104)])
+def test_linear_matches_oracle(cuda, m, k, n):
+    packed, scale, zero = make_weight(n, k, device=cuda, seed=m + k)
+    x = make_activation(m, k, device=cuda, seed=n)
+    y = kernels.linear(x, packed, scale, zero)
+    torch.cuda.synchronize()
+    check_close(y, oracle_linear(x, packed, scale, zero))
+
+
+def test_linear_golden_reference_output(golden, cuda):
+    """The reference's own bf16 F.linear over its dequantized weight (make_golden.py)."""
+    dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
+    x = dev(golden["sweep.x"].view(np.int16)).view(torch.bfloat16)
+    y = kernels.linear(x, dev(golden["sweep.packed"]), dev(golden["sweep.scale"]),
+                       dev(golden["sweep.zero"]))
+    check_close(y, golden["sweep.y_f32"])
+
+
+@pytest.mark.parametrize("k,n", [(16384, 53248), (8192, 28672)])
+@pytest.mark.parametrize("m", [1, 16])
+def test_linear_full_size_sampled_rows(cuda, k, n, m):
+    """Full sweep shapes: the oracle recomputes a seeded sample of output rows."""
+    packed, scale, zero = make_weight(n, k, device=cuda, seed=7)
+    x = make_activation(m, k, device=cuda, seed=8)
+    y = kernels.linear(x, packed, scale, zero)
+    rows = np.sort(np.random.default_rng(0).choice(n, 96, replace=False))
+    rows = np.concatenate([rows, [0, n - 1]])
+    ref = oracle_linear(x, packed, scale, zero, rows=rows)
+    check_close(y[:, torch.from_numpy(rows).to(cuda)], ref)
+
+
+def test_linear_is_linear_in_x(cuda):
+    """Size-independent property: W(a x1 + x2) = a W x1 + W x2 within bf16 rounding."""
+    packed, scale, zero = make_weight(14336, 4096, device=cuda, seed=3)
+    x1 = make_activation(4, 4096, device=cuda, seed=4)
+    y1 = kernels.linear(x1, packed, scale, zero).float()
+    y2 = kernels.linear((2 * x1.float()).to(torch.bfloat16), packed, scale, zero).float()
+    assert torch.allclose(y2, 2 * y1, rtol=1 / 64, atol=1e-2)
+
+
+def test_linear_deterministic(cuda):
+    packed, scale, zero = make_weight(4096, 14336, device=cuda, seed=5)
+    x = make_activation(16, 14336, device=cuda, seed=6)
+    a = kernels.linear(x, packed, scale, zero)
+    b = kernels.linear(x, packed, scale, zero)
+    assert torch.equal(a, b)
