@@ -85,6 +85,12 @@ int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
  * 3 = GEMV over 16-row slices. Negative on invalid shapes. Host-only, launches nothing. */
 int rw4_linear_path(int64_t M, int64_t K, int64_t N);
 
+/* Reads the library's device status word on the current device after the work queued on `stream`
+ * (synchronises that stream): bit 1 = a bounded wait inside a kernel gave up (the kernel returned
+ * early and its outputs are invalid), bit 2 = a tensor-memory allocation failed.  clear != 0 resets
+ * the word.  No reference counterpart: the reference has no device kernels that can wait. */
+int rw4_device_status(uint32_t* word, int32_t clear, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * MoE routed experts (transformers models/mixtral/modeling_mixtral.py:62-98, the experts forward
  * the reference streams; rocketllm/base.py:1375-1464 for its fused-row path).

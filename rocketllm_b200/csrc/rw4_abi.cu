@@ -5,6 +5,7 @@
 #include <vector>
 
 #include "rw4_common.cuh"
+#include "rw4_tma.cuh"
 
 namespace rw4 {
 
@@ -95,4 +96,82 @@ extern "C" int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_
       return fail(RW4_EINVAL, "rw4_linear: no path for M=%lld K=%lld N=%lld", (long long)M,
                   (long long)K, (long long)N);
   }
+}
+
+// ---- device status word and TMA descriptors ---------------------------------------------------
+
+namespace {
+__device__ unsigned int g_device_status_word = 0;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  return fn;
+}
+}  // namespace
+
+namespace rw4 {
+
+unsigned int* device_status_ptr() {
+  static std::mutex mu;
+  static std::vector<unsigned int*> cache;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1, nullptr);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status_word) == cudaSuccess)
+      cache[dev] = static_cast<unsigned int*>(p);
+  }
+  return cache[dev];
+}
+
+int make_tensor_map_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                       int elem_bytes, uint64_t rows, uint64_t cols, uint64_t row_bytes,
+                       uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swizzle) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return fail(RW4_ECUDA, "cuTensorMapEncodeTiled entry point unavailable");
+  if (!aligned(base, 16) || row_bytes % 16 || (box_cols * elem_bytes) % 16)
+    return fail(RW4_EINVAL, "tensor map: base/pitch/box not 16-byte aligned");
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(RW4_ECUDA, "cuTensorMapEncodeTiled failed (%d) rows=%llu cols=%llu box=%ux%u",
+                (int)r, (unsigned long long)rows, (unsigned long long)cols, box_rows, box_cols);
+  return RW4_OK;
+}
+
+}  // namespace rw4
+
+extern "C" int rw4_device_status(uint32_t* word, int32_t clear, void* stream) {
+  using namespace rw4;
+  if (!word) return fail(RW4_EINVAL, "rw4_device_status: null output");
+  unsigned int* p = device_status_ptr();
+  if (!p) return fail(RW4_ECUDA, "rw4_device_status: no device status word");
+  cudaStream_t s = as_stream(stream);
+  unsigned int v = 0;
+  int st = cuda_status(cudaMemcpyAsync(&v, p, sizeof(v), cudaMemcpyDeviceToHost, s),
+                       "rw4_device_status read");
+  if (st == RW4_OK && clear) st = cuda_status(cudaMemsetAsync(p, 0, sizeof(v), s), "clear");
+  if (st == RW4_OK) st = cuda_status(cudaStreamSynchronize(s), "rw4_device_status sync");
+  *word = v;
+  return st;
 }

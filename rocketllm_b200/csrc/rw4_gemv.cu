@@ -30,59 +30,14 @@
 // Exactness: the group partial sum of (128 + c) x is formed by the tensor core in fp32; the later
 // subtraction of 128 * sum(x) cancels ~7 bits, leaving ~2^-17 relative error per group, far below
 // the bf16 output rounding (2^-9).
-#include "rw4_common.cuh"
+#include "rw4_gemv_frag.cuh"
 
 namespace {
 
+using namespace rw4::frag;
+
 constexpr int kWarps = 8;
 constexpr int kGroupsPerChunk = 4;  // 256 values of K per warp iteration
-constexpr uint32_t kMagic = 0x43004300u;   // bf16 pair (128, 128)
-constexpr uint32_t kOnes = 0x3F803F80u;    // bf16 pair (1, 1)
-
-// Codes of nibbles (p, p+4) of `word` as a bf16 pair (128 + c_p, 128 + c_{p+4}).
-__device__ __forceinline__ uint32_t nib_pair(uint32_t word, int shift) {
-  uint32_t r;
-  const uint32_t v = word >> shift;
-  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(v), "n"(0x000F000F), "n"(kMagic));
-  return r;
-}
-
-// x fragment for one group: 16 bf16 values x[16t .. 16t+16) of the thread's batch row, permuted
-// to the K order the code extraction produces.  b[j][0..1] are the two B registers of MMA step j.
-__device__ __forceinline__ void load_x_frag(const __nv_bfloat16* xrow, bool valid,
-                                            uint32_t (&b)[4][2]) {
-  uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
-  if (valid) {
-    lo = ldg_u4(xrow);
-    hi = ldg_u4(xrow + 8);
-  }
-  // natural pairs: lo = (x0,x1)(x2,x3)(x4,x5)(x6,x7); hi = (x8,x9)..(x14,x15)
-  b[0][0] = __byte_perm(lo.x, lo.z, 0x5410);  // (x0, x4)
-  b[0][1] = __byte_perm(lo.x, lo.z, 0x7632);  // (x1, x5)
-  b[1][0] = __byte_perm(lo.y, lo.w, 0x5410);  // (x2, x6)
-  b[1][1] = __byte_perm(lo.y, lo.w, 0x7632);  // (x3, x7)
-  b[2][0] = __byte_perm(hi.x, hi.z, 0x5410);  // (x8, x12)
-  b[2][1] = __byte_perm(hi.x, hi.z, 0x7632);  // (x9, x13)
-  b[3][0] = __byte_perm(hi.y, hi.w, 0x5410);  // (x10, x14)
-  b[3][1] = __byte_perm(hi.y, hi.w, 0x7632);  // (x11, x15)
-}
-
-// A operand of MMA step j for the thread's two rows (g: word wa, g+8: word wb).
-//   reg0 = row g,   logical k (2t, 2t+1)   <- nibbles (p,   p+4)
-//   reg1 = row g+8, logical k (2t, 2t+1)   <- nibbles (p,   p+4)
-//   reg2 = row g,   logical k (2t+8, 2t+9) <- nibbles (p+1, p+5)
-//   reg3 = row g+8, logical k (2t+8, 2t+9) <- nibbles (p+1, p+5)
-// with p = 2 (j & 1) inside word j >> 1 of the thread's 8-byte slice.
-__device__ __forceinline__ void a_frag(uint2 wa, uint2 wb, int j, uint32_t (&a)[4]) {
-  const uint32_t xa = (j < 2) ? wa.x : wa.y;
-  const uint32_t xb = (j < 2) ? wb.x : wb.y;
-  const int p = (j & 1) * 2;
-  a[0] = nib_pair(xa, 4 * p);
-  a[1] = nib_pair(xb, 4 * p);
-  a[2] = nib_pair(xa, 4 * p + 4);
-  a[3] = nib_pair(xb, 4 * p + 4);
-}
-
 
 // Registers holding one chunk (4 groups) of codes and scales for the thread's 2R rows.
 template <int R>
@@ -246,16 +201,12 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int chunks = (G + kGroupsPerChunk - 1) / kGroupsPerChunk;
   const bool vec_scales = (G & 3) == 0;
 
-  // Two register sets: the loads of chunk c + kWarps are issued before chunk c is computed, so
-  // every warp keeps a chunk of codes in flight while it works (bytes in flight per SM double).
-  ChunkRegs<R> cur, nxt;
-  int c = warp;
-  if (c < chunks) load_chunk<R>(cur, c, G, vec_scales, wrow_a, wrow_b, srow_a, srow_b, zrow_a, zrow_b);
-  for (; c < chunks; c += kWarps) {
-    if (c + kWarps < chunks)
-      load_chunk<R>(nxt, c + kWarps, G, vec_scales, wrow_a, wrow_b, srow_a, srow_b, zrow_a, zrow_b);
+  // Register-staged fallback for K not a multiple of 512 (the TMA kernel's scale-box alignment):
+  // each chunk is loaded into registers and then computed.
+  for (int c = warp; c < chunks; c += kWarps) {
+    ChunkRegs<R> cur;
+    load_chunk<R>(cur, c, G, vec_scales, wrow_a, wrow_b, srow_a, srow_b, zrow_a, zrow_b);
     compute_chunk<NT, R>(cur, c, G, K, Ml, g, t, x, out);
-    cur = nxt;
   }
 
   // ---- combine the warps' partial sums and write bf16 -----------------------------------------
@@ -303,6 +254,10 @@ int rows_per_cta_override() {
 namespace rw4 {
 
 // y = x W^T for any M via 16-row batch slices (M <= 16: one slice).
+bool gemv_tma_supported(int64_t K);
+int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
+                    const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles);
+
 int gemv_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                 const void* zr, int64_t N, void* y, cudaStream_t s) {
   const int nt = (M <= 8) ? 1 : 2;
@@ -312,6 +267,8 @@ int gemv_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const vo
     // when there are rows to spare.
     R = (N >= 16 * 2 * 148 * 4) ? 2 : 1;
   }
+  static const bool no_tma = getenv("RW4_GEMV_NO_TMA") != nullptr;
+  if (!no_tma && gemv_tma_supported(K)) return gemv_tma_launch(x, M, K, wq, sc, zr, N, y, s, R);
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* yb = static_cast<__nv_bfloat16*>(y);
   const auto* s16 = static_cast<const __half*>(sc);
