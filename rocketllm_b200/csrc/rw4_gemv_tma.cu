@@ -278,10 +278,11 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
                     const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles) {
   const int Mi = (int)M, Ki = (int)K, Ni = (int)N;
   if (M <= 8) {
+    if (row_tiles == 4) return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
     if (row_tiles == 2) return launch_tma<1, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
     return launch_tma<1, 1, 8>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
   }
-  if (row_tiles == 2) return launch_tma<2, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+  if (row_tiles >= 2) return launch_tma<2, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
   return launch_tma<2, 1, 8>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
 }
 
