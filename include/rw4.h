@@ -92,35 +92,36 @@ int rw4_linear_path(int64_t M, int64_t K, int64_t N);
 int rw4_device_status(uint32_t* word, int32_t clear, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
- * MoE routed experts (transformers models/mixtral/modeling_mixtral.py:62-98, the experts forward
- * the reference streams; rocketllm/base.py:1375-1464 for its fused-row path).
+ * MoE routed experts.  Together these replace the experts forward the reference streams
+ * (transformers models/mixtral/modeling_mixtral.py:62-98, reached through rocketllm/base.py's
+ * expert hooks :1083-1464): permute -> gather -> grouped RW4 GEMV (gate/up with SwiGLU) -> grouped
+ * RW4 GEMV (down) -> combine.  Routing indices come from the model's own router unchanged.
  * ------------------------------------------------------------------------------------------- */
 
 /*
  * rw4_moe_permute: stable counting sort of the T*k (token, slot) pairs by expert id.
- * topk_idx int64 [T, k] with ids in [0, E).  Writes perm int32 [T*k] (perm[row] = t*k + j, rows of
- * expert e are offsets[e]..offsets[e+1]-1 in increasing t*k+j order) and offsets int32 [E+1].
- * Out-of-range ids are counted in an error word and make the call return RW4_EINVAL on the next
- * rw4_moe_check_status (the kernel itself skips them).  E <= 1024.
+ * topk_idx int64 [T, k].  Writes perm int32 [T*k] (perm[row] = t*k + j; rows of expert e are
+ * offsets[e] .. offsets[e+1]-1, in increasing t*k+j order), inv int32 [T*k] (inv[t*k+j] = row;
+ * may be NULL) and offsets int32 [E+1].  Ids outside [0, E) are dropped: their inv entry is -1,
+ * offsets[E] counts only valid slots and the unused tail of perm is -1.  E <= 4096.
  */
 int rw4_moe_permute(const int64_t* topk_idx, int64_t T, int32_t k, int32_t E, int32_t* perm,
-                    int32_t* offsets, void* stream);
+                    int32_t* inv, int32_t* offsets, void* stream);
 
-/*
- * rw4_moe_gather: x_perm[row] = x[perm[row] / k] for row in [0, T*k), bf16 rows of H values.
- */
+/* rw4_moe_gather: x_perm[row] = x[perm[row] / k] (zeros where perm[row] < 0), bf16 rows of H
+ * values, H % 8 == 0. */
 int rw4_moe_gather(const void* x_bf16, const int32_t* perm, int64_t T, int32_t k, int64_t H,
                    void* x_perm_bf16, void* stream);
 
 /*
- * rw4_moe_grouped: y_perm[rows of e] = act(x_perm[rows of e] . W_e^T) for every expert e with at
- * least one routed row; experts with none are never read.  Weights are per-expert RW4 tensors
- * given as device arrays of device pointers (packed_e[E], scale_e[E], zero_e[E]), each W_e of
- * shape [N, K].  `offsets` is the device int32 [E+1] from rw4_moe_permute; `max_rows` is an upper
- * bound on any expert's row count (T*k is always safe).
- * act = 0: plain linear (y_perm [T*k, N]).
- * act = 1: SwiGLU over a stacked gate/up weight of N = 2*I rows: y_perm[r, i] =
- *          silu(g) * u with g = bf16(x.W[i]), u = bf16(x.W[I+i]); y_perm is [T*k, I].
+ * rw4_moe_grouped: for every expert e, y_perm[rows of e] = act(x_perm[rows of e] . W_e^T); an
+ * expert with no routed rows is never read.  Weights are per-expert RW4 tensors W_e [N, K]; their
+ * device pointers are passed in HOST arrays packed_e[E], scale_e[E], zero_e[E] (the host encodes
+ * one TMA descriptor per expert).  `offsets` is the DEVICE int32 [E+1] from rw4_moe_permute;
+ * max_rows bounds any expert's row count (T*k is always safe).  group 64, K % 512 == 0.
+ * act = 0: y_perm [T*k, N].
+ * act = 1: stacked gate/up weight, N = 2*I: y_perm [T*k, I] = bf16(silu(bf16(g)) * bf16(u)) with
+ *          g = x.W[i], u = x.W[I+i] (the rounding sequence of the bf16 model's act_fn(gate) * up).
  */
 int rw4_moe_grouped(const void* x_perm_bf16, const int32_t* offsets, int32_t E, int64_t max_rows,
                     const uint8_t* const* packed_e, const void* const* scale_e,
@@ -128,49 +129,61 @@ int rw4_moe_grouped(const void* x_perm_bf16, const int32_t* offsets, int32_t E, 
                     void* y_perm_bf16, void* stream);
 
 /*
- * rw4_moe_combine: out[t] = bf16( sum_{j<k} w[t, j] * y_perm[inv(t*k+j)] ), fp32 accumulation in
- * slot order j = 0..k-1 (deterministic, no atomics).  topk_w is fp32 [T, k] (w_dtype RW4_F32) or
- * bf16 (RW4_BF16); y_perm bf16 [T*k, H]; out bf16 [T, H].
+ * rw4_moe_combine: out[t] = sum over the token's k slots of w[t, j] * y_perm[inv[t*k+j]], visiting
+ * slots in ascending expert id (topk_idx; NULL = slot order) and rounding to bf16 after every
+ * product and add -- the order and rounding of the reference's index_add_ into a bf16 tensor.
+ * No atomics; deterministic.  topk_w fp32 (w_dtype RW4_F32) or bf16 [T, k]; k <= 8; H % 8 == 0.
  */
-int rw4_moe_combine(const void* y_perm_bf16, const int32_t* perm, const void* topk_w,
-                    int32_t w_dtype, int64_t T, int32_t k, int64_t H, void* out_bf16,
-                    void* stream);
+int rw4_moe_combine(const void* y_perm_bf16, const int32_t* inv, const int64_t* topk_idx,
+                    const void* topk_w, int32_t w_dtype, int64_t T, int32_t k, int64_t H,
+                    void* out_bf16, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
- * Host->device staging ring (rocketllm/streaming/staging.py:80-273 HostStagingPool.lease and
- * rocketllm/streaming/transfer.py:124-292 WeightTransfer.send_buffer / TransferHandle.resolve).
- * A ring owns `slots` pinned host buffers of `slot_bytes` each and `copy_streams` CUDA streams.
+ * Streaming: pinned host staging pool + host->device transfer engine.
+ *
+ * rw4_pool_* replaces HostStagingPool (rocketllm/streaming/staging.py:80-273): pinned buffers in
+ * power-of-two size classes (at least 2^16 bytes), leased, never handed to a second caller while
+ * leased, allocated once and reused; a lease that would exceed the budget fails with RW4_EBUSY
+ * (the Python shim then falls back to a transient buffer, as the reference does).
+ *
+ * rw4_xfer_* replaces WeightTransfer / TransferHandle (rocketllm/streaming/transfer.py:30-292):
+ * each send is split into chunks issued round-robin on the engine's own copy streams (so two DMA
+ * engines work on one layer), and gets a ticket whose completion is an event recorded behind all of
+ * its chunks.  Compute waits on a ticket device-side (rw4_xfer_wait), never on the host.  A pooled
+ * buffer must not be released before its ticket completes (rw4_xfer_query / rw4_xfer_sync).
  * ------------------------------------------------------------------------------------------- */
 
-typedef struct rw4_ring rw4_ring;
+typedef struct rw4_pool rw4_pool;
+typedef struct rw4_xfer rw4_xfer;
 
-int rw4_ring_create(size_t slot_bytes, int32_t slots, int32_t copy_streams, int32_t device,
-                    rw4_ring** out);
-int rw4_ring_destroy(rw4_ring* ring);
+/* Pool with a pinned-byte budget (0 = no pinned buffers: every lease fails with RW4_EBUSY). */
+int rw4_pool_create(size_t budget_bytes, rw4_pool** out);
+int rw4_pool_destroy(rw4_pool* pool);
+/* Lease a pinned buffer of at least `bytes` (smallest free buffer that fits; else a new one of the
+ * size class if the budget allows; else RW4_EBUSY).  Returns its id and host address. */
+int rw4_pool_lease(rw4_pool* pool, size_t bytes, int32_t* id, void** host);
+int rw4_pool_release(rw4_pool* pool, int32_t id);
+/* resident bytes, buffers, leased buffers, hits, misses */
+int rw4_pool_stats(rw4_pool* pool, uint64_t* resident, int32_t* buffers, int32_t* leased,
+                   uint64_t* hits, uint64_t* misses);
 
-/* Lease a free slot (blocking up to timeout_ms for an in-flight one to complete; -1 = forever).
- * Returns the slot index in *slot and its host pointer in *host. RW4_ETIMEOUT if none frees. */
-int rw4_ring_acquire(rw4_ring* ring, int64_t timeout_ms, int32_t* slot, void** host);
-
-/* Copy `n` bytes from host memory `src` into slot `slot` at byte `offset` (host memcpy on the
- * calling thread; io workers may call this). */
-int rw4_ring_stage(rw4_ring* ring, int32_t slot, size_t offset, const void* src, size_t n);
-
-/* Issue the H2D copy of bytes [0, n) of `slot` to device `dst`, split into chunks of
- * chunk_bytes (0 = one copy) spread round-robin over the ring's copy streams, and record the
- * slot's completion event.  The slot stays leased until that event fires. */
-int rw4_ring_submit(rw4_ring* ring, int32_t slot, void* dst, size_t n, size_t chunk_bytes);
-
-/* Make `stream` wait (device-side) for slot `slot`'s copies; never blocks the host. */
-int rw4_ring_wait(rw4_ring* ring, int32_t slot, void* stream);
-
-/* Release a slot once its copy has completed: returns 1 if released, 0 if still in flight
- * (non-blocking), and blocks up to timeout_ms when block != 0 (RW4_ETIMEOUT if it does not
- * complete in time). */
-int rw4_ring_release(rw4_ring* ring, int32_t slot, int32_t block, int64_t timeout_ms);
-
-/* Counters: bytes submitted, copies issued, acquire stalls, slots in flight. */
-int rw4_ring_stats(rw4_ring* ring, uint64_t* bytes, uint64_t* copies, uint64_t* stalls,
+/* Transfer engine for `device` with `copy_streams` (1..8) non-blocking copy streams. */
+int rw4_xfer_create(int32_t device, int32_t copy_streams, rw4_xfer** out);
+int rw4_xfer_destroy(rw4_xfer* x);
+/* Async H2D copy of n bytes host -> device, chunked (chunk_bytes = 0: one copy), after the copy
+ * streams have waited for `after_stream`'s work so far when after_stream != NULL (used to keep a
+ * reused device buffer from being overwritten while compute still reads it).  *ticket identifies
+ * the send. */
+int rw4_xfer_send(rw4_xfer* x, void* dst, const void* src, size_t n, size_t chunk_bytes,
+                  void* after_stream, uint64_t* ticket);
+/* Make `stream` wait device-side for the ticket's copies. */
+int rw4_xfer_wait(rw4_xfer* x, uint64_t ticket, void* stream);
+/* 1 if the ticket's copies completed, 0 if still in flight (never blocks). */
+int rw4_xfer_query(rw4_xfer* x, uint64_t ticket);
+/* Block until the ticket completes or timeout_ms passes (-1 = no limit): RW4_ETIMEOUT then. */
+int rw4_xfer_sync(rw4_xfer* x, uint64_t ticket, int64_t timeout_ms);
+/* Counters: sends, bytes, chunks, tickets still tracked. */
+int rw4_xfer_stats(rw4_xfer* x, uint64_t* sends, uint64_t* bytes, uint64_t* chunks,
                    int32_t* in_flight);
 
 #ifdef __cplusplus

@@ -45,22 +45,30 @@ SIGNATURES = {
     "rw4_linear_path": (ctypes.c_int, [_i64, _i64, _i64]),
     "rw4_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _i32, _c_void_p]),
     "rw4_moe_permute": (ctypes.c_int, [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p,
-                                       _c_void_p]),
+                                       _c_void_p, _c_void_p]),
     "rw4_moe_gather": (ctypes.c_int, [_c_void_p, _c_void_p, _i64, _i32, _i64, _c_void_p,
                                       _c_void_p]),
     "rw4_moe_grouped": (ctypes.c_int, [_c_void_p, _c_void_p, _i32, _i64, _c_void_p, _c_void_p,
                                        _c_void_p, _i64, _i64, _i32, _i32, _c_void_p, _c_void_p]),
-    "rw4_moe_combine": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i32, _i64, _i32, _i64,
-                                       _c_void_p, _c_void_p]),
-    "rw4_ring_create": (ctypes.c_int, [_size, _i32, _i32, _i32, ctypes.POINTER(_c_void_p)]),
-    "rw4_ring_destroy": (ctypes.c_int, [_c_void_p]),
-    "rw4_ring_acquire": (ctypes.c_int, [_c_void_p, _i64, ctypes.POINTER(_i32),
-                                        ctypes.POINTER(_c_void_p)]),
-    "rw4_ring_stage": (ctypes.c_int, [_c_void_p, _i32, _size, _c_void_p, _size]),
-    "rw4_ring_submit": (ctypes.c_int, [_c_void_p, _i32, _c_void_p, _size, _size]),
-    "rw4_ring_wait": (ctypes.c_int, [_c_void_p, _i32, _c_void_p]),
-    "rw4_ring_release": (ctypes.c_int, [_c_void_p, _i32, _i32, _i64]),
-    "rw4_ring_stats": (ctypes.c_int, [_c_void_p, ctypes.POINTER(ctypes.c_uint64),
+    "rw4_moe_combine": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64,
+                                       _i32, _i64, _c_void_p, _c_void_p]),
+    "rw4_pool_create": (ctypes.c_int, [_size, ctypes.POINTER(_c_void_p)]),
+    "rw4_pool_destroy": (ctypes.c_int, [_c_void_p]),
+    "rw4_pool_lease": (ctypes.c_int, [_c_void_p, _size, ctypes.POINTER(_i32),
+                                      ctypes.POINTER(_c_void_p)]),
+    "rw4_pool_release": (ctypes.c_int, [_c_void_p, _i32]),
+    "rw4_pool_stats": (ctypes.c_int, [_c_void_p, ctypes.POINTER(ctypes.c_uint64),
+                                      ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                                      ctypes.POINTER(ctypes.c_uint64),
+                                      ctypes.POINTER(ctypes.c_uint64)]),
+    "rw4_xfer_create": (ctypes.c_int, [_i32, _i32, ctypes.POINTER(_c_void_p)]),
+    "rw4_xfer_destroy": (ctypes.c_int, [_c_void_p]),
+    "rw4_xfer_send": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _size, _size, _c_void_p,
+                                     ctypes.POINTER(ctypes.c_uint64)]),
+    "rw4_xfer_wait": (ctypes.c_int, [_c_void_p, ctypes.c_uint64, _c_void_p]),
+    "rw4_xfer_query": (ctypes.c_int, [_c_void_p, ctypes.c_uint64]),
+    "rw4_xfer_sync": (ctypes.c_int, [_c_void_p, ctypes.c_uint64, _i64]),
+    "rw4_xfer_stats": (ctypes.c_int, [_c_void_p, ctypes.POINTER(ctypes.c_uint64),
                                       ctypes.POINTER(ctypes.c_uint64),
                                       ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(_i32)]),
 }

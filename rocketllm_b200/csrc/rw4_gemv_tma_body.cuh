@@ -1,0 +1,262 @@
+// Body of the TMA-fed RW4 dequant-GEMV, shared by the dense entry point (rw4_gemv_tma.cu) and the
+// grouped routed-expert entry point (rw4_moe.cu).
+//
+//   producer warp (one elected lane)      S-stage ring in shared memory          8 consumer warps
+//   wait empty[s] ---------------------> codes  [2 boxes x 16R rows x 128 B]  --> wait full[s]
+//   expect_tx(full[s]); TMA loads        scales [16R rows x 8 fp16]              copy 2x8 B codes +
+//   (cp.async.bulk.tensor.2d, L2        zeros  [16R rows x 8 fp16]              scales to registers
+//    evict-first hint)                                                            arrive empty[s]
+//                                                                                 MMA + epilogue
+//
+// A stage is 512 values of K (8 groups) of the CTA's 16R rows; consumer warp w always takes group w
+// of the stage, accumulates over all stages, and the 8 partial sums are combined in shared memory
+// at the end (deterministic, no atomics, no scratch memory).  Arithmetic: codes enter the tensor
+// cores as bf16 (128 + c) (rw4_gemv_frag.cuh), each group's fp32 accumulator is scaled by its
+// fp16 scale and the zero term uses the group's sum of x from an all-ones MMA.  The code boxes use
+// the 128-byte TMA swizzle (16-byte chunk index XOR row % 8), which keeps the consumers' 8-byte
+// shared loads within the two wavefronts 256 bytes need.  Rows past the weight's end are
+// zero-filled by the TMA unit and never stored.
+//
+// SWIGLU variant (R == 2): tile 0 holds rows [r0, r0+16) of the gate half of a stacked gate/up
+// weight and tile 1 the matching up rows [r0+I, r0+I+16); the epilogue writes
+// bf16(bf16(silu(bf16(g))) * bf16(u)), the rounding sequence of the bf16 model's own
+// act_fn(gate) * up (transformers models/mixtral/modeling_mixtral.py:84-91).
+//
+// Every mbarrier wait is bounded (rw4_tma.cuh); on a timeout the CTA drains its own copies, writes
+// nothing and sets the library's device status word.
+#pragma once
+
+#include "rw4_gemv_frag.cuh"
+#include "rw4_tma.cuh"
+
+namespace rw4 {
+namespace gemv_tma {
+
+constexpr int kConsumers = 8;                 // consumer warps = groups per stage
+constexpr int kThreads = 32 * (kConsumers + 1);
+constexpr int kStageK = 64 * kConsumers;      // 512 values of K per stage
+
+template <int R, int S>
+struct Layout {
+  static constexpr int BR = 16 * R;                   // rows per CTA
+  static constexpr int kCodeBox = BR * 128;           // one box: BR rows x 128 bytes (256 k)
+  static constexpr int kCodeStage = 2 * kCodeBox;
+  static constexpr int kScaleStage = BR * 16;         // BR rows x 8 fp16
+  static constexpr int kCodes = 0;
+  static constexpr int kScales = S * kCodeStage;
+  static constexpr int kZeros = kScales + S * kScaleStage;
+  static constexpr int kBars = kZeros + S * kScaleStage;
+  static constexpr int kBytes = kBars + 2 * S * 8;
+  static constexpr int kStageTx = kCodeStage + 2 * kScaleStage;
+  static constexpr int kDynSmem = kBytes + 1024;      // slack to align the ring to 1024 bytes
+};
+
+// x: this slice's activation rows (Ml <= 16 of them, row stride K); y: output rows (stride ldy).
+// Plain: writes y[m, r0 + r] for r0 + r < n_out.  SWIGLU: writes y[m, r0 + r] for r0 + r < n_out
+// (= I) from weight rows r0 + r (gate) and r0 + I + r (up).
+template <int NT, int R, int S, bool SWIGLU>
+__device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensorMap* tm_scale,
+                                     const CUtensorMap* tm_zero,
+                                     const __nv_bfloat16* __restrict__ x, int Ml, int K,
+                                     __nv_bfloat16* __restrict__ y, int64_t ldy, int r0,
+                                     int n_out, int up_offset, unsigned int* status) {
+  using namespace rw4::frag;
+  using L = Layout<R, S>;
+  static_assert(!SWIGLU || R == 2, "the SwiGLU epilogue pairs one gate tile with one up tile");
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  __shared__ int aborted;
+  const uint32_t sbase = smem_addr(smem);
+  const uint32_t full0 = sbase + L::kBars;
+  const uint32_t empty0 = full0 + 8 * S;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nstages = K / kStageK;
+
+  if (threadIdx.x == 0) {
+    aborted = 0;
+    for (int s = 0; s < S; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, kConsumers);
+    }
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  float out[R][NT][4];
+#pragma unroll
+  for (int rt = 0; rt < R; ++rt)
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) out[rt][nt][e] = 0.f;
+
+  if (warp == kConsumers) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      prefetch_tensormap(tm_codes);
+      prefetch_tensormap(tm_scale);
+      prefetch_tensormap(tm_zero);
+      const uint64_t pol = policy_evict_first();
+      int issued = 0;
+      for (int s = 0; s < nstages; ++s) {
+        const int st = s % S;
+        const uint32_t par = ((s / S) & 1) ^ 1;
+        if (!mbar_wait(empty0 + 8 * st, par, status)) {
+          aborted = 1;
+          break;
+        }
+        const uint32_t fb = full0 + 8 * st;
+        mbar_arrive_expect_tx(fb, L::kStageTx);
+        const uint32_t cdst = sbase + L::kCodes + st * L::kCodeStage;
+        const uint32_t sdst = sbase + L::kScales + st * L::kScaleStage;
+        const uint32_t zdst = sbase + L::kZeros + st * L::kScaleStage;
+        const int kx = s * (kStageK / 2);
+        if (SWIGLU) {
+          // 16-row boxes: gate tile then up tile (2048 bytes apart, swizzle phase unchanged).
+          const int ru = r0 + up_offset;
+          tma_load_2d_hint(cdst, tm_codes, kx, r0, fb, pol);
+          tma_load_2d_hint(cdst + 2048, tm_codes, kx, ru, fb, pol);
+          tma_load_2d_hint(cdst + L::kCodeBox, tm_codes, kx + 128, r0, fb, pol);
+          tma_load_2d_hint(cdst + L::kCodeBox + 2048, tm_codes, kx + 128, ru, fb, pol);
+          tma_load_2d_hint(sdst, tm_scale, s * kConsumers, r0, fb, pol);
+          tma_load_2d_hint(sdst + 256, tm_scale, s * kConsumers, ru, fb, pol);
+          tma_load_2d_hint(zdst, tm_zero, s * kConsumers, r0, fb, pol);
+          tma_load_2d_hint(zdst + 256, tm_zero, s * kConsumers, ru, fb, pol);
+        } else {
+          tma_load_2d_hint(cdst, tm_codes, kx, r0, fb, pol);
+          tma_load_2d_hint(cdst + L::kCodeBox, tm_codes, kx + 128, r0, fb, pol);
+          tma_load_2d_hint(sdst, tm_scale, s * kConsumers, r0, fb, pol);
+          tma_load_2d_hint(zdst, tm_zero, s * kConsumers, r0, fb, pol);
+        }
+        issued = s + 1;
+      }
+      // Drain: never leave the CTA with copies still landing in its shared memory.
+      for (int s = max(0, issued - S); s < issued; ++s)
+        mbar_wait(full0 + 8 * (s % S), (s / S) & 1, status);
+    }
+  } else {
+    // ---------------- consumers ----------------
+    const int g = lane >> 2, t = lane & 3;
+    const int w = warp;              // group of the stage this warp owns
+    const int half = w >> 2, q = w & 3;
+    const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
+    const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < nstages; ++s) {
+      const int st = s % S;
+      if (!mbar_wait(full0 + 8 * st, (s / S) & 1, status)) {
+        aborted = 1;
+        break;
+      }
+      const uint8_t* cbase = smem + L::kCodes + st * L::kCodeStage + half * L::kCodeBox;
+      const __half* sc = reinterpret_cast<const __half*>(smem + L::kScales + st * L::kScaleStage);
+      const __half* zr = reinterpret_cast<const __half*>(smem + L::kZeros + st * L::kScaleStage);
+      uint2 wa[R], wb[R];
+      float s_a[R], s_b[R], z_a[R], z_b[R];
+#pragma unroll
+      for (int rt = 0; rt < R; ++rt) {
+        const int ra = 16 * rt + g, rb = ra + 8;
+        const int chunk = 2 * q + (t >> 1);
+        wa[rt] = *reinterpret_cast<const uint2*>(cbase + ra * 128 + ((chunk ^ (ra & 7)) << 4) +
+                                                 8 * (t & 1));
+        wb[rt] = *reinterpret_cast<const uint2*>(cbase + rb * 128 + ((chunk ^ (rb & 7)) << 4) +
+                                                 8 * (t & 1));
+        s_a[rt] = __half2float(sc[ra * 8 + w]);
+        s_b[rt] = __half2float(sc[rb * 8 + w]);
+        z_a[rt] = fmaf(-128.f, s_a[rt], __half2float(zr[ra * 8 + w]));
+        z_b[rt] = fmaf(-128.f, s_b[rt], __half2float(zr[rb * 8 + w]));
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * st);
+
+      // x fragment of group (s * 8 + w) and its sums over the group
+      const int kofs = s * kStageK + 64 * w + 16 * t;
+      uint32_t b[NT][4][2];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        const int m = nt * 8 + g;
+        load_x_frag(x + (int64_t)min(m, Ml - 1) * K + kofs, m < Ml, b[nt]);
+      }
+      float xs[NT][4];
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        mma_bf16_16816(xs[nt], ones, b[nt][0][0], b[nt][0][1], zero4);
+#pragma unroll
+        for (int j = 1; j < 4; ++j) mma_bf16_16816(xs[nt], ones, b[nt][j][0], b[nt][j][1], xs[nt]);
+      }
+#pragma unroll
+      for (int rt = 0; rt < R; ++rt) {
+        float acc[NT][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint32_t a[4];
+          a_frag(wa[rt], wb[rt], j, a);
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            if (j == 0)
+              mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], zero4);
+            else
+              mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], acc[nt]);
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          out[rt][nt][0] = fmaf(s_a[rt], acc[nt][0], fmaf(z_a[rt], xs[nt][0], out[rt][nt][0]));
+          out[rt][nt][1] = fmaf(s_a[rt], acc[nt][1], fmaf(z_a[rt], xs[nt][1], out[rt][nt][1]));
+          out[rt][nt][2] = fmaf(s_b[rt], acc[nt][2], fmaf(z_b[rt], xs[nt][2], out[rt][nt][2]));
+          out[rt][nt][3] = fmaf(s_b[rt], acc[nt][3], fmaf(z_b[rt], xs[nt][3], out[rt][nt][3]));
+        }
+      }
+    }
+  }
+
+  // ---- combine the consumer warps' partial sums (ring memory reused) and write bf16 -----------
+  __syncthreads();
+  if (aborted) return;
+  constexpr int kCols = 16 * NT + 1;
+  float* red = reinterpret_cast<float*>(smem);  // [kConsumers][BR][kCols]
+  if (warp < kConsumers) {
+    const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+    for (int rt = 0; rt < R; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float* base = red + (warp * L::BR + 16 * rt + g) * kCols + nt * 8 + 2 * t;
+        base[0] = out[rt][nt][0];
+        base[1] = out[rt][nt][1];
+        base[8 * kCols] = out[rt][nt][2];
+        base[8 * kCols + 1] = out[rt][nt][3];
+      }
+  }
+  __syncthreads();
+  constexpr int kRowsOut = SWIGLU ? 16 : L::BR;
+  for (int o = threadIdx.x; o < kRowsOut * 16 * NT; o += kThreads) {
+    const int r = o % kRowsOut;
+    const int m = o / kRowsOut;
+    const int n = r0 + r;
+    if (n < n_out && m < Ml) {
+      float v = 0.f;
+      if (SWIGLU) {
+        float gsum = 0.f, usum = 0.f;
+#pragma unroll
+        for (int w = 0; w < kConsumers; ++w) {
+          gsum += red[(w * L::BR + r) * kCols + m];
+          usum += red[(w * L::BR + 16 + r) * kCols + m];
+        }
+        const float gb = __bfloat162float(__float2bfloat16_rn(gsum));
+        const float ub = __bfloat162float(__float2bfloat16_rn(usum));
+        const float act = __bfloat162float(__float2bfloat16_rn(gb / (1.f + expf(-gb))));
+        v = act * ub;
+      } else {
+#pragma unroll
+        for (int w = 0; w < kConsumers; ++w) v += red[(w * L::BR + r) * kCols + m];
+      }
+      y[(int64_t)m * ldy + n] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+}  // namespace gemv_tma
+}  // namespace rw4

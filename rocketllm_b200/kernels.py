@@ -5,6 +5,8 @@ and calls the matching ``rw4_*`` entry point on ``torch.cuda.current_stream()``.
 RocketLLM's int4 codec (``rocketllm/quant/kv_cache.py:190-272``) applied to a Linear weight
 ``W[N, K]``: ``packed`` uint8 ``[N, Kp/2]``, ``scale``/``zero`` fp16 ``[N, Kp/64]``.
 """
+import ctypes
+
 import torch
 
 from . import _lib
@@ -99,3 +101,71 @@ def linear(x, packed, scale, zero, out=None):
 def linear_path(m, k, n):
     """Which kernel :func:`linear` launches: 1 GEMV, 2 tcgen05 GEMM, 3 GEMV slices."""
     return _lib.check(_lib.lib().rw4_linear_path(m, k, n), "rw4_linear_path")
+
+
+def device_status(clear=True):
+    """The library's device status word (bit 1: a bounded wait timed out). Synchronises."""
+    word = ctypes.c_uint32()
+    _lib.call("rw4_device_status", ctypes.byref(word), int(clear), _stream())
+    return word.value
+
+
+# ---- routed experts ------------------------------------------------------------------------------
+
+def moe_permute(topk_idx, num_experts):
+    """``(perm, inv, offsets)`` int32 for ``topk_idx`` int64 ``[T, k]`` (stable, by expert)."""
+    _require_cuda(topk_idx)
+    if topk_idx.dtype != torch.int64:
+        raise TypeError("topk_idx must be int64")
+    t, k = topk_idx.shape
+    dev = topk_idx.device
+    perm = torch.empty(t * k, dtype=torch.int32, device=dev)
+    inv = torch.empty(t * k, dtype=torch.int32, device=dev)
+    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+    _lib.call("rw4_moe_permute", topk_idx.data_ptr(), t, k, num_experts, perm.data_ptr(),
+              inv.data_ptr(), offsets.data_ptr(), _stream())
+    return perm, inv, offsets
+
+
+def moe_gather(x, perm, k):
+    """``x_perm[row] = x[perm[row] // k]`` for bf16 ``x [T, H]``."""
+    _require_cuda(x, perm)
+    t, h = x.shape
+    out = torch.empty((perm.numel(), h), dtype=x.dtype, device=x.device)
+    _lib.call("rw4_moe_gather", x.data_ptr(), perm.data_ptr(), t, k, h, out.data_ptr(), _stream())
+    return out
+
+
+def moe_grouped(x_perm, offsets, weights, act=0, max_rows=None, out=None):
+    """Grouped RW4 GEMV over routed experts.
+
+    ``weights`` is a list of ``(packed, scale, zero)`` per expert (all ``[N, K]``); ``act=1`` treats
+    them as stacked gate/up (``N = 2I``) and returns the SwiGLU activation ``[rows, I]``.
+    """
+    _require_cuda(x_perm, offsets)
+    e = len(weights)
+    n = weights[0][0].shape[0]
+    k = x_perm.shape[1]
+    rows = x_perm.shape[0]
+    n_out = n // 2 if act == 1 else n
+    if out is None:
+        out = torch.empty((rows, n_out), dtype=torch.bfloat16, device=x_perm.device)
+    ptrs = [(ctypes.c_void_p * e)(*[w[i].data_ptr() for w in weights]) for i in range(3)]
+    _lib.call("rw4_moe_grouped", x_perm.data_ptr(), offsets.data_ptr(), e,
+              rows if max_rows is None else int(max_rows), ptrs[0], ptrs[1], ptrs[2], k, n, 64,
+              int(act), out.data_ptr(), _stream())
+    return out
+
+
+def moe_combine(y_perm, inv, topk_idx, topk_w, out=None):
+    """Weighted combine of expert rows back to tokens, bf16 ``[T, H]``."""
+    _require_cuda(y_perm, inv, topk_w)
+    t, k = topk_w.shape
+    h = y_perm.shape[1]
+    if out is None:
+        out = torch.empty((t, h), dtype=torch.bfloat16, device=y_perm.device)
+    wd = {torch.float32: _lib.RW4_F32, torch.bfloat16: _lib.RW4_BF16}[topk_w.dtype]
+    _lib.call("rw4_moe_combine", y_perm.data_ptr(), inv.data_ptr(),
+              topk_idx.data_ptr() if topk_idx is not None else None, topk_w.data_ptr(), wd, t, k,
+              h, out.data_ptr(), _stream())
+    return out

@@ -21,7 +21,7 @@ def declared_symbols():
 def test_library_loads_and_exports_every_declared_symbol():
     lib = _lib.lib()
     names = declared_symbols()
-    assert "rw4_linear" in names and "rw4_ring_submit" in names
+    assert "rw4_linear" in names and "rw4_xfer_send" in names and "rw4_moe_grouped" in names
     missing = [n for n in names if getattr(lib, n, None) is None]
     assert not missing, f"declared in rw4.h but not exported: {missing}"
     assert set(names) <= set(_lib.SIGNATURES), "ctypes signatures out of sync with rw4.h"
