@@ -1,0 +1,403 @@
+"""Benchmark of the RW4 4-bit dequant-GEMV hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl rw4|reference]
+
+Workload (the isolated 4-bit dequant-matmul sweep at decode batch M=1): the five RW4 weight shapes
+(K, N) = (4096, 4096), (4096, 14336), (14336, 4096), (8192, 28672), (16384, 53248) -- uniform
+random codes, scales U[0.005, 0.02], zero = -8 * scale, group 64 -- times a bf16 N(0, 1) activation
+row.  One step = one rw4_linear call per shape (five kernel launches).  698 MB of packed weights per
+step, so every step streams its inputs from HBM (inputs larger than the 126 MB L2).
+
+Printed metric: whole-job GB/s of algorithmic bytes (codes + fp16 scales + fp16 zeros + x + y,
+each counted once).  `roofline` is the dominant launch (16384 x 53248) timed with CUDA events inside
+the timed region against the measured HBM copy bandwidth.  `e2e` is the same metric through the
+public API with the weights in pinned host memory: every step streams them through the transfer
+engine (chunked copies on dedicated copy streams) into two device slots while the GEMV of the
+previous weight runs, then reads the outputs back.  `cpu_baseline` / `--impl reference` time the
+CPU oracle (the reference's dequantize-then-matmul algorithm) on the host cores over a row sample.
+
+Multi-GPU (torchrun): every rank runs the same workload on its own GPU (weak scaling, no data-path
+collective); the step time is the max over ranks.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+SHAPES = ((4096, 4096), (4096, 14336), (14336, 4096), (8192, 28672), (16384, 53248))
+M = 1
+GROUP = 64
+DOMINANT = 4
+METRIC = "dequant-GEMV HBM GB/s (4-bit RW4 group 64, decode M=1, isolated sweep shapes)"
+FALLBACK_HBM_GBS = 6650.0
+TRAFFIC_FILE = os.path.join(ROOT, "profiles", "gemv_traffic.json")
+
+
+def alg_bytes(m, k, n):
+    return n * k // 2 + 2 * 2 * (k // GROUP) * n + 2 * m * k + 2 * m * n
+
+
+STEP_BYTES = sum(alg_bytes(M, k, n) for k, n in SHAPES)
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def measured_peak():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            peaks = json.load(f)
+        return float(peaks["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001 - absent on a box the driver did not prepare
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_per_launch():
+    try:
+        with open(TRAFFIC_FILE) as f:
+            rec = json.load(f)
+        return float(rec["dram_bytes_per_launch"])
+    except Exception:  # noqa: BLE001
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+        except Exception:  # noqa: BLE001 - no nvidia-smi: no clock record
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:  # noqa: BLE001
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        rows = [r.split(",") for r in self.file.read().strip().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+                for name, val in zip(names, r[5:9]):
+                    if val.strip().lower() == "active":
+                        reasons.add(name)
+            except (ValueError, IndexError):
+                continue
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------------------
+# CPU: the oracle (test infrastructure) as the reported baseline and the reference arm
+# ----------------------------------------------------------------------------------------------
+
+def cpu_sample_step(pool, weights, x, threads):
+    """Dequantize-then-matmul (fp32) of the sampled rows of every shape on `threads` host threads:
+    the reference's dequant-to-scratch + F.linear, restated by the oracle."""
+    from oracle import rw4_oracle as o
+
+    def one(args):
+        xi, (p, s, z) = args
+        return xi @ o.dequantize(p, s, z).T
+
+    jobs = []
+    for xi, (p, s, z) in zip(x, weights):
+        for c in np.array_split(np.arange(p.shape[0]), threads):
+            if c.size:
+                jobs.append((xi, (p[c], s[c], z[c])))
+    list(pool.map(one, jobs))
+
+
+def cpu_workload(rows_per_shape, seed=0):
+    from oracle import rw4_oracle as o
+    weights, xs, nbytes = [], [], 0
+    rng = np.random.default_rng(seed)
+    for k, n in SHAPES:
+        rows = min(n, rows_per_shape)
+        weights.append(o.synthetic_weight(rows, k, GROUP, seed=seed + k + n))
+        xs.append(rng.standard_normal((M, k)).astype(np.float32))
+        nbytes += alg_bytes(M, k, rows)
+    return weights, xs, nbytes
+
+
+def run_cpu(steps, warmup, rows_per_shape=None, budget_s=None):
+    """Time the CPU oracle.  With `budget_s`, the per-step row sample is sized from a calibration
+    step so that warmup + steps take about `budget_s` seconds."""
+    from concurrent.futures import ThreadPoolExecutor
+    threads = os.cpu_count() or 1
+    with ThreadPoolExecutor(threads) as pool:
+        if budget_s is not None:
+            weights, xs, _ = cpu_workload(256)
+            t0 = time.perf_counter()
+            cpu_sample_step(pool, weights, xs, threads)
+            per_row = (time.perf_counter() - t0) / 256
+            rows_per_shape = int(max(8, min(8192, budget_s / max(1, steps + warmup) / per_row)))
+        weights, xs, nbytes = cpu_workload(rows_per_shape)
+        for _ in range(warmup):
+            cpu_sample_step(pool, weights, xs, threads)
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            cpu_sample_step(pool, weights, xs, threads)
+        dt = (time.perf_counter() - t0) / steps
+    sample = (f"dequantize + fp32 matvec of {rows_per_shape} sampled rows of each of the five "
+              f"shapes at M=1 ({nbytes / 1e6:.2f} MB algorithmic per step), numpy oracle, "
+              f"{threads} threads")
+    return nbytes / dt / 1e9, dt * 1e3, threads, sample
+
+
+def reference_arm(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    value, ms, threads, sample = run_cpu(args.steps, args.warmup, budget_s=90.0)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": config_block(),
+            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                             "kind": "port", "sample": sample},
+            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_block():
+    return {"workload": "isolated 4-bit dequant-matmul sweep, decode M=1, five weight shapes per "
+                        "step",
+            "shapes_kn": [list(s) for s in SHAPES], "M": M, "group": GROUP,
+            "weights": "uniform random codes, scale U[0.005,0.02], zero=-8*scale",
+            "activations": "bf16 N(0,1)",
+            "l2": "inputs larger than L2 (698 MB of weights per step, no flush needed)"}
+
+
+# ----------------------------------------------------------------------------------------------
+# GPU arm
+# ----------------------------------------------------------------------------------------------
+
+def h2d_probe(device, nbytes=256 << 20, reps=10):
+    """Best-of-N pinned host->device copy bandwidth (the method of the reference's profile
+    probe, rocketllm/hw/profile.py:245-269, with more iterations)."""
+    src = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    best = 0.0
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize()
+        best = max(best, nbytes / (a.elapsed_time(b) * 1e-3) / 1e9)
+    del src, dst
+    return best
+
+
+def rw4_arm(args):
+    from rocketllm_b200 import kernels
+    from rocketllm_b200.streaming import WeightTransfer
+    from rocketllm_b200.synthetic import make_activation, make_weight
+
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    weights = [make_weight(n, k, device=device, seed=10 * i + rank) for i, (k, n) in
+               enumerate(SHAPES)]
+    xs = [make_activation(M, k, device=device, seed=100 + i) for i, (k, n) in enumerate(SHAPES)]
+    ys = [torch.empty(M, n, dtype=torch.bfloat16, device=device) for k, n in SHAPES]
+
+    def step(ev=None):
+        for i in range(len(SHAPES)):
+            if ev is not None and i == DOMINANT:
+                ev[0].record()
+            kernels.linear(xs[i], *weights[i], out=ys[i])
+            if ev is not None and i == DOMINANT:
+                ev[1].record()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if kernels.device_status():
+        raise RuntimeError("a kernel reported a timed-out wait during warm-up")
+
+    dom = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks = ClockSampler(local)
+    barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    time.sleep(0.25)  # let the sampler start before the timed region
+    start.record()
+    for s in range(args.steps):
+        step(dom[s])
+    end.record()
+    torch.cuda.synchronize()
+    barrier()
+    clock = clocks.stop()
+    ms_step = start.elapsed_time(end) / args.steps
+    dom_ms = sum(a.elapsed_time(b) for a, b in dom) / args.steps
+    if dist is not None:
+        t = torch.tensor([ms_step], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms_step = float(t.item())
+
+    status = kernels.device_status()
+
+    # ---- end to end: weights streamed from pinned host memory each step ----
+    host_w = [tuple(t.cpu().pin_memory() for t in w) for w in weights]
+    host_x = [x.cpu().pin_memory() for x in xs]
+    host_y = [torch.empty(M, n, dtype=torch.bfloat16).pin_memory() for k, n in SHAPES]
+    xfer = WeightTransfer(device=device, copy_streams=2, chunk_bytes=16 << 20)
+    cap = [max(hw[i].numel() * hw[i].element_size() for hw in host_w) for i in range(3)]
+    slots = [[torch.empty(c, dtype=torch.uint8, device=device) for c in cap] for _ in range(2)]
+    dev_x = [torch.empty_like(x) for x in xs]
+    compute = torch.cuda.current_stream()
+
+    def e2e_step():
+        for i, (k, n) in enumerate(SHAPES):
+            dev_x[i].copy_(host_x[i], non_blocking=True)
+            slot = slots[i % 2]
+            views = []
+            for j, t in enumerate(host_w[i]):
+                nb = t.numel() * t.element_size()
+                dst = slot[j][:nb]
+                h = xfer.send_buffer(t.view(torch.uint8).view(-1), out=dst, after=compute)
+                h.resolve(compute)
+                views.append(dst.view(t.dtype).view(t.shape))
+            kernels.linear(dev_x[i], *views, out=ys[i])
+            host_y[i].copy_(ys[i], non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    b.record()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = a.elapsed_time(b) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    h2d = sum(sum(t.numel() * t.element_size() for t in hw) for hw in host_w) + sum(
+        x.numel() * 2 for x in host_x)
+    d2h = sum(y.numel() * 2 for y in host_y)
+    h2d_peak = h2d_probe(device) if rank == 0 else None
+    xfer.close()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        value, ms, threads, sample = run_cpu(max(1, args.cpu_steps), 1, budget_s=args.cpu_seconds)
+        cpu = {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "sample": sample}
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        k, n = SHAPES[DOMINANT]
+        achieved = alg_bytes(M, k, n) / (dom_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(world * STEP_BYTES / (ms_step * 1e-3) / 1e9, 2),
+            "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms_step, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": config_block(),
+            "roofline": {"bound": "hbm", "kernel": f"rw4 gemv (K={k}, N={n}, M={M})",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "traffic": traffic_per_launch(),
+                         "algorithmic_bytes": alg_bytes(M, k, n),
+                         "avg_launch_ms": round(dom_ms, 5)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(world * STEP_BYTES / (e2e_ms * 1e-3) / 1e9, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms, 4), "path": "pinned host weights -> rw4_xfer "
+                    "(2 copy streams, 16 MB chunks) -> 2 device slots -> rw4_linear -> D2H",
+                    "h2d_gbs": round(h2d / (e2e_ms * 1e-3) / 1e9, 2),
+                    "h2d_probe_gbs": round(h2d_peak, 2) if h2d_peak else None,
+                    "h2d_frac": round(h2d / (e2e_ms * 1e-3) / 1e9 / h2d_peak, 4)
+                    if h2d_peak else None},
+            "gpu_launches": len(SHAPES) * args.steps,
+            "clocks": clock,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("rw4", "reference"), default="rw4")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="approximate CPU time of the CPU baseline leg")
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+    return rw4_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -172,8 +172,8 @@ int rw4_xfer_create(int32_t device, int32_t copy_streams, rw4_xfer** out);
 int rw4_xfer_destroy(rw4_xfer* x);
 /* Async H2D copy of n bytes host -> device, chunked (chunk_bytes = 0: one copy), after the copy
  * streams have waited for `after_stream`'s work so far when after_stream != NULL (used to keep a
- * reused device buffer from being overwritten while compute still reads it).  *ticket identifies
- * the send. */
+ * reused device buffer from being overwritten while compute still reads it; pass cudaStreamLegacy,
+ * (void*)1, to order after the legacy default stream).  *ticket identifies the send. */
 int rw4_xfer_send(rw4_xfer* x, void* dst, const void* src, size_t n, size_t chunk_bytes,
                   void* after_stream, uint64_t* ticket);
 /* Make `stream` wait device-side for the ticket's copies. */

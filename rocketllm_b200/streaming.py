@@ -259,7 +259,9 @@ class WeightTransfer:
         elif out.numel() * out.element_size() < nbytes:
             raise ValueError("send_buffer: destination smaller than the host buffer")
         ticket = ctypes.c_uint64()
-        after_ptr = after.cuda_stream if after is not None else None
+        # NULL means "no ordering" to the C ABI, so the legacy default stream (handle 0) is passed
+        # as cudaStreamLegacy (handle 1).
+        after_ptr = (after.cuda_stream or 1) if after is not None else None
         _lib.call("rw4_xfer_send", self._handle, out.data_ptr(), host.data_ptr(), nbytes,
                   self.chunk_bytes, after_ptr, ctypes.byref(ticket))
         handle = TransferHandle(out, ticket.value, lease, self)
