@@ -18,11 +18,14 @@ def bits(t):
     return t.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
 
 
-def close(y, ref):
+def close(y, ref, rel=1 / 128):
+    """|y - ref| <= rel * |ref| + 2e-3 * rms(ref).  rel = 1/128 is one bf16 rounding; the SwiGLU
+    output passes through three bf16 roundings (gate, up, activation) before the final one, so a
+    one-ulp difference in the gate can move it by up to four ulps: rel = 1/32 there."""
     y = y.float().cpu().numpy()
     rms = float(np.sqrt(np.mean(ref.astype(np.float64) ** 2))) + 1e-12
     err = np.abs(y - ref)
-    bound = np.abs(ref) / 128 + 2e-3 * rms
+    bound = np.abs(ref) * rel + 2e-3 * rms
     assert np.all(err <= bound), f"max err {err.max():.4g}, worst excess {(err - bound).max():.4g}"
 
 
@@ -91,7 +94,7 @@ def test_grouped_matches_oracle(cuda, t, act):
     y = kernels.moe_grouped(xp, offsets, weights, act=act, max_rows=t * k_top)
     torch.cuda.synchronize()
     for rows, ref in oracle_grouped(xp, offsets, weights, act, inter):
-        close(y[rows], ref)
+        close(y[rows], ref, rel=1 / 32 if act == 1 else 1 / 128)
 
 
 def test_combine_reproduces_reference_rounding_order(cuda):
