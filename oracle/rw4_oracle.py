@@ -154,13 +154,18 @@ def dequantize(packed, scale, zero, k=None, out="f32"):
     raise ValueError(out)
 
 
-def linear(x_bf16_bits, packed, scale, zero, k=None):
+def linear(x_bf16_bits, packed, scale, zero, k=None, bf16_weight=False):
     """``y = x . W^T`` in fp32 over the dequantized weight (the reference's dequant-to-scratch
     ``F.linear``; ``rocketllm/quant/registry.py:529-535`` then transformers ``nn.Linear``).
 
+    ``bf16_weight=True`` rounds the dequantized weight to bf16 first -- exactly the weight the
+    reference's bf16 model multiplies by (``dequantize().to(bfloat16)``); the default keeps the
+    exact fp32 weight (the fp32 CPU model's weight).
     Returns fp32 ``[M, N]``; the device returns bf16 and is compared within a tolerance.
     """
     w = dequantize(packed, scale, zero, k=k)
+    if bf16_weight:
+        w = round_bf16(w)
     x = bf16_bits_to_f32(x_bf16_bits)
     return (x.astype(np.float64) @ w.astype(np.float64).T).astype(np.float32)
 

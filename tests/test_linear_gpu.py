@@ -24,11 +24,15 @@ def check_close(y, ref):
 
 
 def oracle_linear(x, packed, scale, zero, rows=None):
+    """The oracle over the weight the selected kernel multiplies by: the tensor-core GEMM uses the
+    reference's bf16-rounded dequantized weight, the GEMV the exact fp32 weight."""
     xb = x.cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
     p, s, z = packed.cpu().numpy(), scale.cpu().numpy(), zero.cpu().numpy()
     if rows is not None:
         p, s, z = p[rows], s[rows], z[rows]
-    return o.linear(xb, p, s, z)
+    m, k = x.shape
+    gemm = kernels.linear_path(m, k, packed.shape[0]) == 2
+    return o.linear(xb, p, s, z, bf16_weight=gemm)
 
 
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 7, 8, 9, 15, 16, 17, 33, 64])
@@ -50,8 +54,19 @@ def test_linear_golden_reference_output(golden, cuda):
     check_close(y, golden["sweep.y_f32"])
 
 
-@pytest.mark.parametrize("k,n", [(16384, 53248), (8192, 28672)])
-@pytest.mark.parametrize("m", [1, 16])
+@pytest.mark.parametrize("m", [17, 64, 255, 256, 300, 512])
+@pytest.mark.parametrize("k,n", [(4096, 4096), (1024, 200)])
+def test_gemm_matches_oracle(cuda, m, k, n):
+    packed, scale, zero = make_weight(n, k, device=cuda, seed=m + n)
+    x = make_activation(m, k, device=cuda, seed=k + m)
+    y = kernels.linear(x, packed, scale, zero)
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    check_close(y, oracle_linear(x, packed, scale, zero))
+
+
+@pytest.mark.parametrize("k,n,m", [(16384, 53248, 1), (16384, 53248, 16), (8192, 28672, 1),
+                                   (8192, 28672, 16), (16384, 53248, 2048), (4096, 14336, 512)])
 def test_linear_full_size_sampled_rows(cuda, k, n, m):
     """Full sweep shapes: the oracle recomputes a seeded sample of output rows."""
     packed, scale, zero = make_weight(n, k, device=cuda, seed=7)
