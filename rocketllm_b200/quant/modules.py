@@ -7,6 +7,8 @@ transformers' experts-implementation registry.  Parameter names follow the check
 suffixes (``weight_packed`` / ``weight_scale`` / ``weight_zero_point``), so a pre-quantized shard
 loads into them by name.  There is no CPU path: a forward on a non-CUDA tensor raises.
 """
+import types
+
 import torch
 from torch import nn
 
@@ -64,11 +66,17 @@ def rw4_experts_params(experts, device=None):
             raise ValueError(f"{name}: K={k} is not a multiple of {GROUP}")
         dev = device if device is not None else dense.device
         del experts._parameters[name]
+        # An empty, non-persistent stand-in keeps code that initialises the dense weight by name
+        # (transformers' _init_weights) working, without a state-dict entry.
+        experts.register_buffer(name, torch.empty(0, device=dev), persistent=False)
         experts.register_parameter(f"{name}_packed", _param((e, n, k // 2), torch.uint8, dev))
         experts.register_parameter(f"{name}_scale", _param((e, n, k // GROUP), torch.float16, dev))
         experts.register_parameter(f"{name}_zero_point",
                                    _param((e, n, k // GROUP), torch.float16, dev))
     experts.rw4 = True
+    # Bound on the instance: transformers may re-resolve config._experts_implementation after the
+    # quantizer ran, and the stock forwards read the dense parameters this module no longer has.
+    experts.forward = types.MethodType(rw4_experts_forward, experts)
     return experts
 
 

@@ -50,7 +50,7 @@ def reference_model(dense, rw4):
 def run_pair(dense, tmp_path, steps=12):
     from transformers import AutoModelForCausalLM
     path = save_rw4_checkpoint(dense, str(tmp_path / "rw4"), device="cuda")
-    rw4 = AutoModelForCausalLM.from_pretrained(path, dtype=torch.bfloat16, device_map="cuda")
+    rw4 = AutoModelForCausalLM.from_pretrained(path, dtype=torch.bfloat16).to("cuda")
     ref = reference_model(dense, rw4)
     ids = torch.randint(0, dense.config.vocab_size, (1, 24),
                         generator=torch.Generator().manual_seed(1)).cuda()

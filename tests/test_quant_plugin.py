@@ -104,7 +104,7 @@ def test_stacked_experts_get_rw4_triples():
     experts = model.model.layers[0].mlp.experts
     assert experts.gate_up_proj_packed.shape == (4, 1024, 256)
     assert experts.down_proj_scale.shape == (4, 512, 8)
-    assert not hasattr(experts, "gate_up_proj")
+    assert experts.gate_up_proj.numel() == 0 and "gate_up_proj" not in experts.state_dict()
     assert model.config._experts_implementation == "rw4"
     assert isinstance(model.model.layers[0].mlp.gate, torch.nn.Module)  # router left alone
     assert not isinstance(model.lm_head, RW4Linear)
@@ -143,3 +143,15 @@ def test_prequantized_checkpoint_loads_by_name_and_has_no_cpu_path(tmp_path):
     assert torch.equal(q.weight_packed, sd["model.layers.1.mlp.up_proj.weight_packed"])
     with pytest.raises(ValueError, match="CUDA"):
         loaded(torch.tensor([[1, 2, 3]]))
+
+
+def test_scales_keep_fp16_through_a_bf16_load(tmp_path):
+    """A bf16 load must not cast the fp16 scale / zero companions (they are part of the format)."""
+    test_prequantized_checkpoint_loads_by_name_and_has_no_cpu_path(tmp_path)
+    from transformers import AutoModelForCausalLM
+    loaded = AutoModelForCausalLM.from_pretrained(str(tmp_path), dtype=torch.bfloat16)
+    lin = loaded.model.layers[0].self_attn.q_proj
+    assert lin.weight_scale.dtype == torch.float16
+    assert lin.weight_zero_point.dtype == torch.float16
+    assert float(lin.weight_scale[0, 0]) == pytest.approx(0.01, rel=1e-3)
+    assert loaded.model.norm.weight.dtype == torch.bfloat16
