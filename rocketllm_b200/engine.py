@@ -1,0 +1,233 @@
+"""Layer streaming engine and the ``AutoModel`` / ``RocketModel`` entry points.
+
+Counterpart of RocketLLM's engine hooks (``rocketllm/base.py``: forward pre-hook ``_pre_hook``
+:1916-1926 -> ``cache.acquire`` -> ``_move_coalesced`` :952-991 -> bind; ``prefetch_window``
+``memory/cache.py:254-272``) for RW4 checkpoints on B200, built the device-first way:
+
+* every streamed decoder layer is packed ONCE into a single pinned host blob (its RW4 codes, fp16
+  scales / zeros and bf16 norms at 256-byte aligned offsets) -- the host tier the reference
+  stages into a leased buffer on every fetch;
+* the device holds ``window`` slots, each the size of the largest blob; layer ``i`` always lives
+  in slot ``i % window`` and its parameters are bound ONCE as views into that slot, so a layer
+  fetch is one chunked host->device send and no Python rebinding;
+* the pre-hook of layer ``i`` makes the compute stream wait (device-side) for layer ``i``'s send
+  and issues the sends of layers ``i+1 .. i+window-1`` into their slots, ordered after the compute
+  already queued (the slot's previous occupant) -- so the next layers cross PCIe while this one
+  computes, and the loop wraps around to layer 0 for the next token.
+
+Transformers still owns the forward, attention, KV cache and ``generate``.  Resident mode (the
+whole model fits the VRAM budget) moves everything to the device and installs no hooks.
+"""
+import os
+
+import torch
+
+from . import quant  # noqa: F401 - registers the rw4 quantizer with transformers
+from .streaming import WeightTransfer
+
+ALIGN = 256
+
+
+class _LayerBlob:
+    __slots__ = ("host", "entries", "nbytes")
+
+    def __init__(self, host, entries, nbytes):
+        self.host = host          # pinned uint8 [nbytes]
+        self.entries = entries    # [(module, leaf, kind, dtype, shape, offset)]
+        self.nbytes = nbytes
+
+
+def _layer_tensors(layer):
+    out = []
+    for mname, module in layer.named_modules():
+        for leaf, p in module._parameters.items():
+            if p is not None:
+                out.append((module, leaf, "param", p))
+        for leaf, b in module._buffers.items():
+            if b is not None and b.numel() and leaf not in module._non_persistent_buffers_set:
+                out.append((module, leaf, "buffer", b))
+    return out
+
+
+def _pack_layer(layer):
+    tensors = _layer_tensors(layer)
+    entries, off = [], 0
+    for module, leaf, kind, t in tensors:
+        off = (off + ALIGN - 1) // ALIGN * ALIGN
+        entries.append((module, leaf, kind, t.dtype, tuple(t.shape), off))
+        off += t.numel() * t.element_size()
+    nbytes = (off + ALIGN - 1) // ALIGN * ALIGN
+    host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    for (module, leaf, kind, dtype, shape, o), (_, _, _, t) in zip(entries, tensors):
+        n = t.numel() * t.element_size()
+        host[o:o + n].copy_(t.detach().contiguous().view(-1).view(torch.uint8))
+    return _LayerBlob(host, entries, nbytes)
+
+
+def _bind(blob, slot):
+    for module, leaf, kind, dtype, shape, off in blob.entries:
+        n = 1
+        for d in shape:
+            n *= d
+        view = slot[off:off + n * torch.empty((), dtype=dtype).element_size()].view(dtype)
+        view = view.view(shape)
+        if kind == "param":
+            module._parameters[leaf] = torch.nn.Parameter(view, requires_grad=False)
+        else:
+            module._buffers[leaf] = view
+
+
+class LayerStreamer:
+    """Streams decoder layers from pinned host blobs through ``window`` device slots."""
+
+    def __init__(self, layers, device, window=2, copy_streams=2, chunk_bytes=16 << 20,
+                 prefetching=True):
+        if window < 1:
+            raise ValueError("window must be >= 1")
+        self.layers = list(layers)
+        self.device = torch.device(device)
+        self.window = min(window, len(self.layers))
+        self.prefetching = prefetching
+        self.blobs = [_pack_layer(layer) for layer in self.layers]
+        self.slot_bytes = max(b.nbytes for b in self.blobs)
+        self.slots = [torch.empty(self.slot_bytes, dtype=torch.uint8, device=self.device)
+                      for _ in range(self.window)]
+        for i, blob in enumerate(self.blobs):
+            _bind(blob, self.slots[i % self.window])
+        self.xfer = WeightTransfer(device=self.device, copy_streams=copy_streams,
+                                   chunk_bytes=chunk_bytes)
+        self.tickets = [None] * len(self.layers)
+        self.resident_slot = [None] * self.window   # which layer's bytes a slot holds (issued)
+        self.fetches = 0
+        self.bytes = 0
+        self.hits = 0
+        self._handles = [layer.register_forward_pre_hook(self._make_pre_hook(i))
+                         for i, layer in enumerate(self.layers)]
+
+    def _send(self, i, compute):
+        s = i % self.window
+        if self.resident_slot[s] == i:
+            return
+        blob = self.blobs[i]
+        handle = self.xfer.send_buffer(blob.host, out=self.slots[s][:blob.nbytes], after=compute)
+        self.tickets[i] = handle
+        self.resident_slot[s] = i
+        self.fetches += 1
+        self.bytes += blob.nbytes
+
+    def _make_pre_hook(self, i):
+        def hook(module, args):
+            compute = torch.cuda.current_stream(self.device)
+            if self.resident_slot[i % self.window] != i:
+                self._send(i, compute)
+            else:
+                self.hits += 1
+            handle = self.tickets[i]
+            if handle is not None:
+                handle.resolve(compute)
+                self.tickets[i] = None
+            if self.prefetching:
+                n = len(self.layers)
+                for d in range(1, self.window):
+                    j = (i + d) % n
+                    # never into the slot of the layer about to run (only possible when the
+                    # layer count is not a multiple of the window and the loop wraps)
+                    if j % self.window != i % self.window:
+                        self._send(j, compute)
+            return None
+        return hook
+
+    def stats(self):
+        return {"layers": len(self.layers), "window": self.window, "slot_bytes": self.slot_bytes,
+                "fetches": self.fetches, "bytes": self.bytes, "slot_hits": self.hits,
+                "transfer": self.xfer.stats()}
+
+    def close(self):
+        for h in self._handles:
+            h.remove()
+        self._handles = []
+        self.xfer.close()
+
+
+def _layers_path(model):
+    for path in ("model.layers", "model.decoder.layers", "transformer.h"):
+        try:
+            model.get_submodule(path)
+            return path
+        except AttributeError:
+            continue
+    raise ValueError("cannot find the decoder layers of this model")
+
+
+def _decoder_layers(model):
+    return model.get_submodule(_layers_path(model))
+
+
+class RocketModel:
+    """An RW4 ``*ForCausalLM`` with layer streaming (the reference's ``RocketModel`` surface:
+    ``generate``, ``__call__``/``forward``, ``stats``, ``close``).
+
+    ``vram_budget`` (bytes) bounds the streamed layers' device slots: if the whole model fits it
+    (or it is None) every layer is resident; otherwise ``window`` slots are used and layers stream
+    from pinned host memory every token.
+    """
+
+    def __init__(self, model_or_path, device="cuda", dtype=torch.bfloat16, vram_budget=None,
+                 window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20, **unused):
+        if isinstance(model_or_path, (str, os.PathLike)):
+            from transformers import AutoModelForCausalLM
+            model = AutoModelForCausalLM.from_pretrained(str(model_or_path), dtype=dtype)
+        else:
+            model = model_or_path
+        self.model = model.eval()
+        self.device = torch.device(device)
+        layers = _decoder_layers(model)
+        layer_bytes = [sum(t.numel() * t.element_size() for *_, t in _layer_tensors(l))
+                       for l in layers]
+        self.streamer = None
+        stream = vram_budget is not None and sum(layer_bytes) > vram_budget
+        if not stream:
+            self.model.to(self.device)
+        else:
+            window = max(1, min(window, int(vram_budget // max(layer_bytes))))
+            # everything outside the decoder layers is resident: move the model with its layer
+            # list detached, then hand the layers to the streamer (they stay on the host)
+            parent_path, _, leaf = _layers_path(model).rpartition(".")
+            parent = self.model.get_submodule(parent_path) if parent_path else self.model
+            setattr(parent, leaf, torch.nn.ModuleList())
+            self.model.to(self.device)
+            setattr(parent, leaf, layers)
+            self.streamer = LayerStreamer(layers, self.device, window=window,
+                                          copy_streams=copy_streams, chunk_bytes=chunk_bytes,
+                                          prefetching=prefetching)
+
+    @property
+    def config(self):
+        return self.model.config
+
+    def generate(self, *args, **kwargs):
+        return self.model.generate(*args, **kwargs)
+
+    def forward(self, *args, **kwargs):
+        return self.model(*args, **kwargs)
+
+    __call__ = forward
+
+    def stats(self):
+        return {"streaming": self.streamer.stats() if self.streamer else None}
+
+    def close(self):
+        if self.streamer is not None:
+            self.streamer.close()
+            self.streamer = None
+
+
+class AutoModel:
+    """``AutoModel.from_pretrained(path, **knobs) -> RocketModel`` (``rocketllm/auto_model.py``)."""
+
+    def __init__(self):
+        raise EnvironmentError("use AutoModel.from_pretrained(path)")
+
+    @classmethod
+    def from_pretrained(cls, pretrained_model_name_or_path, *args, **kwargs):
+        return RocketModel(pretrained_model_name_or_path, *args, **kwargs)
