@@ -78,8 +78,14 @@ def quantize(w, group=64):
 
 
 def linear(x, packed, scale, zero, out=None):
-    """``y = x . W^T`` with ``x`` bf16 ``[..., K]`` and W in RW4; returns bf16 ``[..., N]``."""
-    _require_cuda(x, packed, scale, zero)
+    """``y = x . W^T`` with ``x`` bf16 ``[..., K]`` and W in RW4; returns bf16 ``[..., N]``.
+
+    ``x`` may be a strided view (e.g. the last position of every sequence); it is compacted first.
+    """
+    if not x.is_cuda:
+        raise ValueError("RW4 kernels take CUDA tensors only (there is no CPU path); got a "
+                         f"{x.device} activation")
+    _require_cuda(packed, scale, zero)
     _check_weight(packed, scale, zero)
     if x.dtype != torch.bfloat16:
         raise TypeError(f"rw4 linear takes bf16 activations, not {x.dtype}")

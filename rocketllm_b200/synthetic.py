@@ -27,6 +27,60 @@ def make_activation(m, k, device="cuda", seed=2):
     return torch.randn((m, k), device=device, generator=gen).to(torch.bfloat16)
 
 
+@torch.no_grad()
+def build_rw4_causal_lm(config, device="cuda", seed=0, std=0.02):
+    """A random-init RW4 ``*ForCausalLM`` built directly on ``device``: every Linear / stacked-expert
+    weight drawn N(0, std) in bf16 and encoded with ``rw4_quantize`` (the reference codec), norms 1,
+    other weights N(0, std).  No dense copy of the whole model ever exists."""
+    from transformers import AutoModelForCausalLM
+
+    from . import kernels
+    from .quant.hf import convert_modules
+    from .quant.modules import RW4Linear
+
+    with torch.device("meta"):
+        model = AutoModelForCausalLM.from_config(config, dtype=torch.bfloat16)
+    convert_modules(model)
+    model.to_empty(device=device)
+    gen = torch.Generator(device=device).manual_seed(seed)
+
+    def encode_into(packed, scale, zero, n, k):
+        w = (torch.randn((n, k), device=device, generator=gen) * std).to(torch.bfloat16)
+        p, s, z, _ = kernels.quantize(w, 64)
+        packed.copy_(p), scale.copy_(s), zero.copy_(z)
+
+    for name, mod in model.named_modules():
+        if isinstance(mod, RW4Linear):
+            encode_into(mod.weight_packed, mod.weight_scale, mod.weight_zero_point,
+                        mod.out_features, mod.in_features)
+            if mod.bias is not None:
+                mod.bias.zero_()
+        elif getattr(mod, "rw4", False):
+            for wn in ("gate_up_proj", "down_proj"):
+                p, s, z = (getattr(mod, wn + sfx) for sfx in ("_packed", "_scale", "_zero_point"))
+                for e in range(p.shape[0]):
+                    encode_into(p[e], s[e], z[e], p.shape[1], p.shape[2] * 2)
+    rw4_suffixes = ("_packed", "_scale", "_zero_point")
+    for name, param in model.named_parameters():
+        if name.endswith(rw4_suffixes) or name.endswith(".bias"):
+            continue
+        if "norm" in name:
+            param.fill_(1.0)
+        else:
+            param.copy_((torch.randn(param.shape, device=device, generator=gen) * std)
+                        .to(param.dtype))
+    # non-persistent buffers (rotary inverse frequencies) were left uninitialised by to_empty:
+    # rebuild those modules' buffers on the device
+    for mod in model.modules():
+        if "inv_freq" in mod._buffers and hasattr(mod, "config"):
+            fresh = type(mod)(mod.config, device=device)
+            for bname, buf in fresh._buffers.items():
+                mod._buffers[bname] = buf
+            if hasattr(fresh, "attention_scaling"):
+                mod.attention_scaling = fresh.attention_scaling
+    return model.eval()
+
+
 def algorithmic_bytes(m, k, n, group=64):
     """Bytes one ``y = x W^T`` call must move at least once: codes, scales, zeros, x and y."""
     return n * k // 2 + 2 * 2 * (k // group) * n + 2 * m * k + 2 * m * n
