@@ -232,6 +232,77 @@ def h2d_probe(device, nbytes=256 << 20, reps=10):
     return best
 
 
+LLAMA_8B = dict(hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                num_attention_heads=32, num_key_value_heads=8, vocab_size=128256,
+                max_position_embeddings=8192, rope_theta=500000.0, tie_word_embeddings=False)
+
+
+def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget):
+    """Greedy decode tok/s of a Llama-3.1-8B-architecture RW4 model (random init N(0, 0.02),
+    every Linear incl. lm_head in RW4): resident with a CUDA-graphed step, then streamed from
+    pinned host memory under a VRAM budget."""
+    from transformers import LlamaConfig
+
+    from rocketllm_b200.decode import GraphedDecoder
+    from rocketllm_b200.engine import RocketModel
+    from rocketllm_b200.synthetic import build_rw4_causal_lm
+
+    cfg = LlamaConfig(**LLAMA_8B)
+    model = build_rw4_causal_lm(cfg, device=device, seed=0)
+    out = {"model": "Llama-3.1-8B architecture, RW4 group 64 (random init N(0,0.02))",
+           "prompt_tokens": prompt, "greedy": True}
+    gen = torch.Generator().manual_seed(1)
+    for b in batches:
+        ids = torch.randint(0, cfg.vocab_size, (b, prompt), generator=gen).to(device)
+        dec = GraphedDecoder(model, b, prompt + new_tokens + 8, device=device)  # + 3 warm-up steps
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        dec.prefill(ids)
+        t1.record()
+        dec.capture()
+        for _ in range(3):
+            dec.step()
+        a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(new_tokens):
+            dec.step()
+        c.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(c) / new_tokens
+        out[f"resident_b{b}"] = {"tok_s": round(b * 1000.0 / ms, 1), "ms_per_token": round(ms, 4),
+                                 "prefill_ms": round(t0.elapsed_time(t1), 2),
+                                 "decode_tokens": new_tokens}
+        del dec
+        torch.cuda.empty_cache()
+    # streamed: the decoder layers leave HBM and stream from pinned host RAM every token
+    streamed = RocketModel(model, device=device, vram_budget=vram_budget, window=2)
+    ids = torch.randint(0, cfg.vocab_size, (1, 128), generator=gen).to(device)
+    dec = GraphedDecoder(streamed.model, 1, 128 + stream_tokens + 8, device=device,
+                         use_graph=False)
+    dec.prefill(ids)
+    dec.step()
+    torch.cuda.synchronize()
+    st0 = streamed.stats()["streaming"]["bytes"]
+    a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(stream_tokens):
+        dec.step()
+    c.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(c) / stream_tokens
+    nbytes = (streamed.stats()["streaming"]["bytes"] - st0) / stream_tokens
+    out["streamed_b1"] = {"tok_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 3),
+                          "vram_budget_bytes": vram_budget, "window": streamed.streamer.window,
+                          "h2d_bytes_per_token": int(nbytes),
+                          "h2d_gbs": round(nbytes / (ms * 1e-3) / 1e9, 2),
+                          "decode_tokens": stream_tokens}
+    streamed.close()
+    del model, streamed, dec
+    torch.cuda.empty_cache()
+    return out
+
+
 def rw4_arm(args):
     from rocketllm_b200 import kernels
     from rocketllm_b200.streaming import WeightTransfer
@@ -341,6 +412,13 @@ def rw4_arm(args):
     h2d_peak = h2d_probe(device) if rank == 0 else None
     xfer.close()
 
+    decode = None
+    if not args.no_decode:
+        del weights, host_w, slots
+        torch.cuda.empty_cache()
+        decode = decode_bench(device, args.decode_prompt, args.decode_tokens, (1, 16),
+                              args.stream_tokens, int(4e9))
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         value, ms, threads, sample = run_cpu(max(1, args.cpu_steps), 1, budget_s=args.cpu_seconds)
@@ -372,6 +450,7 @@ def rw4_arm(args):
                     "h2d_probe_gbs": round(h2d_peak, 2) if h2d_peak else None,
                     "h2d_frac": round(h2d / (e2e_ms * 1e-3) / 1e9 / h2d_peak, 4)
                     if h2d_peak else None},
+            "decode": decode,
             "gpu_launches": len(SHAPES) * args.steps,
             "clocks": clock,
             "device_status": status,
@@ -390,6 +469,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=("rw4", "reference"), default="rw4")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-decode", action="store_true", help="skip the model decode section")
+    ap.add_argument("--decode-prompt", type=int, default=2048)
+    ap.add_argument("--decode-tokens", type=int, default=256)
+    ap.add_argument("--stream-tokens", type=int, default=16)
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="approximate CPU time of the CPU baseline leg")
     ap.add_argument("--cpu-steps", type=int, default=3)

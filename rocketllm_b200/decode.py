@@ -28,12 +28,14 @@ class GraphedDecoder:
         self.use_graph = use_graph
         self.graph = None
         self.out = None
+        self.host_pos = 0   # host copy of the next write position (bounds check before launch)
 
     @torch.no_grad()
     def prefill(self, input_ids):
         t = input_ids.shape[1]
         if t + 1 > self.max_len:
             raise ValueError("prompt longer than the static cache")
+        self.host_pos = t
         pos = torch.arange(t, device=self.device)
         logits = self.model(input_ids.to(self.device), past_key_values=self.cache,
                             cache_position=pos, use_cache=True).logits[:, -1]
@@ -56,6 +58,8 @@ class GraphedDecoder:
         """Warm up on a side stream, then capture one step.  Call after ``prefill``; the warm-up
         step's cache writes land at the current position and are overwritten by the first
         replay, since the position is restored."""
+        if self.host_pos + 1 > self.max_len:
+            raise ValueError(f"static KV cache full ({self.max_len} positions)")
         state = self._state()
         saved = [t.clone() for t in state]
         side = torch.cuda.Stream(self.device)
@@ -86,6 +90,9 @@ class GraphedDecoder:
 
     @torch.no_grad()
     def step(self):
+        if self.host_pos + 1 > self.max_len:
+            raise ValueError(f"static KV cache full ({self.max_len} positions)")
+        self.host_pos += 1
         if self.use_graph:
             if self.graph is None:
                 self.capture()

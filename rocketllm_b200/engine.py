@@ -163,13 +163,24 @@ def _decoder_layers(model):
     return model.get_submodule(_layers_path(model))
 
 
+def footprint(model):
+    """``(resident_bytes, [bytes of each decoder layer])`` of ``model``."""
+    layers = _decoder_layers(model)
+    layer_bytes = [sum(t.numel() * t.element_size() for *_, t in _layer_tensors(l))
+                   for l in layers]
+    total = sum(p.numel() * p.element_size() for p in model.parameters())
+    total += sum(b.numel() * b.element_size() for b in model.buffers())
+    return total - sum(layer_bytes), layer_bytes
+
+
 class RocketModel:
     """An RW4 ``*ForCausalLM`` with layer streaming (the reference's ``RocketModel`` surface:
     ``generate``, ``__call__``/``forward``, ``stats``, ``close``).
 
-    ``vram_budget`` (bytes) bounds the streamed layers' device slots: if the whole model fits it
-    (or it is None) every layer is resident; otherwise ``window`` slots are used and layers stream
-    from pinned host memory every token.
+    ``vram_budget`` (bytes) bounds the model's device footprint: if the whole model fits it (or it
+    is None) every layer is resident; otherwise the non-layer modules stay resident and at most
+    ``window`` layer slots fit in what is left (at least one), and layers stream from pinned host
+    memory every token.
     """
 
     def __init__(self, model_or_path, device="cuda", dtype=torch.bfloat16, vram_budget=None,
@@ -182,14 +193,14 @@ class RocketModel:
         self.model = model.eval()
         self.device = torch.device(device)
         layers = _decoder_layers(model)
-        layer_bytes = [sum(t.numel() * t.element_size() for *_, t in _layer_tensors(l))
-                       for l in layers]
+        rest, layer_bytes = footprint(model)   # embeddings, final norm, lm_head: resident
+        total = rest + sum(layer_bytes)
         self.streamer = None
-        stream = vram_budget is not None and sum(layer_bytes) > vram_budget
+        stream = vram_budget is not None and total > vram_budget
         if not stream:
             self.model.to(self.device)
         else:
-            window = max(1, min(window, int(vram_budget // max(layer_bytes))))
+            window = max(1, min(window, int(max(0, vram_budget - rest) // max(layer_bytes))))
             # everything outside the decoder layers is resident: move the model with its layer
             # list detached, then hand the layers to the streamer (they stay on the host)
             parent_path, _, leaf = _layers_path(model).rpartition(".")

@@ -30,3 +30,17 @@ def test_graph_decode_equals_eager(arch, batch):
     with torch.no_grad():
         ref = model.generate(ids, max_new_tokens=10, min_new_tokens=10, do_sample=False)[:, 12:]
     assert torch.equal(eager, ref)
+
+
+def test_full_static_cache_is_refused_on_the_host():
+    from transformers import LlamaConfig
+    cfg = LlamaConfig(hidden_size=512, intermediate_size=1536, num_hidden_layers=1,
+                      num_attention_heads=8, num_key_value_heads=2, vocab_size=2048,
+                      max_position_embeddings=256, tie_word_embeddings=False)
+    model = build_rw4_causal_lm(cfg, device="cuda", seed=1)
+    dec = GraphedDecoder(model, 1, 8, use_graph=False)
+    dec.prefill(torch.zeros(1, 6, dtype=torch.long, device="cuda"))
+    dec.step()
+    dec.step()
+    with pytest.raises(ValueError, match="full"):
+        dec.step()

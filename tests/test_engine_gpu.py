@@ -5,7 +5,7 @@ token."""
 import pytest
 import torch
 
-from rocketllm_b200.engine import AutoModel, RocketModel
+from rocketllm_b200.engine import AutoModel, RocketModel, footprint
 from rocketllm_b200.quant.convert import save_rw4_checkpoint
 
 pytestmark = pytest.mark.gpu
@@ -33,7 +33,8 @@ def test_streamed_equals_resident(checkpoint, window):
     streamed = RocketModel(checkpoint, vram_budget=1, window=window)  # forces streaming
     assert streamed.streamer is not None and streamed.streamer.window == 1
     streamed.close()
-    budget = int(window * 1.8e6)  # a layer is ~1.72 MB in RW4; 4 layers never fit
+    rest, layers = footprint(resident.model)
+    budget = rest + window * max(layers) + 1000  # room for exactly `window` layer slots
     streamed = RocketModel(checkpoint, vram_budget=budget, window=window)
     with torch.no_grad():
         assert torch.equal(resident(ids).logits, streamed(ids).logits)
