@@ -22,9 +22,18 @@
 // bf16(bf16(silu(bf16(g))) * bf16(u)), the rounding sequence of the bf16 model's own
 // act_fn(gate) * up (transformers models/mixtral/modeling_mixtral.py:84-91).
 //
+// K split over a thread-block cluster (KS > 1): the KS CTAs of a cluster take contiguous thirds /
+// quarters / halves of the stages of the same rows; every CTA reduces its 8 warps in its own shared
+// memory, the CTAs of rank > 0 write their partial sums into rank 0's shared memory through the
+// cluster's distributed shared memory, and after one cluster barrier rank 0 adds them and stores.
+// More CTAs (and shorter K loops) for short, narrow projections, with no global scratch and no
+// atomics.
+//
 // Every mbarrier wait is bounded (rw4_tma.cuh); on a timeout the CTA drains its own copies, writes
 // nothing and sets the library's device status word.
 #pragma once
+
+#include <cooperative_groups.h>
 
 #include "rw4_gemv_frag.cuh"
 #include "rw4_tma.cuh"
@@ -54,7 +63,7 @@ struct Layout {
 // x: this slice's activation rows (Ml <= 16 of them, row stride K); y: output rows (stride ldy).
 // Plain: writes y[m, r0 + r] for r0 + r < n_out.  SWIGLU: writes y[m, r0 + r] for r0 + r < n_out
 // (= I) from weight rows r0 + r (gate) and r0 + I + r (up).
-template <int NT, int R, int S, bool SWIGLU>
+template <int NT, int R, int S, bool SWIGLU, int KS = 1>
 __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensorMap* tm_scale,
                                      const CUtensorMap* tm_zero,
                                      const __nv_bfloat16* __restrict__ x, int Ml, int K,
@@ -73,7 +82,13 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int nstages = K / kStageK;
+  // this CTA's range of stages (the whole K unless the cluster splits it)
+  int crank = 0;
+  if (KS > 1) asm("mov.u32 %0, %%cluster_ctarank;" : "=r"(crank));
+  const int nst_all = K / kStageK;
+  const int per = (nst_all + KS - 1) / KS;
+  const int s_begin = min(nst_all, crank * per);
+  const int nstages = min(nst_all, s_begin + per) - s_begin;
 
   if (threadIdx.x == 0) {
     aborted = 0;
@@ -93,6 +108,8 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
 #pragma unroll
       for (int e = 0; e < 4; ++e) out[rt][nt][e] = 0.f;
 
+  // let the next kernel on the stream begin launching (its CTAs start as ours retire)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   if (warp == kConsumers) {
     // ---------------- producer ----------------
     if (lane == 0) {
@@ -100,6 +117,18 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       prefetch_tensormap(tm_scale);
       prefetch_tensormap(tm_zero);
       const uint64_t pol = policy_evict_first();
+      // Before the dependency on the previous kernel resolves, only pull the first stages' weights
+      // into L2 (coherent: if that kernel wrote them, the loads below still see its writes).
+      for (int s = 0; s < min(S, nstages); ++s) {
+        const int kx = (s_begin + s) * (kStageK / 2);
+        tma_prefetch_2d(tm_codes, kx, r0);
+        tma_prefetch_2d(tm_codes, kx + 128, r0);
+        if (SWIGLU) {
+          tma_prefetch_2d(tm_codes, kx, r0 + up_offset);
+          tma_prefetch_2d(tm_codes, kx + 128, r0 + up_offset);
+        }
+      }
+      asm volatile("griddepcontrol.wait;" ::: "memory");
       int issued = 0;
       for (int s = 0; s < nstages; ++s) {
         const int st = s % S;
@@ -113,7 +142,8 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
         const uint32_t cdst = sbase + L::kCodes + st * L::kCodeStage;
         const uint32_t sdst = sbase + L::kScales + st * L::kScaleStage;
         const uint32_t zdst = sbase + L::kZeros + st * L::kScaleStage;
-        const int kx = s * (kStageK / 2);
+        const int kx = (s_begin + s) * (kStageK / 2);
+        const int gx = (s_begin + s) * kConsumers;
         if (SWIGLU) {
           // 16-row boxes: gate tile then up tile (2048 bytes apart, swizzle phase unchanged).
           const int ru = r0 + up_offset;
@@ -121,15 +151,15 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
           tma_load_2d_hint(cdst + 2048, tm_codes, kx, ru, fb, pol);
           tma_load_2d_hint(cdst + L::kCodeBox, tm_codes, kx + 128, r0, fb, pol);
           tma_load_2d_hint(cdst + L::kCodeBox + 2048, tm_codes, kx + 128, ru, fb, pol);
-          tma_load_2d_hint(sdst, tm_scale, s * kConsumers, r0, fb, pol);
-          tma_load_2d_hint(sdst + 256, tm_scale, s * kConsumers, ru, fb, pol);
-          tma_load_2d_hint(zdst, tm_zero, s * kConsumers, r0, fb, pol);
-          tma_load_2d_hint(zdst + 256, tm_zero, s * kConsumers, ru, fb, pol);
+          tma_load_2d_hint(sdst, tm_scale, gx, r0, fb, pol);
+          tma_load_2d_hint(sdst + 256, tm_scale, gx, ru, fb, pol);
+          tma_load_2d_hint(zdst, tm_zero, gx, r0, fb, pol);
+          tma_load_2d_hint(zdst + 256, tm_zero, gx, ru, fb, pol);
         } else {
           tma_load_2d_hint(cdst, tm_codes, kx, r0, fb, pol);
           tma_load_2d_hint(cdst + L::kCodeBox, tm_codes, kx + 128, r0, fb, pol);
-          tma_load_2d_hint(sdst, tm_scale, s * kConsumers, r0, fb, pol);
-          tma_load_2d_hint(zdst, tm_zero, s * kConsumers, r0, fb, pol);
+          tma_load_2d_hint(sdst, tm_scale, gx, r0, fb, pol);
+          tma_load_2d_hint(zdst, tm_zero, gx, r0, fb, pol);
         }
         issued = s + 1;
       }
@@ -139,6 +169,9 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     }
   } else {
     // ---------------- consumers ----------------
+    // x may be the previous kernel's output: wait for that grid (a no-op without a programmatic
+    // dependency) -- the producer is already streaming weights meanwhile.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     const int g = lane >> 2, t = lane & 3;
     const int w = warp;              // group of the stage this warp owns
     const int half = w >> 2, q = w & 3;
@@ -172,7 +205,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       if (lane == 0) mbar_arrive(empty0 + 8 * st);
 
       // x fragment of group (s * 8 + w) and its sums over the group
-      const int kofs = s * kStageK + 64 * w + 16 * t;
+      const int kofs = (s_begin + s) * kStageK + 64 * w + 16 * t;
       uint32_t b[NT][4][2];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
@@ -214,10 +247,11 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
 
   // ---- combine the consumer warps' partial sums (ring memory reused) and write bf16 -----------
   __syncthreads();
-  if (aborted) return;
   constexpr int kCols = 16 * NT + 1;
+  constexpr int kRowsOut = SWIGLU ? 16 : L::BR;
+  constexpr int kOut = kRowsOut * 16 * NT;
   float* red = reinterpret_cast<float*>(smem);  // [kConsumers][BR][kCols]
-  if (warp < kConsumers) {
+  if (!aborted && warp < kConsumers) {
     const int g = lane >> 2, t = lane & 3;
 #pragma unroll
     for (int rt = 0; rt < R; ++rt)
@@ -231,27 +265,69 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       }
   }
   __syncthreads();
-  constexpr int kRowsOut = SWIGLU ? 16 : L::BR;
-  for (int o = threadIdx.x; o < kRowsOut * 16 * NT; o += kThreads) {
-    const int r = o % kRowsOut;
-    const int m = o / kRowsOut;
-    const int n = r0 + r;
-    if (n < n_out && m < Ml) {
-      float v = 0.f;
-      if (SWIGLU) {
-        float gsum = 0.f, usum = 0.f;
+  // per-output partial sums of this CTA (SWIGLU keeps gate and up apart until the final value)
+  constexpr int kPer = (kOut + kThreads - 1) / kThreads;
+  float part[kPer][SWIGLU ? 2 : 1];
 #pragma unroll
-        for (int w = 0; w < kConsumers; ++w) {
-          gsum += red[(w * L::BR + r) * kCols + m];
-          usum += red[(w * L::BR + 16 + r) * kCols + m];
+  for (int i = 0; i < kPer; ++i) {
+    const int o = threadIdx.x + i * kThreads;
+    const int r = o % kRowsOut, m = o / kRowsOut;
+    float a0 = 0.f, a1 = 0.f;
+    if (!aborted && o < kOut) {
+#pragma unroll
+      for (int w = 0; w < kConsumers; ++w) {
+        a0 += red[(w * L::BR + r) * kCols + m];
+        if (SWIGLU) a1 += red[(w * L::BR + 16 + r) * kCols + m];
+      }
+    }
+    part[i][0] = a0;
+    if (SWIGLU) part[i][SWIGLU ? 1 : 0] = a1;
+  }
+  if (KS > 1) {
+    // ranks > 0 deposit their partials in rank 0's shared memory; one cluster barrier
+    __shared__ float xred[KS > 1 ? (KS - 1) : 1][kOut][SWIGLU ? 2 : 1];
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    if (crank > 0 && !aborted) {
+      float(*dst)[kOut][SWIGLU ? 2 : 1] = cluster.map_shared_rank(xred, 0);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int o = threadIdx.x + i * kThreads;
+        if (o < kOut) {
+          dst[crank - 1][o][0] = part[i][0];
+          if (SWIGLU) dst[crank - 1][o][SWIGLU ? 1 : 0] = part[i][SWIGLU ? 1 : 0];
         }
-        const float gb = __bfloat162float(__float2bfloat16_rn(gsum));
-        const float ub = __bfloat162float(__float2bfloat16_rn(usum));
+      }
+    }
+    cluster.sync();
+    if (crank > 0) return;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int o = threadIdx.x + i * kThreads;
+      if (o < kOut) {
+#pragma unroll
+        for (int j = 0; j < KS - 1; ++j) {
+          part[i][0] += xred[j][o][0];
+          if (SWIGLU) part[i][SWIGLU ? 1 : 0] += xred[j][o][SWIGLU ? 1 : 0];
+        }
+      }
+    }
+  }
+  if (aborted) return;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int o = threadIdx.x + i * kThreads;
+    const int r = o % kRowsOut, m = o / kRowsOut;
+    const int n = r0 + r;
+    if (o < kOut && n < n_out && m < Ml) {
+      float v;
+      if (SWIGLU) {
+        const float gb = __bfloat162float(__float2bfloat16_rn(part[i][0]));
+        const float ub = __bfloat162float(__float2bfloat16_rn(part[i][SWIGLU ? 1 : 0]));
         const float act = __bfloat162float(__float2bfloat16_rn(gb / (1.f + expf(-gb))));
         v = act * ub;
       } else {
-#pragma unroll
-        for (int w = 0; w < kConsumers; ++w) v += red[(w * L::BR + r) * kCols + m];
+        v = part[i][0];
       }
       y[(int64_t)m * ldy + n] = __float2bfloat16_rn(v);
     }

@@ -36,7 +36,7 @@ def oracle_linear(x, packed, scale, zero, rows=None):
 
 
 @pytest.mark.parametrize("m", [1, 2, 3, 4, 7, 8, 9, 15, 16, 17, 33, 64])
-@pytest.mark.parametrize("k,n", [(4096, 512), (320, 136), (1024, 4104)])
+@pytest.mark.parametrize("k,n", [(4096, 512), (320, 136), (1024, 4104), (8192, 1024), (4096, 4096)])
 def test_linear_matches_oracle(cuda, m, k, n):
     packed, scale, zero = make_weight(n, k, device=cuda, seed=m + k)
     x = make_activation(m, k, device=cuda, seed=n)
