@@ -22,7 +22,7 @@
 // order.  CTAs sharing a weight tile are adjacent in the grid (tokens fastest), so a weight tile
 // is read from HBM about once and the activations stay in L2.
 //
-// No TMA load uses multicast.  Every mbarrier wait is bounded (rw4_tma.cuh); on a timeout the CTA
+// Every TMA load is a plain per-CTA load.  Every mbarrier wait is bounded (rw4_tma.cuh); on a timeout the CTA
 // stops issuing, waits (bounded) for its own copies and MMAs, frees its TMEM and writes nothing.
 #include <atomic>
 

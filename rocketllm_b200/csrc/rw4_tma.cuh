@@ -4,7 +4,7 @@
 // RW4_DEVERR_TIMEOUT in the library's device status word (passed to kernels as a pointer) and
 // lets the kernel unwind, so a protocol error can never hang the GPU; rw4_device_status() reads
 // (and optionally clears) that word.
-// No load here uses .multicast::cluster: every CTA fetches its own tiles.
+// Every CTA fetches its own tiles with plain (per-CTA) TMA loads.
 #pragma once
 
 #include <cuda.h>
