@@ -1,0 +1,103 @@
+"""Pipeline-parallel greedy decode over NCCL (one process per GPU).
+
+The reference runs every layer on one device (``rocketllm/base.py:336``).  For models whose RW4
+weights do not fit one GPU (the 405B architecture is ~227 GB), rank ``r`` of ``G`` keeps the
+contiguous decoder layers ``[r L/G, (r+1) L/G)``, rank 0 the embedding, the last rank the final
+norm and ``lm_head``.  One forward (prefill or one decode step): rank 0 embeds, every rank runs its
+layers on the hidden states it received from the previous rank (``dist.recv``) and sends the
+result on (``dist.send``; NCCL point-to-point over NVLink), the last rank computes the logits and
+the greedy token, and the token is broadcast to every rank for the next step.  Each rank keeps the
+KV cache of its own layers.  The layers themselves are transformers' modules (RW4Linear inside);
+only the hand-off is new.
+"""
+import torch
+import torch.distributed as dist
+
+
+def layer_range(num_layers, rank, world):
+    """Contiguous, balanced ``[start, stop)`` of the layers rank ``rank`` owns."""
+    base, extra = divmod(num_layers, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+class PipelineDecoder:
+    """Greedy decode of a ``*ForCausalLM`` whose decoder layers are split over ``group``.
+
+    ``model`` is this rank's copy; layers outside the rank's range (and the embedding / head on
+    ranks that do not use them) are dropped to free their memory.
+    """
+
+    def __init__(self, model, group=None, device="cuda", drop_remote=True, local=False):
+        from transformers import DynamicCache
+        self.group = group
+        self.local = local or not dist.is_initialized()   # one rank, no communication
+        self.world = 1 if self.local else dist.get_world_size(group)
+        self.rank = 0 if self.local else dist.get_rank(group)
+        self.device = torch.device(device)
+        self.model = model
+        inner = model.model
+        self.layers = inner.layers
+        self.start, self.stop = layer_range(len(self.layers), self.rank, self.world)
+        self.first = self.rank == 0
+        self.last = self.rank == self.world - 1
+        if drop_remote:
+            for i in range(len(self.layers)):
+                if not self.start <= i < self.stop:
+                    self.layers[i] = torch.nn.Identity()
+            if not self.first:
+                inner.embed_tokens = None
+            if not self.last:
+                model.lm_head = None
+                inner.norm = None
+        self.rotary = inner.rotary_emb
+        self.embed = inner.embed_tokens
+        self.cache = DynamicCache(config=model.config)
+        self.hidden_size = model.config.hidden_size
+        self.dtype = next(p.dtype for p in model.parameters() if p.is_floating_point()
+                          and p.dtype != torch.float16)
+        self.seen = 0
+
+    def _peer(self, delta):
+        ranks = dist.get_process_group_ranks(self.group) if self.group is not None else None
+        r = self.rank + delta
+        return ranks[r] if ranks is not None else r
+
+    @torch.no_grad()
+    def _forward(self, ids, b, t):
+        """One pipeline pass over ``t`` new positions; returns the greedy token [b, 1] (all ranks)."""
+        pos = torch.arange(self.seen, self.seen + t, device=self.device)
+        if self.first:
+            h = self.embed(ids.to(self.device))
+        else:
+            h = torch.empty((b, t, self.hidden_size), dtype=self.dtype, device=self.device)
+            # (the first rank's embedding output has this dtype; `dtype` follows the model)
+            dist.recv(h, src=self._peer(-1), group=self.group)
+        position_ids = pos.unsqueeze(0).expand(b, -1)
+        cos_sin = self.rotary(h, position_ids)
+        for i in range(self.start, self.stop):
+            h = self.layers[i](h, attention_mask=None, position_ids=position_ids,
+                               past_key_values=self.cache, use_cache=True, cache_position=pos,
+                               position_embeddings=cos_sin)
+            if isinstance(h, tuple):
+                h = h[0]
+        tok = torch.empty((b, 1), dtype=torch.long, device=self.device)
+        if not self.last:
+            dist.send(h.contiguous(), dst=self._peer(1), group=self.group)
+        else:
+            logits = self.model.lm_head(self.model.model.norm(h[:, -1:, :]))
+            tok.copy_(logits[:, -1].argmax(-1, keepdim=True))
+        if not self.local:
+            last = dist.get_process_group_ranks(self.group)[-1] if self.group is not None else \
+                self.world - 1
+            dist.broadcast(tok, src=last, group=self.group)
+        self.seen += t
+        return tok
+
+    def generate(self, input_ids, new_tokens):
+        """Greedy tokens ``[B, new_tokens]``; every rank returns them."""
+        b, t = input_ids.shape
+        toks = [self._forward(input_ids, b, t)]
+        for _ in range(new_tokens - 1):
+            toks.append(self._forward(toks[-1], b, 1))
+        return torch.cat(toks, dim=1)

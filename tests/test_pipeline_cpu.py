@@ -1,0 +1,69 @@
+"""Pipeline parallelism over two and three gloo ranks on the CPU: splitting the decoder layers and
+handing the hidden states rank to rank gives exactly the single-rank greedy tokens.  The model is a
+tiny dense fp32 Llama (the pipeline is independent of the Linear implementation; the GPU test runs
+it on RW4 weights)."""
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from rocketllm_b200.pipeline import layer_range
+
+
+def tiny_model():
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(0)
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=128, num_hidden_layers=5,
+                      num_attention_heads=4, num_key_value_heads=2, vocab_size=97,
+                      max_position_embeddings=64, tie_word_embeddings=False)
+    m = LlamaForCausalLM(cfg).eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if "norm" not in n:
+                p.normal_(0, 0.2)
+    return m
+
+
+def test_layer_ranges_cover_every_layer_once():
+    for layers in (1, 5, 32, 126):
+        for world in (1, 2, 3, 8):
+            spans = [layer_range(layers, r, world) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == layers
+            assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+            assert max(b - a for a, b in spans) - min(b - a for a, b in spans) <= 1
+
+
+def test_single_rank_decode_matches_generate():
+    """The layer-by-layer loop (one rank, no communication) is transformers' own greedy decode."""
+    from rocketllm_b200.pipeline import PipelineDecoder
+    ids = torch.randint(0, 97, (2, 7), generator=torch.Generator().manual_seed(3))
+    m = tiny_model()
+    m.generation_config.eos_token_id = None
+    m.generation_config.pad_token_id = 0
+    with torch.no_grad():
+        ref = m.generate(ids, attention_mask=torch.ones_like(ids), max_new_tokens=6,
+                         do_sample=False)[:, 7:]
+    got = PipelineDecoder(tiny_model(), device="cpu", local=True).generate(ids, 6)
+    assert torch.equal(ref, got), (ref, got)
+
+
+def _worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from rocketllm_b200.pipeline import PipelineDecoder
+    ids = torch.randint(0, 97, (2, 7), generator=torch.Generator().manual_seed(3))
+    ref = PipelineDecoder(tiny_model(), device="cpu", local=True).generate(ids, 6)
+    got = PipelineDecoder(tiny_model(), device="cpu").generate(ids, 6)
+    out[rank] = bool(torch.equal(ref, got))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_pipeline_matches_single_rank(world):
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_worker, args=(world, 29711 + world, out), nprocs=world, join=True)
+        assert all(out[r] for r in range(world)), dict(out)
