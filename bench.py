@@ -478,6 +478,68 @@ def rw4_arm(args):
     return 0
 
 
+def sweep(args):
+    """Kernel sweep (not the driver's line): every (K, N) x M of the isolated sweep, one JSON line
+    each with the launch's CUDA-event time over ``--steps`` graphed back-to-back launches (cycling
+    through enough copies of the weight that none is still in L2), its algorithmic GB/s and
+    TFLOP/s against the measured peaks, and which kernel ran (1 GEMV, 2 tcgen05 GEMM, 3 GEMV
+    slices)."""
+    from rocketllm_b200 import kernels
+    from rocketllm_b200.synthetic import make_activation, make_weight
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peak, peak_kind = measured_peak()
+    tflops_peak = None
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            tflops_peak = float(json.load(f)["bf16_tflops"])
+    except Exception:  # noqa: BLE001
+        tflops_peak = 1590.0
+    shapes = SHAPES if args.sweep_shapes == "all" else tuple(
+        tuple(int(v) for v in s.split("x")) for s in args.sweep_shapes.split(","))
+    ms_list = [int(v) for v in args.sweep_m.split(",")]
+    l2_bytes = 126 << 20
+    for i, (k, n) in enumerate(shapes):
+        # enough distinct copies of the weight that consecutive launches never find it in L2
+        wbytes = n * k // 2 + 4 * n * (k // GROUP)
+        copies = max(1, min(64, -(-3 * l2_bytes // wbytes)))
+        ws = [make_weight(n, k, device=device, seed=10 * i + c) for c in range(copies)]
+        for m in ms_list:
+            x = make_activation(m, k, device=device, seed=100 + i)
+            y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+            for _ in range(args.warmup):
+                for w in ws:
+                    kernels.linear(x, *w, out=y)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            reps = max(args.steps, copies)
+            with torch.cuda.graph(g):
+                for r in range(reps):
+                    kernels.linear(x, *ws[r % copies], out=y)
+            g.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / reps
+            gbs = alg_bytes(m, k, n) / (ms * 1e-3) / 1e9
+            tfl = 2 * m * n * k / (ms * 1e-3) / 1e12
+            print(json.dumps({"K": k, "N": n, "M": m, "path": kernels.linear_path(m, k, n),
+                              "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
+                              "hbm_frac": round(gbs / peak, 4), "tflops": round(tfl, 1),
+                              "tensor_frac": round(tfl / tflops_peak, 4),
+                              "peaks": peak_kind, "weight_copies": copies, "launches": reps}),
+                  flush=True)
+            del g
+        del ws
+        torch.cuda.empty_cache()
+    if kernels.device_status():
+        raise RuntimeError("a kernel reported a timed-out wait")
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -492,7 +554,13 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="approximate CPU time of the CPU baseline leg")
     ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--sweep", action="store_true",
+                    help="kernel sweep over the sweep shapes x --sweep-m (one JSON line each)")
+    ap.add_argument("--sweep-m", default="1,4,16,64,512,2048")
+    ap.add_argument("--sweep-shapes", default="all", help="'all' or KxN[,KxN...]")
     args = ap.parse_args()
+    if args.sweep:
+        return sweep(args)
     if args.impl == "reference":
         return reference_arm(args)
     return rw4_arm(args)

@@ -261,16 +261,13 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
 int gemv_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                 const void* zr, int64_t N, void* y, cudaStream_t s) {
   const int nt = (M <= 8) ? 1 : 2;
-  int R = rows_per_cta_override();
-  const bool tma = gemv_tma_supported(K);
-  if (!(R == 1 || R == 2 || (R == 4 && tma && M <= 8))) {
-    // Wider CTAs amortise the per-stage work (x fragment, barrier, all-ones MMA) over more rows,
-    // but need enough rows to keep >= 2 CTAs per SM: 64 rows from N >= 40960 (decode M <= 8 on
-    // the TMA path), 32 rows from N >= 18944, else 16.
-    R = (tma && M <= 8 && N >= 40960) ? 4 : (N >= 16 * 2 * 148 * 4) ? 2 : 1;
-  }
+  const int forced = rows_per_cta_override();
   static const bool no_tma = getenv("RW4_GEMV_NO_TMA") != nullptr;
-  if (!no_tma && gemv_tma_supported(K)) return gemv_tma_launch(x, M, K, wq, sc, zr, N, y, s, R);
+  // the TMA kernel picks its own CTA shape (gemv_tma_policy) unless RW4_GEMV_ROW_TILES forces one
+  if (!no_tma && gemv_tma_supported(K))
+    return gemv_tma_launch(x, M, K, wq, sc, zr, N, y, s, forced);
+  // register-staged kernel (K % 512 != 0): 32-row CTAs from N >= 18944, else 16
+  const int R = (forced == 1 || forced == 2) ? forced : (N >= 16 * 2 * 148 * 4) ? 2 : 1;
   const auto* xb = static_cast<const __nv_bfloat16*>(x);
   auto* yb = static_cast<__nv_bfloat16*>(y);
   const auto* s16 = static_cast<const __half*>(sc);

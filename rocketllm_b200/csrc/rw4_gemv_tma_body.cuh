@@ -4,12 +4,14 @@
 //   producer warp (one elected lane)      S-stage ring in shared memory          8 consumer warps
 //   wait empty[s] ---------------------> codes  [2 boxes x 16R rows x 128 B]  --> wait full[s]
 //   expect_tx(full[s]); TMA loads        scales [16R rows x 8 fp16]              copy 2x8 B codes +
-//   (cp.async.bulk.tensor.2d, L2        zeros  [16R rows x 8 fp16]              scales to registers
-//    evict-first hint)                                                            arrive empty[s]
+//   (cp.async.bulk.tensor.2d, L2        zeros  [16R rows x 8 fp16]              scales + 32 B of x
+//    evict-first hint on weights)        x      [2 boxes x BM rows x 256 bf16]   to registers
+//                                                                                 arrive empty[s]
 //                                                                                 MMA + epilogue
 //
-// A stage is 512 values of K (8 groups) of the CTA's 16R rows; consumer warp w always takes group w
-// of the stage, accumulates over all stages, and the 8 partial sums are combined in shared memory
+// A stage is 512 values of K (8 groups) of the CTA's 16R rows together with the same 512 values of
+// the slice's BM activation rows (x travels in the ring with the weights, so no consumer ever
+// waits on a global load); consumer warp w always takes group w of the stage, accumulates over all stages, and the 8 partial sums are combined in shared memory
 // at the end (deterministic, no atomics, no scratch memory).  Arithmetic: codes enter the tensor
 // cores as bf16 (128 + c) (rw4_gemv_frag.cuh), each group's fp32 accumulator is scaled by its
 // fp16 scale and the zero term uses the group's sum of x from an all-ones MMA.  The code boxes use
@@ -57,21 +59,68 @@ struct Layout {
   static constexpr int kBars = kZeros + S * kScaleStage;
   static constexpr int kBytes = kBars + 2 * S * 8;
   static constexpr int kStageTx = kCodeStage + 2 * kScaleStage;
-  static constexpr int kDynSmem = kBytes + 1024;      // slack to align the ring to 1024 bytes
+  // x ring after the weights: S stages of two [bm rows x 256 bf16] boxes (bm = activation rows
+  // of one slice, <= 16, chosen per launch)
+  static constexpr int kX = (kBytes + 1023) / 1024 * 1024;
+  __host__ __device__ static constexpr int x_stage(int bm) { return bm * 1024; }
+  __host__ __device__ static constexpr int dyn_smem(int bm) { return kX + S * x_stage(bm) + 1024; }
 };
 
-// x: this slice's activation rows (Ml <= 16 of them, row stride K); y: output rows (stride ldy).
+// Shared-memory loads by shared-window address (always LDS, never a generic load).
+__device__ __forceinline__ uint2 lds_v2(uint32_t a) {
+  uint2 v;
+  asm volatile("ld.shared.v2.b32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+  return v;
+}
+__device__ __forceinline__ uint4 lds_v4(uint32_t a) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(a));
+  return v;
+}
+__device__ __forceinline__ float lds_half(uint32_t a) {
+  unsigned short h;
+  asm volatile("ld.shared.b16 %0, [%1];" : "=h"(h) : "r"(a));
+  return __half2float(__ushort_as_half(h));
+}
+
+// 16 bf16 x values from shared memory (two 16-byte loads), permuted like load_x_frag.
+__device__ __forceinline__ void x_frag_smem(uint32_t a, bool valid, uint32_t (&b)[4][2]) {
+  uint4 lo = make_uint4(0, 0, 0, 0), hi = make_uint4(0, 0, 0, 0);
+  if (valid) {
+    lo = lds_v4(a);
+    hi = lds_v4(a + 16);
+  }
+  b[0][0] = __byte_perm(lo.x, lo.z, 0x5410);
+  b[0][1] = __byte_perm(lo.x, lo.z, 0x7632);
+  b[1][0] = __byte_perm(lo.y, lo.w, 0x5410);
+  b[1][1] = __byte_perm(lo.y, lo.w, 0x7632);
+  b[2][0] = __byte_perm(hi.x, hi.z, 0x5410);
+  b[2][1] = __byte_perm(hi.x, hi.z, 0x7632);
+  b[3][0] = __byte_perm(hi.y, hi.w, 0x5410);
+  b[3][1] = __byte_perm(hi.y, hi.w, 0x7632);
+}
+
+// XT (x by TMA): tm_x maps the activations [rows, K] bf16 with a [bm, 256] box; this slice is its
+// rows [x_row0, x_row0 + Ml) (Ml <= bm <= 16; box rows past the tensor's end arrive as zeros, rows
+// of the box past Ml are ignored).  Without XT (the routed-expert kernel, whose row count lives on
+// the device) the consumers read rows [x_row0, x_row0 + Ml) of x (row stride K) from global memory.
+// y: output rows (stride ldy).
 // Plain: writes y[m, r0 + r] for r0 + r < n_out.  SWIGLU: writes y[m, r0 + r] for r0 + r < n_out
 // (= I) from weight rows r0 + r (gate) and r0 + I + r (up).
-template <int NT, int R, int S, bool SWIGLU, int KS = 1>
+// M1: the launch has exactly one activation row (NT == 1, M == 1).
+template <int NT, int R, int S, bool SWIGLU, int KS = 1, bool XT = true, bool M1 = false>
 __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensorMap* tm_scale,
-                                     const CUtensorMap* tm_zero,
-                                     const __nv_bfloat16* __restrict__ x, int Ml, int K,
+                                     const CUtensorMap* tm_zero, const CUtensorMap* tm_x,
+                                     const __nv_bfloat16* __restrict__ x, int x_row0, int bm,
+                                     int Ml, int K,
                                      __nv_bfloat16* __restrict__ y, int64_t ldy, int r0,
                                      int n_out, int up_offset, unsigned int* status) {
   using namespace rw4::frag;
   using L = Layout<R, S>;
   static_assert(!SWIGLU || R == 2, "the SwiGLU epilogue pairs one gate tile with one up tile");
+  static_assert(!M1 || NT == 1, "one activation row fits one MMA column tile");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -116,6 +165,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       prefetch_tensormap(tm_codes);
       prefetch_tensormap(tm_scale);
       prefetch_tensormap(tm_zero);
+      if (XT) prefetch_tensormap(tm_x);
       const uint64_t pol = policy_evict_first();
       // Before the dependency on the previous kernel resolves, only pull the first stages' weights
       // into L2 (coherent: if that kernel wrote them, the loads below still see its writes).
@@ -138,12 +188,17 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
           break;
         }
         const uint32_t fb = full0 + 8 * st;
-        mbar_arrive_expect_tx(fb, L::kStageTx);
+        mbar_arrive_expect_tx(fb, L::kStageTx + (XT ? L::x_stage(bm) : 0));
         const uint32_t cdst = sbase + L::kCodes + st * L::kCodeStage;
         const uint32_t sdst = sbase + L::kScales + st * L::kScaleStage;
         const uint32_t zdst = sbase + L::kZeros + st * L::kScaleStage;
         const int kx = (s_begin + s) * (kStageK / 2);
         const int gx = (s_begin + s) * kConsumers;
+        if (XT) {
+          const uint32_t xdst = sbase + L::kX + st * L::x_stage(bm);
+          tma_load_2d(xdst, tm_x, (s_begin + s) * kStageK, x_row0, fb);
+          tma_load_2d(xdst + bm * 512, tm_x, (s_begin + s) * kStageK + 256, x_row0, fb);
+        }
         if (SWIGLU) {
           // 16-row boxes: gate tile then up tile (2048 bytes apart, swizzle phase unchanged).
           const int ru = r0 + up_offset;
@@ -169,55 +224,71 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     }
   } else {
     // ---------------- consumers ----------------
-    // x may be the previous kernel's output: wait for that grid (a no-op without a programmatic
-    // dependency) -- the producer is already streaming weights meanwhile.
+    // The producer loads x only after the previous grid completed; waiting here as well keeps this
+    // warp's stores of y behind that grid too (a no-op without a programmatic dependency).
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int g = lane >> 2, t = lane & 3;
     const int w = warp;              // group of the stage this warp owns
     const int half = w >> 2, q = w & 3;
     const uint32_t ones[4] = {kOnes, kOnes, kOnes, kOnes};
     const float zero4[4] = {0.f, 0.f, 0.f, 0.f};
+    // Shared-window byte offsets that do not change from stage to stage.  Rows 16 rt + g and
+    // 16 rt + g + 8 share the swizzle phase g, so every tile's codes sit at a constant stride.
+    const uint32_t code_off = L::kCodes + half * L::kCodeBox + g * 128 +
+                              (((2 * q + (t >> 1)) ^ g) << 4) + 8 * (t & 1);
+    const uint32_t scale_off = L::kScales + g * 16 + 2 * w;
+    const uint32_t zero_off = L::kZeros + g * 16 + 2 * w;
+    const uint32_t x_off = L::kX + half * bm * 512 + (64 * q + 16 * t) * 2;
     for (int s = 0; s < nstages; ++s) {
       const int st = s % S;
       if (!mbar_wait(full0 + 8 * st, (s / S) & 1, status)) {
         aborted = 1;
         break;
       }
-      const uint8_t* cbase = smem + L::kCodes + st * L::kCodeStage + half * L::kCodeBox;
-      const __half* sc = reinterpret_cast<const __half*>(smem + L::kScales + st * L::kScaleStage);
-      const __half* zr = reinterpret_cast<const __half*>(smem + L::kZeros + st * L::kScaleStage);
+      const uint32_t cb = sbase + code_off + st * L::kCodeStage;
+      const uint32_t sb = sbase + scale_off + st * L::kScaleStage;
+      const uint32_t zb = sbase + zero_off + st * L::kScaleStage;
       uint2 wa[R], wb[R];
       float s_a[R], s_b[R], z_a[R], z_b[R];
 #pragma unroll
       for (int rt = 0; rt < R; ++rt) {
-        const int ra = 16 * rt + g, rb = ra + 8;
-        const int chunk = 2 * q + (t >> 1);
-        wa[rt] = *reinterpret_cast<const uint2*>(cbase + ra * 128 + ((chunk ^ (ra & 7)) << 4) +
-                                                 8 * (t & 1));
-        wb[rt] = *reinterpret_cast<const uint2*>(cbase + rb * 128 + ((chunk ^ (rb & 7)) << 4) +
-                                                 8 * (t & 1));
-        s_a[rt] = __half2float(sc[ra * 8 + w]);
-        s_b[rt] = __half2float(sc[rb * 8 + w]);
-        z_a[rt] = fmaf(-128.f, s_a[rt], __half2float(zr[ra * 8 + w]));
-        z_b[rt] = fmaf(-128.f, s_b[rt], __half2float(zr[rb * 8 + w]));
+        wa[rt] = lds_v2(cb + rt * 2048);
+        wb[rt] = lds_v2(cb + rt * 2048 + 1024);
+        s_a[rt] = lds_half(sb + rt * 256);
+        s_b[rt] = lds_half(sb + rt * 256 + 128);
+        z_a[rt] = lds_half(zb + rt * 256);
+        z_b[rt] = lds_half(zb + rt * 256 + 128);
+      }
+      // x fragment of group (s * 8 + w) (box w / 4 of the stage), then release the slot
+      uint32_t b[NT][4][2];
+      if (XT) {
+        const uint32_t xb = sbase + x_off + st * L::x_stage(bm);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int m = nt * 8 + g;
+          x_frag_smem(xb + m * 512, m < Ml && m < bm, b[nt]);
+        }
+      } else {
+        const int kofs = (s_begin + s) * kStageK + 64 * w + 16 * t;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int m = nt * 8 + g;
+          load_x_frag(x + (int64_t)(x_row0 + min(m, Ml - 1)) * K + kofs, m < Ml, b[nt]);
+        }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * st);
 
-      // x fragment of group (s * 8 + w) and its sums over the group
-      const int kofs = (s_begin + s) * kStageK + 64 * w + 16 * t;
-      uint32_t b[NT][4][2];
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        const int m = nt * 8 + g;
-        load_x_frag(x + (int64_t)min(m, Ml - 1) * K + kofs, m < Ml, b[nt]);
-      }
-      float xs[NT][4];
+      // sums of x over the group; the code MMAs start from -128 * sum(x), which removes the
+      // +128 of the bf16 code encoding: acc = sum(x * c)
+      float xs[NT][4], c0[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         mma_bf16_16816(xs[nt], ones, b[nt][0][0], b[nt][0][1], zero4);
 #pragma unroll
         for (int j = 1; j < 4; ++j) mma_bf16_16816(xs[nt], ones, b[nt][j][0], b[nt][j][1], xs[nt]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) c0[nt][e] = -128.f * xs[nt][e];
       }
 #pragma unroll
       for (int rt = 0; rt < R; ++rt) {
@@ -229,17 +300,20 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
             if (j == 0)
-              mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], zero4);
+              mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], c0[nt]);
             else
               mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], acc[nt]);
           }
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
+          // one activation row (M1): only column 0 of the MMA tile carries data
           out[rt][nt][0] = fmaf(s_a[rt], acc[nt][0], fmaf(z_a[rt], xs[nt][0], out[rt][nt][0]));
-          out[rt][nt][1] = fmaf(s_a[rt], acc[nt][1], fmaf(z_a[rt], xs[nt][1], out[rt][nt][1]));
+          if (!M1)
+            out[rt][nt][1] = fmaf(s_a[rt], acc[nt][1], fmaf(z_a[rt], xs[nt][1], out[rt][nt][1]));
           out[rt][nt][2] = fmaf(s_b[rt], acc[nt][2], fmaf(z_b[rt], xs[nt][2], out[rt][nt][2]));
-          out[rt][nt][3] = fmaf(s_b[rt], acc[nt][3], fmaf(z_b[rt], xs[nt][3], out[rt][nt][3]));
+          if (!M1)
+            out[rt][nt][3] = fmaf(s_b[rt], acc[nt][3], fmaf(z_b[rt], xs[nt][3], out[rt][nt][3]));
         }
       }
     }

@@ -104,8 +104,8 @@ __global__ void __launch_bounds__(gemv_tma::kThreads)
   const int m0 = blockIdx.y * 16;
   if (m0 >= rows) return;  // unrouted expert (or past its rows): no weight is read
   constexpr int kRowsPerCta = SWIGLU ? 16 : 16 * R;
-  gemv_tma::body<NT, R, S, SWIGLU>(&maps.codes[z], &maps.scale[z], &maps.zero[z],
-                                   x + (int64_t)(beg + m0) * K, min(16, rows - m0), K,
+  gemv_tma::body<NT, R, S, SWIGLU, 1, false>(&maps.codes[z], &maps.scale[z], &maps.zero[z],
+                                             nullptr, x, beg + m0, 16, min(16, rows - m0), K,
                                    y + (int64_t)(beg + m0) * ldy, ldy, blockIdx.x * kRowsPerCta,
                                    n_out, up_offset, status);
 }
@@ -124,7 +124,7 @@ int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_row
   int dev = 0;
   cudaGetDevice(&dev);
   if (!((attr_set.load() >> dev) & 1)) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kDynSmem) !=
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kX + 1024) !=
         cudaSuccess)
       return fail(RW4_ECUDA, "moe_grouped: cannot set dynamic shared memory size");
     attr_set.fetch_or(1ull << dev);
@@ -149,7 +149,7 @@ int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_row
       if (st != RW4_OK) return st;
     }
     dim3 grid((n_out + rows_per_cta - 1) / rows_per_cta, (unsigned)((max_rows + 15) / 16), ne);
-    kern<<<grid, gemv_tma::kThreads, L::kDynSmem, stream>>>(
+    kern<<<grid, gemv_tma::kThreads, L::kX + 1024, stream>>>(
         maps, e0, offsets, static_cast<const __nv_bfloat16*>(x), K, n_out, n_out,
         static_cast<__nv_bfloat16*>(y), n_out, status);
     int st = launch_status("rw4_moe_grouped launch");
