@@ -277,6 +277,10 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
                                  "decode_tokens": new_tokens}
         del dec
         torch.cuda.empty_cache()
+    if stream_tokens <= 0:
+        del model
+        torch.cuda.empty_cache()
+        return out
     # streamed: the decoder layers leave HBM and stream from pinned host RAM every token
     streamed = RocketModel(model, device=device, vram_budget=vram_budget, window=2)
     ids = torch.randint(0, cfg.vocab_size, (1, 128), generator=gen).to(device)
@@ -432,7 +436,8 @@ def rw4_arm(args):
     if not args.no_decode:
         del weights, host_w, slots
         torch.cuda.empty_cache()
-        decode = decode_bench(device, args.decode_prompt, args.decode_tokens, (1, 16),
+        decode = decode_bench(device, args.decode_prompt, args.decode_tokens,
+                              tuple(int(b) for b in args.decode_batches.split(",")),
                               args.stream_tokens, int(4e9))
 
     cpu = None
@@ -558,9 +563,19 @@ def main():
                     help="kernel sweep over the sweep shapes x --sweep-m (one JSON line each)")
     ap.add_argument("--sweep-m", default="1,4,16,64,512,2048")
     ap.add_argument("--sweep-shapes", default="all", help="'all' or KxN[,KxN...]")
+    ap.add_argument("--decode-only", action="store_true",
+                    help="only the model decode section (one JSON line)")
+    ap.add_argument("--decode-batches", default="1,16")
     args = ap.parse_args()
     if args.sweep:
         return sweep(args)
+    if args.decode_only:
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        batches = tuple(int(b) for b in args.decode_batches.split(","))
+        print(json.dumps(decode_bench(device, args.decode_prompt, args.decode_tokens, batches,
+                                      args.stream_tokens, int(4e9))), flush=True)
+        return 0
     if args.impl == "reference":
         return reference_arm(args)
     return rw4_arm(args)

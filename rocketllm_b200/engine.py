@@ -23,6 +23,7 @@ import os
 import torch
 
 from . import quant  # noqa: F401 - registers the rw4 quantizer with transformers
+from .expert_stream import ExpertStreamer, expert_blob_bytes, is_rw4_experts
 from .streaming import WeightTransfer
 
 ALIGN = 256
@@ -37,9 +38,11 @@ class _LayerBlob:
         self.nbytes = nbytes
 
 
-def _layer_tensors(layer):
+def _layer_tensors(layer, skip_experts=False):
     out = []
     for mname, module in layer.named_modules():
+        if skip_experts and is_rw4_experts(module):
+            continue  # streamed per expert (expert_stream.py)
         for leaf, p in module._parameters.items():
             if p is not None:
                 out.append((module, leaf, "param", p))
@@ -49,8 +52,8 @@ def _layer_tensors(layer):
     return out
 
 
-def _pack_layer(layer):
-    tensors = _layer_tensors(layer)
+def _pack_layer(layer, skip_experts=False):
+    tensors = _layer_tensors(layer, skip_experts)
     entries, off = [], 0
     for module, leaf, kind, t in tensors:
         off = (off + ALIGN - 1) // ALIGN * ALIGN
@@ -81,14 +84,16 @@ class LayerStreamer:
     """Streams decoder layers from pinned host blobs through ``window`` device slots."""
 
     def __init__(self, layers, device, window=2, copy_streams=2, chunk_bytes=16 << 20,
-                 prefetching=True):
+                 prefetching=True, expert_slots=None):
         if window < 1:
             raise ValueError("window must be >= 1")
         self.layers = list(layers)
         self.device = torch.device(device)
         self.window = min(window, len(self.layers))
         self.prefetching = prefetching
-        self.blobs = [_pack_layer(layer) for layer in self.layers]
+        # routed experts stream one by one (expert_stream.py) when expert_slots is given
+        stream_experts = expert_slots is not None
+        self.blobs = [_pack_layer(layer, stream_experts) for layer in self.layers]
         self.slot_bytes = max(b.nbytes for b in self.blobs)
         self.slots = [torch.empty(self.slot_bytes, dtype=torch.uint8, device=self.device)
                       for _ in range(self.window)]
@@ -96,6 +101,12 @@ class LayerStreamer:
             _bind(blob, self.slots[i % self.window])
         self.xfer = WeightTransfer(device=self.device, copy_streams=copy_streams,
                                    chunk_bytes=chunk_bytes)
+        self.experts = None
+        if stream_experts:
+            moe = [(i, m) for i, layer in enumerate(self.layers) for m in layer.modules()
+                   if is_rw4_experts(m)]
+            if moe:
+                self.experts = ExpertStreamer(moe, self.device, expert_slots, self.xfer)
         self.tickets = [None] * len(self.layers)
         self.resident_slot = [None] * self.window   # which layer's bytes a slot holds (issued)
         self.fetches = 0
@@ -140,6 +151,7 @@ class LayerStreamer:
     def stats(self):
         return {"layers": len(self.layers), "window": self.window, "slot_bytes": self.slot_bytes,
                 "fetches": self.fetches, "bytes": self.bytes, "slot_hits": self.hits,
+                "experts": self.experts.stats() if self.experts else None,
                 "transfer": self.xfer.stats()}
 
     def close(self):
@@ -163,11 +175,18 @@ def _decoder_layers(model):
     return model.get_submodule(_layers_path(model))
 
 
-def footprint(model):
-    """``(resident_bytes, [bytes of each decoder layer])`` of ``model``."""
+def footprint(model, skip_experts=False):
+    """``(resident_bytes, [bytes of each decoder layer])`` of ``model`` (without the routed
+    experts' stacked weights when ``skip_experts``)."""
     layers = _decoder_layers(model)
     layer_bytes = [sum(t.numel() * t.element_size() for *_, t in _layer_tensors(l))
                    for l in layers]
+    if skip_experts:
+        dense = [sum(t.numel() * t.element_size() for *_, t in _layer_tensors(l, True))
+                 for l in layers]
+        total = sum(p.numel() * p.element_size() for p in model.parameters())
+        total += sum(b.numel() * b.element_size() for b in model.buffers())
+        return total - sum(layer_bytes), dense
     total = sum(p.numel() * p.element_size() for p in model.parameters())
     total += sum(b.numel() * b.element_size() for b in model.buffers())
     return total - sum(layer_bytes), layer_bytes
@@ -180,11 +199,14 @@ class RocketModel:
     ``vram_budget`` (bytes) bounds the model's device footprint: if the whole model fits it (or it
     is None) every layer is resident; otherwise the non-layer modules stay resident and at most
     ``window`` layer slots fit in what is left (at least one), and layers stream from pinned host
-    memory every token.
+    memory every token.  In a mixture-of-experts model the routed experts stream one by one
+    (``expert_streaming``): the layer slots hold the attention / router / norms only, and the rest
+    of the budget becomes an expert cache of at least one layer's experts.
     """
 
     def __init__(self, model_or_path, device="cuda", dtype=torch.bfloat16, vram_budget=None,
-                 window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20, **unused):
+                 window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
+                 expert_streaming=True, **unused):
         if isinstance(model_or_path, (str, os.PathLike)):
             from transformers import AutoModelForCausalLM
             model = AutoModelForCausalLM.from_pretrained(str(model_or_path), dtype=dtype)
@@ -199,18 +221,29 @@ class RocketModel:
         stream = vram_budget is not None and total > vram_budget
         if not stream:
             self.model.to(self.device)
+            return
+        experts = [m for m in layers.modules() if is_rw4_experts(m)]
+        expert_slots = None
+        if experts and expert_streaming:
+            _, dense_bytes = footprint(model, skip_experts=True)
+            per_layer = max(m.gate_up_proj_packed.shape[0] for m in experts)
+            eb = max(expert_blob_bytes(m) for m in experts)
+            left = max(0, vram_budget - rest - per_layer * eb)
+            window = max(1, min(window, int(left // max(dense_bytes))))
+            expert_slots = max(per_layer, int((vram_budget - rest - window * max(dense_bytes))
+                                              // eb))
         else:
             window = max(1, min(window, int(max(0, vram_budget - rest) // max(layer_bytes))))
-            # everything outside the decoder layers is resident: move the model with its layer
-            # list detached, then hand the layers to the streamer (they stay on the host)
-            parent_path, _, leaf = _layers_path(model).rpartition(".")
-            parent = self.model.get_submodule(parent_path) if parent_path else self.model
-            setattr(parent, leaf, torch.nn.ModuleList())
-            self.model.to(self.device)
-            setattr(parent, leaf, layers)
-            self.streamer = LayerStreamer(layers, self.device, window=window,
-                                          copy_streams=copy_streams, chunk_bytes=chunk_bytes,
-                                          prefetching=prefetching)
+        # everything outside the decoder layers is resident: move the model with its layer
+        # list detached, then hand the layers to the streamer (they stay on the host)
+        parent_path, _, leaf = _layers_path(model).rpartition(".")
+        parent = self.model.get_submodule(parent_path) if parent_path else self.model
+        setattr(parent, leaf, torch.nn.ModuleList())
+        self.model.to(self.device)
+        setattr(parent, leaf, layers)
+        self.streamer = LayerStreamer(layers, self.device, window=window,
+                                      copy_streams=copy_streams, chunk_bytes=chunk_bytes,
+                                      prefetching=prefetching, expert_slots=expert_slots)
 
     @property
     def config(self):

@@ -1,0 +1,201 @@
+"""Per-expert streaming of routed experts (the reference's fused expert-row reads and expert
+residency: ``rocketllm/base.py:1375-1464``, ``rocketllm/moe/expert_cache.py:261-316``).
+
+When an RW4 mixture-of-experts model does not fit the VRAM budget, each expert of each layer is
+packed once into its own pinned host blob (gate/up and down codes, fp16 scales and zeros at
+256-byte aligned offsets).  The device keeps a cache of expert slots.  In a streamed experts
+forward the routing is permuted on the device, the routed set is read back (one device->host sync
+per MoE layer, as the reference's ``.tolist()``), the sends of every routed expert that is not
+resident are issued together on the copy streams (``on_router``), the token gather runs meanwhile,
+and the grouped RW4 GEMV waits (device-side) for exactly those sends.  Experts no token routed to
+never cross PCIe.  Slots are recycled least-recently-used, never one holding an expert of the
+running layer; a send into a slot is ordered after all compute already queued, so the previous
+occupant's last reader has finished before its bytes are overwritten.
+"""
+import collections
+import types
+
+import torch
+
+from . import kernels
+
+ALIGN = 256
+_NAMES = ("gate_up_proj", "down_proj")
+_SUFFIXES = ("_packed", "_scale", "_zero_point")
+
+
+def is_rw4_experts(module):
+    return bool(getattr(module, "rw4", False))
+
+
+def expert_tensors(module, e):
+    """The six tensors of expert ``e`` of an RW4 stacked-experts module, in blob order."""
+    return [getattr(module, name + sfx)[e] for name in _NAMES for sfx in _SUFFIXES]
+
+
+class _ExpertBlob:
+    __slots__ = ("host", "entries", "nbytes")
+
+    def __init__(self, tensors):
+        self.entries, off = [], 0
+        for t in tensors:
+            off = (off + ALIGN - 1) // ALIGN * ALIGN
+            self.entries.append((t.dtype, tuple(t.shape), off))
+            off += t.numel() * t.element_size()
+        self.nbytes = (off + ALIGN - 1) // ALIGN * ALIGN
+        self.host = torch.empty(self.nbytes, dtype=torch.uint8).pin_memory()
+        for (dtype, shape, o), t in zip(self.entries, tensors):
+            n = t.numel() * t.element_size()
+            self.host[o:o + n].copy_(t.detach().contiguous().view(-1).view(torch.uint8))
+
+    def views(self, slot):
+        out = []
+        for dtype, shape, off in self.entries:
+            n = 1
+            for d in shape:
+                n *= d
+            size = n * torch.empty((), dtype=dtype).element_size()
+            out.append(slot[off:off + size].view(dtype).view(shape))
+        return out
+
+
+def expert_blob_bytes(module):
+    """Bytes of one expert's blob (the device slot size it needs)."""
+    off = 0
+    for t in expert_tensors(module, 0):
+        off = (off + ALIGN - 1) // ALIGN * ALIGN + t.numel() * t.element_size()
+    return (off + ALIGN - 1) // ALIGN * ALIGN
+
+
+class ExpertStreamer:
+    """Routed experts of ``moe`` (a list of ``(layer_index, experts_module)``) streamed from pinned
+    host blobs into ``num_slots`` device slots through ``xfer`` (a ``WeightTransfer``)."""
+
+    def __init__(self, moe, device, num_slots, xfer):
+        self.device = torch.device(device)
+        self.xfer = xfer
+        self.blobs = {}
+        self.num_experts = {}
+        for layer, module in moe:
+            e_count = module.gate_up_proj_packed.shape[0]
+            self.num_experts[layer] = e_count
+            for e in range(e_count):
+                self.blobs[(layer, e)] = _ExpertBlob(expert_tensors(module, e))
+        max_e = max(self.num_experts.values())
+        if num_slots < max_e:
+            raise ValueError(f"{num_slots} expert slots cannot hold one layer's {max_e} experts")
+        self.slot_bytes = max(b.nbytes for b in self.blobs.values())
+        self.slots = [torch.empty(self.slot_bytes, dtype=torch.uint8, device=self.device)
+                      for _ in range(min(num_slots, len(self.blobs)))]
+        self.owner = [None] * len(self.slots)     # slot -> (layer, expert)
+        self.where = {}                           # (layer, expert) -> slot
+        self.lru = collections.OrderedDict()      # resident keys, least recently used first
+        self.tickets = {}
+        self.frequency = collections.Counter()    # routed count per (layer, expert)
+        self.fetches = 0
+        self.hits = 0
+        self.bytes = 0
+        for layer, module in moe:
+            # the stacked tensors now live in the host blobs; the module keeps empty stand-ins
+            for name in _NAMES:
+                for sfx in _SUFFIXES:
+                    p = getattr(module, name + sfx)
+                    module._parameters[name + sfx] = torch.nn.Parameter(
+                        torch.empty((0,) + tuple(p.shape[1:]), dtype=p.dtype, device=self.device),
+                        requires_grad=False)
+            module._rw4_stream = (self, layer)
+            module.forward = types.MethodType(streamed_experts_forward, module)
+
+    # -- residency ---------------------------------------------------------------------------------
+
+    def _slot_for(self, protect):
+        for s, key in enumerate(self.owner):
+            if key is None:
+                return s
+        for key in self.lru:
+            if key not in protect:
+                return self.where[key]
+        raise RuntimeError("no expert slot can be recycled")
+
+    def on_router(self, layer, selected, compute):
+        """The layer's router chose ``selected``: issue the sends of the ones not resident, all
+        together, ordered after the compute queued on ``compute``.  Returns how many started."""
+        protect = {(layer, e) for e in selected}
+        started = 0
+        for e in selected:
+            key = (layer, e)
+            self.frequency[key] += 1
+            if key in self.where:
+                self.hits += 1
+                self.lru.move_to_end(key)
+                continue
+            s = self._slot_for(protect)
+            old = self.owner[s]
+            if old is not None:
+                del self.where[old]
+                del self.lru[old]
+                self.tickets.pop(old, None)
+            blob = self.blobs[key]
+            self.tickets[key] = self.xfer.send_buffer(blob.host, out=self.slots[s][:blob.nbytes],
+                                                      after=compute)
+            self.owner[s] = key
+            self.where[key] = s
+            self.lru[key] = None
+            self.fetches += 1
+            self.bytes += blob.nbytes
+            started += 1
+        return started
+
+    def wait(self, layer, selected, compute):
+        """Make ``compute`` wait (device-side) for the sends of the selected experts."""
+        for e in selected:
+            handle = self.tickets.pop((layer, e), None)
+            if handle is not None:
+                handle.resolve(compute)
+
+    def triples(self, layer, selected):
+        """Per-expert ``(packed, scale, zero)`` lists for gate/up and down; experts outside
+        ``selected`` get the first selected expert's views (the kernel never reads them)."""
+        views = {e: self.blobs[(layer, e)].views(self.slots[self.where[(layer, e)]])
+                 for e in selected}
+        first = views[selected[0]]
+        gate_up, down = [], []
+        for e in range(self.num_experts[layer]):
+            v = views.get(e, first)
+            gate_up.append(tuple(v[0:3]))
+            down.append(tuple(v[3:6]))
+        return gate_up, down
+
+    def stats(self):
+        return {"expert_slots": len(self.slots), "slot_bytes": self.slot_bytes,
+                "fetches": self.fetches, "hits": self.hits, "bytes": self.bytes,
+                "resident": len(self.where)}
+
+
+def streamed_experts_forward(self, hidden_states, top_k_index, top_k_weights):
+    """``rw4_experts_forward`` for a module whose experts stream (same signature and result)."""
+    streamer, layer = self._rw4_stream
+    t, h = hidden_states.shape
+    k = top_k_index.shape[1]
+    x = hidden_states if hidden_states.dtype == torch.bfloat16 else hidden_states.to(torch.bfloat16)
+    if not x.is_contiguous():
+        x = x.contiguous()
+    idx = top_k_index.to(torch.int64).contiguous()
+    w = top_k_weights.contiguous()
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    n_exp = streamer.num_experts[layer]
+    compute = torch.cuda.current_stream(streamer.device)
+    perm, inv, offsets = kernels.moe_permute(idx, n_exp)
+    counts = offsets.cpu().tolist()          # the routed set: one device->host sync per layer
+    selected = [e for e in range(n_exp) if counts[e + 1] > counts[e]]
+    if not selected:
+        return torch.zeros_like(hidden_states)
+    streamer.on_router(layer, selected, compute)
+    xp = kernels.moe_gather(x, perm, k)      # runs while the experts cross PCIe
+    streamer.wait(layer, selected, compute)
+    gate_up, down = streamer.triples(layer, selected)
+    act = kernels.moe_grouped(xp, offsets, gate_up, act=1, max_rows=t * k)
+    yp = kernels.moe_grouped(act, offsets, down, act=0, max_rows=t * k)
+    out = kernels.moe_combine(yp, inv, idx, w)
+    return out if hidden_states.dtype == torch.bfloat16 else out.to(hidden_states.dtype)
