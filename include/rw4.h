@@ -74,8 +74,8 @@ int rw4_quantize(const void* w, int32_t w_dtype, int64_t N, int64_t K, int32_t g
  * rw4_linear: y[M, N] = x[M, K] . W[N, K]^T, bf16 in and out, fp32 accumulation, W in RW4.
  * Replaces the nn.Linear / F.linear call a transformers module makes on a dequantized weight
  * (transformers models/llama/modeling_llama.py:171-184 via rocketllm/base.py:848-855).
- * M <= 16 runs the dequant-GEMV; larger M the tensor-core GEMM.  group must be 64 and K a
- * multiple of 64; x, y, packed, scale and zero must be 16-byte aligned.
+ * M <= 16 runs the dequant-GEMV; larger M the tensor-core GEMM (rw4_linear_path).  group must be 64 and K a multiple of 64; x, y and packed
+ * must be 16-byte aligned, scale and zero 8-byte aligned.
  */
 int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
@@ -84,6 +84,12 @@ int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
 /* Which kernel rw4_linear would launch for (M, K, N): 1 = GEMV, 2 = tcgen05 GEMM,
  * 3 = GEMV over 16-row slices. Negative on invalid shapes. Host-only, launches nothing. */
 int rw4_linear_path(int64_t M, int64_t K, int64_t N);
+
+/* rw4_linear on a given path (1 or 3: GEMV / GEMV slices, 2: tcgen05 GEMM, which needs M > 16)
+ * instead of the one rw4_linear_path picks; for tests and measurements of each kernel. */
+int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                       const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
+                       void* y_bf16, int32_t path, void* stream);
 
 /* Reads the library's device status word on the current device after the work queued on `stream`
  * (synchronises that stream): bit 1 = a bounded wait inside a kernel gave up (the kernel returned

@@ -71,6 +71,11 @@ extern "C" int rw4_last_error(char* buf, size_t n) {
   return (int)e.size();
 }
 
+// Above 16 rows the tensor-core GEMM runs whenever it applies: it multiplies by the reference's
+// bf16-rounded dequantized weight, as the reference does, while the GEMV multiplies by the exact
+// weight.  (Measured: GEMV batch slices would be faster up to M = 32 on every sweep shape and up to
+// M = 128 on small weights, but mixing the two roundings inside one prefill moved a Mixtral
+// model's logits past the 2e-2 parity bar; rw4_linear_on_path runs either kernel on request.)
 extern "C" int rw4_linear_path(int64_t M, int64_t K, int64_t N) {
   if (M < 0 || K <= 0 || N < 0 || K % 64) return RW4_EINVAL;
   if (M <= 16) return 1;
@@ -78,24 +83,35 @@ extern "C" int rw4_linear_path(int64_t M, int64_t K, int64_t N) {
   return 3;
 }
 
-extern "C" int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
-                          const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
-                          void* y_bf16, void* stream) {
+extern "C" int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                                  const void* scale_f16, const void* zero_f16, int64_t N,
+                                  int32_t group, void* y_bf16, int32_t path, void* stream) {
   using namespace rw4;
   int st = check_linear_args("rw4_linear", x_bf16, M, K, packed, scale_f16, zero_f16, N, group,
                              y_bf16);
   if (st != RW4_OK || M == 0 || N == 0) return st;
+  if (path == 2 && !gemm_tc_supported(M, K, N))
+    return fail(RW4_EINVAL, "rw4_linear: the tensor-core GEMM needs M > 16 (M=%lld)",
+                (long long)M);
   cudaStream_t s = as_stream(stream);
-  switch (rw4_linear_path(M, K, N)) {
+  switch (path) {
     case 1:
     case 3:
       return gemv_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s);
     case 2:
       return gemm_tc_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s);
     default:
-      return fail(RW4_EINVAL, "rw4_linear: no path for M=%lld K=%lld N=%lld", (long long)M,
-                  (long long)K, (long long)N);
+      return fail(RW4_EINVAL, "rw4_linear: no path %d for M=%lld K=%lld N=%lld", path,
+                  (long long)M, (long long)K, (long long)N);
   }
+}
+
+extern "C" int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                          const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
+                          void* y_bf16, void* stream) {
+  const int path = rw4_linear_path(M, K, N);
+  return rw4_linear_on_path(x_bf16, M, K, packed, scale_f16, zero_f16, N, group, y_bf16,
+                            path < 0 ? 1 : path, stream);
 }
 
 // ---- device status word and TMA descriptors ---------------------------------------------------

@@ -23,10 +23,12 @@ __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
                         const __grid_constant__ CUtensorMap tm_x,
                         const __nv_bfloat16* __restrict__ x, int bm, int M, int K, int N,
                         __nv_bfloat16* __restrict__ y, unsigned int* status) {
-  const int m0 = blockIdx.y * 16;
+  // batch slices are the fastest grid dimension: the CTAs of all slices of one row tile run
+  // together, so the slices after the first find the tile's weights in L2
+  const int m0 = blockIdx.x * 16;
   body<NT, R, S, false, KS, XT, M1>(&tm_codes, &tm_scale, &tm_zero, &tm_x, x, m0, bm,
                                     min(16, M - m0), K, y + (int64_t)m0 * N, N,
-                                    blockIdx.x * Layout<R, S>::BR, N, 0, status);
+                                    blockIdx.y * Layout<R, S>::BR, N, 0, status);
 }
 
 bool pdl_enabled() {
@@ -87,7 +89,9 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   }
   unsigned int* status = device_status_ptr();
   if (!status) return fail(RW4_ECUDA, "gemv_tma: device status word unavailable");
-  dim3 grid((N + L::BR - 1) / L::BR, (M + 15) / 16, KS);
+  const int64_t tiles = (N + L::BR - 1) / L::BR;
+  if (tiles > 65535) return fail(RW4_EINVAL, "gemv_tma: N=%d needs more than 65535 row tiles", N);
+  dim3 grid((M + 15) / 16, (unsigned)tiles, KS);
   // Programmatic dependent launch: this grid may start while the previous kernel on the stream
   // drains; it streams its weights at once and waits (griddepcontrol.wait) only before it reads x.
   cudaLaunchConfig_t cfg = {};

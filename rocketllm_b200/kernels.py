@@ -77,10 +77,11 @@ def quantize(w, group=64):
     return packed, scale, zero, groups * g - k
 
 
-def linear(x, packed, scale, zero, out=None):
+def linear(x, packed, scale, zero, out=None, path=None):
     """``y = x . W^T`` with ``x`` bf16 ``[..., K]`` and W in RW4; returns bf16 ``[..., N]``.
 
     ``x`` may be a strided view (e.g. the last position of every sequence); it is compacted first.
+    ``path`` forces a kernel (1 / 3 GEMV, 2 tcgen05 GEMM) instead of the library's choice.
     """
     if not x.is_cuda:
         raise ValueError("RW4 kernels take CUDA tensors only (there is no CPU path); got a "
@@ -99,8 +100,12 @@ def linear(x, packed, scale, zero, out=None):
     m = x2.shape[0]
     if out is None:
         out = torch.empty((*x.shape[:-1], n), dtype=torch.bfloat16, device=x.device)
-    _lib.call("rw4_linear", x2.data_ptr(), m, k, packed.data_ptr(), scale.data_ptr(),
-              zero.data_ptr(), n, 64, out.data_ptr(), _stream())
+    if path is None:
+        _lib.call("rw4_linear", x2.data_ptr(), m, k, packed.data_ptr(), scale.data_ptr(),
+                  zero.data_ptr(), n, 64, out.data_ptr(), _stream())
+    else:
+        _lib.call("rw4_linear_on_path", x2.data_ptr(), m, k, packed.data_ptr(), scale.data_ptr(),
+                  zero.data_ptr(), n, 64, out.data_ptr(), int(path), _stream())
     return out
 
 
