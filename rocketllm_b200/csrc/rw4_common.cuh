@@ -76,6 +76,17 @@ __device__ __forceinline__ uint2 ldg_u2(const void* p) {
   return __ldg(reinterpret_cast<const uint2*>(p));
 }
 
+// D = A(16x16 f16, row) * B(16x8 f16, col) + C, fp32 accumulate (warp-wide).
+__device__ __forceinline__ void mma_f16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                              uint32_t b1, const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%10,%11,%12,%13};\n"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
+        "f"(c[2]), "f"(c[3]));
+}
+
 // D = A(16x16 bf16, row) * B(16x8 bf16, col) + C, fp32 accumulate (warp-wide).
 __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                                uint32_t b1, const float (&c)[4]) {

@@ -14,8 +14,10 @@ using namespace rw4::gemv_tma;
 // schedule (16 consumer warps per SM sharing the ALU pipe with the producers).  KS > 1 splits K
 // over a (1, 1, KS) thread-block cluster (grid.z = KS) reduced through distributed shared memory.
 // XT: activations through the TMA ring (default); otherwise the consumers load them from global
-// memory (RW4_GEMV_X_GLOBAL=1, kept for comparison).
-template <int NT, int R, int S, int KS, bool XT, bool M1>
+// memory (RW4_GEMV_X_GLOBAL=1, kept for comparison).  M1: one activation row.  XF: one row, in
+// fp16 from shared memory (rw4_gemv_frag.cuh), the default for M = 1 when the CTA's K range fits
+// 32 KB of shared memory (RW4_GEMV_NO_F16=1 keeps bf16).
+template <int NT, int R, int S, int KS, bool XT, bool M1, bool XF = false>
 __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
     rw4_gemv_tma_kernel(const __grid_constant__ CUtensorMap tm_codes,
                         const __grid_constant__ CUtensorMap tm_scale,
@@ -26,9 +28,9 @@ __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
   // batch slices are the fastest grid dimension: the CTAs of all slices of one row tile run
   // together, so the slices after the first find the tile's weights in L2
   const int m0 = blockIdx.x * 16;
-  body<NT, R, S, false, KS, XT, M1>(&tm_codes, &tm_scale, &tm_zero, &tm_x, x, m0, bm,
-                                    min(16, M - m0), K, y + (int64_t)m0 * N, N,
-                                    blockIdx.y * Layout<R, S>::BR, N, 0, status);
+  body<NT, R, S, false, KS, XT, M1, XF>(&tm_codes, &tm_scale, &tm_zero, &tm_x, x, m0, bm,
+                                        min(16, M - m0), K, y + (int64_t)m0 * N, N,
+                                        blockIdx.y * Layout<R, S>::BR, N, 0, status);
 }
 
 bool pdl_enabled() {
@@ -39,6 +41,13 @@ bool pdl_enabled() {
 // Smallest dynamic shared memory request that keeps a third CTA off an SM (228 KB per SM, 1 KB
 // reserved per CTA).
 constexpr int kTwoPerSmSmem = 228 * 1024 / 3 + 1024;
+
+constexpr int kF16MaxStages = 32;  // fp16 activation row in shared memory: 1 KB per stage
+
+bool no_f16() {
+  static const bool on = getenv("RW4_GEMV_NO_F16") != nullptr;
+  return on;
+}
 
 bool x_global() {
   static const bool on = getenv("RW4_GEMV_X_GLOBAL") != nullptr;
@@ -70,22 +79,26 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   if (st != RW4_OK) return st;
   const bool xt = !x_global();
   const bool m1 = NT == 1 && M == 1;
-  auto kern = xt ? (m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, true, NT == 1>
-                       : rw4_gemv_tma_kernel<NT, R, S, KS, true, false>)
-                 : (m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, false, NT == 1>
-                       : rw4_gemv_tma_kernel<NT, R, S, KS, false, false>);
+  const int cta_stages = ((K / kStageK) + KS - 1) / KS;
+  const bool xf = m1 && xt && !no_f16() && cta_stages <= kF16MaxStages;
+  const int variant = xf ? 4 : (xt ? 0 : 1) + (m1 ? 2 : 0);
+  auto kern = xf ? rw4_gemv_tma_kernel<NT, R, S, KS, false, NT == 1, NT == 1>
+              : xt ? (m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, true, NT == 1>
+                         : rw4_gemv_tma_kernel<NT, R, S, KS, true, false>)
+                   : (m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, false, NT == 1>
+                         : rw4_gemv_tma_kernel<NT, R, S, KS, false, false>);
   // The dynamic shared memory limit is a per-device function attribute: set it once per device
-  // and kernel (bit 16 * variant + dev).
-  static std::atomic<uint64_t> attr_set{0};
+  // and kernel variant.
+  static std::atomic<uint32_t> attr_set[5];
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint64_t bit = 1ull << (dev + 16 * ((xt ? 0 : 1) + (m1 ? 2 : 0)));
-  if (!(attr_set.load() & bit)) {
-    const int most = L::dyn_smem(8 * NT) > kTwoPerSmSmem ? L::dyn_smem(8 * NT) : kTwoPerSmSmem;
+  if (!(attr_set[variant].load() & (1u << dev))) {
+    const int need = xf ? L::kX + kF16MaxStages * 1024 + 1024 : L::dyn_smem(8 * NT);
+    const int most = need > kTwoPerSmSmem ? need : kTwoPerSmSmem;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most) !=
         cudaSuccess)
       return fail(RW4_ECUDA, "gemv_tma: cannot set dynamic shared memory size");
-    attr_set.fetch_or(bit);
+    attr_set[variant].fetch_or(1u << dev);
   }
   unsigned int* status = device_status_ptr();
   if (!status) return fail(RW4_ECUDA, "gemv_tma: device status word unavailable");
@@ -100,7 +113,8 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   // At most two CTAs per SM: with smaller rings the block scheduler may stack three or four CTAs
   // of a one-wave grid on some SMs and leave others idle (measured: M=1 slower than M=8 on the
   // 4096-row shapes until the shared-memory request made a third CTA impossible).
-  const int smem_need = xt ? L::dyn_smem(bm) : L::kX + 1024;
+  const int smem_need = xf ? L::kX + cta_stages * 1024 + 1024
+                        : xt ? L::dyn_smem(bm) : L::kX + 1024;
   cfg.dynamicSmemBytes = smem_need > kTwoPerSmSmem ? smem_need : kTwoPerSmSmem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];

@@ -110,7 +110,11 @@ __device__ __forceinline__ void x_frag_smem(uint32_t a, bool valid, uint32_t (&b
 // Plain: writes y[m, r0 + r] for r0 + r < n_out.  SWIGLU: writes y[m, r0 + r] for r0 + r < n_out
 // (= I) from weight rows r0 + r (gate) and r0 + I + r (up).
 // M1: the launch has exactly one activation row (NT == 1, M == 1).
-template <int NT, int R, int S, bool SWIGLU, int KS = 1, bool XT = true, bool M1 = false>
+// XF (with M1, without XT): the consumers first convert the CTA's activation row into fp16 pair
+// registers in shared memory (x16_to_f16_frag, 1 KB per stage) and the MMAs run in fp16
+// (a_frag_f16: one shift per four codes); requires nstages * 1 KB of shared memory at kX.
+template <int NT, int R, int S, bool SWIGLU, int KS = 1, bool XT = true, bool M1 = false,
+          bool XF = false>
 __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensorMap* tm_scale,
                                      const CUtensorMap* tm_zero, const CUtensorMap* tm_x,
                                      const __nv_bfloat16* __restrict__ x, int x_row0, int bm,
@@ -121,6 +125,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
   using L = Layout<R, S>;
   static_assert(!SWIGLU || R == 2, "the SwiGLU epilogue pairs one gate tile with one up tile");
   static_assert(!M1 || NT == 1, "one activation row fits one MMA column tile");
+  static_assert(!XF || (M1 && !XT && !SWIGLU), "the fp16 path is the one-row dense GEMV");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -239,6 +244,21 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     const uint32_t scale_off = L::kScales + g * 16 + 2 * w;
     const uint32_t zero_off = L::kZeros + g * 16 + 2 * w;
     const uint32_t x_off = L::kX + half * bm * 512 + (64 * q + 16 * t) * 2;
+    if (XF) {
+      // the CTA's activation row -> fp16 pair registers, 32 bytes per 16 values, in shared memory
+      const __nv_bfloat16* xr = x + (int64_t)x_row0 * K + (int64_t)s_begin * kStageK;
+      const int chunks = nstages * (kStageK / 16);
+      for (int c = threadIdx.x; c < chunks; c += kConsumers * 32) {
+        uint32_t o[8];
+        x16_to_f16_frag(ldg_u4(xr + 16 * c), ldg_u4(xr + 16 * c + 8), o);
+        const uint32_t a = sbase + L::kX + 32 * c;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(o[0]), "r"(o[1]),
+                     "r"(o[2]), "r"(o[3]) : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a + 16), "r"(o[4]),
+                     "r"(o[5]), "r"(o[6]), "r"(o[7]) : "memory");
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");  // consumers only
+    }
     for (int s = 0; s < nstages; ++s) {
       const int st = s % S;
       if (!mbar_wait(full0 + 8 * st, (s / S) & 1, status)) {
@@ -261,7 +281,12 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       }
       // x fragment of group (s * 8 + w) (box w / 4 of the stage), then release the slot
       uint32_t b[NT][4][2];
-      if (XT) {
+      if (XF) {
+        const uint32_t xa = sbase + L::kX + 32 * (32 * s + 4 * w + t);
+        const uint4 v0 = lds_v4(xa), v1 = lds_v4(xa + 16);
+        b[0][0][0] = v0.x; b[0][0][1] = v0.y; b[0][1][0] = v0.z; b[0][1][1] = v0.w;
+        b[0][2][0] = v1.x; b[0][2][1] = v1.y; b[0][3][0] = v1.z; b[0][3][1] = v1.w;
+      } else if (XT) {
         const uint32_t xb = sbase + x_off + st * L::x_stage(bm);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -282,13 +307,32 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       // sums of x over the group; the code MMAs start from -128 * sum(x), which removes the
       // +128 of the bf16 code encoding: acc = sum(x * c)
       float xs[NT][4], c0[NT][4];
+      if (XF) {
+        // 2^-8 sum(x) (A = 1 on even-k slots, 16 on odd-k slots) and the code offset
+        // sum(1024 * scaled x) that the code MMAs start from (negated); everything accumulated is
+        // then 2^-8 times the true value, undone once per output in the epilogue
+        const uint32_t unscale[4] = {kF16_1, kF16_1, kF16_16, kF16_16};
+        const uint32_t k1024[4] = {kMagicF16, kMagicF16, kMagicF16, kMagicF16};
+        float off[4];
+        mma_f16_16816(xs[0], unscale, b[0][0][0], b[0][0][1], zero4);
+        mma_f16_16816(off, k1024, b[0][0][0], b[0][0][1], zero4);
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        mma_bf16_16816(xs[nt], ones, b[nt][0][0], b[nt][0][1], zero4);
+        for (int j = 1; j < 4; ++j) {
+          mma_f16_16816(xs[0], unscale, b[0][j][0], b[0][j][1], xs[0]);
+          mma_f16_16816(off, k1024, b[0][j][0], b[0][j][1], off);
+        }
 #pragma unroll
-        for (int j = 1; j < 4; ++j) mma_bf16_16816(xs[nt], ones, b[nt][j][0], b[nt][j][1], xs[nt]);
+        for (int e = 0; e < 4; ++e) c0[0][e] = -off[e];
+      } else {
 #pragma unroll
-        for (int e = 0; e < 4; ++e) c0[nt][e] = -128.f * xs[nt][e];
+        for (int nt = 0; nt < NT; ++nt) {
+          mma_bf16_16816(xs[nt], ones, b[nt][0][0], b[nt][0][1], zero4);
+#pragma unroll
+          for (int j = 1; j < 4; ++j)
+            mma_bf16_16816(xs[nt], ones, b[nt][j][0], b[nt][j][1], xs[nt]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) c0[nt][e] = -128.f * xs[nt][e];
+        }
       }
 #pragma unroll
       for (int rt = 0; rt < R; ++rt) {
@@ -296,6 +340,11 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           uint32_t a[4];
+          if (XF) {
+            a_frag_f16(wa[rt], wb[rt], j, a);
+            mma_f16_16816(acc[0], a, b[0][j][0], b[0][j][1], j == 0 ? c0[0] : acc[0]);
+            continue;
+          }
           a_frag(wa[rt], wb[rt], j, a);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
@@ -305,6 +354,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
               mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], acc[nt]);
           }
         }
+
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           // one activation row (M1): only column 0 of the MMA tile carries data
@@ -401,7 +451,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
         const float act = __bfloat162float(__float2bfloat16_rn(gb / (1.f + expf(-gb))));
         v = act * ub;
       } else {
-        v = part[i][0];
+        v = XF ? part[i][0] * 256.f : part[i][0];
       }
       y[(int64_t)m * ldy + n] = __float2bfloat16_rn(v);
     }
