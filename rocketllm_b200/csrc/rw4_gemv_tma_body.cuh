@@ -125,7 +125,8 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
   using L = Layout<R, S>;
   static_assert(!SWIGLU || R == 2, "the SwiGLU epilogue pairs one gate tile with one up tile");
   static_assert(!M1 || NT == 1, "one activation row fits one MMA column tile");
-  static_assert(!XF || (M1 && !XT && !SWIGLU), "the fp16 path is the one-row dense GEMV");
+  static_assert(!XF || (M1 && !XT), "the fp16 path is the one-row GEMV");
+  if (M1) Ml = min(Ml, 1);  // a one-row launch never computes or stores a second row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -446,8 +447,9 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     if (o < kOut && n < n_out && m < Ml) {
       float v;
       if (SWIGLU) {
-        const float gb = __bfloat162float(__float2bfloat16_rn(part[i][0]));
-        const float ub = __bfloat162float(__float2bfloat16_rn(part[i][SWIGLU ? 1 : 0]));
+        const float unit = XF ? 256.f : 1.f;
+        const float gb = __bfloat162float(__float2bfloat16_rn(part[i][0] * unit));
+        const float ub = __bfloat162float(__float2bfloat16_rn(part[i][SWIGLU ? 1 : 0] * unit));
         const float act = __bfloat162float(__float2bfloat16_rn(gb / (1.f + expf(-gb))));
         v = act * ub;
       } else {

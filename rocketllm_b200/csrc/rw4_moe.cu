@@ -92,25 +92,30 @@ struct ExpertMaps {
   CUtensorMap zero[kMaxExperts];
 };
 
-template <int NT, int R, int S, bool SWIGLU>
+// XF: every expert has at most one row (a one-token step): the fp16 one-row GEMV body.
+template <int NT, int R, int S, bool SWIGLU, bool XF = false>
 __global__ void __launch_bounds__(gemv_tma::kThreads)
     moe_grouped_kernel(const __grid_constant__ ExpertMaps maps, int e0,
                        const int32_t* __restrict__ offsets, const __nv_bfloat16* __restrict__ x,
                        int K, int n_out, int up_offset, __nv_bfloat16* __restrict__ y,
-                       int64_t ldy, unsigned int* status) {
+                       int64_t ldy, int max_rows, unsigned int* status) {
   const int z = blockIdx.z;
   const int beg = offsets[e0 + z];
   const int rows = offsets[e0 + z + 1] - beg;
   const int m0 = blockIdx.y * 16;
+  // more rows than the launch's max_rows: flag it (those rows get no output)
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && rows > max_rows)
+    atomicOr(status, RW4_DEVERR_ROWS);
   if (m0 >= rows) return;  // unrouted expert (or past its rows): no weight is read
   constexpr int kRowsPerCta = SWIGLU ? 16 : 16 * R;
-  gemv_tma::body<NT, R, S, SWIGLU, 1, false>(&maps.codes[z], &maps.scale[z], &maps.zero[z],
-                                             nullptr, x, beg + m0, 16, min(16, rows - m0), K,
+  gemv_tma::body<NT, R, S, SWIGLU, 1, false, XF, XF>(&maps.codes[z], &maps.scale[z],
+                                                     &maps.zero[z], nullptr, x, beg + m0, 16,
+                                                     min(16, rows - m0), K,
                                    y + (int64_t)(beg + m0) * ldy, ldy, blockIdx.x * kRowsPerCta,
                                    n_out, up_offset, status);
 }
 
-template <int NT, int R, int S, bool SWIGLU>
+template <int NT, int R, int S, bool SWIGLU, bool XF = false>
 int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_rows,
                    const uint8_t* const* packed_e, const void* const* scale_e,
                    const void* const* zero_e, int K, int N, void* y, cudaStream_t stream) {
@@ -119,12 +124,15 @@ int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_row
   const int n_out = SWIGLU ? N / 2 : N;
   const int rows_per_cta = SWIGLU ? 16 : L::BR;
   const int G = K / 64;
-  auto kern = moe_grouped_kernel<NT, R, S, SWIGLU>;
+  auto kern = moe_grouped_kernel<NT, R, S, SWIGLU, XF>;
+  const int smem = L::kX + (XF ? K / 512 + 1 : 1) * 1024;  // + fp16 activation row (1 KB/stage)
   static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!((attr_set.load() >> dev) & 1)) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kX + 1024) !=
+    // the largest request this kernel can make (K / 512 <= 32 on the fp16 one-row path)
+    const int most = L::kX + (XF ? 33 : 1) * 1024;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most) !=
         cudaSuccess)
       return fail(RW4_ECUDA, "moe_grouped: cannot set dynamic shared memory size");
     attr_set.fetch_or(1ull << dev);
@@ -149,9 +157,10 @@ int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_row
       if (st != RW4_OK) return st;
     }
     dim3 grid((n_out + rows_per_cta - 1) / rows_per_cta, (unsigned)((max_rows + 15) / 16), ne);
-    kern<<<grid, gemv_tma::kThreads, L::kX + 1024, stream>>>(
+    kern<<<grid, gemv_tma::kThreads, smem, stream>>>(
         maps, e0, offsets, static_cast<const __nv_bfloat16*>(x), K, n_out, n_out,
-        static_cast<__nv_bfloat16*>(y), n_out, status);
+        static_cast<__nv_bfloat16*>(y), n_out,
+        (int)max_rows, status);
     int st = launch_status("rw4_moe_grouped launch");
     if (st) return st;
   }
@@ -258,7 +267,8 @@ extern "C" int rw4_moe_grouped(const void* x_perm_bf16, const int32_t* offsets, 
   if (act != 0 && act != 1) return fail(RW4_EINVAL, "rw4_moe_grouped: act %d", act);
   if (act == 1 && (N % 2 || (N / 2) % 8))
     return fail(RW4_EINVAL, "rw4_moe_grouped: SwiGLU needs N = 2*I with I %% 8 == 0");
-  if (N > (1 << 30) || K > (1 << 30)) return fail(RW4_EINVAL, "rw4_moe_grouped: too large");
+  if (N > (1 << 30) || K > (1 << 30) || max_rows > (1 << 30))
+    return fail(RW4_EINVAL, "rw4_moe_grouped: too large");
   if (max_rows == 0) return RW4_OK;
   if (!x_perm_bf16 || !offsets || !packed_e || !scale_e || !zero_e || !y_perm_bf16)
     return fail(RW4_EINVAL, "rw4_moe_grouped: null pointer");
@@ -266,6 +276,16 @@ extern "C" int rw4_moe_grouped(const void* x_perm_bf16, const int32_t* offsets, 
     return fail(RW4_EINVAL, "rw4_moe_grouped: activations must be 16-byte aligned");
   cudaStream_t s = rw4::as_stream(stream);
   const bool wide = max_rows > 8;
+  // one row per expert (a one-token step: a token's top-k experts are distinct) and a K range
+  // whose fp16 activation row fits 32 KB of shared memory: the fp16 one-row GEMV
+  const bool one = max_rows == 1 && K / 512 <= 32;
+  if (one) {
+    if (act == 1)
+      return launch_grouped<1, 2, 6, true, true>(x_perm_bf16, offsets, E, max_rows, packed_e,
+                                                 scale_e, zero_e, (int)K, (int)N, y_perm_bf16, s);
+    return launch_grouped<1, 2, 6, false, true>(x_perm_bf16, offsets, E, max_rows, packed_e,
+                                                scale_e, zero_e, (int)K, (int)N, y_perm_bf16, s);
+  }
   if (act == 1) {
     if (wide)
       return launch_grouped<2, 2, 6, true>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,

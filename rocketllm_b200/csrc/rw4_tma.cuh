@@ -13,6 +13,7 @@
 
 #define RW4_DEVERR_TIMEOUT 1u
 #define RW4_DEVERR_TMEM 2u
+#define RW4_DEVERR_ROWS 4u  // a grouped launch saw an expert with more rows than max_rows
 
 namespace rw4 {
 

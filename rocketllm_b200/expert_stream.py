@@ -187,6 +187,9 @@ def streamed_experts_forward(self, hidden_states, top_k_index, top_k_weights):
     n_exp = streamer.num_experts[layer]
     compute = torch.cuda.current_stream(streamer.device)
     perm, inv, offsets = kernels.moe_permute(idx, n_exp)
+    # rows per expert: a token's top-k experts are distinct, so one token gives each at most one
+    # row (the one-row fp16 kernel); otherwise bound by all of the token-slot pairs
+    rows = 1 if t == 1 else t * k
     counts = offsets.cpu().tolist()          # the routed set: one device->host sync per layer
     selected = [e for e in range(n_exp) if counts[e + 1] > counts[e]]
     if not selected:
@@ -195,7 +198,7 @@ def streamed_experts_forward(self, hidden_states, top_k_index, top_k_weights):
     xp = kernels.moe_gather(x, perm, k)      # runs while the experts cross PCIe
     streamer.wait(layer, selected, compute)
     gate_up, down = streamer.triples(layer, selected)
-    act = kernels.moe_grouped(xp, offsets, gate_up, act=1, max_rows=t * k)
-    yp = kernels.moe_grouped(act, offsets, down, act=0, max_rows=t * k)
+    act = kernels.moe_grouped(xp, offsets, gate_up, act=1, max_rows=rows)
+    yp = kernels.moe_grouped(act, offsets, down, act=0, max_rows=rows)
     out = kernels.moe_combine(yp, inv, idx, w)
     return out if hidden_states.dtype == torch.bfloat16 else out.to(hidden_states.dtype)

@@ -103,10 +103,13 @@ def rw4_experts_forward(self, hidden_states, top_k_index, top_k_weights):
         w = w.float()
     n_exp = getattr(self, "num_experts", None) or self.gate_up_proj_packed.shape[0]
     perm, inv, offsets = kernels.moe_permute(idx, n_exp)
+    # rows per expert: a token's top-k experts are distinct, so one token gives each at most one
+    # row (the one-row fp16 kernel); otherwise bound by all of the token-slot pairs
+    rows = 1 if t == 1 else t * k
     xp = kernels.moe_gather(x, perm, k)
     act = kernels.moe_grouped(xp, offsets, _expert_triples(self, "gate_up_proj"), act=1,
-                              max_rows=t * k)
+                              max_rows=rows)
     yp = kernels.moe_grouped(act, offsets, _expert_triples(self, "down_proj"), act=0,
-                             max_rows=t * k)
+                             max_rows=rows)
     out = kernels.moe_combine(yp, inv, idx, w)
     return out if hidden_states.dtype == torch.bfloat16 else out.to(hidden_states.dtype)

@@ -97,6 +97,37 @@ def test_grouped_matches_oracle(cuda, t, act):
         close(y[rows], ref, rel=1 / 32 if act == 1 else 1 / 128)
 
 
+@pytest.mark.parametrize("act", [0, 1])
+@pytest.mark.parametrize("hid", [1024, 4096])
+def test_grouped_one_token_fp16_path(cuda, act, hid):
+    """One token (each routed expert gets one row, max_rows=1): the fp16 one-row kernel."""
+    e, k_top, inter = 8, 2, 512
+    n = 2 * inter if act == 1 else hid
+    weights = expert_weights(e, n, hid, cuda, seed=21 + act)
+    idx = routing(1, k_top, e, 7).to(cuda)
+    x = torch.randn(1, hid, device=cuda).to(torch.bfloat16)
+    perm, inv, offsets = kernels.moe_permute(idx, e)
+    xp = kernels.moe_gather(x, perm, k_top)
+    y = kernels.moe_grouped(xp, offsets, weights, act=act, max_rows=1)
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    for rows, ref in oracle_grouped(xp, offsets, weights, act, inter):
+        close(y[rows], ref, rel=1 / 32 if act == 1 else 1 / 128)
+
+
+def test_grouped_flags_rows_beyond_max_rows(cuda):
+    """An expert with more rows than max_rows covers is reported in the device status word."""
+    e, hid = 4, 1024
+    weights = expert_weights(e, hid, hid, cuda, seed=3)
+    idx = torch.tensor([[0], [0], [1]], dtype=torch.int64, device=cuda)   # expert 0: two rows
+    x = torch.randn(3, hid, device=cuda).to(torch.bfloat16)
+    perm, inv, offsets = kernels.moe_permute(idx, e)
+    xp = kernels.moe_gather(x, perm, 1)
+    kernels.moe_grouped(xp, offsets, weights, act=0, max_rows=1)
+    torch.cuda.synchronize()
+    assert kernels.device_status() & 4
+
+
 def test_combine_reproduces_reference_rounding_order(cuda):
     t, k, e, h = 9, 2, 4, 64
     idx = routing(t, k, e, 5)
