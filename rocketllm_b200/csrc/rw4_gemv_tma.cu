@@ -187,8 +187,19 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
   if (row_tiles == 4 && M > 8) row_tiles = 2;
   if (forced_ks == 1 || forced_ks == 2 || forced_ks == 4) ks = forced_ks;
   if (row_tiles >= 4) ks = 1;
+  if (M == 1 && !no_f16()) {
+    // the fp16 one-row path holds the CTA's activation row in shared memory (<= 32 stages):
+    // split a longer K over a cluster, 64-row CTAs included
+    int need = 1;
+    while (need < 4 && (K / kStageK + need - 1) / need > kF16MaxStages) need *= 2;
+    if (need > ks) ks = need;
+  }
   if (M <= 8) {
-    if (row_tiles == 4) return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+    if (row_tiles == 4) {
+      if (ks == 4) return launch_tma<1, 4, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+      if (ks == 2) return launch_tma<1, 4, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+      return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+    }
     if (row_tiles == 2) {
       if (ks == 4) return launch_tma<1, 2, 6, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
       if (ks == 2) return launch_tma<1, 2, 6, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, s);

@@ -374,7 +374,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
   __syncthreads();
   constexpr int kCols = 16 * NT + 1;
   constexpr int kRowsOut = SWIGLU ? 16 : L::BR;
-  constexpr int kOut = kRowsOut * 16 * NT;
+  constexpr int kOut = kRowsOut * (M1 ? 1 : 16 * NT);  // one row: only MMA column 0 carries data
   float* red = reinterpret_cast<float*>(smem);  // [kConsumers][BR][kCols]
   if (!aborted && warp < kConsumers) {
     const int g = lane >> 2, t = lane & 3;

@@ -45,6 +45,19 @@ def test_linear_matches_oracle(cuda, m, k, n):
     check_close(y, oracle_linear(x, packed, scale, zero))
 
 
+@pytest.mark.parametrize("k,n", [(32768, 512), (53248, 1024), (53248, 16384)])
+def test_linear_long_k_one_row(cuda, k, n):
+    """One activation row with K beyond the fp16 row's 32 KB: K split over a cluster."""
+    packed, scale, zero = make_weight(n, k, device=cuda, seed=k + n)
+    x = make_activation(1, k, device=cuda, seed=5)
+    y = kernels.linear(x, packed, scale, zero)
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    rows = np.arange(0, n, max(1, n // 256))
+    check_close(y[:, torch.from_numpy(rows).to(cuda)],
+                oracle_linear(x, packed, scale, zero, rows=rows))
+
+
 def test_linear_golden_reference_output(golden, cuda):
     """The reference's own bf16 F.linear over its dequantized weight (make_golden.py)."""
     dev = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(cuda)
