@@ -84,7 +84,7 @@ class LayerStreamer:
     """Streams decoder layers from pinned host blobs through ``window`` device slots."""
 
     def __init__(self, layers, device, window=2, copy_streams=2, chunk_bytes=16 << 20,
-                 prefetching=True, expert_slots=None):
+                 prefetching=True, expert_slots=None, blobs=None):
         if window < 1:
             raise ValueError("window must be >= 1")
         self.layers = list(layers)
@@ -93,7 +93,9 @@ class LayerStreamer:
         self.prefetching = prefetching
         # routed experts stream one by one (expert_stream.py) when expert_slots is given
         stream_experts = expert_slots is not None
-        self.blobs = [_pack_layer(layer, stream_experts) for layer in self.layers]
+        # blobs: prebuilt host blobs (read from layer shards on disk); else packed from the layers
+        self.blobs = blobs if blobs is not None else [_pack_layer(layer, stream_experts)
+                                                      for layer in self.layers]
         self.slot_bytes = max(b.nbytes for b in self.blobs)
         self.slots = [torch.empty(self.slot_bytes, dtype=torch.uint8, device=self.device)
                       for _ in range(self.window)]
@@ -207,6 +209,12 @@ class RocketModel:
     def __init__(self, model_or_path, device="cuda", dtype=torch.bfloat16, vram_budget=None,
                  window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
                  expert_streaming=True, **unused):
+        from .shards import INDEX
+        if isinstance(model_or_path, (str, os.PathLike)) and \
+                os.path.exists(os.path.join(str(model_or_path), INDEX)):
+            self._init_from_shards(str(model_or_path), device, dtype, vram_budget, window,
+                                   prefetching, copy_streams, chunk_bytes)
+            return
         if isinstance(model_or_path, (str, os.PathLike)):
             from transformers import AutoModelForCausalLM
             model = AutoModelForCausalLM.from_pretrained(str(model_or_path), dtype=dtype)
@@ -244,6 +252,51 @@ class RocketModel:
         self.streamer = LayerStreamer(layers, self.device, window=window,
                                       copy_streams=copy_streams, chunk_bytes=chunk_bytes,
                                       prefetching=prefetching, expert_slots=expert_slots)
+
+    def _init_from_shards(self, root, device, dtype, vram_budget, window, prefetching,
+                          copy_streams, chunk_bytes):
+        """Layer shards written by ``shards.split_rw4_layers``: the model is built on the meta
+        device, the non-layer tensors come from ``rest.safetensors`` straight to the device, and
+        each layer's blob is read from its file into pinned memory in one positioned read (no
+        CPU copy of the model ever exists).  Routed experts stream with their layer."""
+        from .shards import LayerShardReader, _materialize_rest, build_skeleton
+        self.device = torch.device(device)
+        reader = LayerShardReader(root)
+        self.shards = reader
+        model = build_skeleton(root, dtype).eval()
+        self.model = model
+        layers_path = reader.index["layers_path"]
+        _materialize_rest(model, root, self.device, layers_path)
+        layers = model.get_submodule(layers_path)
+        plans = [reader.plan(i) for i in range(len(reader))]
+        rest = sum(p.numel() * p.element_size() for n, p in model.named_parameters()
+                   if not n.startswith(layers_path + "."))
+        layer_bytes = [nbytes for _, nbytes in plans]
+        self.streamer = None
+
+        def resolve(layer, entries):
+            return [(layer.get_submodule(m) if m else layer, leaf, kind, dt, shape, off)
+                    for m, leaf, kind, dt, shape, off in entries]
+
+        if vram_budget is None or rest + sum(layer_bytes) <= vram_budget:
+            staging = torch.empty(max(layer_bytes), dtype=torch.uint8).pin_memory()
+            for i, layer in enumerate(layers):
+                entries, nbytes = plans[i]
+                reader.read_into(i, staging)
+                slot = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+                slot.copy_(staging[:nbytes])   # synchronous: the staging buffer is reused
+                _bind(_LayerBlob(None, resolve(layer, entries), nbytes), slot)
+            return
+        blobs = []
+        for i, layer in enumerate(layers):
+            entries, nbytes = plans[i]
+            host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+            reader.read_into(i, host)
+            blobs.append(_LayerBlob(host, resolve(layer, entries), nbytes))
+        window = max(1, min(window, int(max(0, vram_budget - rest) // max(layer_bytes))))
+        self.streamer = LayerStreamer(layers, self.device, window=window,
+                                      copy_streams=copy_streams, chunk_bytes=chunk_bytes,
+                                      prefetching=prefetching, blobs=blobs)
 
     @property
     def config(self):

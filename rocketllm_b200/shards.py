@@ -1,0 +1,257 @@
+"""RW4 layer shards on disk, laid out exactly as the engine's pinned host blobs.
+
+Counterpart of the reference's per-layer checkpoint split (``rocketllm/utils.py:470-621``,
+``split_and_save_layers``: one safetensors file per layer plus a ``.done`` marker) and of its
+byte-range reader (``rocketllm/streaming/shards.py``, ``streaming/loader.py:161-236``:
+``LayerLoader.plan`` reads only the header, ``load``/``_fill`` read the tensors into one leased
+buffer).  Here a layer file's data section IS the layer's host blob: every tensor sits at the
+256-byte aligned offset the engine binds device views at, so loading a layer is one positioned
+read straight into pinned memory -- no per-tensor copy, no repacking -- and the data section starts
+on a 4096-byte boundary so the read can bypass the page cache (``O_DIRECT``) where the file system
+allows it.
+
+Each file is still a valid safetensors container: the JSON header names every tensor with its
+dtype, shape and data offsets, gaps between aligned tensors are covered by ``__rw4_pad_<n>`` uint8
+entries (safetensors wants the offsets contiguous), and the header is padded with spaces up to the
+aligned data start.  ``rw4_layers.json`` indexes the layers (module path, leaf, dtype, shape,
+offset of every tensor; the blob size), ``rest.safetensors`` holds everything outside the decoder
+layers, ``config.json`` the model config with its ``quantization_config``.
+"""
+import json
+import os
+
+import torch
+
+ALIGN = 256
+DATA_ALIGN = 4096
+INDEX = "rw4_layers.json"
+REST = "rest.safetensors"
+
+_ST_DTYPES = {torch.float32: "F32", torch.float16: "F16", torch.bfloat16: "BF16",
+              torch.uint8: "U8", torch.int8: "I8", torch.int32: "I32", torch.int64: "I64",
+              torch.bool: "BOOL", torch.float64: "F64", torch.int16: "I16"}
+_FROM_ST = {v: k for k, v in _ST_DTYPES.items()}
+
+
+def _dtype_name(dtype):
+    return str(dtype).replace("torch.", "")
+
+
+def _layer_file(i):
+    return os.path.join("layers", f"layer.{i}.safetensors")
+
+
+def layer_entries(layer, skip_experts=False):
+    """``[(module_path, leaf, kind, dtype, shape, offset)]`` and the blob size: the engine's blob
+    layout of ``layer`` (parameters and persistent buffers, 256-byte aligned, in module order)."""
+    from .engine import _layer_tensors
+    names = {id(m): n for n, m in layer.named_modules()}
+    entries, off = [], 0
+    for module, leaf, kind, t in _layer_tensors(layer, skip_experts):
+        off = (off + ALIGN - 1) // ALIGN * ALIGN
+        entries.append((names[id(module)], leaf, kind, t.dtype, tuple(t.shape), off))
+        off += t.numel() * t.element_size()
+    return entries, (off + ALIGN - 1) // ALIGN * ALIGN
+
+
+def _write_layer_file(path, layer, entries, nbytes):
+    from .engine import _layer_tensors
+    tensors = [t for *_, t in _layer_tensors(layer)]
+    header, pos, pad = {}, 0, 0
+    for (mname, leaf, kind, dtype, shape, off), t in zip(entries, tensors):
+        if off > pos:
+            header[f"__rw4_pad_{pad}"] = {"dtype": "U8", "shape": [off - pos],
+                                          "data_offsets": [pos, off]}
+            pad += 1
+        n = t.numel() * t.element_size()
+        key = f"{mname}.{leaf}" if mname else leaf
+        header[key] = {"dtype": _ST_DTYPES[dtype], "shape": list(shape),
+                       "data_offsets": [off, off + n]}
+        pos = off + n
+    if nbytes > pos:
+        header[f"__rw4_pad_{pad}"] = {"dtype": "U8", "shape": [nbytes - pos],
+                                      "data_offsets": [pos, nbytes]}
+    header["__metadata__"] = {"format": "pt", "layout": "rw4-layer-blob"}
+    text = json.dumps(header, separators=(",", ":")).encode()
+    hlen = (8 + len(text) + DATA_ALIGN - 1) // DATA_ALIGN * DATA_ALIGN - 8
+    text = text + b" " * (hlen - len(text))
+    blob = bytearray(nbytes)
+    for (mname, leaf, kind, dtype, shape, off), t in zip(entries, tensors):
+        raw = t.detach().contiguous().cpu().view(-1).view(torch.uint8).numpy().tobytes()
+        blob[off:off + len(raw)] = raw
+    tmp = path + ".tmp"
+    with open(tmp, "wb") as f:
+        f.write(len(text).to_bytes(8, "little"))
+        f.write(text)
+        f.write(blob)
+    os.replace(tmp, path)
+    return 8 + len(text)
+
+
+def split_rw4_layers(model, out_dir):
+    """Write ``model`` (an RW4 ``*ForCausalLM``) as per-layer blob files under ``out_dir``.
+
+    Returns ``out_dir``.  A layer whose ``.done`` marker exists is not rewritten (the reference's
+    resumable split)."""
+    from safetensors.torch import save_file
+
+    from .engine import _decoder_layers, _layers_path
+    os.makedirs(os.path.join(out_dir, "layers"), exist_ok=True)
+    layers = _decoder_layers(model)
+    index = {"align": ALIGN, "data_align": DATA_ALIGN, "layers_path": _layers_path(model),
+             "layers": []}
+    for i, layer in enumerate(layers):
+        entries, nbytes = layer_entries(layer)
+        rel = _layer_file(i)
+        path = os.path.join(out_dir, rel)
+        done = path + ".done"
+        if os.path.exists(done):
+            with open(path, "rb") as f:
+                data_start = 8 + int.from_bytes(f.read(8), "little")
+        else:
+            data_start = _write_layer_file(path, layer, entries, nbytes)
+            open(done, "w").close()
+        index["layers"].append({
+            "file": rel, "data_start": data_start, "nbytes": nbytes,
+            "entries": [[m, leaf, kind, _dtype_name(dt), list(shape), off]
+                        for m, leaf, kind, dt, shape, off in entries]})
+    lp = index["layers_path"] + "."
+    rest = {k: v.detach().contiguous().cpu() for k, v in model.state_dict().items()
+            if not k.startswith(lp)}
+    seen = {}
+    for k, v in list(rest.items()):   # tied weights: safetensors refuses aliases
+        key = (v.data_ptr(), v.numel()) if v.numel() else None
+        if key is not None and key in seen:
+            rest[k] = v.clone()
+        elif key is not None:
+            seen[key] = k
+    save_file(rest, os.path.join(out_dir, REST), metadata={"format": "pt"})
+    cfg = model.config.to_dict()
+    with open(os.path.join(out_dir, "config.json"), "w") as f:
+        json.dump(cfg, f, indent=1)
+    with open(os.path.join(out_dir, INDEX), "w") as f:
+        json.dump(index, f)
+    return out_dir
+
+
+class LayerShardReader:
+    """Reads layer blobs of a directory written by :func:`split_rw4_layers`."""
+
+    def __init__(self, root):
+        self.root = str(root)
+        with open(os.path.join(self.root, INDEX)) as f:
+            self.index = json.load(f)
+        self.layers = self.index["layers"]
+        self.reads = 0
+        self.bytes_read = 0
+        self.direct_reads = 0
+
+    def __len__(self):
+        return len(self.layers)
+
+    def plan(self, i):
+        """``(entries, nbytes)`` of layer ``i`` from the index alone (nothing else is read)."""
+        rec = self.layers[i]
+        entries = [(m, leaf, kind, getattr(torch, dt), tuple(shape), off)
+                   for m, leaf, kind, dt, shape, off in rec["entries"]]
+        return entries, rec["nbytes"]
+
+    def read_into(self, i, buffer):
+        """Read layer ``i``'s blob into ``buffer`` (a CPU uint8 tensor of at least ``nbytes``,
+        pinned or not) with positioned reads; ``O_DIRECT`` when the buffer, size and file
+        offset are 4096-aligned and the file system accepts it."""
+        rec = self.layers[i]
+        nbytes, start = rec["nbytes"], rec["data_start"]
+        if buffer.dtype != torch.uint8 or buffer.numel() < nbytes or buffer.is_cuda:
+            raise ValueError("read_into needs a CPU uint8 buffer of at least the blob's size")
+        path = os.path.join(self.root, rec["file"])
+        view = memoryview(buffer[:nbytes].numpy()).cast("B")
+        fd, direct = None, False
+        if hasattr(os, "O_DIRECT") and buffer.data_ptr() % DATA_ALIGN == 0 \
+                and start % DATA_ALIGN == 0:
+            try:
+                fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
+                direct = True
+            except OSError:
+                fd = None
+        if fd is None:
+            fd = os.open(path, os.O_RDONLY)
+        try:
+            done = 0
+            while done < nbytes:
+                want = nbytes - done
+                if direct:
+                    if want % DATA_ALIGN:   # the tail of an O_DIRECT read must stay aligned
+                        os.close(fd)
+                        fd, direct = os.open(path, os.O_RDONLY), False
+                        continue
+                    want = min(want, 1 << 30)
+                try:
+                    got = os.preadv(fd, [view[done:done + want]], start + done)
+                except OSError:
+                    if not direct:
+                        raise
+                    os.close(fd)
+                    fd, direct = os.open(path, os.O_RDONLY), False
+                    continue
+                if got <= 0:
+                    raise IOError(f"{path}: short read at {start + done}")
+                done += got
+        finally:
+            os.close(fd)
+        self.reads += 1
+        self.bytes_read += nbytes
+        self.direct_reads += int(direct)
+        return buffer
+
+    def stats(self):
+        return {"layers": len(self.layers), "reads": self.reads, "bytes_read": self.bytes_read,
+                "direct_reads": self.direct_reads}
+
+
+def build_skeleton(root, dtype=torch.bfloat16):
+    """The RW4 ``*ForCausalLM`` of ``root`` on the meta device (no storage allocated)."""
+    from transformers import AutoConfig, AutoModelForCausalLM
+
+    from .quant.hf import convert_modules
+    config = AutoConfig.from_pretrained(root)
+    q = getattr(config, "quantization_config", None)
+    skip = (q.get("modules_to_not_convert") if isinstance(q, dict)
+            else getattr(q, "modules_to_not_convert", None)) or ()
+    with torch.device("meta"):
+        model = AutoModelForCausalLM.from_config(config, dtype=dtype)
+    convert_modules(model, skip)
+    return model
+
+
+def _materialize_rest(model, root, device, layers_path):
+    """Allocate everything outside the decoder layers on ``device`` and fill it from
+    ``rest.safetensors``; rebuild non-persistent buffers (rotary frequencies)."""
+    from safetensors.torch import load_file
+    parent_path, _, leaf = layers_path.rpartition(".")
+    parent = model.get_submodule(parent_path) if parent_path else model
+    layers = getattr(parent, leaf)
+    setattr(parent, leaf, torch.nn.ModuleList())
+    model.to_empty(device=device)
+    setattr(parent, leaf, layers)
+    rest = load_file(os.path.join(root, REST), device=str(device))
+    missing = []
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if name.startswith(layers_path + "."):
+                continue
+            if name in rest:
+                p.copy_(rest[name])
+            else:
+                missing.append(name)
+    if missing:
+        raise ValueError(f"{REST} lacks {missing[:4]}")
+    for mod in model.modules():
+        if "inv_freq" in mod._buffers and hasattr(mod, "config"):
+            fresh = type(mod)(mod.config, device=device)
+            for bname, buf in fresh._buffers.items():
+                mod._buffers[bname] = buf
+            if hasattr(fresh, "attention_scaling"):
+                mod.attention_scaling = fresh.attention_scaling
+    if getattr(model.config, "tie_word_embeddings", False) and hasattr(model, "tie_weights"):
+        model.tie_weights()

@@ -1,0 +1,80 @@
+"""RW4 layer shards (the reference's per-layer split + byte-range reader, rocketllm/utils.py:470-621,
+streaming/shards.py, streaming/loader.py:161-236), on the CPU: every file is a valid safetensors
+container whose tensors equal the model's, a layer's blob read with one positioned read holds
+every tensor at the engine's aligned offset, the index alone plans a layer, and a finished layer
+(.done marker) is not rewritten."""
+import os
+
+import torch
+
+from rocketllm_b200.engine import _layer_tensors, _pack_layer
+from rocketllm_b200.shards import INDEX, LayerShardReader, layer_entries, split_rw4_layers
+
+
+def tiny_rw4_model(seed=0):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    from rocketllm_b200.quant.hf import convert_modules
+    cfg = LlamaConfig(hidden_size=128, intermediate_size=256, num_hidden_layers=3,
+                      num_attention_heads=4, num_key_value_heads=2, vocab_size=320,
+                      max_position_embeddings=64, tie_word_embeddings=False)
+    model = LlamaForCausalLM(cfg)
+    convert_modules(model)
+    g = torch.Generator().manual_seed(seed)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if p.dtype == torch.uint8:
+                p.copy_(torch.randint(0, 256, p.shape, generator=g, dtype=torch.uint8))
+            else:
+                p.copy_(torch.randn(p.shape, generator=g).to(p.dtype))
+    return model
+
+
+def test_files_are_safetensors_with_the_models_tensors(tmp_path):
+    from safetensors import safe_open
+    model = tiny_rw4_model()
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    reader = LayerShardReader(root)
+    assert len(reader) == 3
+    for i, layer in enumerate(model.model.layers):
+        path = os.path.join(root, reader.layers[i]["file"])
+        assert os.path.exists(path + ".done")
+        names = {id(m): n for n, m in layer.named_modules()}
+        with safe_open(path, framework="pt") as f:
+            keys = set(f.keys())
+            for module, leaf, kind, t in _layer_tensors(layer):
+                key = f"{names[id(module)]}.{leaf}" if names[id(module)] else leaf
+                assert key in keys
+                assert torch.equal(f.get_tensor(key), t)
+        assert reader.layers[i]["data_start"] % 4096 == 0
+
+
+def test_read_into_gives_the_engines_blob(tmp_path):
+    model = tiny_rw4_model(1)
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    reader = LayerShardReader(root)
+    for i, layer in enumerate(model.model.layers):
+        entries, nbytes = reader.plan(i)
+        want, want_bytes = layer_entries(layer)
+        assert nbytes == want_bytes
+        assert [e[:2] + e[3:] for e in entries] == [e[:2] + e[3:] for e in want]
+        buf = torch.zeros(nbytes + 4096, dtype=torch.uint8)
+        reader.read_into(i, buf)
+        packed = _pack_layer(layer) if torch.cuda.is_available() else None
+        for (m, leaf, kind, dt, shape, off), (_, _, _, t) in zip(entries, _layer_tensors(layer)):
+            n = t.numel() * t.element_size()
+            assert torch.equal(buf[off:off + n], t.contiguous().view(-1).view(torch.uint8))
+        if packed is not None:
+            assert torch.equal(buf[:nbytes], packed.host[:nbytes])
+    assert reader.stats()["bytes_read"] == sum(l["nbytes"] for l in reader.layers)
+
+
+def test_done_layers_are_not_rewritten(tmp_path):
+    model = tiny_rw4_model(2)
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    path = os.path.join(root, "layers", "layer.1.safetensors")
+    before = os.stat(path).st_mtime_ns
+    os.remove(os.path.join(root, INDEX))
+    split_rw4_layers(model, root)
+    assert os.stat(path).st_mtime_ns == before
+    assert os.path.exists(os.path.join(root, INDEX))

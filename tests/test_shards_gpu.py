@@ -1,0 +1,53 @@
+"""A model loaded from RW4 layer shards (built on the meta device, layers read from disk straight
+into pinned memory) equals the same model loaded from its checkpoint: resident and streamed,
+dense and mixture-of-experts."""
+import pytest
+import torch
+
+from rocketllm_b200.engine import AutoModel, RocketModel, footprint
+from rocketllm_b200.quant.convert import save_rw4_checkpoint
+from rocketllm_b200.shards import split_rw4_layers
+
+pytestmark = pytest.mark.gpu
+
+
+def dense_model(kind):
+    from transformers import LlamaConfig, LlamaForCausalLM, MixtralConfig, MixtralForCausalLM
+    torch.manual_seed(0)
+    if kind == "llama":
+        cfg = LlamaConfig(hidden_size=512, intermediate_size=1536, num_hidden_layers=4,
+                          num_attention_heads=8, num_key_value_heads=2, vocab_size=2048,
+                          max_position_embeddings=512, tie_word_embeddings=False)
+        model = LlamaForCausalLM(cfg)
+    else:
+        cfg = MixtralConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=3,
+                            num_attention_heads=8, num_key_value_heads=2, vocab_size=2048,
+                            num_local_experts=8, num_experts_per_tok=2,
+                            max_position_embeddings=512, tie_word_embeddings=False)
+        model = MixtralForCausalLM(cfg)
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            p.copy_(torch.ones_like(p) if "norm" in n else torch.randn_like(p) * 0.02)
+    return model
+
+
+@pytest.mark.parametrize("kind", ["llama", "mixtral"])
+def test_shards_equal_checkpoint(tmp_path, kind):
+    ckpt = save_rw4_checkpoint(dense_model(kind), str(tmp_path / "rw4"), device="cuda")
+    resident = AutoModel.from_pretrained(ckpt)
+    root = split_rw4_layers(resident.model, str(tmp_path / "shards"))
+    ids = torch.randint(0, 2048, (1, 16), generator=torch.Generator().manual_seed(4)).cuda()
+    from_shards = RocketModel(root)
+    assert from_shards.streamer is None
+    rest, layers = footprint(resident.model)
+    streamed = RocketModel(root, vram_budget=rest + 2 * max(layers) + 1000, window=2)
+    assert streamed.streamer is not None and streamed.streamer.window == 2
+    with torch.no_grad():
+        ref = resident(ids).logits
+        assert torch.equal(from_shards(ids).logits, ref)
+        assert torch.equal(streamed(ids).logits, ref)
+        a = resident.generate(ids, max_new_tokens=6, do_sample=False, min_new_tokens=6)
+        b = streamed.generate(ids, max_new_tokens=6, do_sample=False, min_new_tokens=6)
+    assert torch.equal(a, b)
+    assert from_shards.shards.stats()["bytes_read"] == sum(layers)
+    streamed.close()
