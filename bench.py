@@ -439,6 +439,18 @@ def rw4_arm(args):
         decode = decode_bench(device, args.decode_prompt, args.decode_tokens,
                               tuple(int(b) for b in args.decode_batches.split(",")),
                               args.stream_tokens, int(4e9))
+        if dist is not None:
+            # every rank decodes its own model copy (data-parallel replicas, no exchange): the
+            # job's throughput is the sum over ranks, its per-token latency the slowest rank's
+            for key in sorted(k for k, v in decode.items() if isinstance(v, dict) and "tok_s" in v):
+                t = torch.tensor([decode[key]["tok_s"], decode[key]["ms_per_token"]],
+                                 dtype=torch.float64, device=device)
+                tot, worst = t.clone(), t.clone()
+                dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+                dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+                decode[key]["aggregate_tok_s"] = round(float(tot[0]), 2)
+                decode[key]["max_ms_per_token"] = round(float(worst[1]), 4)
+            decode["replicas"] = world
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
