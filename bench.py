@@ -239,6 +239,85 @@ LLAMA_8B = dict(hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
                 max_position_embeddings=8192, rope_theta=500000.0, tie_word_embeddings=False)
 
 
+LLAMA_405B = dict(hidden_size=16384, intermediate_size=53248, num_hidden_layers=126,
+                  num_attention_heads=128, num_key_value_heads=8, vocab_size=128256,
+                  max_position_embeddings=8192, rope_theta=500000.0, tie_word_embeddings=False)
+
+
+def pp_decode(args):
+    """Pipeline-parallel greedy decode (not the driver's line): the model's decoder layers split
+    over the ranks (contiguous ranges; each rank builds only its own layers), hidden states handed
+    rank to rank over NCCL (NVLink), every rank's per-token stage replayed from a CUDA graph.
+    Default: the Llama-3.1-405B architecture in RW4, batch 1 and 32, prompt
+    1024, 64 new tokens.  Prints one JSON line on rank 0; timings are CUDA events, max over
+    ranks."""
+    import datetime
+
+    import torch.distributed as dist
+    from transformers import LlamaConfig
+
+    from rocketllm_b200.pipeline import GraphedPipelineDecoder, layer_range
+    from rocketllm_b200.synthetic import build_rw4_causal_lm
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    spec = dict(LLAMA_405B if args.pp_model == "405b" else LLAMA_8B)
+    if args.pp_layers:
+        spec["num_hidden_layers"] = args.pp_layers
+    cfg = LlamaConfig(**spec)
+    n_layers = cfg.num_hidden_layers
+    start, stop = layer_range(n_layers, rank, world)
+    t0 = time.time()
+    model = build_rw4_causal_lm(cfg, device=device, seed=0, layers=(start, stop),
+                                keep_embed=rank == 0, keep_head=rank == world - 1)
+    torch.cuda.synchronize()
+    build_s = time.time() - t0
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    out = {"mode": "pipeline-parallel greedy decode", "model":
+           f"Llama-3.1-{args.pp_model.upper()} architecture ({n_layers} layers), RW4 group 64, "
+           "random init N(0,0.02)", "data": "synthetic", "n_gpus": world,
+           "layers_per_rank": [list(layer_range(n_layers, r, world)) for r in range(world)],
+           "prompt_tokens": args.pp_prompt, "new_tokens": args.pp_tokens,
+           "rank0_weight_bytes": weight_bytes, "rank0_build_s": round(build_s, 1)}
+
+    def worst(v):
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for b in tuple(int(v) for v in args.pp_batches.split(",")):
+        dec = GraphedPipelineDecoder(model, b, args.pp_prompt + args.pp_tokens + 8, device=device)
+        ids = torch.randint(0, cfg.vocab_size, (b, args.pp_prompt),
+                            generator=torch.Generator().manual_seed(1))
+        dist.barrier()
+        torch.cuda.synchronize()
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a0.record()
+        dec.prefill(ids)
+        a1.record()
+        for _ in range(3):   # capture + warm-up replays
+            dec.step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.pp_tokens):
+            dec.step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = worst(e0.elapsed_time(e1) / args.pp_tokens)
+        out[f"b{b}"] = {"tok_s": round(b * 1000.0 / ms, 2), "ms_per_token": round(ms, 3),
+                        "prefill_ms": round(worst(a0.elapsed_time(a1)), 1)}
+        del dec
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget):
     """Greedy decode tok/s of a Llama-3.1-8B-architecture RW4 model (random init N(0, 0.02),
     every Linear incl. lm_head in RW4): resident with a CUDA-graphed step, then streamed from
@@ -578,9 +657,18 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="only the model decode section (one JSON line)")
     ap.add_argument("--decode-batches", default="1,16")
+    ap.add_argument("--pp-decode", action="store_true",
+                    help="pipeline-parallel decode over the torchrun ranks (one JSON line)")
+    ap.add_argument("--pp-model", choices=("405b", "8b"), default="405b")
+    ap.add_argument("--pp-layers", type=int, default=0, help="override the layer count")
+    ap.add_argument("--pp-batches", default="1,32")
+    ap.add_argument("--pp-prompt", type=int, default=1024)
+    ap.add_argument("--pp-tokens", type=int, default=64)
     args = ap.parse_args()
     if args.sweep:
         return sweep(args)
+    if args.pp_decode:
+        return pp_decode(args)
     if args.decode_only:
         device = torch.device("cuda", 0)
         torch.cuda.set_device(device)

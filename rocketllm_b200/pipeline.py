@@ -101,3 +101,143 @@ class PipelineDecoder:
         for _ in range(new_tokens - 1):
             toks.append(self._forward(toks[-1], b, 1))
         return torch.cat(toks, dim=1)
+
+
+class GraphedPipelineDecoder(PipelineDecoder):
+    """:class:`PipelineDecoder` with a static KV cache and each rank's per-token stage captured in a
+    CUDA graph: the hand-off (``recv`` before, ``send`` after) and the token broadcast stay outside
+    the graph, everything a stage computes (embedding on the first rank, its decoder layers, the
+    norm / lm_head / argmax on the last) replays from it.  ``batch`` sequences, at most
+    ``max_len`` positions.
+
+    The prefill runs the prompt through an empty cache with causal attention (no mask: queries
+    never reach the unwritten cache slots); decode steps attend over the whole static cache under a
+    mask of the positions written so far."""
+
+    def __init__(self, model, batch, max_len, group=None, device="cuda", drop_remote=True,
+                 local=False, use_graph=True):
+        super().__init__(model, group, device, drop_remote, local)
+        from transformers import StaticCache
+        self.cache = StaticCache(config=model.config, max_cache_len=max_len)
+        self.batch, self.max_len = batch, max_len
+        h = self.hidden_size
+        self.ids = torch.zeros(batch, 1, dtype=torch.long, device=self.device)
+        self.pos = torch.zeros(1, dtype=torch.long, device=self.device)
+        self.h_in = torch.zeros(batch, 1, h, dtype=self.dtype, device=self.device)
+        self.h_out = torch.zeros(batch, 1, h, dtype=self.dtype, device=self.device)
+        self.key_pos = torch.arange(max_len, device=self.device)
+        self.use_graph = use_graph
+        self.graph = None
+        self.host_pos = 0
+
+    def _run_layers(self, h, pos, masked):
+        b = h.shape[0]
+        position_ids = pos.unsqueeze(0).expand(b, -1)
+        cos_sin = self.rotary(h, position_ids)
+        mask = None
+        if masked:   # [b, 1, q, max_len]: key j visible to the query at position p iff j <= p
+            mask = (self.key_pos[None, :] <= pos[:, None])[None, None].expand(b, 1, -1, -1)
+        for i in range(self.start, self.stop):
+            h = self.layers[i](h, attention_mask=mask, position_ids=position_ids,
+                               past_key_values=self.cache, use_cache=True, cache_position=pos,
+                               position_embeddings=cos_sin)
+            if isinstance(h, tuple):
+                h = h[0]
+        return h
+
+    def _last_rank(self):
+        if self.local:
+            return 0
+        return dist.get_process_group_ranks(self.group)[-1] if self.group is not None else \
+            self.world - 1
+
+    @torch.no_grad()
+    def prefill(self, input_ids):
+        b, t = input_ids.shape
+        if b != self.batch or t + 1 > self.max_len:
+            raise ValueError(f"prompt [{b}, {t}] does not fit batch {self.batch} / "
+                             f"{self.max_len} positions")
+        pos = torch.arange(t, device=self.device)
+        if self.first:
+            h = self.embed(input_ids.to(self.device))
+        else:
+            h = torch.empty((b, t, self.hidden_size), dtype=self.dtype, device=self.device)
+            dist.recv(h, src=self._peer(-1), group=self.group)
+        h = self._run_layers(h, pos, masked=False)
+        if not self.last:
+            dist.send(h.contiguous(), dst=self._peer(1), group=self.group)
+        else:
+            logits = self.model.lm_head(self.model.model.norm(h[:, -1:, :]))
+            self.ids.copy_(logits[:, -1].argmax(-1, keepdim=True))
+        if not self.local:
+            dist.broadcast(self.ids, src=self._last_rank(), group=self.group)
+        self.pos.fill_(t)
+        self.host_pos = t
+        return self.ids.clone()
+
+    def _stage(self):
+        h = self.embed(self.ids) if self.first else self.h_in
+        h = self._run_layers(h, self.pos, masked=True)
+        if self.last:
+            logits = self.model.lm_head(self.model.model.norm(h))
+            self.ids.copy_(logits[:, -1].argmax(-1, keepdim=True))
+        else:
+            self.h_out.copy_(h)
+        self.pos.add_(1)
+
+    def _state(self):
+        state = [self.ids, self.pos]
+        for layer in getattr(self.cache, "layers", []):
+            c = getattr(layer, "cumulative_length", None)
+            if torch.is_tensor(c) and c.is_cuda:
+                state.append(c)
+        return state
+
+    @torch.no_grad()
+    def capture(self):
+        """Warm up on a side stream and capture the stage (no communication inside); the state a
+        step advances is restored afterwards, so the first replay starts where the prefill
+        ended."""
+        state = self._state()
+        saved = [t.clone() for t in state]
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._stage()
+            for t, v in zip(state, saved):
+                t.copy_(v)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._stage()
+        for t, v in zip(state, saved):
+            t.copy_(v)
+        torch.cuda.synchronize(self.device)
+
+    @torch.no_grad()
+    def step(self):
+        """One greedy token for every sequence; returns ``ids`` [batch, 1] (all ranks)."""
+        if self.host_pos + 1 > self.max_len:
+            raise ValueError(f"static KV cache full ({self.max_len} positions)")
+        if self.use_graph and self.graph is None:
+            self.capture()
+        if not self.first:
+            dist.recv(self.h_in, src=self._peer(-1), group=self.group)
+        if self.use_graph:
+            self.graph.replay()
+        else:
+            self._stage()
+        if not self.last:
+            dist.send(self.h_out, dst=self._peer(1), group=self.group)
+        if not self.local:
+            dist.broadcast(self.ids, src=self._last_rank(), group=self.group)
+        self.host_pos += 1
+        return self.ids
+
+    @torch.no_grad()
+    def generate(self, input_ids, new_tokens):
+        toks = [self.prefill(input_ids)]
+        for _ in range(new_tokens - 1):
+            toks.append(self.step().clone())
+        return torch.cat(toks, dim=1)

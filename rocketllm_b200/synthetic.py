@@ -28,10 +28,19 @@ def make_activation(m, k, device="cuda", seed=2):
 
 
 @torch.no_grad()
-def build_rw4_causal_lm(config, device="cuda", seed=0, std=0.02):
+def build_rw4_causal_lm(config, device="cuda", seed=0, std=0.02, layers=None, keep_embed=True,
+                        keep_head=True):
     """A random-init RW4 ``*ForCausalLM`` built directly on ``device``: every Linear / stacked-expert
     weight drawn N(0, std) in bf16 and encoded with ``rw4_quantize`` (the reference codec), norms 1,
-    other weights N(0, std).  No dense copy of the whole model ever exists."""
+    other weights N(0, std).  No dense copy of the whole model ever exists.
+
+    ``layers = (start, stop)`` materialises only those decoder layers (the others become
+    ``nn.Identity``), ``keep_embed`` / ``keep_head`` the embedding and the final norm + lm_head: one
+    pipeline stage of a model too large for one GPU.  Every tensor draws from its own generator
+    seeded by ``seed`` and its name, so a stage holds exactly the values of the same layers of the
+    whole model."""
+    import zlib
+
     from transformers import AutoModelForCausalLM
 
     from . import kernels
@@ -41,17 +50,31 @@ def build_rw4_causal_lm(config, device="cuda", seed=0, std=0.02):
     with torch.device("meta"):
         model = AutoModelForCausalLM.from_config(config, dtype=torch.bfloat16)
     convert_modules(model)
+    inner = model.model
+    if layers is not None:
+        for i in range(len(inner.layers)):
+            if not layers[0] <= i < layers[1]:
+                inner.layers[i] = torch.nn.Identity()
+    if not keep_embed:
+        inner.embed_tokens = None
+    if not keep_head:
+        model.lm_head = None
+        inner.norm = None
     model.to_empty(device=device)
-    gen = torch.Generator(device=device).manual_seed(seed)
 
-    def encode_into(packed, scale, zero, n, k):
-        w = (torch.randn((n, k), device=device, generator=gen) * std).to(torch.bfloat16)
+    def gen_for(name):
+        return torch.Generator(device=device).manual_seed(
+            (seed * 1000003 + zlib.crc32(name.encode())) % (1 << 62))
+
+    def encode_into(name, packed, scale, zero, n, k):
+        w = (torch.randn((n, k), device=device, generator=gen_for(name)) * std).to(torch.bfloat16)
         p, s, z, _ = kernels.quantize(w, 64)
         packed.copy_(p), scale.copy_(s), zero.copy_(z)
+        del w, p, s, z
 
     for name, mod in model.named_modules():
         if isinstance(mod, RW4Linear):
-            encode_into(mod.weight_packed, mod.weight_scale, mod.weight_zero_point,
+            encode_into(name, mod.weight_packed, mod.weight_scale, mod.weight_zero_point,
                         mod.out_features, mod.in_features)
             if mod.bias is not None:
                 mod.bias.zero_()
@@ -59,7 +82,8 @@ def build_rw4_causal_lm(config, device="cuda", seed=0, std=0.02):
             for wn in ("gate_up_proj", "down_proj"):
                 p, s, z = (getattr(mod, wn + sfx) for sfx in ("_packed", "_scale", "_zero_point"))
                 for e in range(p.shape[0]):
-                    encode_into(p[e], s[e], z[e], p.shape[1], p.shape[2] * 2)
+                    encode_into(f"{name}.{wn}.{e}", p[e], s[e], z[e], p.shape[1],
+                                p.shape[2] * 2)
     rw4_suffixes = ("_packed", "_scale", "_zero_point")
     for name, param in model.named_parameters():
         if name.endswith(rw4_suffixes) or name.endswith(".bias"):
@@ -67,7 +91,7 @@ def build_rw4_causal_lm(config, device="cuda", seed=0, std=0.02):
         if "norm" in name:
             param.fill_(1.0)
         else:
-            param.copy_((torch.randn(param.shape, device=device, generator=gen) * std)
+            param.copy_((torch.randn(param.shape, device=device, generator=gen_for(name)) * std)
                         .to(param.dtype))
     # non-persistent buffers (rotary inverse frequencies) were left uninitialised by to_empty:
     # rebuild those modules' buffers on the device

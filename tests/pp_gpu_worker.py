@@ -16,7 +16,7 @@ sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 def main():
     from transformers import LlamaConfig
     from rocketllm_b200 import kernels
-    from rocketllm_b200.pipeline import PipelineDecoder, layer_range
+    from rocketllm_b200.pipeline import GraphedPipelineDecoder, PipelineDecoder, layer_range
     from rocketllm_b200.synthetic import build_rw4_causal_lm
     local = int(os.environ["LOCAL_RANK"])
     torch.cuda.set_device(local)
@@ -37,6 +37,17 @@ def main():
     ok = torch.equal(ref, got) and kept == stop - start and kernels.device_status() == 0
     if not ok:
         print(f"rank {rank}: kept {kept} layers, tokens\n{ref}\n{got}", flush=True)
+    # static cache + CUDA-graphed stages on a model each rank built only partly (its layers,
+    # the embedding on the first rank, the head on the last): the single-rank graphed decode
+    gref = GraphedPipelineDecoder(build_rw4_causal_lm(cfg, device=dev, seed=0, std=0.05), 3, 40,
+                                  device=dev, local=True).generate(ids, 10)
+    stage = build_rw4_causal_lm(cfg, device=dev, seed=0, std=0.05, layers=(start, stop),
+                                keep_embed=rank == 0, keep_head=rank == world - 1)
+    ggot = GraphedPipelineDecoder(stage, 3, 40, device=dev).generate(ids, 10)
+    torch.cuda.synchronize()
+    if not torch.equal(gref, ggot):
+        ok = False
+        print(f"rank {rank}: graphed pipeline tokens\n{gref}\n{ggot}", flush=True)
     f = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(f)
     dist.destroy_process_group()

@@ -61,6 +61,28 @@ def _worker(rank, world, port, out):
     dist.destroy_process_group()
 
 
+def _graphed_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from rocketllm_b200.pipeline import GraphedPipelineDecoder, PipelineDecoder
+    ids = torch.randint(0, 97, (2, 7), generator=torch.Generator().manual_seed(3))
+    ref = PipelineDecoder(tiny_model(), device="cpu", local=True).generate(ids, 6)
+    dec = GraphedPipelineDecoder(tiny_model(), batch=2, max_len=16, device="cpu",
+                                 use_graph=False)
+    got = dec.generate(ids, 6)
+    out[rank] = bool(torch.equal(ref, got))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_static_cache_stage_decoder_matches(tmp_path):
+    """The static-cache stage decoder (eager stage on CPU) gives the dynamic-cache tokens."""
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_graphed_worker, args=(2, 29721, out), nprocs=2, join=True)
+        assert all(out[r] for r in range(2)), dict(out)
+
+
 @pytest.mark.parametrize("world", [2, 3])
 def test_pipeline_matches_single_rank(world):
     with mp.Manager() as mgr:
