@@ -36,7 +36,12 @@ constexpr int BM = 128;          // weight rows per CTA (UMMA M)
 constexpr int BK = 64;           // K per stage (one group, one 128-byte bf16 swizzle atom)
 constexpr int kDequantWarps = 8;
 constexpr int kThreads = 32 * (3 + kDequantWarps);  // codes, MMA, dequant x8, activations
-constexpr int kCodeBytes = BM * (BK / 2);      // 4096
+// A codes stage covers 4 k-blocks: 128 rows x 128 bytes (256 k), one 128-byte-swizzled TMA box.
+// (Measured with device timestamps: a 128 x 32-byte box -- one k-block -- took ~2.7 us from
+// issue to landing, and with one box per k-block the ring, not the tensor core or the dequant,
+// set the pace: ~0.55 us per k-block.)
+constexpr int kKbPerCodeStage = 4;
+constexpr int kCodeBytes = BM * (BK / 2) * kKbPerCodeStage;  // 16384
 constexpr int kABytes = BM * BK * 2;           // 16384
 
 template <int BN>
@@ -46,8 +51,8 @@ struct Cfg {
   // therefore as deep as shared memory allows (4 / 6 / 8 stages for BN = 256 / 128 / 64).  The raw
   // codes (4 KB a k-block) are released as soon as the dequant warps have them in registers, so a
   // shorter ring keeps enough HBM reads in flight.
-  static constexpr int S1 = 6;                                   // codes stages
-  static constexpr int S2 = BN == 256 ? 4 : BN == 128 ? 6 : 8;  // x / A stages
+  static constexpr int S1 = BN == 256 ? 2 : 3;                  // codes stages (4 k-blocks each)
+  static constexpr int S2 = BN == 256 ? 4 : BN == 128 ? 5 : 7;  // x / A stages
   static constexpr int kXBytes = BN * BK * 2;
   static constexpr int kOffX = 0;
   static constexpr int kOffA = kOffX + S2 * kXBytes;
@@ -62,7 +67,8 @@ struct Cfg {
   static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) |
                                      ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
   static_assert(kDynSmem <= 227 * 1024, "shared memory budget");
-  static_assert(kOffA % 1024 == 0 && kXBytes % 1024 == 0, "swizzle atoms stay 1024-aligned");
+  static_assert(kOffA % 1024 == 0 && kXBytes % 1024 == 0 && kOffCodes % 1024 == 0,
+                "swizzle atoms stay 1024-aligned");
 };
 
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 bytes apart.
@@ -187,8 +193,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(cempty0 + 8 * s, kDequantWarps);
     }
     for (int s = 0; s < S2; ++s) {
-      mbar_init(xfull0 + 8 * s, 1);
-      mbar_init(aready0 + 8 * s, kDequantWarps);
+      mbar_init(xfull0 + 8 * s, 1);  // unused: the activation tile completes on a_ready
+      // a_ready: the 8 dequant warps' arrivals plus the activation producer's arrive.expect_tx,
+      // completed by its TMA bytes -- the MMA thread waits on this one barrier per k-block
+      mbar_init(aready0 + 8 * s, kDequantWarps + 1);
       mbar_init(sempty0 + 8 * s, 1);
     }
     mbar_init(accum, 1);
@@ -206,19 +214,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       prefetch_tensormap(&tm_codes);
       const uint64_t pol = policy_evict_first();
       int issued = 0;
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % S1;
-        if (!mbar_wait(cempty0 + 8 * s, ((kb / S1) & 1) ^ 1, status)) {
+      const int ncs = (nkb + kKbPerCodeStage - 1) / kKbPerCodeStage;
+      for (int cs = 0; cs < ncs; ++cs) {
+        const int s = cs % S1;
+        if (!mbar_wait(cempty0 + 8 * s, ((cs / S1) & 1) ^ 1, status)) {
           aborted = 1;
           break;
         }
         mbar_arrive_expect_tx(cfull0 + 8 * s, kCodeBytes);
-        tma_load_2d_hint(sb + C::kOffCodes + s * kCodeBytes, &tm_codes, kb * (BK / 2), n0,
-                         cfull0 + 8 * s, pol);
-        issued = kb + 1;
+        tma_load_2d_hint(sb + C::kOffCodes + s * kCodeBytes, &tm_codes,
+                         cs * (BK / 2) * kKbPerCodeStage, n0, cfull0 + 8 * s, pol);
+        issued = cs + 1;
       }
-      for (int kb = max(0, issued - S1); kb < issued; ++kb)  // drain own copies
-        mbar_wait(cfull0 + 8 * (kb % S1), (kb / S1) & 1, status);
+      for (int cs = max(0, issued - S1); cs < issued; ++cs)  // drain own copies
+        mbar_wait(cfull0 + 8 * (cs % S1), (cs / S1) & 1, status);
     }
   } else if (warp == kThreads / 32 - 1) {
     // ---------------- activation producer (shallow ring) ----------------
@@ -231,12 +240,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           aborted = 1;
           break;
         }
-        mbar_arrive_expect_tx(xfull0 + 8 * s, C::kXBytes);
-        tma_load_2d(sb + C::kOffX + s * C::kXBytes, &tm_x, kb * BK, m0, xfull0 + 8 * s);
+        mbar_arrive_expect_tx(aready0 + 8 * s, C::kXBytes);
+        tma_load_2d(sb + C::kOffX + s * C::kXBytes, &tm_x, kb * BK, m0, aready0 + 8 * s);
         issued = kb + 1;
       }
       for (int kb = max(0, issued - S2); kb < issued; ++kb)  // drain own copies
-        mbar_wait(xfull0 + 8 * (kb % S2), (kb / S2) & 1, status);
+        mbar_wait(aready0 + 8 * (kb % S2), (kb / S2) & 1, status);
     }
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
@@ -244,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % S2;
         const uint32_t par = (kb / S2) & 1;
-        if (!mbar_wait(xfull0 + 8 * s, par, status) || !mbar_wait(aready0 + 8 * s, par, status)) {
+        if (!mbar_wait(aready0 + 8 * s, par, status)) {
           aborted = 1;
           break;
         }
@@ -292,44 +301,55 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     load8(0, sc_cur, zr_cur);
     load8(8, sc_nxt, zr_nxt);
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s1 = kb % S1, s2 = kb % S2;
-      const int gi = kb & 7;
-      if (gi == 0 && kb > 0) {
-        sc_cur = sc_nxt;
-        zr_cur = zr_nxt;
-        load8(kb + 8, sc_nxt, zr_nxt);
-      }
-      const uint32_t sw = (gi < 4) ? ((gi < 2) ? sc_cur.x : sc_cur.y)
-                                   : ((gi < 6) ? sc_cur.z : sc_cur.w);
-      const uint32_t zw = (gi < 4) ? ((gi < 2) ? zr_cur.x : zr_cur.y)
-                                   : ((gi < 6) ? zr_cur.z : zr_cur.w);
-      const float sc = __half2float(__ushort_as_half((unsigned short)(sw >> (16 * (gi & 1)))));
-      const float zr = __half2float(__ushort_as_half((unsigned short)(zw >> (16 * (gi & 1)))));
-      const float s4[4] = {sc, sc * 0.0625f, sc * 0.00390625f, sc * 0.000244140625f};
-      if (!mbar_wait(cfull0 + 8 * s1, (kb / S1) & 1, status)) {
+    const int ncs = (nkb + kKbPerCodeStage - 1) / kKbPerCodeStage;
+    for (int cs = 0; cs < ncs && !aborted; ++cs) {
+      // this thread's 16 code bytes of each of the stage's k-blocks, then release the stage
+      const int s1 = cs % S1;
+      if (!mbar_wait(cfull0 + 8 * s1, (cs / S1) & 1, status)) {
         aborted = 1;
         break;
       }
-      const uint4 cw =
-          *reinterpret_cast<const uint4*>(smem + C::kOffCodes + s1 * kCodeBytes + r * 32 + 16 * h);
+      uint4 cw[kKbPerCodeStage];
+      const uint8_t* crow = smem + C::kOffCodes + s1 * kCodeBytes + r * 128;
+#pragma unroll
+      for (int j = 0; j < kKbPerCodeStage; ++j)   // 128-byte swizzle: chunk c at c ^ (r % 8)
+        cw[j] = *reinterpret_cast<const uint4*>(crow + (((2 * j + h) ^ (r & 7)) << 4));
       __syncwarp();
       if (lane == 0) mbar_arrive(cempty0 + 8 * s1);  // codes slot may be refilled
-      // the A slot is free once the MMAs of k-block kb - S2 have finished
-      if (!mbar_wait(sempty0 + 8 * s2, ((kb / S2) & 1) ^ 1, status)) {
-        aborted = 1;
-        break;
-      }
-      uint8_t* arow = smem + C::kOffA + s2 * kABytes + r * 128;
-      const uint32_t words[4] = {cw.x, cw.y, cw.z, cw.w};
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {  // chunk 4h + c = k 8(4h+c) .. +7
-        const int chunk = 4 * h + c;
-        *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = dequant8(words[c], s4, zr);
+      for (int j = 0; j < kKbPerCodeStage; ++j) {
+        const int kb = cs * kKbPerCodeStage + j;
+        if (kb >= nkb) break;
+        const int s2 = kb % S2;
+        const int gi = kb & 7;
+        if (gi == 0 && kb > 0) {
+          sc_cur = sc_nxt;
+          zr_cur = zr_nxt;
+          load8(kb + 8, sc_nxt, zr_nxt);
+        }
+        const uint32_t sw = (gi < 4) ? ((gi < 2) ? sc_cur.x : sc_cur.y)
+                                     : ((gi < 6) ? sc_cur.z : sc_cur.w);
+        const uint32_t zw = (gi < 4) ? ((gi < 2) ? zr_cur.x : zr_cur.y)
+                                     : ((gi < 6) ? zr_cur.z : zr_cur.w);
+        const float sc = __half2float(__ushort_as_half((unsigned short)(sw >> (16 * (gi & 1)))));
+        const float zr = __half2float(__ushort_as_half((unsigned short)(zw >> (16 * (gi & 1)))));
+        const float s4[4] = {sc, sc * 0.0625f, sc * 0.00390625f, sc * 0.000244140625f};
+        // the A slot is free once the MMAs of k-block kb - S2 have finished
+        if (!mbar_wait(sempty0 + 8 * s2, ((kb / S2) & 1) ^ 1, status)) {
+          aborted = 1;
+          break;
+        }
+        uint8_t* arow = smem + C::kOffA + s2 * kABytes + r * 128;
+        const uint32_t words[4] = {cw[j].x, cw[j].y, cw[j].z, cw[j].w};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {  // chunk 4h + c = k 8(4h+c) .. +7
+          const int chunk = 4 * h + c;
+          *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) << 4)) = dequant8(words[c], s4, zr);
+        }
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        __syncwarp();
+        if (lane == 0) mbar_arrive(aready0 + 8 * s2);
       }
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-      __syncwarp();
-      if (lane == 0) mbar_arrive(aready0 + 8 * s2);
     }
     // epilogue: wait for every MMA, then TMEM -> registers -> bf16 y
     if (!aborted && mbar_wait(accum, 0, status)) {
@@ -376,7 +396,7 @@ int launch_bn(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void
   using C = Cfg<BN>;
   CUtensorMap tc, tx;
   int st = make_tensor_map_2d(&tc, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K / 2, K / 2, BM,
-                              BK / 2, CU_TENSOR_MAP_SWIZZLE_NONE);
+                              BK / 2 * kKbPerCodeStage, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st == RW4_OK)
     st = make_tensor_map_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, (uint64_t)K * 2,
                             BN, BK, CU_TENSOR_MAP_SWIZZLE_128B);
