@@ -379,6 +379,8 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
     nbytes = (streamed.stats()["streaming"]["bytes"] - st0) / stream_tokens
     out["streamed_b1"] = {"tok_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 3),
                           "vram_budget_bytes": vram_budget, "window": streamed.streamer.window,
+                          "pinned_layers": streamed.streamer.pinned,
+                          "streamed_layers": streamed.streamer.streamed,
                           "h2d_bytes_per_token": int(nbytes),
                           "h2d_gbs": round(nbytes / (ms * 1e-3) / 1e9, 2),
                           "decode_tokens": stream_tokens}

@@ -81,26 +81,42 @@ def _bind(blob, slot):
 
 
 class LayerStreamer:
-    """Streams decoder layers from pinned host blobs through ``window`` device slots."""
+    """Streams decoder layers from pinned host blobs through ``window`` device slots.
+
+    The last ``pinned`` layers are kept resident instead (uploaded once, no hooks): every token
+    reads every dense layer, so each resident byte saves one streamed byte per token -- the
+    reference's pin placement for dense blocks (``rocketllm/memory/placement.py``).  They are the
+    last ones so that their compute covers the prefetch of the next token's first streamed
+    layers."""
 
     def __init__(self, layers, device, window=2, copy_streams=2, chunk_bytes=16 << 20,
-                 prefetching=True, expert_slots=None, blobs=None):
+                 prefetching=True, expert_slots=None, blobs=None, pinned=0):
         if window < 1:
             raise ValueError("window must be >= 1")
         self.layers = list(layers)
         self.device = torch.device(device)
-        self.window = min(window, len(self.layers))
+        self.pinned = max(0, min(int(pinned), len(self.layers)))
+        self.streamed = len(self.layers) - self.pinned
+        self.window = min(window, self.streamed)
         self.prefetching = prefetching
         # routed experts stream one by one (expert_stream.py) when expert_slots is given
         stream_experts = expert_slots is not None
         # blobs: prebuilt host blobs (read from layer shards on disk); else packed from the layers
         self.blobs = blobs if blobs is not None else [_pack_layer(layer, stream_experts)
                                                       for layer in self.layers]
-        self.slot_bytes = max(b.nbytes for b in self.blobs)
+        self.slot_bytes = max((b.nbytes for b in self.blobs[:self.streamed]), default=0)
         self.slots = [torch.empty(self.slot_bytes, dtype=torch.uint8, device=self.device)
                       for _ in range(self.window)]
-        for i, blob in enumerate(self.blobs):
-            _bind(blob, self.slots[i % self.window])
+        for i in range(self.streamed):
+            _bind(self.blobs[i], self.slots[i % self.window])
+        self.resident = []   # device storage of the pinned layers
+        for i in range(self.streamed, len(self.layers)):
+            blob = self.blobs[i]
+            dev = torch.empty(blob.nbytes, dtype=torch.uint8, device=self.device)
+            dev.copy_(blob.host[:blob.nbytes])
+            _bind(blob, dev)
+            self.resident.append(dev)
+            self.blobs[i] = _LayerBlob(None, blob.entries, blob.nbytes)  # host copy released
         self.xfer = WeightTransfer(device=self.device, copy_streams=copy_streams,
                                    chunk_bytes=chunk_bytes)
         self.experts = None
@@ -114,8 +130,8 @@ class LayerStreamer:
         self.fetches = 0
         self.bytes = 0
         self.hits = 0
-        self._handles = [layer.register_forward_pre_hook(self._make_pre_hook(i))
-                         for i, layer in enumerate(self.layers)]
+        self._handles = [self.layers[i].register_forward_pre_hook(self._make_pre_hook(i))
+                         for i in range(self.streamed)]
 
     def _send(self, i, compute):
         s = i % self.window
@@ -140,7 +156,7 @@ class LayerStreamer:
                 handle.resolve(compute)
                 self.tickets[i] = None
             if self.prefetching:
-                n = len(self.layers)
+                n = self.streamed
                 for d in range(1, self.window):
                     j = (i + d) % n
                     # never into the slot of the layer about to run (only possible when the
@@ -151,7 +167,8 @@ class LayerStreamer:
         return hook
 
     def stats(self):
-        return {"layers": len(self.layers), "window": self.window, "slot_bytes": self.slot_bytes,
+        return {"layers": len(self.layers), "pinned": self.pinned, "streamed": self.streamed,
+                "window": self.window, "slot_bytes": self.slot_bytes,
                 "fetches": self.fetches, "bytes": self.bytes, "slot_hits": self.hits,
                 "experts": self.experts.stats() if self.experts else None,
                 "transfer": self.xfer.stats()}
@@ -200,8 +217,9 @@ class RocketModel:
 
     ``vram_budget`` (bytes) bounds the model's device footprint: if the whole model fits it (or it
     is None) every layer is resident; otherwise the non-layer modules stay resident and at most
-    ``window`` layer slots fit in what is left (at least one), and layers stream from pinned host
-    memory every token.  In a mixture-of-experts model the routed experts stream one by one
+    ``window`` layer slots fit in what is left (at least one); the last layers that still fit
+    beside those slots stay resident (pinned) and the others stream from pinned host memory every
+    token.  In a mixture-of-experts model the routed experts stream one by one
     (``expert_streaming``): the layer slots hold the attention / router / norms only, and the rest
     of the budget becomes an expert cache of at least one layer's experts.
     """
@@ -233,15 +251,21 @@ class RocketModel:
         experts = [m for m in layers.modules() if is_rw4_experts(m)]
         expert_slots = None
         if experts and expert_streaming:
+            # attention / norms / router of every layer before routed experts (the reference's
+            # priority classes): window slots, then as many dense parts pinned as fit beside one
+            # layer's worth of expert slots, then the rest of the budget as expert cache
             _, dense_bytes = footprint(model, skip_experts=True)
             per_layer = max(m.gate_up_proj_packed.shape[0] for m in experts)
             eb = max(expert_blob_bytes(m) for m in experts)
             left = max(0, vram_budget - rest - per_layer * eb)
             window = max(1, min(window, int(left // max(dense_bytes))))
-            expert_slots = max(per_layer, int((vram_budget - rest - window * max(dense_bytes))
-                                              // eb))
+            pinned = self._pin_count(dense_bytes, left, window)
+            used = rest + self._plan_bytes(dense_bytes, window, pinned)
+            expert_slots = max(per_layer, int((vram_budget - used) // eb))
         else:
-            window = max(1, min(window, int(max(0, vram_budget - rest) // max(layer_bytes))))
+            left = max(0, vram_budget - rest)
+            window = max(1, min(window, int(left // max(layer_bytes))))
+            pinned = self._pin_count(layer_bytes, left, window)
         # everything outside the decoder layers is resident: move the model with its layer
         # list detached, then hand the layers to the streamer (they stay on the host)
         parent_path, _, leaf = _layers_path(model).rpartition(".")
@@ -251,7 +275,24 @@ class RocketModel:
         setattr(parent, leaf, layers)
         self.streamer = LayerStreamer(layers, self.device, window=window,
                                       copy_streams=copy_streams, chunk_bytes=chunk_bytes,
-                                      prefetching=prefetching, expert_slots=expert_slots)
+                                      prefetching=prefetching, expert_slots=expert_slots,
+                                      pinned=pinned)
+
+    @staticmethod
+    def _plan_bytes(layer_bytes, window, pinned):
+        """Device bytes of ``window`` slots for the streamed layers plus the pinned last layers."""
+        n = len(layer_bytes)
+        streamed = layer_bytes[:n - pinned]
+        return (window * max(streamed) if streamed else 0) + sum(layer_bytes[n - pinned:])
+
+    @classmethod
+    def _pin_count(cls, layer_bytes, free, window):
+        """How many of the last layers fit resident beside the window slots in ``free`` bytes."""
+        pinned = 0
+        while pinned < len(layer_bytes) and \
+                cls._plan_bytes(layer_bytes, window, pinned + 1) <= free:
+            pinned += 1
+        return pinned
 
     def _init_from_shards(self, root, device, dtype, vram_budget, window, prefetching,
                           copy_streams, chunk_bytes):
@@ -293,10 +334,12 @@ class RocketModel:
             host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
             reader.read_into(i, host)
             blobs.append(_LayerBlob(host, resolve(layer, entries), nbytes))
-        window = max(1, min(window, int(max(0, vram_budget - rest) // max(layer_bytes))))
+        left = max(0, vram_budget - rest)
+        window = max(1, min(window, int(left // max(layer_bytes))))
         self.streamer = LayerStreamer(layers, self.device, window=window,
                                       copy_streams=copy_streams, chunk_bytes=chunk_bytes,
-                                      prefetching=prefetching, blobs=blobs)
+                                      prefetching=prefetching, blobs=blobs,
+                                      pinned=self._pin_count(layer_bytes, left, window))
 
     @property
     def config(self):

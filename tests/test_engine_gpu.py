@@ -46,3 +46,23 @@ def test_streamed_equals_resident(checkpoint, window):
     assert st["fetches"] >= 4 * (1 + 8)          # every layer, every forward
     assert st["transfer"]["stalls"] == 0
     streamed.close()
+
+
+def test_pinned_layers_within_budget(checkpoint):
+    """Budget beyond the window slots keeps the last layers resident (the reference's pin
+    placement); only the others stream, and the result is unchanged."""
+    ids = torch.randint(0, 2048, (1, 16), generator=torch.Generator().manual_seed(6)).cuda()
+    resident = AutoModel.from_pretrained(checkpoint)
+    rest, layers = footprint(resident.model)
+    budget = rest + 1 * max(layers) + 2 * max(layers) + 1000   # one slot + two pinned layers
+    streamed = RocketModel(checkpoint, vram_budget=budget, window=1)
+    st = streamed.stats()["streaming"]
+    assert st["pinned"] == 2 and st["streamed"] == 2 and st["window"] == 1
+    with torch.no_grad():
+        assert torch.equal(resident(ids).logits, streamed(ids).logits)
+        a = resident.generate(ids, max_new_tokens=6, do_sample=False, min_new_tokens=6)
+        b = streamed.generate(ids, max_new_tokens=6, do_sample=False, min_new_tokens=6)
+    assert torch.equal(a, b)
+    st = streamed.stats()["streaming"]
+    assert st["bytes"] <= 2 * max(layers) * (1 + 1 + 6)   # only the two streamed layers move
+    streamed.close()

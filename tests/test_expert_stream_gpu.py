@@ -46,7 +46,8 @@ def test_streamed_experts_equal_resident(checkpoint, slots):
     streamed = RocketModel(checkpoint, vram_budget=budget, window=1)
     st = streamed.streamer
     assert st is not None and st.experts is not None
-    assert len(st.experts.slots) == slots
+    # the budget beyond one layer's experts goes to pinning dense parts first, then expert slots
+    assert E <= len(st.experts.slots) <= slots
     with torch.no_grad():
         assert torch.equal(resident(ids).logits, streamed(ids).logits)
         before = st.experts.stats()
@@ -59,9 +60,9 @@ def test_streamed_experts_equal_resident(checkpoint, slots):
     # routes 12 tokens, up to every expert)
     assert after["bytes"] - before["bytes"] <= (E + 5 * 2) * LAYERS * eb
     assert after["fetches"] > before["fetches"] or after["hits"] > before["hits"]
-    if slots == LAYERS * E:   # every expert fits: each routed expert crossed PCIe exactly once
+    if len(st.experts.slots) >= LAYERS * E:   # every expert fits: each crossed PCIe once
         assert after["fetches"] == after["resident"] <= LAYERS * E
-    assert after["resident"] <= slots
+    assert after["resident"] <= len(st.experts.slots)
     assert st.stats()["transfer"]["stalls"] == 0
     streamed.close()
 
