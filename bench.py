@@ -318,6 +318,80 @@ def pp_decode(args):
     return 0
 
 
+MIXTRAL_8X7B = dict(hidden_size=4096, intermediate_size=14336, num_hidden_layers=32,
+                    num_attention_heads=32, num_key_value_heads=8, vocab_size=32000,
+                    num_local_experts=8, num_experts_per_tok=2, max_position_embeddings=4096,
+                    rope_theta=1000000.0, tie_word_embeddings=False)
+
+
+def moe_decode(args):
+    """Mixtral-8x7B-architecture RW4 greedy decode with routed experts streamed one by one from
+    pinned host memory into an expert cache (not the driver's line): random
+    init N(0, 0.02) incl. the router, prompt ``--moe-prompt``, ``--moe-tokens`` new tokens per
+    batch size, under ``--moe-budget-gb`` of VRAM.  Prints one JSON line."""
+    from transformers import MixtralConfig
+
+    from rocketllm_b200.decode import GraphedDecoder
+    from rocketllm_b200.engine import RocketModel
+    from rocketllm_b200.synthetic import build_rw4_causal_lm
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = MixtralConfig(**MIXTRAL_8X7B)
+    t0 = time.time()
+    model = build_rw4_causal_lm(cfg, device=device, seed=0)
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    streamed = RocketModel(model, device=device, vram_budget=int(args.moe_budget_gb * 1e9),
+                           window=2)
+    del model
+    torch.cuda.empty_cache()
+    setup_s = time.time() - t0
+    st = streamed.streamer
+    out = {"mode": "streamed mixture-of-experts greedy decode",
+           "model": "Mixtral-8x7B architecture, RW4 group 64 (random init N(0,0.02))",
+           "data": "synthetic", "weight_bytes": weight_bytes,
+           "vram_budget_bytes": int(args.moe_budget_gb * 1e9),
+           "pinned_layers": st.pinned, "streamed_layers": st.streamed,
+           "expert_slots": len(st.experts.slots) if st.experts else 0,
+           "expert_blob_bytes": st.experts.slot_bytes if st.experts else 0,
+           "prompt_tokens": args.moe_prompt, "setup_s": round(setup_s, 1)}
+    gen = torch.Generator().manual_seed(1)
+    for b in tuple(int(v) for v in args.moe_batches.split(",")):
+        ids = torch.randint(0, cfg.vocab_size, (b, args.moe_prompt), generator=gen).to(device)
+        dec = GraphedDecoder(streamed.model, b, args.moe_prompt + args.moe_tokens + 8,
+                             device=device, use_graph=False)
+        p0 = time.time()
+        dec.prefill(ids)
+        dec.step()
+        torch.cuda.synchronize()
+        prefill_s = time.time() - p0
+        s0 = st.stats()
+        e0 = st.experts.stats() if st.experts else {"bytes": 0, "fetches": 0, "hits": 0}
+        a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.moe_tokens):
+            dec.step()
+        c.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(c) / args.moe_tokens
+        s1 = st.stats()
+        e1 = st.experts.stats() if st.experts else {"bytes": 0, "fetches": 0, "hits": 0}
+        layer_bytes = (s1["bytes"] - s0["bytes"]) / args.moe_tokens
+        expert_bytes = (e1["bytes"] - e0["bytes"]) / args.moe_tokens
+        out[f"b{b}"] = {"tok_s": round(b * 1000.0 / ms, 2), "ms_per_token": round(ms, 2),
+                        "prefill_s": round(prefill_s, 2),
+                        "h2d_bytes_per_token": int(layer_bytes + expert_bytes),
+                        "expert_bytes_per_token": int(expert_bytes),
+                        "h2d_gbs": round((layer_bytes + expert_bytes) / (ms * 1e-3) / 1e9, 2),
+                        "expert_fetches": e1["fetches"] - e0["fetches"],
+                        "expert_hits": e1["hits"] - e0["hits"]}
+        del dec
+        torch.cuda.empty_cache()
+    out["h2d_probe_gbs"] = round(h2d_probe(device), 2)
+    print(json.dumps(out), flush=True)
+    streamed.close()
+    return 0
+
+
 def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget):
     """Greedy decode tok/s of a Llama-3.1-8B-architecture RW4 model (random init N(0, 0.02),
     every Linear incl. lm_head in RW4): resident with a CUDA-graphed step, then streamed from
@@ -666,9 +740,17 @@ def main():
     ap.add_argument("--pp-batches", default="1,32")
     ap.add_argument("--pp-prompt", type=int, default=1024)
     ap.add_argument("--pp-tokens", type=int, default=64)
+    ap.add_argument("--moe-decode", action="store_true",
+                    help="streamed Mixtral-architecture decode with per-expert streaming")
+    ap.add_argument("--moe-budget-gb", type=float, default=8.0)
+    ap.add_argument("--moe-batches", default="1,32")
+    ap.add_argument("--moe-prompt", type=int, default=512)
+    ap.add_argument("--moe-tokens", type=int, default=16)
     args = ap.parse_args()
     if args.sweep:
         return sweep(args)
+    if args.moe_decode:
+        return moe_decode(args)
     if args.pp_decode:
         return pp_decode(args)
     if args.decode_only:
