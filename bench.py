@@ -392,6 +392,66 @@ def moe_decode(args):
     return 0
 
 
+def ep_decode(args):
+    """Expert-parallel greedy decode over the torchrun ranks (not the driver's line): the
+    Mixtral-8x7B architecture in RW4 with its routed experts split E/G per rank (NCCL all-to-all
+    dispatch and return in every MoE layer), attention replicated, every rank decoding its own
+    batch.  Eager steps (the exchange sizes are read on the host).  One JSON line on rank 0;
+    throughput summed over ranks, step time the slowest rank's."""
+    import datetime
+
+    import torch.distributed as dist
+    from transformers import MixtralConfig
+
+    from rocketllm_b200.expert_parallel import enable_expert_parallel
+    from rocketllm_b200.pipeline import PipelineDecoder
+    from rocketllm_b200.synthetic import build_rw4_causal_lm
+    world, rank, local = dist_env()
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
+    cfg = MixtralConfig(**MIXTRAL_8X7B)
+    model = build_rw4_causal_lm(cfg, device=device, seed=0)
+    enable_expert_parallel(model)
+    torch.cuda.empty_cache()
+    out = {"mode": "expert-parallel greedy decode",
+           "model": "Mixtral-8x7B architecture, RW4 group 64 (random init N(0,0.02))",
+           "data": "synthetic", "n_gpus": world, "experts_per_rank": 8 // world,
+           "rank0_weight_bytes": sum(p.numel() * p.element_size() for p in model.parameters()),
+           "prompt_tokens": args.moe_prompt, "new_tokens": args.moe_tokens}
+
+    def reduce(v, op):
+        t = torch.tensor([v], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=op)
+        return float(t.item())
+
+    for b in tuple(int(v) for v in args.moe_batches.split(",")):
+        ids = torch.randint(0, cfg.vocab_size, (b, args.moe_prompt),
+                            generator=torch.Generator().manual_seed(100 + rank))
+        dec = PipelineDecoder(model, device=device, local=True, drop_remote=False)
+        dist.barrier()
+        tok = dec._forward(ids, b, args.moe_prompt)    # prefill
+        tok = dec._forward(tok, b, 1)                   # one warm-up step
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.moe_tokens):
+            tok = dec._forward(tok, b, 1)
+        c.record()
+        torch.cuda.synchronize()
+        ms = reduce(a.elapsed_time(c) / args.moe_tokens, dist.ReduceOp.MAX)
+        out[f"b{b}_per_rank"] = {"tok_s": round(world * b * 1000.0 / ms, 2),
+                                 "ms_per_token": round(ms, 2)}
+        del dec
+        torch.cuda.empty_cache()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget):
     """Greedy decode tok/s of a Llama-3.1-8B-architecture RW4 model (random init N(0, 0.02),
     every Linear incl. lm_head in RW4): resident with a CUDA-graphed step, then streamed from
@@ -746,9 +806,13 @@ def main():
     ap.add_argument("--moe-batches", default="1,32")
     ap.add_argument("--moe-prompt", type=int, default=512)
     ap.add_argument("--moe-tokens", type=int, default=16)
+    ap.add_argument("--ep-decode", action="store_true",
+                    help="expert-parallel Mixtral-architecture decode over the torchrun ranks")
     args = ap.parse_args()
     if args.sweep:
         return sweep(args)
+    if args.ep_decode:
+        return ep_decode(args)
     if args.moe_decode:
         return moe_decode(args)
     if args.pp_decode:
