@@ -412,9 +412,10 @@ def ep_decode(args):
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=device)
     cfg = MixtralConfig(**MIXTRAL_8X7B)
     model = build_rw4_causal_lm(cfg, device=device, seed=0)
-    enable_expert_parallel(model)
+    enable_expert_parallel(model, fixed_capacity=args.ep_graph)
     torch.cuda.empty_cache()
-    out = {"mode": "expert-parallel greedy decode",
+    out = {"mode": "expert-parallel greedy decode" + (
+               ", fixed-capacity exchange, CUDA-graphed steps" if args.ep_graph else ""),
            "model": "Mixtral-8x7B architecture, RW4 group 64 (random init N(0,0.02))",
            "data": "synthetic", "n_gpus": world, "experts_per_rank": 8 // world,
            "rank0_weight_bytes": sum(p.numel() * p.element_size() for p in model.parameters()),
@@ -425,25 +426,38 @@ def ep_decode(args):
         dist.all_reduce(t, op=op)
         return float(t.item())
 
+    from rocketllm_b200.decode import GraphedDecoder
     for b in tuple(int(v) for v in args.moe_batches.split(",")):
         ids = torch.randint(0, cfg.vocab_size, (b, args.moe_prompt),
                             generator=torch.Generator().manual_seed(100 + rank))
-        dec = PipelineDecoder(model, device=device, local=True, drop_remote=False)
         dist.barrier()
-        tok = dec._forward(ids, b, args.moe_prompt)    # prefill
-        tok = dec._forward(tok, b, 1)                   # one warm-up step
+        if args.ep_graph:
+            dec = GraphedDecoder(model, b, args.moe_prompt + args.moe_tokens + 8, device=device)
+            dec.prefill(ids)
+            for _ in range(3):   # capture (collectives inside the graph) + warm-up replays
+                dec.step()
+            step = dec.step
+        else:
+            dec = PipelineDecoder(model, device=device, local=True, drop_remote=False)
+            tok = dec._forward(ids, b, args.moe_prompt)    # prefill
+            tok = dec._forward(tok, b, 1)                   # one warm-up step
+            state = {"tok": tok}
+
+            def step():
+                state["tok"] = dec._forward(state["tok"], b, 1)
         torch.cuda.synchronize()
         dist.barrier()
         a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(args.moe_tokens):
-            tok = dec._forward(tok, b, 1)
+            step()
         c.record()
         torch.cuda.synchronize()
         ms = reduce(a.elapsed_time(c) / args.moe_tokens, dist.ReduceOp.MAX)
         out[f"b{b}_per_rank"] = {"tok_s": round(world * b * 1000.0 / ms, 2),
                                  "ms_per_token": round(ms, 2)}
-        del dec
+        del dec, step   # a graph holding NCCL calls goes before the process group
+        torch.cuda.synchronize()
         torch.cuda.empty_cache()
     if rank == 0:
         print(json.dumps(out), flush=True)
@@ -808,6 +822,8 @@ def main():
     ap.add_argument("--moe-tokens", type=int, default=16)
     ap.add_argument("--ep-decode", action="store_true",
                     help="expert-parallel Mixtral-architecture decode over the torchrun ranks")
+    ap.add_argument("--ep-graph", type=int, default=1,
+                    help="1: fixed-capacity exchange and CUDA-graphed steps; 0: eager")
     args = ap.parse_args()
     if args.sweep:
         return sweep(args)

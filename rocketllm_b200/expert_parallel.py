@@ -50,7 +50,7 @@ class ExpertParallelMoE:
     expert ``first_expert + i`` at index ``i``).
     """
 
-    def __init__(self, num_experts, gate_up, down, group=None, ops=None):
+    def __init__(self, num_experts, gate_up, down, group=None, ops=None, fixed_capacity=False):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -64,6 +64,10 @@ class ExpertParallelMoE:
         self.gate_up = gate_up
         self.down = down
         self.ops = ops if ops is not None else CudaExpertOps()
+        # fixed_capacity: every rank sends every peer a buffer of T*k rows (zero-padded, the
+        # worst case of one token's k slots) -- equal split sizes, no host round trip, so a step
+        # can be captured in a CUDA graph; all ranks must then call with the same token count T
+        self.fixed_capacity = fixed_capacity
 
     def _exchange_counts(self, send_counts):
         recv = torch.empty_like(send_counts)
@@ -71,6 +75,8 @@ class ExpertParallelMoE:
         return recv
 
     def forward(self, hidden, top_k_index, top_k_weights):
+        if self.fixed_capacity:
+            return self._forward_fixed(hidden, top_k_index, top_k_weights)
         t, h = hidden.shape
         k = top_k_index.shape[1]
         idx = top_k_index.to(torch.int64).contiguous()
@@ -110,6 +116,55 @@ class ExpertParallelMoE:
             y_back = torch.cat([y_back, pad])
         return ops.combine(y_back, inv, idx, top_k_weights.contiguous())
 
+    def _forward_fixed(self, hidden, top_k_index, top_k_weights):
+        """The same exchange with fixed, zero-padded per-peer buffers (device-side only)."""
+        t, h = hidden.shape
+        k = top_k_index.shape[1]
+        cap = max(1, t * k)
+        world, dev = self.world, hidden.device
+        idx = top_k_index.to(torch.int64).contiguous()
+        ops = self.ops
+        perm, inv, offsets = ops.permute(idx, self.num_experts)
+        x_sorted = ops.gather(hidden.contiguous(), perm, k)
+        ids_sorted = idx.reshape(-1)[perm.long().clamp(min=0)] if t else \
+            torch.zeros(0, dtype=torch.int64, device=dev)
+        bounds = offsets[::self.per_rank].to(torch.int64)                 # [world + 1]
+        counts = bounds[1:] - bounds[:-1]
+        j = torch.arange(cap, device=dev)
+        valid = j[None, :] < counts[:, None]                              # [world, cap]
+        src = (bounds[:-1, None] + j[None, :]).clamp(0, max(t * k - 1, 0))
+        if t:
+            send_x = torch.where(valid[..., None], x_sorted[src], torch.zeros((), dtype=hidden.dtype,
+                                                                               device=dev))
+            send_ids = torch.where(valid, ids_sorted[src], torch.full((), -1, dtype=torch.int64,
+                                                                        device=dev))
+        else:
+            send_x = torch.zeros((world, cap, h), dtype=hidden.dtype, device=dev)
+            send_ids = torch.full((world, cap), -1, dtype=torch.int64, device=dev)
+        recv_x = torch.empty_like(send_x)
+        recv_ids = torch.empty_like(send_ids)
+        dist.all_to_all_single(recv_x.view(world * cap, h), send_x.view(world * cap, h),
+                               group=self.group)
+        dist.all_to_all_single(recv_ids.view(-1), send_ids.reshape(-1), group=self.group)
+        # local experts; padding rows carry id -1 and fall outside [0, per_rank): dropped
+        local = torch.where(recv_ids >= 0, recv_ids - self.first_expert,
+                            torch.full((), self.per_rank, dtype=torch.int64, device=dev))
+        perm2, inv2, off2 = ops.permute(local.reshape(-1, 1).contiguous(), self.per_rank)
+        rows = ops.gather(recv_x.view(world * cap, h), perm2, 1)
+        y_rows = ops.experts(rows, off2, self.gate_up, self.down, world * cap)
+        y_recv = ops.gather(y_rows, inv2, 1)                              # padding rows: zeros
+        y_back = torch.empty_like(y_recv)
+        dist.all_to_all_single(y_back, y_recv, group=self.group)
+        y_back = y_back.view(world, cap, h)
+        # back to this rank's expert-sorted order: position p went to rank r at slot p - bounds[r]
+        p = torch.arange(t * k, device=dev)
+        r = (p[:, None] >= bounds[None, 1:]).sum(1)                       # world = dropped slot
+        rc = r.clamp(max=world - 1)
+        y_sorted = y_back[rc, (p - bounds[rc]).clamp(0, cap - 1)]
+        y_sorted = torch.where((r < world)[:, None], y_sorted,
+                               torch.zeros((), dtype=y_sorted.dtype, device=dev))
+        return ops.combine(y_sorted, inv, idx, top_k_weights.contiguous())
+
     __call__ = forward
 
 
@@ -128,7 +183,7 @@ def shard_experts(experts_module, rank, world):
     return triples("gate_up_proj"), triples("down_proj")
 
 
-def enable_expert_parallel(model, group=None, ops=None, drop_remote=True):
+def enable_expert_parallel(model, group=None, ops=None, drop_remote=True, fixed_capacity=False):
     """Partition every RW4 stacked-experts module of ``model`` over ``group``: keep this rank's
     experts (views of the stacked tensors; the other experts' memory is released when
     ``drop_remote``) and bind a forward that runs :class:`ExpertParallelMoE`.  Attention and the
@@ -152,10 +207,11 @@ def enable_expert_parallel(model, group=None, ops=None, drop_remote=True):
                                getattr(module, name + "_scale")[i],
                                getattr(module, name + "_zero_point")[i]) for i in range(per)]
                        for name in ("gate_up_proj", "down_proj")}
-            moe = ExpertParallelMoE(e, triples["gate_up_proj"], triples["down_proj"], group, ops)
+            moe = ExpertParallelMoE(e, triples["gate_up_proj"], triples["down_proj"], group, ops,
+                                    fixed_capacity)
         else:
             gu, dn = shard_experts(module, rank, world)
-            moe = ExpertParallelMoE(e, gu, dn, group, ops)
+            moe = ExpertParallelMoE(e, gu, dn, group, ops, fixed_capacity)
         module.expert_parallel = moe
         module.forward = types.MethodType(
             lambda self, hidden, idx, w: self.expert_parallel(hidden, idx, w), module)

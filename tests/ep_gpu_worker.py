@@ -39,14 +39,27 @@ def main():
         x = torch.randn(t, H, device=dev, generator=g).to(torch.bfloat16)
         idx = torch.stack([torch.randperm(E, device=dev, generator=g)[:K_TOP] for _ in range(t)])
         w = torch.softmax(torch.randn(t, K_TOP, device=dev, generator=g), -1)
-        ref = rw4_experts_forward(ex, x, idx, w)
+        # the single-GPU routed experts on the same kernels (max_rows = t*k: the bf16 grouped
+        # GEMV, as the exchange's receiving side uses; a one-token step on one GPU would take the
+        # fp16 one-row kernel, equal within rounding but not bit for bit)
+        trip = {n: [(getattr(ex, n + "_packed")[e], getattr(ex, n + "_scale")[e],
+                     getattr(ex, n + "_zero_point")[e]) for e in range(E)]
+                for n in ("gate_up_proj", "down_proj")}
+        perm, inv, off = kernels.moe_permute(idx, E)
+        xp = kernels.moe_gather(x, perm, K_TOP)
+        act = kernels.moe_grouped(xp, off, trip["gate_up_proj"], act=1, max_rows=t * K_TOP)
+        yp = kernels.moe_grouped(act, off, trip["down_proj"], act=0, max_rows=t * K_TOP)
+        ref = kernels.moe_combine(yp, inv, idx, w)
+        if t > 1:
+            assert torch.equal(ref, rw4_experts_forward(ex, x, idx, w))
         gu, dn = shard_experts(ex, rank, world)
-        y = ExpertParallelMoE(E, gu, dn)(x, idx, w)
-        torch.cuda.synchronize()
-        if not torch.equal(y, ref):
-            failures += 1
-            print(f"rank {rank} t={t}: max diff {(y.float() - ref.float()).abs().max().item()}",
-                  flush=True)
+        for fixed in (False, True):
+            y = ExpertParallelMoE(E, gu, dn, fixed_capacity=fixed)(x, idx, w)
+            torch.cuda.synchronize()
+            if not torch.equal(y, ref):
+                failures += 1
+                print(f"rank {rank} t={t} fixed={fixed}: max diff "
+                      f"{(y.float() - ref.float()).abs().max().item()}", flush=True)
     assert kernels.device_status() == 0
     f = torch.tensor([failures], device=dev)
     dist.all_reduce(f)

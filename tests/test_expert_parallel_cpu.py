@@ -20,7 +20,13 @@ class CpuOps:
         self.w = weights  # {global expert: (w_gate_up [2I, H], w_down [H, I])}
 
     def permute(self, idx, num_experts):
-        perm, off = o.moe_permute(idx.numpy(), num_experts)
+        # the CUDA kernel's contract: slots whose id is outside [0, E) are dropped (perm -1 at
+        # the end, inv -1); the rest are the oracle's stable sort
+        flat = idx.numpy().reshape(-1)
+        ok = (flat >= 0) & (flat < num_experts)
+        sub, off = o.moe_permute(flat[ok].reshape(-1, 1), num_experts)
+        perm = np.full(flat.shape, -1, np.int32)
+        perm[:sub.size] = np.nonzero(ok)[0][sub].astype(np.int32)
         inv = np.full(perm.shape, -1, np.int32)
         valid = perm >= 0
         inv[perm[valid]] = np.arange(perm.size, dtype=np.int32)[valid]
@@ -77,14 +83,15 @@ def single_process(x, idx, w, weights):
     return ops.combine(y, inv, idx, w)
 
 
-def _worker(rank, world, port, t_per_rank, out):
+def _worker(rank, world, port, t_per_rank, out, fixed=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     from rocketllm_b200.expert_parallel import ExpertParallelMoE
     weights = make_problem(0)
     per = E // world
     mine = weights[rank * per:(rank + 1) * per]
-    moe = ExpertParallelMoE(E, [a for a, _ in mine], [b for _, b in mine], ops=CpuOps(None))
+    moe = ExpertParallelMoE(E, [a for a, _ in mine], [b for _, b in mine], ops=CpuOps(None),
+                            fixed_capacity=fixed)
     x, idx, w = tokens(rank, t_per_rank[rank])
     y = moe(x, idx, w)
     ref = single_process(x, idx, w, weights)
@@ -101,4 +108,15 @@ def test_expert_parallel_matches_single_process(t_per_rank):
         out = mgr.dict()
         mp.spawn(_worker, args=(world, port, t_per_rank, out), nprocs=world, join=True)
         # fp32 matmuls batch rows differently on each side: equal to rounding
+        assert all(out[r] <= 1e-6 for r in range(world)), dict(out)
+
+
+@pytest.mark.parametrize("world,t", [(2, 5), (2, 1), (4, 3)])
+def test_fixed_capacity_exchange_matches_single_process(world, t):
+    """Zero-padded fixed-size buffers (no host round trip): the same result (equal token counts
+    on every rank, as the mode requires)."""
+    port = 29900 + world * 10 + t
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_worker, args=(world, port, (t,) * world, out, True), nprocs=world, join=True)
         assert all(out[r] <= 1e-6 for r in range(world)), dict(out)
