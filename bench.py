@@ -786,6 +786,89 @@ def sweep(args):
     return 0
 
 
+KV_CASES = (   # (model architecture, batch, query heads, kv heads, head_dim, context tokens)
+    ("llama3-8b", 1, 32, 8, 128, 4096), ("llama3-8b", 1, 32, 8, 128, 32768),
+    ("llama3-8b", 16, 32, 8, 128, 4096), ("llama3-8b", 16, 32, 8, 128, 32768),
+    ("llama3-70b", 1, 64, 8, 128, 32768), ("llama3-405b", 4, 128, 8, 128, 32768),
+)
+
+
+def kv_attn_bench(args):
+    """Decode attention of one layer over an int4 KV cache: the packed-history kernel vs the
+    reference's behaviour on the same device (expand every quantized group to bf16, then SDPA over
+    the whole history) and vs SDPA over an unquantized bf16 cache.  L2 is flushed (a 256 MB write)
+    before every timed launch; each launch is timed alone with CUDA events.  One JSON line per
+    case: algorithmic bytes (codes + scales + zeros of the quantized groups, the bf16 window) per
+    launch, GB/s, and the fraction of the measured HBM copy bandwidth."""
+    import torch.nn.functional as F
+
+    from rocketllm_b200 import kernels
+    from rocketllm_b200.kv_cache import RW4KVCache
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peak, peak_kind = measured_peak()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    iters = max(5, min(args.steps, 50))
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        total = 0.0
+        for _ in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            total += a.elapsed_time(b)
+        return total / iters
+
+    picked = KV_CASES if args.kv_cases == "all" else tuple(
+        KV_CASES[int(i)] for i in args.kv_cases.split(","))
+    for name, bsz, h, kvh, d, ctx in picked:
+        g = torch.Generator(device=device).manual_seed(ctx + bsz)
+        cache = RW4KVCache(fused=True)
+        k = torch.randn(bsz, kvh, ctx - 1, d, device=device, generator=g).to(torch.bfloat16)
+        v = torch.randn(bsz, kvh, ctx - 1, d, device=device, generator=g).to(torch.bfloat16)
+        cache.update(k, v, 0)
+        del k, v
+        cache.update(torch.randn(bsz, kvh, 1, d, device=device, generator=g).to(torch.bfloat16),
+                     torch.randn(bsz, kvh, 1, d, device=device, generator=g).to(torch.bfloat16), 0)
+        layer = cache._kv[0]
+        q = torch.randn(bsz, h, 1, d, device=device, generator=g).to(torch.bfloat16)
+        scaling = d ** -0.5
+        ms = timed(lambda: cache.attend(0, q, scaling))
+
+        def reference_step():
+            hk, hv = cache.history(0)
+            F.scaled_dot_product_attention(q, hk, hv, scale=scaling, enable_gqa=True)
+
+        ms_ref = timed(reference_step)
+        hk, hv = cache.history(0)
+        ms_bf16 = timed(lambda: F.scaled_dot_product_attention(q, hk, hv, scale=scaling,
+                                                               enable_gqa=True))
+        vg = d // 64
+        alg = bsz * kvh * (layer.groups * (36 * d + 32 * d + 64 * vg * 4) + layer.rlen * 4 * d) \
+            + 2 * bsz * h * d * 2
+        bf16_bytes = 2 * hk.numel() * 2
+        gbs = alg / (ms * 1e-3) / 1e9
+        print(json.dumps({
+            "kv_attention": name, "batch": bsz, "heads": h, "kv_heads": kvh, "head_dim": d,
+            "context": ctx, "quantized_tokens": layer.groups * 64, "window_tokens": layer.rlen,
+            "us": round(ms * 1e3, 2), "alg_bytes": alg, "gbs": round(gbs, 1),
+            "hbm_frac": round(gbs / peak, 4), "peak": peak_kind,
+            "reference_us": round(ms_ref * 1e3, 2), "speedup_vs_reference": round(ms_ref / ms, 2),
+            "bf16_cache_sdpa_us": round(ms_bf16 * 1e3, 2), "bf16_cache_bytes": bf16_bytes,
+            "speedup_vs_bf16_cache": round(ms_bf16 / ms, 2), "l2": "flushed before each launch",
+            "launches_timed": iters}), flush=True)
+        del cache, hk, hv
+        torch.cuda.empty_cache()
+    if kernels.device_status():
+        raise RuntimeError("a kernel reported a timed-out wait")
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -820,11 +903,16 @@ def main():
     ap.add_argument("--moe-batches", default="1,32")
     ap.add_argument("--moe-prompt", type=int, default=512)
     ap.add_argument("--moe-tokens", type=int, default=16)
+    ap.add_argument("--kv-attn", action="store_true",
+                    help="decode attention over the int4 KV cache (one JSON line per case)")
+    ap.add_argument("--kv-cases", default="all", help="'all' or indices into KV_CASES")
     ap.add_argument("--ep-decode", action="store_true",
                     help="expert-parallel Mixtral-architecture decode over the torchrun ranks")
     ap.add_argument("--ep-graph", type=int, default=1,
                     help="1: fixed-capacity exchange and CUDA-graphed steps; 0: eager")
     args = ap.parse_args()
+    if args.kv_attn:
+        return kv_attn_bench(args)
     if args.sweep:
         return sweep(args)
     if args.ep_decode:

@@ -145,6 +145,31 @@ int rw4_moe_combine(const void* y_perm_bf16, const int32_t* inv, const int64_t* 
                     void* out_bf16, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Decode attention over the int4 KV cache.  Replaces what the reference runs for one decode step
+ * with its QuantizedKVCache (rocketllm/quant/kv_cache.py:277-316: every quantized block expanded
+ * to the compute dtype, concatenated with the fp16 window, then the model's attention): softmax
+ * attention of one query token straight over the packed history plus the window.
+ *
+ * Layout of each (batch, kv head) slot hs = b * kv_heads + kvh (all contiguous, 16-byte aligned):
+ *   k_codes u8  [hs][groups_cap][head_dim][32]   group g, channel c: tokens 64g.. two per byte
+ *   k_sz    f16 [hs][groups_cap][head_dim][2]    (scale, zero) per channel per group
+ *   v_codes u8  [hs][groups_cap*64][head_dim/2]  per token, channels two per byte
+ *   v_sz    f16 [hs][groups_cap*64][head_dim/64][2]  (scale, zero) per token per 64 channels
+ *   k_res / v_res bf16 [hs][res_cap][head_dim]   the window, first res_len tokens valid
+ * Codes and scales are the reference's quantize(K, axis=2, 64) / quantize(V, axis=3, 64) output
+ * (value = code * scale + zero).  q bf16 [batch][heads][head_dim] with element strides
+ * (q_stride_b, q_stride_h, 1); out bf16 likewise.  Query head h reads kv head h / (heads /
+ * kv_heads).  head_dim 64 or 128, heads / kv_heads <= 16, groups + res_len >= 1.
+ * ------------------------------------------------------------------------------------------- */
+int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, int32_t batch,
+                            int32_t heads, int32_t kv_heads, int32_t head_dim,
+                            const uint8_t* k_codes, const void* k_sz, const uint8_t* v_codes,
+                            const void* v_sz, int64_t groups_cap, int64_t groups,
+                            const void* k_res, const void* v_res, int64_t res_cap, int64_t res_len,
+                            float scaling, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                            void* stream);
+
+/* ---------------------------------------------------------------------------------------------
  * Streaming: pinned host staging pool + host->device transfer engine.
  *
  * rw4_pool_* replaces HostStagingPool (rocketllm/streaming/staging.py:80-273): pinned buffers in

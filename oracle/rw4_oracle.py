@@ -16,10 +16,16 @@ to the RocketLLM project root):
 * transformers ``models/mixtral/modeling_mixtral.py:101-116`` ``MixtralTopKRouter`` (softmax fp32,
   top-k, renormalise) and ``:62-98`` ``MixtralExperts.forward`` (gate/up, SiLU, down, weighted sum)
 * ``rocketllm/moe/router.py:70-94`` ``RouterSelection.observe`` (sorted unique expert ids)
+* ``rocketllm/quant/kv_cache.py:277-352`` ``QuantizedKVCache.update`` / ``_flush`` (window of exact
+  tokens, whole groups moved into quantized blocks) and the attention a decode step runs over the
+  expanded history (transformers ``integrations/sdpa_attention.py``)
 
 Parity is pinned: ``tests/test_oracle_golden.py`` checks every function here against fixtures in
 ``tests/golden/`` that ``tests/golden/make_golden.py`` produced by running the reference's own
-``kv_cache`` codec and transformers' own Mixtral router on the same seeded inputs.
+``kv_cache`` codec and transformers' own Mixtral router on the same seeded inputs, and
+``tests/test_kv_oracle.py`` checks the KV-cache functions against ``tests/golden/reference_kv.npz``,
+which ``tests/golden/make_kv_golden.py`` produced by running the reference's ``QuantizedKVCache``
+and transformers' SDPA attention.
 
 bf16 has no numpy dtype, so bf16 tensors travel as their raw ``uint16`` bit patterns; conversion
 to and from fp32 uses round-to-nearest-even on the bit pattern, the rounding torch's ``.to()``
@@ -259,3 +265,84 @@ def expert_mlp(x_bf16_bits, gate_up, down, inter):
     h = linear(x_bf16_bits, *gate_up)
     act = round_bf16(silu(round_bf16(h[:, :inter])) * round_bf16(h[:, inter:]))
     return linear(f32_to_bf16_bits(act), *down)
+
+
+# ----------------------------------------------------------------------------------------------
+# int4 KV cache (KIVI layout): K grouped along tokens, V along channels, recent tokens exact
+# ----------------------------------------------------------------------------------------------
+
+def kv_quantize(x, axis, group=64, dtype="bf16"):
+    """The reference ``quantize(tensor, axis, group_size)`` on an N-d tensor (``kv_cache.py:190-221``).
+
+    The grouped axis is moved last and every leading index is one row of :func:`quantize`.
+    Returns ``(packed u8 [..., Lp/2], scale f16 [..., Lp/g], zero f16 [..., Lp/g], padding)``
+    in the moved layout, exactly the fields of the reference's ``QuantizedTensor``.
+    """
+    x = np.asarray(x)
+    moved = np.moveaxis(x, axis, -1)
+    lead = moved.shape[:-1]
+    packed, scale, zero, padding = quantize(moved.reshape(-1, moved.shape[-1]), group, dtype)
+    return (packed.reshape(lead + packed.shape[1:]), scale.reshape(lead + scale.shape[1:]),
+            zero.reshape(lead + zero.shape[1:]), padding)
+
+
+def kv_dequantize(packed, scale, zero, axis, length, out="bf16"):
+    """``QuantizedTensor.dequantize`` (``kv_cache.py:249-257``): rows of the moved layout expanded,
+    narrowed to ``length`` along the grouped axis, the axis moved back, cast to ``out``."""
+    lead = packed.shape[:-1]
+    flat = dequantize(packed.reshape(-1, packed.shape[-1]), scale.reshape(-1, scale.shape[-1]),
+                      zero.reshape(-1, zero.shape[-1]), k=length, out=out)
+    return np.moveaxis(flat.reshape(lead + (length,)), -1, axis)
+
+
+class KiviCache:
+    """The reference ``QuantizedKVCache`` restated for one layer (``kv_cache.py:277-352``).
+
+    ``update(k, v)`` takes bf16 bit patterns ``[b, kvh, t, d]``, appends them to the exact window,
+    moves whole groups of the oldest tokens past ``residual`` into append-only quantized blocks
+    (K along tokens, V along channels) and returns the whole history in bf16 bits: the expanded
+    blocks, oldest first, then the window.
+    """
+
+    def __init__(self, group=64, residual=128):
+        self.group, self.residual = group, residual
+        self.k = self.v = None
+        self.blocks = []          # (k_block, v_block): kv_quantize outputs of each flush
+
+    def update(self, k, v):
+        k = np.asarray(k, dtype=np.uint16)
+        v = np.asarray(v, dtype=np.uint16)
+        self.k = k if self.k is None else np.concatenate([self.k, k], axis=2)
+        self.v = v if self.v is None else np.concatenate([self.v, v], axis=2)
+        excess = self.k.shape[2] - self.residual
+        take = (excess // self.group) * self.group if excess > 0 else 0
+        if take > 0:
+            self.blocks.append((kv_quantize(self.k[:, :, :take], 2, self.group),
+                                kv_quantize(self.v[:, :, :take], 3, self.group), take))
+            self.k = self.k[:, :, take:]
+            self.v = self.v[:, :, take:]
+        return self.history()
+
+    def quantized_tokens(self):
+        return sum(t for _, _, t in self.blocks)
+
+    def history(self):
+        ks = [kv_dequantize(*kb[:3], axis=2, length=t) for kb, _, t in self.blocks]
+        vs = [kv_dequantize(*vb[:3], axis=3, length=self.k.shape[3]) for _, vb, t in self.blocks]
+        return (np.concatenate(ks + [self.k], axis=2), np.concatenate(vs + [self.v], axis=2))
+
+
+def attention_decode(q, k, v, scaling):
+    """One query token's softmax attention over ``k``/``v`` ``[b, kvh, T, d]`` (fp32 inputs),
+    query ``[b, h, d]``; query head ``h`` reads kv head ``h // (h_total / kvh)`` (transformers
+    ``repeat_kv``).  fp64 arithmetic, fp32 result ``[b, h, d]``."""
+    b, h, d = q.shape
+    kvh = k.shape[1]
+    rep = h // kvh
+    kk = np.repeat(k.astype(np.float64), rep, axis=1)
+    vv = np.repeat(v.astype(np.float64), rep, axis=1)
+    logits = np.einsum("bhd,bhtd->bht", q.astype(np.float64), kk) * scaling
+    logits -= logits.max(axis=-1, keepdims=True)
+    p = np.exp(logits)
+    p /= p.sum(axis=-1, keepdims=True)
+    return np.einsum("bht,bhtd->bhd", p, vv).astype(np.float32)

@@ -54,6 +54,10 @@ SIGNATURES = {
                                        _c_void_p, _i64, _i64, _i32, _i32, _c_void_p, _c_void_p]),
     "rw4_moe_combine": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64,
                                        _i32, _i64, _c_void_p, _c_void_p]),
+    "rw4_kv_attention_decode": (ctypes.c_int, [_c_void_p, _i64, _i64, _i32, _i32, _i32, _i32,
+                                               _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64,
+                                               _i64, _c_void_p, _c_void_p, _i64, _i64,
+                                               ctypes.c_float, _c_void_p, _i64, _i64, _c_void_p]),
     "rw4_pool_create": (ctypes.c_int, [_size, ctypes.POINTER(_c_void_p)]),
     "rw4_pool_destroy": (ctypes.c_int, [_c_void_p]),
     "rw4_pool_lease": (ctypes.c_int, [_c_void_p, _size, ctypes.POINTER(_i32),

@@ -1,0 +1,79 @@
+"""The oracle's int4 KV cache against the reference's own ``QuantizedKVCache`` (CPU, no GPU).
+
+``tests/golden/reference_kv.npz`` holds what the reference cache returned for a seeded prefill of
+260 tokens followed by 60 single-token decode steps (``make_kv_golden.py``), and transformers' SDPA
+attention of one query over the final history.  Everything here is bit-exact except the attention
+(fp64 oracle vs the reference's fp32 / bf16 SDPA), which is held to a stated tolerance.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import ROOT
+from oracle import rw4_oracle as O
+
+KV = os.path.join(ROOT, "tests", "golden", "reference_kv.npz")
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return dict(np.load(KV))
+
+
+@pytest.fixture(scope="module")
+def replay(gold):
+    b, kvh, h, d, prefill, steps = gold["shape"].tolist()
+    cache = O.KiviCache(group=64, residual=128)
+    hk, hv = cache.update(gold["k.0"], gold["v.0"])
+    first_len = hk.shape[2]
+    for s in range(1, steps + 1):
+        hk, hv = cache.update(gold[f"k.{s}"], gold[f"v.{s}"])
+    return cache, hk, hv, first_len
+
+
+def test_prefill_history_length(gold, replay):
+    assert replay[3] == int(gold["hist_len.0"])
+
+
+def test_history_bit_exact(gold, replay):
+    _, hk, hv, _ = replay
+    np.testing.assert_array_equal(hk, gold["hist_k.last"])
+    np.testing.assert_array_equal(hv, gold["hist_v.last"])
+
+
+def test_blocks_bit_exact(gold, replay):
+    cache = replay[0]
+    assert [t for _, _, t in cache.blocks] == gold["blocks"].tolist()
+    assert cache.k.shape[2] == int(gold["residual"])
+    for i, (kb, vb, _) in enumerate(cache.blocks):
+        for name, blk in (("kb", kb), ("vb", vb)):
+            np.testing.assert_array_equal(blk[0], gold[f"{name}{i}.packed"])
+            np.testing.assert_array_equal(blk[1].view(np.uint16),
+                                          gold[f"{name}{i}.scale"].view(np.uint16))
+            np.testing.assert_array_equal(blk[2].view(np.uint16),
+                                          gold[f"{name}{i}.zero"].view(np.uint16))
+
+
+def test_attention_matches_sdpa(gold, replay):
+    _, hk, hv, _ = replay
+    d = hk.shape[-1]
+    q = O.bf16_bits_to_f32(gold["q"])[:, :, 0, :]
+    out = O.attention_decode(q, O.bf16_bits_to_f32(hk), O.bf16_bits_to_f32(hv), d ** -0.5)
+    ref32 = gold["attn_f32"][:, 0]                      # [b, h, d] fp32 SDPA
+    np.testing.assert_allclose(out, ref32, rtol=0, atol=2e-6)
+    ref16 = O.bf16_bits_to_f32(gold["attn"])[:, 0]      # the bf16 model's SDPA output
+    assert np.abs(out - ref16).max() <= 2e-2
+
+
+def test_window_never_flushes_a_partial_group():
+    # 128 + 63 tokens stay exact; the 192nd moves exactly one group of 64
+    rng = np.random.default_rng(0)
+    cache = O.KiviCache(group=64, residual=128)
+    for t in range(191):
+        x = O.f32_to_bf16_bits(rng.standard_normal((1, 1, 1, 64)).astype(np.float32))
+        cache.update(x, x)
+    assert cache.quantized_tokens() == 0 and cache.k.shape[2] == 191
+    x = O.f32_to_bf16_bits(rng.standard_normal((1, 1, 1, 64)).astype(np.float32))
+    hk, _ = cache.update(x, x)
+    assert cache.quantized_tokens() == 64 and cache.k.shape[2] == 128 and hk.shape[2] == 192
