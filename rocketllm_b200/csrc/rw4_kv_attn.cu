@@ -34,6 +34,7 @@
 #include <cooperative_groups.h>
 
 #include <atomic>
+#include <cstdlib>
 
 #include "rw4_common.cuh"
 #include "rw4_tma.cuh"
@@ -44,9 +45,13 @@ using namespace rw4;
 namespace {
 
 constexpr int kTok = 64;
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 2;
+// warps per CTA (one CTA per SM: 255 registers a thread).  12 warps at 168 registers measured
+// no faster at batch 16 and slower at batch 1 (more warps without items, a longer combine).
+template <int NT>
+struct KvWarps {
+  static constexpr int value = 8;
+};
 constexpr float kNegBig = -1.0e30f;
 
 template <int D>
@@ -106,10 +111,16 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// two codes (bits 0-3 or 4-7 of each half, selected by `mask`) -> fp16 pair of exact integers
+// two codes (bits 0-3 or 4-7 of each half, selected by `mask`) -> fp16 pair 1024 + code (or
+// 1024 + 16 code): exact, with an offset of 1024 that an all-ones MMA removes per chunk
 __device__ __forceinline__ uint32_t codes_f16(uint32_t x, uint32_t mask) {
-  uint32_t v = (x & mask) | 0x64006400u;  // 1024 + code (or 1024 + 16 code)
-  __half2 h = __hsub2(*reinterpret_cast<__half2*>(&v), __half2(__half(1024.f), __half(1024.f)));
+  return (x & mask) | 0x64006400u;
+}
+
+constexpr uint32_t kOnesF16 = 0x3C003C00u;  // (1.0, 1.0)
+
+__device__ __forceinline__ uint32_t hmul2_u(uint32_t a, uint32_t b) {
+  __half2 h = __hmul2(*reinterpret_cast<__half2*>(&a), *reinterpret_cast<__half2*>(&b));
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
@@ -143,7 +154,7 @@ __device__ __forceinline__ float half_hi(uint32_t w) {
 template <int NT, int VM, int VG>
 __device__ __forceinline__ void softmax_step(float (&s)[NT][4][4], float (&m_run)[NT][2],
                                              float (&l_run)[NT][2], float (&zp)[NT][VG][2],
-                                             float (&o)[NT][VM][4]) {
+                                             float (&o)[NT][VM][4], float (&offv)[NT][VG][4]) {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -159,7 +170,11 @@ __device__ __forceinline__ void softmax_step(float (&s)[NT][4][4], float (&m_run
       m_run[nt][j] = mnew;
       float l = l_run[nt][j] * alpha;
 #pragma unroll
-      for (int g = 0; g < VG; ++g) zp[nt][g][j] *= alpha;
+      for (int g = 0; g < VG; ++g) {
+        zp[nt][g][j] *= alpha;
+        offv[nt][g][j] *= alpha;
+        offv[nt][g][j + 2] *= alpha;
+      }
 #pragma unroll
       for (int vm = 0; vm < VM; ++vm) {
         o[nt][vm][j] *= alpha;
@@ -178,8 +193,9 @@ __device__ __forceinline__ void softmax_step(float (&s)[NT][4][4], float (&m_run
   }
 }
 
-template <int D, int NT>
-__global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a) {
+template <int D, int NT, int kWarps = KvWarps<NT>::value>
+__global__ void __launch_bounds__(kWarps * 32, 1) rw4_kv_attn_kernel(const KvArgs a) {
+  constexpr int kThreads = kWarps * 32;
   using L = KvLayout<D>;
   constexpr int KC = D / 16;  // 16-channel chunks of the QK^T reduction
   constexpr int VG = L::VG;
@@ -214,14 +230,17 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
   }
   __syncthreads();
 
-  // query fragment of the quantized path: head nt*8 + n, channels 16kc + qd + 4e
-  float qf[NT][KC][4];
+  // query fragment of the quantized path as fp16 pairs: head nt*8 + n, channels
+  // (16kc + qd, 16kc + qd + 4) and (16kc + qd + 8, 16kc + qd + 12)
+  uint32_t qh[NT][KC][2];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int kc = 0; kc < KC; ++kc)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) qf[nt][kc][e] = qs[(nt * 8 + n) * D + 16 * kc + qd + 4 * e];
+    for (int kc = 0; kc < KC; ++kc) {
+      const float* qr = qs + (nt * 8 + n) * D + 16 * kc + qd;
+      qh[nt][kc][0] = pack_f16(qr[0], qr[4]);
+      qh[nt][kc][1] = pack_f16(qr[8], qr[12]);
+    }
 
   const int64_t nw = static_cast<int64_t>(csize) * kWarps;
   const int64_t wg = static_cast<int64_t>(crank) * kWarps + warp;
@@ -256,6 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
   __syncwarp();
 
   float m_run[NT][2], l_run[NT][2], zp[NT][VG][2], o[NT][VM][4];
+  float offv[NT][VG][4];  // sum_t B[t, head] of the V MMAs: their 1024 offset, per head
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
 #pragma unroll
@@ -265,6 +285,10 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
 #pragma unroll
       for (int g = 0; g < VG; ++g) zp[nt][g][j] = 0.f;
     }
+#pragma unroll
+    for (int g = 0; g < VG; ++g)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) offv[nt][g][i] = 0.f;
 #pragma unroll
     for (int vm = 0; vm < VM; ++vm)
 #pragma unroll
@@ -294,28 +318,34 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
       const uint8_t* sb = my + st * L::kStage;
       const uint8_t* kcs = sb + L::oK;
       const uint8_t* kss = sb + L::oKsz;
-      float zq[NT];
+      // offk: sum_c B'[c, head] (the 1024 offset of the codes); zk: sum_c q'[head, c] z_c
+      float offk[NT][4], zk[NT][4];
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) zq[nt] = 0.f;
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) offk[nt][i] = zk[nt][i] = 0.f;
+      const uint32_t ones[4] = {kOnesF16, kOnesF16, kOnesF16, kOnesF16};
 #pragma unroll
       for (int kc = 0; kc < KC; ++kc) {
-        uint32_t w[4];
-        float sc[4], zr[4];
+        uint32_t w[4], sz[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int c = 16 * kc + qd + 4 * e;
           w[e] = lds_u32(kcs + 32 * c + 4 * n);
-          const uint32_t sz = lds_u32(kss + 4 * c);
-          sc[e] = half_lo(sz);
-          zr[e] = half_hi(sz);
+          sz[e] = lds_u32(kss + 4 * c);
         }
+        const uint32_t s01 = __byte_perm(sz[0], sz[1], 0x5410);
+        const uint32_t s23 = __byte_perm(sz[2], sz[3], 0x5410);
+        const uint32_t z01 = __byte_perm(sz[0], sz[1], 0x7632);
+        const uint32_t z23 = __byte_perm(sz[2], sz[3], 0x7632);
         uint32_t bq[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          bq[nt][0] = pack_f16(qf[nt][kc][0] * sc[0], qf[nt][kc][1] * sc[1]);
-          bq[nt][1] = pack_f16(qf[nt][kc][2] * sc[2], qf[nt][kc][3] * sc[3]);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) zq[nt] = fmaf(qf[nt][kc][e], zr[e], zq[nt]);
+          bq[nt][0] = hmul2_u(qh[nt][kc][0], s01);
+          bq[nt][1] = hmul2_u(qh[nt][kc][1], s23);
+          mma_f16_16816(offk[nt], ones, bq[nt][0], bq[nt][1], offk[nt]);
+          mma_f16_16816(zk[nt], ones, hmul2_u(qh[nt][kc][0], z01), hmul2_u(qh[nt][kc][1], z23),
+                        zk[nt]);
         }
 #pragma unroll
         for (int mt = 0; mt < 4; ++mt) {
@@ -328,23 +358,23 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
           for (int nt = 0; nt < NT; ++nt) mma_f16_16816(s[nt][mt], af, bq[nt][0], bq[nt][1], s[nt][mt]);
         }
       }
-      // zero-point term per head, moved from the B layout (head n) to the C layout (2qd + j)
+      // S = (acc - 1024 offk) [/ 16 on the high-nibble rows] + zk; the all-ones MMAs leave the
+      // per-head sums in every row, columns 2qd and 2qd + 1 as the scores' own fragment
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        float z = zq[nt];
-        z += __shfl_xor_sync(0xffffffffu, z, 1);
-        z += __shfl_xor_sync(0xffffffffu, z, 2);
-        const float z0 = __shfl_sync(0xffffffffu, z, 8 * qd);
-        const float z1 = __shfl_sync(0xffffffffu, z, 8 * qd + 4);
+        const float ce0 = fmaf(-1024.f, offk[nt][0], zk[nt][0]);
+        const float ce1 = fmaf(-1024.f, offk[nt][1], zk[nt][1]);
+        const float co0 = fmaf(-64.f, offk[nt][0], zk[nt][0]);
+        const float co1 = fmaf(-64.f, offk[nt][1], zk[nt][1]);
 #pragma unroll
         for (int mt = 0; mt < 4; ++mt) {
-          s[nt][mt][0] += z0;
-          s[nt][mt][1] += z1;
-          s[nt][mt][2] = fmaf(s[nt][mt][2], 0.0625f, z0);
-          s[nt][mt][3] = fmaf(s[nt][mt][3], 0.0625f, z1);
+          s[nt][mt][0] += ce0;
+          s[nt][mt][1] += ce1;
+          s[nt][mt][2] = fmaf(s[nt][mt][2], 0.0625f, co0);
+          s[nt][mt][3] = fmaf(s[nt][mt][3], 0.0625f, co1);
         }
       }
-      softmax_step<NT, VM, VG>(s, m_run, l_run, zp, o);
+      softmax_step<NT, VM, VG>(s, m_run, l_run, zp, o, offv);
 
       // P V: scales of this thread's tokens 8n..8n+7 (C-fragment rows)
       const uint8_t* vcs = sb + L::oV;
@@ -361,19 +391,25 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
       const uint8_t* blk = vcs + qd * L::kVBlk;
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
-        uint32_t bv[NT][VG][2];
+        uint32_t bv[NT][VG][2], pe[NT], po[NT];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          pe[nt] = pack_f16(s[nt][mt][0], s[nt][mt][1]);
+          po[nt] = pack_f16(s[nt][mt][2], s[nt][mt][3]);
+        }
 #pragma unroll
         for (int g = 0; g < VG; ++g) {
           const uint32_t e = vz[(2 * mt) * VG + g], od = vz[(2 * mt + 1) * VG + g];
-          const float se = half_lo(e), ze = half_hi(e), so = half_lo(od), zo = half_hi(od);
+          const float ze = half_hi(e), zo = half_hi(od);
+          const uint32_t se2 = __byte_perm(e, e, 0x1010), so2 = __byte_perm(od, od, 0x1010);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            const float p0 = s[nt][mt][0], p1 = s[nt][mt][1], p2 = s[nt][mt][2],
-                        p3 = s[nt][mt][3];
-            zp[nt][g][0] = fmaf(p0, ze, fmaf(p2, zo, zp[nt][g][0]));
-            zp[nt][g][1] = fmaf(p1, ze, fmaf(p3, zo, zp[nt][g][1]));
-            bv[nt][g][0] = movtrans(pack_f16(p0 * se, p1 * se));
-            bv[nt][g][1] = movtrans(pack_f16(p2 * so, p3 * so));
+            zp[nt][g][0] = fmaf(s[nt][mt][0], ze, fmaf(s[nt][mt][2], zo, zp[nt][g][0]));
+            zp[nt][g][1] = fmaf(s[nt][mt][1], ze, fmaf(s[nt][mt][3], zo, zp[nt][g][1]));
+            bv[nt][g][0] = movtrans(hmul2_u(pe[nt], se2));
+            bv[nt][g][1] = movtrans(hmul2_u(po[nt], so2));
+            const uint32_t ones[4] = {kOnesF16, kOnesF16, kOnesF16, kOnesF16};
+            mma_f16_16816(offv[nt][g], ones, bv[nt][g][0], bv[nt][g][1], offv[nt][g]);
           }
         }
 #pragma unroll
@@ -438,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
           if (!vo) s[nt][mt][2] = s[nt][mt][3] = -INFINITY;
         }
       }
-      softmax_step<NT, VM, VG>(s, m_run, l_run, zp, o);
+      softmax_step<NT, VM, VG>(s, m_run, l_run, zp, o, offv);
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
         uint32_t bv[NT][2];
@@ -513,7 +549,8 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
       for (int i = 0; i < 4; ++i) {
         const int j = i & 1;
         const int h = nt * 8 + 2 * qd + j;
-        const float v = (i < 2 ? o[nt][vm][i] : o[nt][vm][i] * 0.0625f) + zp[nt][g][j];
+        const float a = fmaf(-1024.f, offv[nt][g][j], o[nt][vm][i]);
+        const float v = (i < 2 ? a : a * 0.0625f) + zp[nt][g][j];
         mine[h * D + ch + (i >> 1)] = v;
       }
     }
@@ -573,12 +610,14 @@ __global__ void __launch_bounds__(kThreads, 1) rw4_kv_attn_kernel(const KvArgs a
 template <int D, int NT>
 size_t kv_smem() {
   using L = KvLayout<D>;
+  constexpr int kWarps = KvWarps<NT>::value;
   return static_cast<size_t>(8 * NT * D * 4) + kWarps * kStages * L::kStage + kWarps * kStages * 8;
 }
 
 template <int D, int NT>
 int launch_kv(const KvArgs& args, int hs_count, int csize, cudaStream_t stream) {
   using L = KvLayout<D>;
+  constexpr int kWarps = KvWarps<NT>::value;
   static_assert(kWarps * (8 * NT * (D + 2)) * 4 + 8 * NT * (D + 2) * 4 <=
                     kWarps * kStages * L::kStage,
                 "partials must fit the stage area");
@@ -589,13 +628,15 @@ int launch_kv(const KvArgs& args, int hs_count, int csize, cudaStream_t stream) 
   cudaGetDevice(&dev);
   if (!(attr_set.load() & (1u << dev))) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem)) != cudaSuccess)
-      return fail(RW4_ECUDA, "kv_attention: cannot set dynamic shared memory size");
+                             static_cast<int>(smem)) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+            cudaSuccess)
+      return fail(RW4_ECUDA, "kv_attention: cannot set the kernel's launch attributes");
     attr_set.fetch_or(1u << dev);
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(csize, hs_count);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kWarps * 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -616,9 +657,9 @@ namespace rw4 {
 
 // CTAs per head slot: enough to give every SM one CTA when the batch is small, at most a portable
 // cluster of 8, and no more than the items keep busy (at least two per warp where possible).
-int kv_cluster_size(int64_t head_slots, int64_t items) {
+int kv_cluster_size(int64_t head_slots, int64_t items, int warps) {
   int s = 1;
-  while (s < 8 && head_slots * (2 * s) <= sm_count() && static_cast<int64_t>(2 * s) * kWarps * 2 <= items)
+  while (s < 8 && head_slots * (2 * s) <= sm_count() && static_cast<int64_t>(2 * s) * warps * 2 <= items)
     s *= 2;
   return s;
 }
@@ -676,7 +717,13 @@ extern "C" int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_
   args.o_sh = out_stride_h;
   args.status = status;
   const int64_t items = groups + (res_len + kTok - 1) / kTok;
-  const int cs = kv_cluster_size(hs_count, items);
+  int cs = kv_cluster_size(hs_count, items, G <= 8 ? KvWarps<1>::value : KvWarps<2>::value);
+  if (const char* forced = getenv("RW4_KV_CLUSTER")) {   // launch-shape switch for measurements
+    const int f = atoi(forced);
+    if (f != 1 && f != 2 && f != 4 && f != 8 && f != 16)
+      return fail(RW4_EINVAL, "RW4_KV_CLUSTER=%s (1, 2, 4, 8 or 16)", forced);
+    cs = f;
+  }
   cudaStream_t st = as_stream(stream);
   const int hsc = static_cast<int>(hs_count);
   if (head_dim == 128)
