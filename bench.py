@@ -341,7 +341,7 @@ def moe_decode(args):
     model = build_rw4_causal_lm(cfg, device=device, seed=0)
     weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
     streamed = RocketModel(model, device=device, vram_budget=int(args.moe_budget_gb * 1e9),
-                           window=2)
+                           window=2, kv_cache="fp16")
     del model
     torch.cuda.empty_cache()
     setup_s = time.time() - t0
@@ -509,7 +509,8 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
         torch.cuda.empty_cache()
         return out
     # streamed: the decoder layers leave HBM and stream from pinned host RAM every token
-    streamed = RocketModel(model, device=device, vram_budget=vram_budget, window=2)
+    streamed = RocketModel(model, device=device, vram_budget=vram_budget, window=2,
+                           kv_cache="fp16")
     ids = torch.randint(0, cfg.vocab_size, (1, 128), generator=gen).to(device)
     dec = GraphedDecoder(streamed.model, 1, 128 + stream_tokens + 8, device=device,
                          use_graph=False)

@@ -222,12 +222,23 @@ class RocketModel:
     token.  In a mixture-of-experts model the routed experts stream one by one
     (``expert_streaming``): the layer slots hold the attention / router / norms only, and the rest
     of the budget becomes an expert cache of at least one layer's experts.
+
+    ``kv_cache`` (``rocketllm/base.py:208-411``, ``quant/kv_cache.py:449-503``): ``"int4"`` gives
+    every ``generate`` an :class:`~rocketllm_b200.kv_cache.RW4KVCache` whose decode attention reads
+    the packed history; ``"fp16"`` keeps transformers' own cache; ``"auto"`` (default) quantizes the
+    context exactly when the weights do not fit the budget (they stream).  ``hqq`` / ``quanto``
+    (transformers' optional caches) fall back to the stock cache.
     """
 
     def __init__(self, model_or_path, device="cuda", dtype=torch.bfloat16, vram_budget=None,
                  window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
-                 expert_streaming=True, **unused):
+                 expert_streaming=True, kv_cache="auto", **unused):
+        from .kv_cache import KV_CHOICES
         from .shards import INDEX
+        if kv_cache not in KV_CHOICES:
+            raise ValueError(f"kv_cache must be one of {', '.join(KV_CHOICES)}, not {kv_cache!r}")
+        self.kv_cache_setting = kv_cache
+        self._kv_attention = False
         if isinstance(model_or_path, (str, os.PathLike)) and \
                 os.path.exists(os.path.join(str(model_or_path), INDEX)):
             self._init_from_shards(str(model_or_path), device, dtype, vram_budget, window,
@@ -345,7 +356,23 @@ class RocketModel:
     def config(self):
         return self.model.config
 
+    @property
+    def kv_cache_choice(self):
+        from .kv_cache import KV_AUTO, KV_FP16, KV_INT4
+        if self.kv_cache_setting != KV_AUTO:
+            return self.kv_cache_setting
+        return KV_INT4 if self.streamer is not None else KV_FP16
+
     def generate(self, *args, **kwargs):
+        from .kv_cache import KV_INT4, RW4KVCache, enable_kv_attention
+        # a quantized context has to be handed in (transformers builds its own cache otherwise);
+        # a cache the caller passed is kept
+        if kwargs.get("past_key_values") is None and self.kv_cache_choice == KV_INT4:
+            if not self._kv_attention:
+                enable_kv_attention(self.model)
+                self._kv_attention = True
+            kwargs["past_key_values"] = RW4KVCache(fused=True)
+            kwargs.setdefault("use_cache", True)
         return self.model.generate(*args, **kwargs)
 
     def forward(self, *args, **kwargs):

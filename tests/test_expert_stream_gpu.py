@@ -43,7 +43,7 @@ def test_streamed_experts_equal_resident(checkpoint, slots):
     resident = AutoModel.from_pretrained(checkpoint)
     assert resident.streamer is None
     budget = budget_for(resident.model, slots)
-    streamed = RocketModel(checkpoint, vram_budget=budget, window=1)
+    streamed = RocketModel(checkpoint, vram_budget=budget, window=1, kv_cache="fp16")
     st = streamed.streamer
     assert st is not None and st.experts is not None
     # the budget beyond one layer's experts goes to pinning dense parts first, then expert slots
@@ -70,7 +70,8 @@ def test_streamed_experts_equal_resident(checkpoint, slots):
 def test_whole_layer_streaming_still_available(checkpoint):
     ids = torch.randint(0, 2048, (1, 8), generator=torch.Generator().manual_seed(5)).cuda()
     resident = AutoModel.from_pretrained(checkpoint)
-    streamed = RocketModel(checkpoint, vram_budget=1, window=1, expert_streaming=False)
+    streamed = RocketModel(checkpoint, vram_budget=1, window=1, expert_streaming=False,
+                           kv_cache="fp16")
     assert streamed.streamer.experts is None
     with torch.no_grad():
         assert torch.equal(resident(ids).logits, streamed(ids).logits)

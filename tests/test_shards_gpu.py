@@ -40,7 +40,8 @@ def test_shards_equal_checkpoint(tmp_path, kind):
     from_shards = RocketModel(root)
     assert from_shards.streamer is None
     rest, layers = footprint(resident.model)
-    streamed = RocketModel(root, vram_budget=rest + 2 * max(layers) + 1000, window=2)
+    streamed = RocketModel(root, vram_budget=rest + 2 * max(layers) + 1000, window=2,
+                           kv_cache="fp16")
     assert streamed.streamer is not None and streamed.streamer.window == 2
     with torch.no_grad():
         ref = resident(ids).logits
