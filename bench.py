@@ -870,6 +870,91 @@ def kv_attn_bench(args):
     return 0
 
 
+class _ReplayDraft:
+    """A draft that proposes the target's own greedy continuation (an ideal draft): the spec-decode
+    lines then measure what one verify pass of k+1 positions costs against k+1 one-token steps."""
+
+    def __init__(self, continuation, prompt, vocab):
+        self.cont, self.prompt, self.vocab = continuation, prompt, vocab
+        self.seconds = 0.0
+
+    def reset(self):
+        pass
+
+    def crop(self, length):
+        pass
+
+    def propose(self, sequence, cached, k, sampling, generator=None):
+        at = sequence.shape[1] - self.prompt
+        toks = self.cont[at:at + k]
+        probs = torch.zeros(toks.shape[0], self.vocab, device=toks.device)
+        probs.scatter_(1, toks.view(-1, 1), 1.0)
+        return toks, probs if toks.shape[0] else None, cached
+
+
+def spec_decode(args):
+    """Speculative decoding on the streamed Llama-3-8B architecture (the decode bench's 4 GB
+    budget: 19 layers pinned, 13 streamed every pass).  A one-token step streams the 13 layers; a
+    verify pass streams them once for k+1 positions (RW4 GEMV at M = k+1).  The draft replays the
+    target's greedy continuation, so the acceptance rate is measured, not assumed (a (k+1)-row pass
+    may resolve a near-tie differently from a one-row step).  One JSON line per lookahead."""
+    from transformers import DynamicCache, LlamaConfig
+
+    from rocketllm_b200.engine import RocketModel
+    from rocketllm_b200.speculative import SpeculativeDecoder
+    from rocketllm_b200.synthetic import build_rw4_causal_lm
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    cfg = LlamaConfig(**LLAMA_8B)
+    model = build_rw4_causal_lm(cfg, device=device, seed=0)
+    target = RocketModel(model, device=device, vram_budget=int(4e9), window=2, kv_cache="fp16")
+    n = args.spec_tokens
+    ids = torch.randint(0, cfg.vocab_size, (1, 128),
+                        generator=torch.Generator().manual_seed(0)).to(device)
+
+    def plain():
+        cache = DynamicCache()
+        with torch.inference_mode():
+            tok = target(input_ids=ids, past_key_values=cache, use_cache=True).logits[:, -1:] \
+                .argmax(-1)
+            out = [tok]
+            for _ in range(n - 1):
+                tok = target(input_ids=tok, past_key_values=cache, use_cache=True) \
+                    .logits[:, -1:].argmax(-1)
+                out.append(tok)
+        return torch.cat(out, dim=1)[0]
+
+    plain()                                   # warm-up (first-touch of every slot and stream)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    cont = plain()
+    b.record()
+    torch.cuda.synchronize()
+    plain_ms = a.elapsed_time(b)
+    base = {"spec_decode": "llama3-8b architecture, RW4, streamed (4 GB budget)",
+            "prompt_tokens": 128, "new_tokens": n, "draft": "replay of the target's greedy tokens"}
+    print(json.dumps({**base, "lookahead": 0, "tok_s": round(n / (plain_ms * 1e-3), 2),
+                      "passes": n, "ms_per_pass": round(plain_ms / n, 2)}), flush=True)
+    for k in (1, 3, 7):
+        dec = SpeculativeDecoder(target, _ReplayDraft(cont, 128, cfg.vocab_size), lookahead=k,
+                                 max_lookahead=k)
+        a.record()
+        out = dec.generate(ids, n)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b)
+        st = dec.stats
+        print(json.dumps({**base, "lookahead": k, "tok_s": round(n / (ms * 1e-3), 2),
+                          "speedup_vs_plain": round(plain_ms / ms, 2), "passes": st.passes,
+                          "ms_per_pass": round(ms / st.passes, 2),
+                          "acceptance_rate": round(st.acceptance_rate, 4),
+                          "tokens_per_pass": round(st.tokens_per_pass, 2),
+                          "same_tokens_as_plain": bool(torch.equal(out[0, 128:], cont))}),
+              flush=True)
+    target.close()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -907,6 +992,9 @@ def main():
     ap.add_argument("--kv-attn", action="store_true",
                     help="decode attention over the int4 KV cache (one JSON line per case)")
     ap.add_argument("--kv-cases", default="all", help="'all' or indices into KV_CASES")
+    ap.add_argument("--spec-decode", action="store_true",
+                    help="speculative decoding on the streamed 8B (one JSON line per lookahead)")
+    ap.add_argument("--spec-tokens", type=int, default=48)
     ap.add_argument("--ep-decode", action="store_true",
                     help="expert-parallel Mixtral-architecture decode over the torchrun ranks")
     ap.add_argument("--ep-graph", type=int, default=1,
@@ -914,6 +1002,8 @@ def main():
     args = ap.parse_args()
     if args.kv_attn:
         return kv_attn_bench(args)
+    if args.spec_decode:
+        return spec_decode(args)
     if args.sweep:
         return sweep(args)
     if args.ep_decode:

@@ -228,17 +228,33 @@ class RocketModel:
     the packed history; ``"fp16"`` keeps transformers' own cache; ``"auto"`` (default) quantizes the
     context exactly when the weights do not fit the budget (they stream).  ``hqq`` / ``quanto``
     (transformers' optional caches) fall back to the stock cache.
+
+    ``draft_model`` / ``speculative`` (``rocketllm/spec/draft.py``): with a draft (a path, a
+    transformers model or a :class:`~rocketllm_b200.speculative.DraftModel`) one-sequence
+    ``generate`` calls run :class:`~rocketllm_b200.speculative.SpeculativeDecoder` -- ``"on"``
+    always, ``"auto"`` when the weights stream, ``"off"`` never; ``lookahead`` proposals per pass
+    to start, adapted up to ``max_lookahead``.
     """
 
     def __init__(self, model_or_path, device="cuda", dtype=torch.bfloat16, vram_budget=None,
                  window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
-                 expert_streaming=True, kv_cache="auto", **unused):
+                 expert_streaming=True, kv_cache="auto", draft_model=None, speculative="auto",
+                 lookahead=4, max_lookahead=8, **unused):
         from .kv_cache import KV_CHOICES
         from .shards import INDEX
+        from .speculative import SPEC_CHOICES
         if kv_cache not in KV_CHOICES:
             raise ValueError(f"kv_cache must be one of {', '.join(KV_CHOICES)}, not {kv_cache!r}")
+        if speculative not in SPEC_CHOICES:
+            raise ValueError(f"speculative must be one of {', '.join(SPEC_CHOICES)}, not "
+                             f"{speculative!r}")
         self.kv_cache_setting = kv_cache
         self._kv_attention = False
+        self.speculative_setting = speculative
+        self._draft_arg = draft_model
+        self._draft = None
+        self.lookahead, self.max_lookahead = lookahead, max_lookahead
+        self.speculation = None   # SpeculationStats of the last speculative generate
         if isinstance(model_or_path, (str, os.PathLike)) and \
                 os.path.exists(os.path.join(str(model_or_path), INDEX)):
             self._init_from_shards(str(model_or_path), device, dtype, vram_budget, window,
@@ -363,17 +379,58 @@ class RocketModel:
             return self.kv_cache_setting
         return KV_INT4 if self.streamer is not None else KV_FP16
 
+    def draft(self):
+        """The draft model (loaded on first use), or None."""
+        from .speculative import DraftModel
+        if self._draft is None and self._draft_arg is not None:
+            d = self._draft_arg
+            if isinstance(d, DraftModel):
+                self._draft = d
+            elif isinstance(d, (str, os.PathLike)):
+                self._draft = DraftModel.load(str(d), target_config=self.model.config,
+                                              device=self.device, dtype=torch.bfloat16)
+            else:
+                self._draft = DraftModel(d.to(self.device).eval())
+        return self._draft
+
+    def speculation_enabled(self):
+        from .speculative import resolve_speculation
+        return resolve_speculation(self.speculative_setting, self._draft_arg,
+                                   streamed=self.streamer is not None)
+
     def generate(self, *args, **kwargs):
         from .kv_cache import KV_INT4, RW4KVCache, enable_kv_attention
+        int4 = self.kv_cache_choice == KV_INT4
+        if int4 and not self._kv_attention:
+            enable_kv_attention(self.model)
+            self._kv_attention = True
+        ids = args[0] if args else kwargs.get("input_ids")
+        if ids is not None and ids.shape[0] == 1 and self.speculation_enabled()[0]:
+            return self._speculative_generate(ids, int4, **kwargs)
         # a quantized context has to be handed in (transformers builds its own cache otherwise);
         # a cache the caller passed is kept
-        if kwargs.get("past_key_values") is None and self.kv_cache_choice == KV_INT4:
-            if not self._kv_attention:
-                enable_kv_attention(self.model)
-                self._kv_attention = True
+        if kwargs.get("past_key_values") is None and int4:
             kwargs["past_key_values"] = RW4KVCache(fused=True)
             kwargs.setdefault("use_cache", True)
         return self.model.generate(*args, **kwargs)
+
+    def _speculative_generate(self, ids, int4, max_new_tokens=None, generator=None,
+                              past_key_values=None, **kwargs):
+        from .kv_cache import RW4KVCache
+        from .speculative import SamplingParams, SpeculativeDecoder
+        gc = self.model.generation_config
+        if max_new_tokens is None:
+            max_new_tokens = getattr(gc, "max_new_tokens", None) or 20
+        eos = kwargs.get("eos_token_id", getattr(gc, "eos_token_id", None))
+        sampling = SamplingParams.from_generation(gc, **{k: kwargs.get(k) for k in (
+            "do_sample", "temperature", "top_k", "top_p")})
+        dec = SpeculativeDecoder(self, self.draft(), self.lookahead, self.max_lookahead,
+                                 new_cache=(lambda: RW4KVCache(fused=True)) if int4 else None,
+                                 eos_token_id=eos)
+        out = dec.generate(ids.to(self.device), int(max_new_tokens), sampling, generator,
+                           past_key_values, int(kwargs.get("min_new_tokens") or 0))
+        self.speculation = dec.stats
+        return out
 
     def forward(self, *args, **kwargs):
         return self.model(*args, **kwargs)

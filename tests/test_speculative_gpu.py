@@ -1,0 +1,84 @@
+"""Speculative decoding with an RW4 target on the B200: every verify pass runs the RW4 layers at
+M = k+1 (the dequant-GEMV reads each weight once for all candidate positions), streamed or
+resident, with the stock or the int4 KV cache.
+
+Greedy speculation must reproduce the target's plain greedy decoding.  In bf16 a (k+1)-row pass can
+resolve a near-tie differently from a one-row step (the reference documents the same caveat,
+``rocketllm/spec/draft.py:45-64``), so the sequences must agree up to the first position where the
+plain run's top-1 margin is below 4e-2, and that position must exist only there.
+"""
+import pytest
+import torch
+
+from rocketllm_b200.engine import AutoModel, RocketModel
+from rocketllm_b200.quant.convert import save_rw4_checkpoint
+
+pytestmark = pytest.mark.gpu
+
+NEAR_TIE = 4e-2
+
+
+@pytest.fixture(scope="module")
+def checkpoint(tmp_path_factory):
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(hidden_size=512, intermediate_size=1536, num_hidden_layers=4,
+                      num_attention_heads=8, num_key_value_heads=2, vocab_size=2048,
+                      max_position_embeddings=1024, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    model = LlamaForCausalLM(cfg)
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            p.copy_(torch.ones_like(p) if "norm" in n else torch.randn_like(p) * 0.02)
+    return save_rw4_checkpoint(model, str(tmp_path_factory.mktemp("rw4")), device="cuda")
+
+
+def _draft(checkpoint):
+    """The same RW4 checkpoint, resident, as the draft: it proposes what the target would say."""
+    from transformers import AutoModelForCausalLM
+    return AutoModelForCausalLM.from_pretrained(checkpoint, dtype=torch.bfloat16).to("cuda")
+
+
+def _agree_up_to_near_tie(spec, plain, prompt):
+    seq, logits = plain.sequences, plain.logits
+    n = min(spec.shape[1], seq.shape[1])
+    diff = (spec[0, :n] != seq[0, :n]).nonzero()
+    if diff.numel() == 0:
+        return n
+    j = int(diff[0, 0])
+    assert j >= prompt
+    top2 = logits[j - prompt][0].float().topk(2).values
+    assert float(top2[0] - top2[1]) < NEAR_TIE, f"diverged at {j} with margin {top2}"
+    return j
+
+
+@pytest.mark.parametrize("kv", ["fp16", "int4"])
+def test_streamed_speculation_matches_greedy(checkpoint, kv):
+    ids = torch.randint(0, 2048, (1, 190), generator=torch.Generator().manual_seed(5)).cuda()
+    n = 40
+    plain = RocketModel(checkpoint, vram_budget=1, window=1, kv_cache=kv)
+    plain.model.generation_config.eos_token_id = None      # exactly n tokens, nothing masked
+    with torch.no_grad():
+        ref = plain.generate(ids, max_new_tokens=n, do_sample=False,
+                             return_dict_in_generate=True, output_logits=True)
+    plain.close()
+    spec = RocketModel(checkpoint, vram_budget=1, window=1, kv_cache=kv,
+                       draft_model=_draft(checkpoint), speculative="auto", lookahead=4)
+    spec.model.generation_config.eos_token_id = None
+    assert spec.speculation_enabled()[0]          # streamed weights: "auto" speculates
+    out = spec.generate(ids, max_new_tokens=n, do_sample=False)
+    assert out.shape == (1, 190 + n)
+    st = spec.speculation
+    agree = _agree_up_to_near_tie(out, ref, 190)
+    if kv == "fp16":
+        assert agree >= 190 + 8
+    # (int4: the first verify pass writes 194 positions and flushes a group before the plain run
+    # does, so its first tokens attend over quantized keys -- the reference cache does the same)
+    assert st.passes < n and st.tokens_per_pass > 2.0
+    assert st.acceptance_rate > 0.8
+    spec.close()
+
+
+def test_resident_auto_does_not_speculate(checkpoint):
+    m = AutoModel.from_pretrained(checkpoint, draft_model=_draft(checkpoint))
+    assert m.speculation_enabled() == (False, "the weights are resident; pass speculative='on' "
+                                              "to force it")
