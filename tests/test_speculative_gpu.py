@@ -74,7 +74,9 @@ def test_streamed_speculation_matches_greedy(checkpoint, kv):
     # (int4: the first verify pass writes 194 positions and flushes a group before the plain run
     # does, so its first tokens attend over quantized keys -- the reference cache does the same)
     assert st.passes < n and st.tokens_per_pass > 2.0
-    assert st.acceptance_rate > 0.8
+    # the draft keeps exact keys while an int4 target attends over quantized ones, so near-ties
+    # of this random-init model resolve differently more often
+    assert st.acceptance_rate > (0.8 if kv == "fp16" else 0.5)
     spec.close()
 
 
