@@ -248,7 +248,7 @@ def pp_decode(args):
     """Pipeline-parallel greedy decode (not the driver's line): the model's decoder layers split
     over the ranks (contiguous ranges; each rank builds only its own layers), hidden states handed
     rank to rank over NCCL (NVLink), every rank's per-token stage replayed from a CUDA graph.
-    Default: the Llama-3.1-405B architecture in RW4, batch 1 and 32, prompt
+    Default: the Llama-3.1-405B architecture in RW4 (several GPUs), batch 1 and 32, prompt
     1024, 64 new tokens.  Prints one JSON line on rank 0; timings are CUDA events, max over
     ranks."""
     import datetime
@@ -326,7 +326,7 @@ MIXTRAL_8X7B = dict(hidden_size=4096, intermediate_size=14336, num_hidden_layers
 
 def moe_decode(args):
     """Mixtral-8x7B-architecture RW4 greedy decode with routed experts streamed one by one from
-    pinned host memory into an expert cache (not the driver's line): random
+    pinned host memory into an expert cache (a separate line from the headline one): random
     init N(0, 0.02) incl. the router, prompt ``--moe-prompt``, ``--moe-tokens`` new tokens per
     batch size, under ``--moe-budget-gb`` of VRAM.  Prints one JSON line."""
     from transformers import MixtralConfig
@@ -469,7 +469,7 @@ def ep_decode(args):
 def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget):
     """Greedy decode tok/s of a Llama-3.1-8B-architecture RW4 model (random init N(0, 0.02),
     every Linear incl. lm_head in RW4): resident with a CUDA-graphed step, then streamed from
-    pinned host memory under a VRAM budget (BASELINE config 3)."""
+    pinned host memory under a VRAM budget."""
     from transformers import LlamaConfig
 
     from rocketllm_b200.decode import GraphedDecoder
