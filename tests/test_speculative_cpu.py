@@ -116,3 +116,34 @@ def test_compatibility_and_resolution():
     assert resolve_speculation("on", object())[0] is True
     with pytest.raises(ValueError):
         resolve_speculation("maybe", object())
+
+
+def test_speculation_over_int4_cache_crops_the_window():
+    """Verify passes write k+1 positions into the int4 cache (crossing flushes) and rejected ones
+    come back out of the exact window; the cache ends holding every token but the last."""
+    from test_kv_cache_cpu import CpuKVOps
+
+    from rocketllm_b200.kv_cache import RW4KVCache, enable_kv_attention
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(0)
+    cfg = LlamaConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                      num_attention_heads=4, num_key_value_heads=2, vocab_size=512,
+                      max_position_embeddings=1024)
+    target = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    draft = LlamaForCausalLM(LlamaConfig(**{**cfg.to_dict(), "num_hidden_layers": 1})) \
+        .to(torch.bfloat16).eval()
+    enable_kv_attention(target)
+    caches = []
+
+    def new_cache():
+        caches.append(RW4KVCache(ops=CpuKVOps(), fused=True))
+        return caches[-1]
+
+    ids = torch.randint(0, 512, (1, 180), generator=torch.Generator().manual_seed(2))
+    dec = SpeculativeDecoder(target, DraftModel(draft), lookahead=4, new_cache=new_cache)
+    out = dec.generate(ids, 60)
+    assert out.shape == (1, 240)
+    cache = caches[0]
+    assert cache.get_seq_length(0) == 239                 # every token but the last emitted
+    assert cache._kv[0].groups >= 1 and cache.flushes >= 1
+    assert dec.stats.passes <= 60 and dec.stats.emitted == 60
