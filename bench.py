@@ -940,9 +940,27 @@ def spec_decode(args):
             "prompt_tokens": 128, "new_tokens": n, "draft": "replay of the target's greedy tokens"}
     print(json.dumps({**base, "lookahead": 0, "tok_s": round(n / (plain_ms * 1e-3), 2),
                       "passes": n, "ms_per_pass": round(plain_ms / n, 2)}), flush=True)
-    for k in (1, 3, 7):
+    # raw target passes of w positions over the same 129-position cache (cropped back after each)
+    cache = DynamicCache()
+    with torch.inference_mode():
+        target(input_ids=ids, past_key_values=cache, use_cache=True)
+        widths = {}
+        for w in (1, 2, 3, 4, 8):
+            x = cont[:w].view(1, -1)
+            for rep in range(4):
+                if rep == 1:
+                    a.record()
+                target(input_ids=x, past_key_values=cache, use_cache=True)
+                cache.crop(128)
+            b.record()
+            torch.cuda.synchronize()
+            widths[w] = round(a.elapsed_time(b) / 3, 2)
+    print(json.dumps({**base, "pass_ms_by_width": widths}), flush=True)
+    for k in args.spec_lookaheads:
+        # warm-up: a whole untimed run (the first speculative run of a process measured 2.3x
+        # slower per pass than the same run repeated)
         SpeculativeDecoder(target, _ReplayDraft(cont, 128, cfg.vocab_size), lookahead=k,
-                           max_lookahead=k).generate(ids, 8)          # warm-up of these shapes
+                           max_lookahead=k).generate(ids, n)
         dec = SpeculativeDecoder(target, _ReplayDraft(cont, 128, cfg.vocab_size), lookahead=k,
                                  max_lookahead=k)
         a.record()
@@ -1008,6 +1026,8 @@ def main():
     ap.add_argument("--spec-decode", action="store_true",
                     help="speculative decoding on the streamed 8B (one JSON line per lookahead)")
     ap.add_argument("--spec-tokens", type=int, default=48)
+    ap.add_argument("--spec-lookaheads", type=lambda v: [int(x) for x in v.split(",")],
+                    default=[1, 3, 7])
     ap.add_argument("--ep-decode", action="store_true",
                     help="expert-parallel Mixtral-architecture decode over the torchrun ranks")
     ap.add_argument("--ep-graph", type=int, default=1,
