@@ -341,7 +341,7 @@ def moe_decode(args):
     model = build_rw4_causal_lm(cfg, device=device, seed=0)
     weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
     streamed = RocketModel(model, device=device, vram_budget=int(args.moe_budget_gb * 1e9),
-                           window=2, kv_cache="fp16")
+                           window=2, kv_cache="fp16", expert_routing=args.moe_routing)
     del model
     torch.cuda.empty_cache()
     setup_s = time.time() - t0
@@ -351,8 +351,9 @@ def moe_decode(args):
            "data": "synthetic", "weight_bytes": weight_bytes,
            "vram_budget_bytes": int(args.moe_budget_gb * 1e9),
            "pinned_layers": st.pinned, "streamed_layers": st.streamed,
-           "expert_slots": len(st.experts.slots) if st.experts else 0,
-           "expert_blob_bytes": st.experts.slot_bytes if st.experts else 0,
+           "expert_routing": args.moe_routing,
+           "expert_slots": st.experts.stats()["expert_slots"] if st.experts else 0,
+           "expert_blob_bytes": st.experts.stats()["slot_bytes"] if st.experts else 0,
            "prompt_tokens": args.moe_prompt, "setup_s": round(setup_s, 1)}
     gen = torch.Generator().manual_seed(1)
     for b in tuple(int(v) for v in args.moe_batches.split(",")):
@@ -1020,6 +1021,8 @@ def main():
     ap.add_argument("--moe-batches", default="1,32")
     ap.add_argument("--moe-prompt", type=int, default=512)
     ap.add_argument("--moe-tokens", type=int, default=16)
+    ap.add_argument("--moe-routing", choices=("host", "device"), default="host",
+                    help="routed-set read back to the host per MoE layer, or decided on the device")
     ap.add_argument("--kv-attn", action="store_true",
                     help="decode attention over the int4 KV cache (one JSON line per case)")
     ap.add_argument("--kv-cases", default="all", help="'all' or indices into KV_CASES")

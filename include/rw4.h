@@ -145,6 +145,49 @@ int rw4_moe_combine(const void* y_perm_bf16, const int32_t* inv, const int64_t* 
                     void* out_bf16, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
+ * Device-side routing into the expert cache.  Together these replace the routed-set read-back
+ * and host-issued expert reads of the reference's streaming MoE path (rocketllm/moe/router.py:
+ * 88-93, rocketllm/base.py:1375-1464, rocketllm/moe/expert_cache.py:261-316): nothing on the host
+ * waits for the router.
+ *
+ * rw4_slot_maps_create: encode one TMA tensor-map set per expert-cache slot (slot s holds an
+ * expert's [N, K] RW4 weight at slot_packed[s] / slot_scale[s] / slot_zero[s]), once, when the
+ * slots are allocated; nslots <= 80.  act = 1: stacked gate/up with the fused SwiGLU (as
+ * rw4_moe_grouped).
+ * rw4_moe_grouped_slots: rw4_moe_grouped where routed expert e's weight is the one in slot
+ * slot_of[e] (DEVICE int32 [E], written by rw4_expert_residency); a routed expert without a valid
+ * slot gets no output and sets RW4_DEVERR_SLOT (8) in the device status word.
+ * rw4_expert_residency: one-thread kernel; from the permutation offsets (DEVICE int32 [E+1]) of
+ * MoE layer `layer`, claim the slots of routed experts already resident, give each other routed
+ * expert a free or least-recently-used slot not claimed in this call, and list those (copy_expert
+ * / copy_slot int32 [E], ncopy int32 [1]).  State: where int32 [layers*E], owner int32 [S],
+ * stamp int32 [S], clock int32 [1] (all initialised to -1 / -1 / 0 / 0 by the caller), counters
+ * uint64 [2] (hits, fetches).
+ * rw4_expert_copy: copy every listed expert's blob (host_blobs uint64 [layers*E]: DEVICE-visible
+ * addresses of mapped pinned host blobs, each blob_bytes long) into its slot (slots + s *
+ * slot_bytes); grid ctas_per_expert x E.
+ * rw4_host_ptr_device: the device-visible address of pinned host memory, or an error for memory
+ * that is not pinned and mapped (so a copy kernel is never given an address it cannot read).
+ * ------------------------------------------------------------------------------------------- */
+typedef struct rw4_slot_maps rw4_slot_maps;
+int rw4_slot_maps_create(const uint8_t* const* slot_packed, const void* const* slot_scale,
+                         const void* const* slot_zero, int32_t nslots, int64_t K, int64_t N,
+                         int32_t act, rw4_slot_maps** out);
+int rw4_slot_maps_destroy(rw4_slot_maps* maps);
+int rw4_moe_grouped_slots(const void* x_perm_bf16, const int32_t* offsets, int32_t E,
+                          int64_t max_rows, const rw4_slot_maps* maps, const int32_t* slot_of,
+                          void* y_perm_bf16, void* stream);
+int rw4_expert_residency(const int32_t* offsets, int32_t E, int32_t layer, int32_t* where,
+                         int32_t* owner, int32_t* stamp, int32_t S, int32_t* clock,
+                         int32_t* slot_of, int32_t* copy_expert, int32_t* copy_slot,
+                         int32_t* ncopy, uint64_t* counters, void* stream);
+int rw4_expert_copy(const int32_t* copy_expert, const int32_t* copy_slot, const int32_t* ncopy,
+                    int32_t layer, int32_t E, const uint64_t* host_blobs, int64_t blob_bytes,
+                    uint8_t* slots, int64_t slot_bytes, int32_t S, int32_t ctas_per_expert,
+                    void* stream);
+int rw4_host_ptr_device(const void* host, void** device_ptr);
+
+/* ---------------------------------------------------------------------------------------------
  * Decode attention over the int4 KV cache.  Replaces what the reference runs for one decode step
  * with its QuantizedKVCache (rocketllm/quant/kv_cache.py:277-316: every quantized block expanded
  * to the compute dtype, concatenated with the fp16 window, then the model's attention): softmax

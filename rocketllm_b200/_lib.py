@@ -54,6 +54,17 @@ SIGNATURES = {
                                        _c_void_p, _i64, _i64, _i32, _i32, _c_void_p, _c_void_p]),
     "rw4_moe_combine": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _c_void_p, _i32, _i64,
                                        _i32, _i64, _c_void_p, _c_void_p]),
+    "rw4_slot_maps_create": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i32, _i64, _i64,
+                                            _i32, ctypes.POINTER(_c_void_p)]),
+    "rw4_slot_maps_destroy": (ctypes.c_int, [_c_void_p]),
+    "rw4_moe_grouped_slots": (ctypes.c_int, [_c_void_p, _c_void_p, _i32, _i64, _c_void_p,
+                                             _c_void_p, _c_void_p, _c_void_p]),
+    "rw4_expert_residency": (ctypes.c_int, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p,
+                                            _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p,
+                                            _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "rw4_expert_copy": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p,
+                                       _i64, _c_void_p, _i64, _i32, _i32, _c_void_p]),
+    "rw4_host_ptr_device": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
     "rw4_kv_attention_decode": (ctypes.c_int, [_c_void_p, _i64, _i64, _i32, _i32, _i32, _i32,
                                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64,
                                                _i64, _c_void_p, _c_void_p, _i64, _i64,

@@ -8,6 +8,7 @@
 // routes to two.  Here an expert with no routed rows costs one CTA that reads two offsets and exits:
 // its weights are never read.
 #include <atomic>
+#include <new>
 
 #include "rw4_gemv_tma_body.cuh"
 
@@ -167,6 +168,86 @@ int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_row
   return RW4_OK;
 }
 
+// ---- grouped GEMV over an expert cache (device-side routing) -----------------------------------
+
+// One tensor-map set per SLOT of a device expert cache, encoded once when the slots are allocated;
+// the kernel finds expert e's weights through a device slot index (slot_of[e]) that a residency
+// kernel wrote after the router, so no host step depends on the routing.  80 slots x 3 maps x 128
+// bytes = 30 KB of kernel parameters (the limit is 32,764 bytes).
+constexpr int kMaxSlots = 80;
+
+struct SlotMaps {
+  CUtensorMap codes[kMaxSlots];
+  CUtensorMap scale[kMaxSlots];
+  CUtensorMap zero[kMaxSlots];
+};
+
+template <int NT, int R, int S, bool SWIGLU, bool XF = false>
+__global__ void __launch_bounds__(gemv_tma::kThreads)
+    moe_grouped_slots_kernel(const __grid_constant__ SlotMaps maps, int nslots,
+                             const int32_t* __restrict__ slot_of,
+                             const int32_t* __restrict__ offsets,
+                             const __nv_bfloat16* __restrict__ x, int K, int n_out, int up_offset,
+                             __nv_bfloat16* __restrict__ y, int64_t ldy, int max_rows,
+                             unsigned int* status) {
+  const int z = blockIdx.z;
+  const int beg = offsets[z];
+  const int rows = offsets[z + 1] - beg;
+  const int m0 = blockIdx.y * 16;
+  if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && rows > max_rows)
+    atomicOr(status, RW4_DEVERR_ROWS);
+  if (m0 >= rows) return;  // unrouted expert: neither its slot index nor its weights are read
+  const int slot = slot_of[z];
+  if (slot < 0 || slot >= nslots) {  // a routed expert without a slot: no output, flagged
+    if (threadIdx.x == 0) atomicOr(status, RW4_DEVERR_SLOT);
+    return;
+  }
+  constexpr int kRowsPerCta = SWIGLU ? 16 : 16 * R;
+  gemv_tma::body<NT, R, S, SWIGLU, 1, false, XF, XF>(
+      &maps.codes[slot], &maps.scale[slot], &maps.zero[slot], nullptr, x, beg + m0, 16,
+      min(16, rows - m0), K, y + (int64_t)(beg + m0) * ldy, ldy, blockIdx.x * kRowsPerCta, n_out,
+      up_offset, status);
+}
+
+}  // namespace
+
+struct rw4_slot_maps {
+  SlotMaps maps;
+  int nslots;
+  int K, N, act;
+};
+
+namespace {
+
+template <int NT, int R, int S, bool SWIGLU, bool XF = false>
+int launch_grouped_slots(const rw4_slot_maps* sm, const int32_t* slot_of, const void* x,
+                         const int32_t* offsets, int E, int64_t max_rows, void* y,
+                         cudaStream_t stream) {
+  using L = gemv_tma::Layout<R, S>;
+  const int K = sm->K, N = sm->N;
+  const int n_out = SWIGLU ? N / 2 : N;
+  const int rows_per_cta = SWIGLU ? 16 : L::BR;
+  auto kern = moe_grouped_slots_kernel<NT, R, S, SWIGLU, XF>;
+  const int smem = L::kX + (XF ? K / 512 + 1 : 1) * 1024;
+  static std::atomic<uint64_t> attr_set{0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!((attr_set.load() >> dev) & 1)) {
+    const int most = L::kX + (XF ? 33 : 1) * 1024;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most) !=
+        cudaSuccess)
+      return fail(RW4_ECUDA, "moe_grouped_slots: cannot set dynamic shared memory size");
+    attr_set.fetch_or(1ull << dev);
+  }
+  unsigned int* status = device_status_ptr();
+  if (!status) return fail(RW4_ECUDA, "moe_grouped_slots: device status word unavailable");
+  dim3 grid((n_out + rows_per_cta - 1) / rows_per_cta, (unsigned)((max_rows + 15) / 16), E);
+  kern<<<grid, gemv_tma::kThreads, smem, stream>>>(
+      sm->maps, sm->nslots, slot_of, offsets, static_cast<const __nv_bfloat16*>(x), K, n_out,
+      n_out, static_cast<__nv_bfloat16*>(y), n_out, (int)max_rows, status);
+  return launch_status("rw4_moe_grouped_slots launch");
+}
+
 // ---- combine -----------------------------------------------------------------------------------
 
 // One thread per (token, 8 hidden values).  The k contributions are visited in ascending expert
@@ -324,4 +405,88 @@ extern "C" int rw4_moe_combine(const void* y_perm_bf16, const int32_t* inv,
   else
     return fail(RW4_EINVAL, "rw4_moe_combine: w_dtype %d", w_dtype);
   return launch_status("rw4_moe_combine launch");
+}
+
+extern "C" int rw4_slot_maps_create(const uint8_t* const* slot_packed, const void* const* slot_scale,
+                                    const void* const* slot_zero, int32_t nslots, int64_t K,
+                                    int64_t N, int32_t act, rw4_slot_maps** out) {
+  if (!out) return fail(RW4_EINVAL, "rw4_slot_maps_create: null output");
+  *out = nullptr;
+  if (nslots < 1 || nslots > kMaxSlots)
+    return fail(RW4_EINVAL, "rw4_slot_maps_create: %d slots (1..%d)", nslots, kMaxSlots);
+  if (K <= 0 || K % 512 || N <= 0 || N > (1 << 30) || K > (1 << 30))
+    return fail(RW4_EINVAL, "rw4_slot_maps_create: K=%lld N=%lld (K %% 512 == 0)", (long long)K,
+                (long long)N);
+  if (act != 0 && act != 1) return fail(RW4_EINVAL, "rw4_slot_maps_create: act %d", act);
+  if (act == 1 && (N % 2 || (N / 2) % 8))
+    return fail(RW4_EINVAL, "rw4_slot_maps_create: SwiGLU needs N = 2*I with I %% 8 == 0");
+  if (!slot_packed || !slot_scale || !slot_zero)
+    return fail(RW4_EINVAL, "rw4_slot_maps_create: null pointer array");
+  auto* sm = new (std::nothrow) rw4_slot_maps();
+  if (!sm) return fail(RW4_ENOMEM, "rw4_slot_maps_create: out of host memory");
+  using L = gemv_tma::Layout<2, 6>;  // the only ring every grouped instantiation uses
+  const int box_rows = act == 1 ? 16 : L::BR;
+  const int G = (int)(K / 64);
+  for (int s = 0; s < nslots; ++s) {
+    if (!slot_packed[s] || !slot_scale[s] || !slot_zero[s]) {
+      delete sm;
+      return fail(RW4_EINVAL, "rw4_slot_maps_create: null pointer for slot %d", s);
+    }
+    int st = make_tensor_map_2d(&sm->maps.codes[s], slot_packed[s], CU_TENSOR_MAP_DATA_TYPE_UINT8,
+                                1, N, K / 2, K / 2, box_rows, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (st == RW4_OK)
+      st = make_tensor_map_2d(&sm->maps.scale[s], slot_scale[s], CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                              2, N, G, (uint64_t)G * 2, box_rows, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st == RW4_OK)
+      st = make_tensor_map_2d(&sm->maps.zero[s], slot_zero[s], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                              N, G, (uint64_t)G * 2, box_rows, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != RW4_OK) {
+      delete sm;
+      return st;
+    }
+  }
+  sm->nslots = nslots;
+  sm->K = (int)K;
+  sm->N = (int)N;
+  sm->act = act;
+  *out = sm;
+  return RW4_OK;
+}
+
+extern "C" int rw4_slot_maps_destroy(rw4_slot_maps* maps) {
+  delete maps;
+  return RW4_OK;
+}
+
+extern "C" int rw4_moe_grouped_slots(const void* x_perm_bf16, const int32_t* offsets, int32_t E,
+                                     int64_t max_rows, const rw4_slot_maps* maps,
+                                     const int32_t* slot_of, void* y_perm_bf16, void* stream) {
+  if (!maps) return fail(RW4_EINVAL, "rw4_moe_grouped_slots: null slot maps");
+  if (E < 1 || E > 65535 || max_rows < 0 || max_rows > (1 << 30))
+    return fail(RW4_EINVAL, "rw4_moe_grouped_slots: bad E=%d max_rows=%lld", E,
+                (long long)max_rows);
+  if (max_rows == 0) return RW4_OK;
+  if (!x_perm_bf16 || !offsets || !slot_of || !y_perm_bf16)
+    return fail(RW4_EINVAL, "rw4_moe_grouped_slots: null pointer");
+  if (!aligned(x_perm_bf16, 16) || !aligned(y_perm_bf16, 16))
+    return fail(RW4_EINVAL, "rw4_moe_grouped_slots: activations must be 16-byte aligned");
+  cudaStream_t s = rw4::as_stream(stream);
+  const bool wide = max_rows > 8;
+  const bool one = max_rows == 1 && maps->K / 512 <= 32;
+  const int a = maps->act;
+  if (one)
+    return a == 1 ? launch_grouped_slots<1, 2, 6, true, true>(maps, slot_of, x_perm_bf16, offsets,
+                                                              E, max_rows, y_perm_bf16, s)
+                  : launch_grouped_slots<1, 2, 6, false, true>(maps, slot_of, x_perm_bf16,
+                                                               offsets, E, max_rows, y_perm_bf16,
+                                                               s);
+  if (a == 1)
+    return wide ? launch_grouped_slots<2, 2, 6, true>(maps, slot_of, x_perm_bf16, offsets, E,
+                                                      max_rows, y_perm_bf16, s)
+                : launch_grouped_slots<1, 2, 6, true>(maps, slot_of, x_perm_bf16, offsets, E,
+                                                      max_rows, y_perm_bf16, s);
+  return wide ? launch_grouped_slots<2, 2, 6, false>(maps, slot_of, x_perm_bf16, offsets, E,
+                                                     max_rows, y_perm_bf16, s)
+              : launch_grouped_slots<1, 2, 6, false>(maps, slot_of, x_perm_bf16, offsets, E,
+                                                     max_rows, y_perm_bf16, s);
 }

@@ -14,6 +14,7 @@
 #define RW4_DEVERR_TIMEOUT 1u
 #define RW4_DEVERR_TMEM 2u
 #define RW4_DEVERR_ROWS 4u  // a grouped launch saw an expert with more rows than max_rows
+#define RW4_DEVERR_SLOT 8u  // a routed expert had no expert-cache slot (device-side residency)
 
 namespace rw4 {
 

@@ -23,7 +23,8 @@ import os
 import torch
 
 from . import quant  # noqa: F401 - registers the rw4 quantizer with transformers
-from .expert_stream import ExpertStreamer, expert_blob_bytes, is_rw4_experts
+from .expert_stream import (DeviceExpertStreamer, ExpertStreamer, expert_blob_bytes,
+                            is_rw4_experts)
 from .streaming import WeightTransfer
 
 ALIGN = 256
@@ -90,7 +91,8 @@ class LayerStreamer:
     layers."""
 
     def __init__(self, layers, device, window=2, copy_streams=2, chunk_bytes=16 << 20,
-                 prefetching=True, expert_slots=None, blobs=None, pinned=0):
+                 prefetching=True, expert_slots=None, blobs=None, pinned=0,
+                 expert_routing="host"):
         if window < 1:
             raise ValueError("window must be >= 1")
         self.layers = list(layers)
@@ -123,7 +125,9 @@ class LayerStreamer:
         if stream_experts:
             moe = [(i, m) for i, layer in enumerate(self.layers) for m in layer.modules()
                    if is_rw4_experts(m)]
-            if moe:
+            if moe and expert_routing == "device":
+                self.experts = DeviceExpertStreamer(moe, self.device, expert_slots)
+            elif moe:
                 self.experts = ExpertStreamer(moe, self.device, expert_slots, self.xfer)
         self.tickets = [None] * len(self.layers)
         self.resident_slot = [None] * self.window   # which layer's bytes a slot holds (issued)
@@ -177,6 +181,8 @@ class LayerStreamer:
         for h in self._handles:
             h.remove()
         self._handles = []
+        if hasattr(self.experts, "close"):
+            self.experts.close()
         self.xfer.close()
 
 
@@ -221,7 +227,10 @@ class RocketModel:
     beside those slots stay resident (pinned) and the others stream from pinned host memory every
     token.  In a mixture-of-experts model the routed experts stream one by one
     (``expert_streaming``): the layer slots hold the attention / router / norms only, and the rest
-    of the budget becomes an expert cache of at least one layer's experts.
+    of the budget becomes an expert cache of at least one layer's experts.  ``expert_routing``:
+    ``"host"`` reads the routed set back per MoE layer and issues the sends from the host (the
+    reference's scheme); ``"device"`` decides residency and copies on the device
+    (:class:`~rocketllm_b200.expert_stream.DeviceExpertStreamer`, at most 80 expert slots).
 
     ``kv_cache`` (``rocketllm/base.py:208-411``, ``quant/kv_cache.py:449-503``): ``"int4"`` gives
     every ``generate`` an :class:`~rocketllm_b200.kv_cache.RW4KVCache` whose decode attention reads
@@ -239,12 +248,14 @@ class RocketModel:
     def __init__(self, model_or_path, device="cuda", dtype=torch.bfloat16, vram_budget=None,
                  window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
                  expert_streaming=True, kv_cache="auto", draft_model=None, speculative="auto",
-                 lookahead=4, max_lookahead=8, **unused):
+                 lookahead=4, max_lookahead=8, expert_routing="host", **unused):
         from .kv_cache import KV_CHOICES
         from .shards import INDEX
         from .speculative import SPEC_CHOICES
         if kv_cache not in KV_CHOICES:
             raise ValueError(f"kv_cache must be one of {', '.join(KV_CHOICES)}, not {kv_cache!r}")
+        if expert_routing not in ("host", "device"):
+            raise ValueError(f"expert_routing must be 'host' or 'device', not {expert_routing!r}")
         if speculative not in SPEC_CHOICES:
             raise ValueError(f"speculative must be one of {', '.join(SPEC_CHOICES)}, not "
                              f"{speculative!r}")
@@ -303,7 +314,7 @@ class RocketModel:
         self.streamer = LayerStreamer(layers, self.device, window=window,
                                       copy_streams=copy_streams, chunk_bytes=chunk_bytes,
                                       prefetching=prefetching, expert_slots=expert_slots,
-                                      pinned=pinned)
+                                      pinned=pinned, expert_routing=expert_routing)
 
     @staticmethod
     def _plan_bytes(layer_bytes, window, pinned):

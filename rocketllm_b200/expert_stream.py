@@ -11,6 +11,9 @@ and the grouped RW4 GEMV waits (device-side) for exactly those sends.  Experts n
 never cross PCIe.  Slots are recycled least-recently-used, never one holding an expert of the
 running layer; a send into a slot is ordered after all compute already queued, so the previous
 occupant's last reader has finished before its bytes are overwritten.
+
+:class:`DeviceExpertStreamer` does the same with the routing decision on the device: nothing on the
+host reads the routed set (see its docstring).
 """
 import collections
 import types
@@ -200,5 +203,113 @@ def streamed_experts_forward(self, hidden_states, top_k_index, top_k_weights):
     gate_up, down = streamer.triples(layer, selected)
     act = kernels.moe_grouped(xp, offsets, gate_up, act=1, max_rows=rows)
     yp = kernels.moe_grouped(act, offsets, down, act=0, max_rows=rows)
+    out = kernels.moe_combine(yp, inv, idx, w)
+    return out if hidden_states.dtype == torch.bfloat16 else out.to(hidden_states.dtype)
+
+
+class DeviceExpertStreamer:
+    """Routed experts of ``moe`` streamed with device-side routing (no host sync per MoE layer).
+
+    The experts' blobs stay in pinned host memory (mapped into the device address space); the
+    device keeps ``num_slots`` expert slots (<= 80: one TMA tensor-map set per slot travels as
+    kernel parameters) and the residency tables.  In a forward, everything runs on the compute
+    stream without the host waiting: permute -> residency kernel (claims resident slots, assigns
+    free / least-recently-used ones to the others, lists them) -> copy kernel (reads the listed
+    blobs over PCIe into their slots) -> gather -> grouped GEMVs that reach each expert's weights
+    through its slot index -> combine.  Policy: the same least-recently-used cache as
+    :class:`ExpertStreamer` (a free slot first, never a slot the running layer's routed experts
+    hold); ties between slots last used in the same call go to the lower slot index.
+    """
+
+    MAX_SLOTS = 80
+
+    def __init__(self, moe, device, num_slots, ctas_per_expert=64):
+        self.device = torch.device(device)
+        counts = {m.gate_up_proj_packed.shape[0] for _, m in moe}
+        shapes = {(tuple(m.gate_up_proj_packed.shape[1:]), tuple(m.down_proj_packed.shape[1:]))
+                  for _, m in moe}
+        if len(counts) != 1 or len(shapes) != 1:
+            raise ValueError("device-side routing needs every MoE layer to have the same experts")
+        self.num_experts = counts.pop()
+        self.index = {layer: i for i, (layer, _) in enumerate(moe)}
+        e_count = self.num_experts
+        slots = min(int(num_slots), self.MAX_SLOTS, len(moe) * e_count)
+        if slots < e_count:
+            raise ValueError(f"{slots} expert slots cannot hold one layer's {e_count} experts")
+        self.blobs = []
+        host = []
+        for layer, module in moe:
+            for e in range(e_count):
+                blob = _ExpertBlob(expert_tensors(module, e))
+                if blob.host.data_ptr() % 16:
+                    raise RuntimeError("pinned expert blob is not 16-byte aligned")
+                host.append(kernels.host_ptr_device(blob.host.data_ptr()))
+                self.blobs.append(blob)
+        self.blob_bytes = self.blobs[0].nbytes
+        self.host_ptrs = torch.tensor(host, dtype=torch.int64, device=self.device)
+        self.slots = torch.empty(slots * self.blob_bytes, dtype=torch.uint8, device=self.device)
+        entries = self.blobs[0].entries          # every blob has the same layout
+        base = self.slots.data_ptr()
+        ptr = [[base + s * self.blob_bytes + off for s in range(slots)]
+               for (_, _, off) in entries]
+        gu_shape, dn_shape = shapes.pop()
+        n_gu, k_gu = gu_shape[0], gu_shape[1] * 2
+        n_dn, k_dn = dn_shape[0], dn_shape[1] * 2
+        self.gate_up_maps = kernels.SlotMaps(ptr[0], ptr[1], ptr[2], k_gu, n_gu, act=1)
+        self.down_maps = kernels.SlotMaps(ptr[3], ptr[4], ptr[5], k_dn, n_dn, act=0)
+        i32 = dict(dtype=torch.int32, device=self.device)
+        self.where = torch.full((len(moe) * e_count,), -1, **i32)
+        self.owner = torch.full((slots,), -1, **i32)
+        self.stamp = torch.zeros(slots, **i32)
+        self.clock = torch.zeros(1, **i32)
+        self.counters = torch.zeros(2, dtype=torch.int64, device=self.device)
+        self.slot_of = torch.empty(e_count, **i32)
+        self.copy_expert = torch.empty(e_count, **i32)
+        self.copy_slot = torch.empty(e_count, **i32)
+        self.ncopy = torch.zeros(1, **i32)
+        self.ctas_per_expert = ctas_per_expert
+        for layer, module in moe:
+            for name in _NAMES:
+                for sfx in _SUFFIXES:
+                    p = getattr(module, name + sfx)
+                    module._parameters[name + sfx] = torch.nn.Parameter(
+                        torch.empty((0,) + tuple(p.shape[1:]), dtype=p.dtype, device=self.device),
+                        requires_grad=False)
+            module._rw4_device_stream = (self, self.index[layer])
+            module.forward = types.MethodType(device_streamed_experts_forward, module)
+
+    def stats(self):
+        """Counters (reading them synchronises the device)."""
+        hits, fetches = self.counters.tolist()
+        return {"expert_slots": self.owner.numel(), "slot_bytes": self.blob_bytes,
+                "fetches": fetches, "hits": hits, "bytes": fetches * self.blob_bytes,
+                "resident": int((self.owner >= 0).sum()), "routing": "device"}
+
+    def close(self):
+        self.gate_up_maps.close()
+        self.down_maps.close()
+
+
+def device_streamed_experts_forward(self, hidden_states, top_k_index, top_k_weights):
+    """``rw4_experts_forward`` with device-side routing into the expert cache (same result)."""
+    st, li = self._rw4_device_stream
+    t, h = hidden_states.shape
+    k = top_k_index.shape[1]
+    x = hidden_states if hidden_states.dtype == torch.bfloat16 else hidden_states.to(torch.bfloat16)
+    if not x.is_contiguous():
+        x = x.contiguous()
+    idx = top_k_index.to(torch.int64).contiguous()
+    w = top_k_weights.contiguous()
+    if w.dtype not in (torch.float32, torch.bfloat16):
+        w = w.float()
+    perm, inv, offsets = kernels.moe_permute(idx, st.num_experts)
+    kernels.expert_residency(offsets, li, st.where, st.owner, st.stamp, st.clock, st.slot_of,
+                             st.copy_expert, st.copy_slot, st.ncopy, st.counters)
+    kernels.expert_copy(st.copy_expert, st.copy_slot, st.ncopy, li, st.num_experts, st.host_ptrs,
+                        st.blob_bytes, st.slots, st.blob_bytes, st.ctas_per_expert)
+    rows = 1 if t == 1 else t * k
+    xp = kernels.moe_gather(x, perm, k)
+    act = kernels.moe_grouped_slots(xp, offsets, st.gate_up_maps, st.slot_of, max_rows=rows)
+    yp = kernels.moe_grouped_slots(act, offsets, st.down_maps, st.slot_of, max_rows=rows)
     out = kernels.moe_combine(yp, inv, idx, w)
     return out if hidden_states.dtype == torch.bfloat16 else out.to(hidden_states.dtype)

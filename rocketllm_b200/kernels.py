@@ -209,3 +209,69 @@ def kv_attention_decode(query, k_codes, k_sz, v_codes, v_sz, groups, k_res, v_re
               gcap, int(groups), k_res.data_ptr(), v_res.data_ptr(), rcap, int(res_len),
               float(scaling), out.data_ptr(), out.stride(0), out.stride(2), _stream())
     return out
+
+
+# ---- device-side routing into the expert cache ---------------------------------------------------
+
+class SlotMaps:
+    """Tensor maps of every slot of a device expert cache for one projection (``[N, K]`` RW4
+    weights at per-slot device addresses), encoded once (``rw4_slot_maps_create``)."""
+
+    def __init__(self, packed_ptrs, scale_ptrs, zero_ptrs, k, n, act):
+        s = len(packed_ptrs)
+        arrs = [(ctypes.c_void_p * s)(*p) for p in (packed_ptrs, scale_ptrs, zero_ptrs)]
+        handle = ctypes.c_void_p()
+        _lib.call("rw4_slot_maps_create", arrs[0], arrs[1], arrs[2], s, int(k), int(n), int(act),
+                  ctypes.byref(handle))
+        self.handle, self.slots, self.k, self.n, self.act = handle, s, int(k), int(n), int(act)
+
+    def close(self):
+        if self.handle:
+            _lib.call("rw4_slot_maps_destroy", self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
+
+
+def moe_grouped_slots(x_perm, offsets, maps, slot_of, max_rows=None, out=None):
+    """Grouped RW4 GEMV where routed expert ``e`` reads the weight in slot ``slot_of[e]``."""
+    _require_cuda(x_perm, offsets, slot_of)
+    rows = x_perm.shape[0]
+    n_out = maps.n // 2 if maps.act == 1 else maps.n
+    if out is None:
+        out = torch.empty((rows, n_out), dtype=torch.bfloat16, device=x_perm.device)
+    _lib.call("rw4_moe_grouped_slots", x_perm.data_ptr(), offsets.data_ptr(),
+              offsets.numel() - 1, rows if max_rows is None else int(max_rows), maps.handle,
+              slot_of.data_ptr(), out.data_ptr(), _stream())
+    return out
+
+
+def expert_residency(offsets, layer, where, owner, stamp, clock, slot_of, copy_expert, copy_slot,
+                     ncopy, counters):
+    """Device-side residency step of one MoE layer (``rw4_expert_residency``)."""
+    _require_cuda(offsets, where, owner, stamp, clock, slot_of, copy_expert, copy_slot, ncopy,
+                  counters)
+    _lib.call("rw4_expert_residency", offsets.data_ptr(), offsets.numel() - 1, int(layer),
+              where.data_ptr(), owner.data_ptr(), stamp.data_ptr(), owner.numel(),
+              clock.data_ptr(), slot_of.data_ptr(), copy_expert.data_ptr(), copy_slot.data_ptr(),
+              ncopy.data_ptr(), counters.data_ptr(), _stream())
+
+
+def expert_copy(copy_expert, copy_slot, ncopy, layer, num_experts, host_blobs, blob_bytes, slots,
+                slot_bytes, ctas_per_expert=64):
+    """Copy the listed experts' mapped host blobs into their slots (``rw4_expert_copy``)."""
+    _lib.call("rw4_expert_copy", copy_expert.data_ptr(), copy_slot.data_ptr(), ncopy.data_ptr(),
+              int(layer), int(num_experts), host_blobs.data_ptr(), int(blob_bytes),
+              slots.data_ptr(), int(slot_bytes), slots.numel() // int(slot_bytes),
+              int(ctas_per_expert), _stream())
+
+
+def host_ptr_device(ptr):
+    """The device-visible address of pinned host memory at ``ptr`` (raises if it is not mapped)."""
+    out = ctypes.c_void_p()
+    _lib.call("rw4_host_ptr_device", ctypes.c_void_p(ptr), ctypes.byref(out))
+    return out.value
