@@ -718,7 +718,9 @@ extern "C" int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_
   args.status = status;
   const int64_t items = groups + (res_len + kTok - 1) / kTok;
   int cs = kv_cluster_size(hs_count, items, G <= 8 ? KvWarps<1>::value : KvWarps<2>::value);
-  if (const char* forced = getenv("RW4_KV_CLUSTER")) {   // launch-shape switch for measurements
+  // launch-shape switch for measurements, read once per process
+  static const char* const forced = getenv("RW4_KV_CLUSTER");
+  if (forced) {
     const int f = atoi(forced);
     if (f != 1 && f != 2 && f != 4 && f != 8 && f != 16)
       return fail(RW4_EINVAL, "RW4_KV_CLUSTER=%s (1, 2, 4, 8 or 16)", forced);

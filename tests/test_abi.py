@@ -53,3 +53,50 @@ def test_invalid_arguments_are_rejected_before_launch():
 def test_errors_raise_with_message():
     with pytest.raises(_lib.RW4Error, match="RW4_EINVAL"):
         _lib.call("rw4_linear", 256, 1, 4096, 256, 256, 256, 4096, 32, 256, None)
+
+
+def test_kv_and_expert_routing_entry_points_reject_bad_arguments():
+    """The int4-KV attention and device-side expert routing entry points validate shapes, counts
+    and pointers on the host, before any device call."""
+    lib = _lib.lib()
+    p = ctypes.c_void_p(256)
+    kv = lib.rw4_kv_attention_decode
+    # 6 query heads over 4 kv heads
+    assert kv(p, 0, 0, 1, 6, 4, 128, p, p, p, p, 1, 1, p, p, 64, 1, 1.0, p, 0, 0, None) \
+        == _lib.RW4_EINVAL
+    # head_dim 96 and 32 query heads per kv head are not built
+    assert kv(p, 0, 0, 1, 8, 2, 96, p, p, p, p, 1, 1, p, p, 64, 1, 1.0, p, 0, 0, None) \
+        == _lib.RW4_EUNSUPPORTED
+    assert kv(p, 0, 0, 1, 64, 2, 128, p, p, p, p, 1, 1, p, p, 64, 1, 1.0, p, 0, 0, None) \
+        == _lib.RW4_EUNSUPPORTED
+    # more groups than the capacity, more window tokens than the window, nothing at all
+    assert kv(p, 0, 0, 1, 8, 2, 128, p, p, p, p, 1, 2, p, p, 64, 1, 1.0, p, 0, 0, None) \
+        == _lib.RW4_EINVAL
+    assert kv(p, 0, 0, 1, 8, 2, 128, p, p, p, p, 1, 1, p, p, 64, 65, 1.0, p, 0, 0, None) \
+        == _lib.RW4_EINVAL
+    assert kv(p, 0, 0, 1, 8, 2, 128, p, p, p, p, 1, 0, p, p, 64, 0, 1.0, p, 0, 0, None) \
+        == _lib.RW4_EINVAL
+    # misaligned packed storage
+    odd = ctypes.c_void_p(264)
+    assert kv(p, 0, 0, 1, 8, 2, 128, odd, p, p, p, 1, 1, p, p, 64, 1, 1.0, p, 0, 0, None) \
+        == _lib.RW4_EINVAL
+
+    out = ctypes.c_void_p()
+    arr = (ctypes.c_void_p * 1)(256)
+    assert lib.rw4_slot_maps_create(arr, arr, arr, 0, 4096, 2048, 1, ctypes.byref(out)) \
+        == _lib.RW4_EINVAL                                    # no slots
+    assert lib.rw4_slot_maps_create(arr, arr, arr, 81, 4096, 2048, 1, ctypes.byref(out)) \
+        == _lib.RW4_EINVAL                                    # more than fit the parameters
+    assert lib.rw4_slot_maps_create(arr, arr, arr, 1, 4000, 2048, 1, ctypes.byref(out)) \
+        == _lib.RW4_EINVAL                                    # K % 512
+    assert out.value is None
+    assert lib.rw4_moe_grouped_slots(p, p, 8, 1, None, p, p, None) == _lib.RW4_EINVAL
+    assert lib.rw4_expert_residency(p, 0, 0, p, p, p, 8, p, p, p, p, p, p, None) \
+        == _lib.RW4_EINVAL
+    # a blob larger than a slot, a blob that is not whole 16-byte vectors
+    assert lib.rw4_expert_copy(p, p, p, 0, 8, p, 1 << 21, p, 1 << 20, 4, 8, None) \
+        == _lib.RW4_EINVAL
+    assert lib.rw4_expert_copy(p, p, p, 0, 8, p, 1000, p, 1 << 20, 4, 8, None) \
+        == _lib.RW4_EINVAL
+    dev = ctypes.c_void_p()
+    assert lib.rw4_host_ptr_device(None, ctypes.byref(dev)) == _lib.RW4_EINVAL
