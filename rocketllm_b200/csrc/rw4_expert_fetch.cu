@@ -79,7 +79,8 @@ __global__ void expert_residency_kernel(const int32_t* __restrict__ offsets, int
 }
 
 // grid (chunks, E): block (c, i) copies chunk c of the i-th listed expert (if there is one);
-// 16-byte loads from the mapped host blob, 16-byte stores into the slot.
+// 16-byte loads from the mapped host blob (four independent loads in flight per thread: PCIe
+// latency is microseconds), 16-byte stores into the slot.
 __global__ void __launch_bounds__(256)
     expert_copy_kernel(const int32_t* __restrict__ copy_expert,
                        const int32_t* __restrict__ copy_slot, const int32_t* __restrict__ ncopy,
@@ -97,7 +98,17 @@ __global__ void __launch_bounds__(256)
   const int64_t per = (vecs + gridDim.x - 1) / gridDim.x;
   const int64_t beg = (int64_t)blockIdx.x * per;
   const int64_t end = beg + per < vecs ? beg + per : vecs;
-  for (int64_t v = beg + threadIdx.x; v < end; v += blockDim.x) dst[v] = src[v];
+  constexpr int kUnroll = 4;
+  const int64_t step = blockDim.x;
+  int64_t v = beg + threadIdx.x;
+  for (; v + (kUnroll - 1) * step < end; v += kUnroll * step) {
+    uint4 r[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) r[u] = ldg_stream_u4(src + v + u * step);
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) dst[v + u * step] = r[u];
+  }
+  for (; v < end; v += step) dst[v] = ldg_stream_u4(src + v);
 }
 
 }  // namespace

@@ -656,10 +656,11 @@ int launch_kv(const KvArgs& args, int hs_count, int csize, cudaStream_t stream) 
 namespace rw4 {
 
 // CTAs per head slot: enough to give every SM one CTA when the batch is small, at most a portable
-// cluster of 8, and no more than the items keep busy (at least two per warp where possible).
+// cluster of 8, and no more than the items keep busy (at least one per warp).
 int kv_cluster_size(int64_t head_slots, int64_t items, int warps) {
   int s = 1;
-  while (s < 8 && head_slots * (2 * s) <= sm_count() && static_cast<int64_t>(2 * s) * warps * 2 <= items)
+  while (s < 8 && head_slots * (2 * s) <= sm_count() &&
+         static_cast<int64_t>(2 * s) * warps <= items)
     s *= 2;
   return s;
 }
