@@ -204,6 +204,19 @@ int rw4_host_ptr_device(const void* host, void** device_ptr);
  * (q_stride_b, q_stride_h, 1); out bf16 likewise.  Query head h reads kv head h / (heads /
  * kv_heads).  head_dim 64 or 128, heads / kv_heads <= 16, groups + res_len >= 1.
  * ------------------------------------------------------------------------------------------- */
+/* rw4_kv_attention: the same over q_len >= 1 query positions that are the window's LAST q_len
+ * tokens (a speculative verify pass or a short chunk of one unpadded sequence per batch row):
+ * position i attends to every quantized token and to the window's first res_len - q_len + 1 + i
+ * tokens (causal).  q [batch][heads][q_len][head_dim] with element strides (q_stride_b,
+ * q_stride_h, q_stride_q, 1), out likewise (out_stride_q for the position); q_len * heads /
+ * kv_heads <= 16, q_len <= res_len. */
+int rw4_kv_attention(const void* q, int64_t q_stride_b, int64_t q_stride_h, int64_t q_stride_q,
+                     int32_t batch, int32_t heads, int32_t kv_heads, int32_t head_dim,
+                     int32_t q_len, const uint8_t* k_codes, const void* k_sz,
+                     const uint8_t* v_codes, const void* v_sz, int64_t groups_cap, int64_t groups,
+                     const void* k_res, const void* v_res, int64_t res_cap, int64_t res_len,
+                     float scaling, void* out, int64_t out_stride_b, int64_t out_stride_h,
+                     int64_t out_stride_q, void* stream);
 int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h, int32_t batch,
                             int32_t heads, int32_t kv_heads, int32_t head_dim,
                             const uint8_t* k_codes, const void* k_sz, const uint8_t* v_codes,

@@ -346,3 +346,16 @@ def attention_decode(q, k, v, scaling):
     p = np.exp(logits)
     p /= p.sum(axis=-1, keepdims=True)
     return np.einsum("bht,bhtd->bhd", p, vv).astype(np.float32)
+
+
+def attention_causal(q, k, v, scaling):
+    """``Q`` query positions ``[b, h, Q, d]`` that are the last ``Q`` of the ``T`` keys / values
+    ``[b, kvh, T, d]``: position ``i`` attends to keys ``0 .. T - Q + i`` (transformers' causal
+    SDPA over a cache).  fp64 arithmetic, fp32 result ``[b, h, Q, d]``."""
+    b, h, nq, d = q.shape
+    t = k.shape[2]
+    out = np.empty((b, h, nq, d), dtype=np.float32)
+    for i in range(nq):
+        n = t - nq + i + 1
+        out[:, :, i] = attention_decode(q[:, :, i], k[:, :, :n], v[:, :, :n], scaling)
+    return out

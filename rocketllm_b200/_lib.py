@@ -65,6 +65,10 @@ SIGNATURES = {
     "rw4_expert_copy": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p,
                                        _i64, _c_void_p, _i64, _i32, _i32, _c_void_p]),
     "rw4_host_ptr_device": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),
+    "rw4_kv_attention": (ctypes.c_int, [_c_void_p, _i64, _i64, _i64, _i32, _i32, _i32, _i32, _i32,
+                                        _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64, _i64,
+                                        _c_void_p, _c_void_p, _i64, _i64, ctypes.c_float,
+                                        _c_void_p, _i64, _i64, _i64, _c_void_p]),
     "rw4_kv_attention_decode": (ctypes.c_int, [_c_void_p, _i64, _i64, _i32, _i32, _i32, _i32,
                                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64,
                                                _i64, _c_void_p, _c_void_p, _i64, _i64,

@@ -72,7 +72,7 @@ struct KvLayout {
 
 struct KvArgs {
   const __nv_bfloat16* q;
-  int64_t q_sb, q_sh;
+  int64_t q_sb, q_sh, q_sq;
   const uint8_t* kc;
   const uint8_t* ksz;
   const uint8_t* vc;
@@ -82,9 +82,10 @@ struct KvArgs {
   const __nv_bfloat16* vr;
   int64_t rcap, rlen;
   int KVH, G;
+  int Q;         // query positions: the last Q window tokens, each attending causally
   float qscale;  // softmax scaling * log2(e)
   __nv_bfloat16* out;
-  int64_t o_sb, o_sh;
+  int64_t o_sb, o_sh, o_sq;
   unsigned int* status;
 };
 
@@ -214,11 +215,13 @@ __global__ void __launch_bounds__(kWarps * 32, 1) rw4_kv_attn_kernel(const KvArg
   const int hs = blockIdx.y;
   const int b = hs / a.KVH, kvh = hs % a.KVH;
 
+  // column h of the MMAs = (query position h / G, query head kvh * G + h % G)
   for (int i = threadIdx.x; i < QH * D; i += kThreads) {
     const int h = i / D, c = i % D;
     float v = 0.f;
-    if (h < a.G)
-      v = __bfloat162float(a.q[b * a.q_sb + static_cast<int64_t>(kvh * a.G + h) * a.q_sh + c]) *
+    if (h < a.Q * a.G)
+      v = __bfloat162float(a.q[b * a.q_sb + static_cast<int64_t>(kvh * a.G + h % a.G) * a.q_sh +
+                               static_cast<int64_t>(h / a.G) * a.q_sq + c]) *
           a.qscale;
     qs[i] = v;
   }
@@ -464,15 +467,20 @@ __global__ void __launch_bounds__(kWarps * 32, 1) rw4_kv_attn_kernel(const KvArg
             mma_bf16_16816(s[nt][mt], af, bq[nt][0], bq[nt][1], s[nt][mt]);
         }
       }
+      // window token t is visible to query position qi iff t <= rlen - Q + qi (the query tokens
+      // are the window's last Q); padding columns see the whole window
 #pragma unroll
       for (int mt = 0; mt < 4; ++mt) {
         const int64_t te = t0 + 8 * n + 2 * mt;
-        const bool ve = te < a.rlen, vo = te + 1 < a.rlen;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          if (!ve) s[nt][mt][0] = s[nt][mt][1] = -INFINITY;
-          if (!vo) s[nt][mt][2] = s[nt][mt][3] = -INFINITY;
-        }
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int col = nt * 8 + 2 * qd + (i & 1);
+            const int64_t limit =
+                col < a.Q * a.G ? a.rlen - a.Q + 1 + col / a.G : a.rlen;
+            if (te + (i >> 1) >= limit) s[nt][mt][i] = -INFINITY;
+          }
       }
       softmax_step<NT, VM, VG>(s, m_run, l_run, zp, o, offv);
 #pragma unroll
@@ -586,7 +594,7 @@ __global__ void __launch_bounds__(kWarps * 32, 1) rw4_kv_attn_kernel(const KvArg
   }
   cluster.sync();
   if (crank == 0) {
-    for (int i = threadIdx.x; i < a.G * D; i += kThreads) {
+    for (int i = threadIdx.x; i < a.Q * a.G * D; i += kThreads) {
       const int h = i / D, c = i % D;
       float mx = kNegBig;
       for (int r = 0; r < csize; ++r) {
@@ -600,8 +608,8 @@ __global__ void __launch_bounds__(kWarps * 32, 1) rw4_kv_attn_kernel(const KvArg
         acc = fmaf(rp[h * D + c], f, acc);
         l = fmaf(rp[QH * D + QH + h], f, l);
       }
-      a.out[b * a.o_sb + static_cast<int64_t>(kvh * a.G + h) * a.o_sh + c] =
-          __float2bfloat16(acc / l);
+      a.out[b * a.o_sb + static_cast<int64_t>(h / a.G) * a.o_sq +
+            static_cast<int64_t>(kvh * a.G + h % a.G) * a.o_sh + c] = __float2bfloat16(acc / l);
     }
   }
   cluster.sync();  // rank 0 has read every CTA's partials
@@ -667,26 +675,33 @@ int kv_cluster_size(int64_t head_slots, int64_t items, int warps) {
 
 }  // namespace rw4
 
-extern "C" int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
-                                       int32_t batch, int32_t heads, int32_t kv_heads,
-                                       int32_t head_dim, const uint8_t* k_codes, const void* k_sz,
-                                       const uint8_t* v_codes, const void* v_sz,
-                                       int64_t groups_cap, int64_t groups, const void* k_res,
-                                       const void* v_res, int64_t res_cap, int64_t res_len,
-                                       float scaling, void* out, int64_t out_stride_b,
-                                       int64_t out_stride_h, void* stream) {
+extern "C" int rw4_kv_attention(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                int64_t q_stride_q, int32_t batch, int32_t heads,
+                                int32_t kv_heads, int32_t head_dim, int32_t q_len,
+                                const uint8_t* k_codes, const void* k_sz, const uint8_t* v_codes,
+                                const void* v_sz, int64_t groups_cap, int64_t groups,
+                                const void* k_res, const void* v_res, int64_t res_cap,
+                                int64_t res_len, float scaling, void* out, int64_t out_stride_b,
+                                int64_t out_stride_h, int64_t out_stride_q, void* stream) {
   using namespace rw4;
   if (!q || !out || batch <= 0 || heads <= 0 || kv_heads <= 0 || heads % kv_heads)
     return fail(RW4_EINVAL, "kv_attention: bad query / head arguments (%d heads, %d kv heads)",
                 heads, kv_heads);
   const int G = heads / kv_heads;
   if (G > 16) return fail(RW4_EUNSUPPORTED, "kv_attention: %d query heads per kv head (max 16)", G);
+  if (q_len < 1 || q_len * G > 16)
+    return fail(RW4_EUNSUPPORTED,
+                "kv_attention: %d query positions x %d heads per kv head (at most 16 columns)",
+                q_len, G);
   if (head_dim != 64 && head_dim != 128)
     return fail(RW4_EUNSUPPORTED, "kv_attention: head_dim %d (64 or 128 supported)", head_dim);
   if (groups < 0 || groups > groups_cap || res_len < 0 || res_len > res_cap)
     return fail(RW4_EINVAL, "kv_attention: %lld groups of %lld, %lld window tokens of %lld",
                 (long long)groups, (long long)groups_cap, (long long)res_len, (long long)res_cap);
   if (groups + res_len == 0) return fail(RW4_EINVAL, "kv_attention: empty cache");
+  if (res_len < q_len)
+    return fail(RW4_EINVAL, "kv_attention: the %d query tokens must be the window's last (%lld)",
+                q_len, (long long)res_len);
   if (groups_cap > 0 && (!k_codes || !k_sz || !v_codes || !v_sz || !aligned(k_codes, 16) ||
                          !aligned(k_sz, 16) || !aligned(v_codes, 16) || !aligned(v_sz, 16)))
     return fail(RW4_EINVAL, "kv_attention: packed arrays must be non-null and 16-byte aligned");
@@ -700,6 +715,7 @@ extern "C" int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_
   args.q = static_cast<const __nv_bfloat16*>(q);
   args.q_sb = q_stride_b;
   args.q_sh = q_stride_h;
+  args.q_sq = q_stride_q;
   args.kc = k_codes;
   args.ksz = static_cast<const uint8_t*>(k_sz);
   args.vc = v_codes;
@@ -712,13 +728,16 @@ extern "C" int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_
   args.rlen = res_len;
   args.KVH = kv_heads;
   args.G = G;
+  args.Q = q_len;
   args.qscale = scaling * 1.4426950408889634f;
   args.out = static_cast<__nv_bfloat16*>(out);
   args.o_sb = out_stride_b;
   args.o_sh = out_stride_h;
+  args.o_sq = out_stride_q;
   args.status = status;
+  const int cols = q_len * G;
   const int64_t items = groups + (res_len + kTok - 1) / kTok;
-  int cs = kv_cluster_size(hs_count, items, G <= 8 ? KvWarps<1>::value : KvWarps<2>::value);
+  int cs = kv_cluster_size(hs_count, items, cols <= 8 ? KvWarps<1>::value : KvWarps<2>::value);
   // launch-shape switch for measurements, read once per process
   static const char* const forced = getenv("RW4_KV_CLUSTER");
   if (forced) {
@@ -730,6 +749,19 @@ extern "C" int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_
   cudaStream_t st = as_stream(stream);
   const int hsc = static_cast<int>(hs_count);
   if (head_dim == 128)
-    return G <= 8 ? launch_kv<128, 1>(args, hsc, cs, st) : launch_kv<128, 2>(args, hsc, cs, st);
-  return G <= 8 ? launch_kv<64, 1>(args, hsc, cs, st) : launch_kv<64, 2>(args, hsc, cs, st);
+    return cols <= 8 ? launch_kv<128, 1>(args, hsc, cs, st) : launch_kv<128, 2>(args, hsc, cs, st);
+  return cols <= 8 ? launch_kv<64, 1>(args, hsc, cs, st) : launch_kv<64, 2>(args, hsc, cs, st);
+}
+
+extern "C" int rw4_kv_attention_decode(const void* q, int64_t q_stride_b, int64_t q_stride_h,
+                                       int32_t batch, int32_t heads, int32_t kv_heads,
+                                       int32_t head_dim, const uint8_t* k_codes, const void* k_sz,
+                                       const uint8_t* v_codes, const void* v_sz,
+                                       int64_t groups_cap, int64_t groups, const void* k_res,
+                                       const void* v_res, int64_t res_cap, int64_t res_len,
+                                       float scaling, void* out, int64_t out_stride_b,
+                                       int64_t out_stride_h, void* stream) {
+  return rw4_kv_attention(q, q_stride_b, q_stride_h, 0, batch, heads, kv_heads, head_dim, 1,
+                          k_codes, k_sz, v_codes, v_sz, groups_cap, groups, k_res, v_res, res_cap,
+                          res_len, scaling, out, out_stride_b, out_stride_h, 0, stream);
 }

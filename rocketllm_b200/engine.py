@@ -436,7 +436,8 @@ class RocketModel:
         sampling = SamplingParams.from_generation(gc, **{k: kwargs.get(k) for k in (
             "do_sample", "temperature", "top_k", "top_p")})
         dec = SpeculativeDecoder(self, self.draft(), self.lookahead, self.max_lookahead,
-                                 new_cache=(lambda: RW4KVCache(fused=True)) if int4 else None,
+                                 new_cache=(lambda: RW4KVCache(fused=True, causal_chunks=True))
+                                 if int4 else None,
                                  eos_token_id=eos)
         out = dec.generate(ids.to(self.device), int(max_new_tokens), sampling, generator,
                            past_key_values, int(kwargs.get("min_new_tokens") or 0))

@@ -186,28 +186,30 @@ def moe_combine(y_perm, inv, topk_idx, topk_w, out=None):
 
 def kv_attention_decode(query, k_codes, k_sz, v_codes, v_sz, groups, k_res, v_res, res_len,
                         scaling, out=None):
-    """One query token's attention over an int4 KV cache (``rw4_kv_attention_decode``).
+    """Attention of ``q_len`` query positions over an int4 KV cache (``rw4_kv_attention``): the
+    queries are the window's last ``q_len`` tokens and attend causally (``q_len = 1``: a decode
+    step).
 
-    ``query`` bf16 ``[b, h, 1, d]`` (any strides with a unit last stride).  The cache arrays are
+    ``query`` bf16 ``[b, h, q_len, d]`` (any strides with a unit last stride).  The cache arrays are
     the layouts ``include/rw4.h`` documents: ``k_codes [b, kvh, gcap, d, 32]``, ``k_sz [b, kvh,
     gcap, d, 2]`` f16, ``v_codes [b, kvh, gcap*64, d/2]``, ``v_sz [b, kvh, gcap*64, d/64, 2]`` f16,
     ``k_res`` / ``v_res`` bf16 ``[b, kvh, rcap, d]``; ``groups`` and ``res_len`` say how much of
-    each is valid.  Returns bf16 ``[b, 1, h, d]`` (the layout transformers' attention returns).
+    each is valid.  Returns bf16 ``[b, q_len, h, d]`` (the layout transformers' attention
+    returns).
     """
     _require_cuda(k_codes, k_sz, v_codes, v_sz, k_res, v_res)
     if not query.is_cuda or query.dtype != torch.bfloat16 or query.stride(-1) != 1:
         raise ValueError("query must be a CUDA bf16 tensor with unit last stride")
     b, h, q_len, d = query.shape
-    if q_len != 1:
-        raise ValueError(f"decode attention takes one query token, not {q_len}")
     kvh, gcap = k_codes.shape[1], k_codes.shape[2]
     rcap = k_res.shape[2]
     if out is None:
-        out = torch.empty((b, 1, h, d), dtype=torch.bfloat16, device=query.device)
-    _lib.call("rw4_kv_attention_decode", query.data_ptr(), query.stride(0), query.stride(1), b, h,
-              kvh, d, k_codes.data_ptr(), k_sz.data_ptr(), v_codes.data_ptr(), v_sz.data_ptr(),
-              gcap, int(groups), k_res.data_ptr(), v_res.data_ptr(), rcap, int(res_len),
-              float(scaling), out.data_ptr(), out.stride(0), out.stride(2), _stream())
+        out = torch.empty((b, q_len, h, d), dtype=torch.bfloat16, device=query.device)
+    _lib.call("rw4_kv_attention", query.data_ptr(), query.stride(0), query.stride(1),
+              query.stride(2), b, h, kvh, d, q_len, k_codes.data_ptr(), k_sz.data_ptr(),
+              v_codes.data_ptr(), v_sz.data_ptr(), gcap, int(groups), k_res.data_ptr(),
+              v_res.data_ptr(), rcap, int(res_len), float(scaling), out.data_ptr(),
+              out.stride(0), out.stride(2), out.stride(1), _stream())
     return out
 
 

@@ -12,8 +12,10 @@ back to the compute dtype on every step and hands the model's attention the whol
 ``rw4_kv_attention_decode``) and, once :func:`enable_kv_attention` has installed the ``"rw4_kv"``
 attention implementation, a one-token step returns only the window from ``update`` -- tagged with
 its cache and layer -- and the attention function runs the CUDA kernel over packed history +
-window.  Anything else (a prefill, a masked or multi-token query, a cache used without the
-attention implementation) gets the reference's behaviour: the expanded history, then SDPA.
+window; so does a short multi-token chunk (a speculative verify pass) of a cache created with
+``causal_chunks``, causally masked inside the window.  Anything else (a prefill, a masked query, a
+cache used without the attention implementation) gets the reference's behaviour: the expanded
+history, then SDPA.
 
 The codec and attention operations are injected (``ops``): the default runs the RW4 CUDA kernels;
 the CPU tests drive the same bookkeeping with a numpy implementation of the three operations.
@@ -141,11 +143,16 @@ class RW4KVCache(Cache):
     ``fused``: a one-token ``update`` returns the window only, tagged for the ``"rw4_kv"``
     attention implementation (see :func:`enable_kv_attention`, which must be active on the model);
     otherwise ``update`` returns the expanded history as the reference does.
+
+    ``causal_chunks``: the caller promises that every multi-token update (up to 16 tokens) is the
+    causal continuation of one unpadded sequence per batch row -- a speculative verify pass -- so
+    those queries too can run on the packed history (causally masked inside the window) whatever
+    mask transformers builds for them.
     """
 
     is_compileable = False
 
-    def __init__(self, config=None, ops=None, fused=False):
+    def __init__(self, config=None, ops=None, fused=False, causal_chunks=False):
         try:
             Cache.__init__(self, layers=[])
         except (TypeError, ValueError):
@@ -153,6 +160,7 @@ class RW4KVCache(Cache):
         self.config = config if config is not None else KVCacheConfig()
         self.ops = ops if ops is not None else CudaKVOps()
         self.fused = fused
+        self.causal_chunks = causal_chunks
         self._kv = []
         self._seen_tokens = 0
         self.flushes = 0
@@ -171,7 +179,7 @@ class RW4KVCache(Cache):
         layer.v_res[:, :, layer.rlen:layer.rlen + t].copy_(value_states)
         layer.rlen += t
         self._flush(layer)
-        if self.fused and t == 1:
+        if self.fused and (t == 1 or (self.causal_chunks and t <= 16)):
             k = layer.k_res[:, :, :layer.rlen]
             v = layer.v_res[:, :, :layer.rlen]
             k._rw4_kv = (self, layer_idx)
@@ -244,8 +252,8 @@ class RW4KVCache(Cache):
         return torch.cat([kq, kr], dim=2), torch.cat([vq, vr], dim=2)
 
     def attend(self, layer_idx, query, scaling):
-        """One query token ``[b, h, 1, d]`` over the layer's packed history and window; returns
-        ``[b, 1, h, d]`` in the compute dtype."""
+        """Queries ``[b, h, q, d]`` -- the window's last ``q`` tokens, attending causally -- over
+        the layer's packed history and window; returns ``[b, q, h, d]`` in the compute dtype."""
         return self.ops.attend(query, self._kv[layer_idx], scaling)
 
     def quantized(self, layer_idx):
@@ -342,8 +350,9 @@ class RW4KVCache(Cache):
 def rw4_kv_attention(module, query, key, value, attention_mask, dropout=0.0, scaling=None,
                      is_causal=None, **kwargs):
     """transformers attention interface ``"rw4_kv"``: the packed-history kernel for a one-token
-    query whose keys came from a fused :class:`RW4KVCache`, SDPA over the expanded history for
-    every other case."""
+    query whose keys came from a fused :class:`RW4KVCache` (or a chunk of up to 16 / (heads per kv
+    head) positions of a ``causal_chunks`` cache), SDPA over the expanded history for every other
+    case."""
     from transformers.integrations.sdpa_attention import sdpa_attention_forward
     tag = getattr(key, "_rw4_kv", None)
     if tag is not None:
@@ -351,7 +360,10 @@ def rw4_kv_attention(module, query, key, value, attention_mask, dropout=0.0, sca
         if scaling is None:
             scaling = query.shape[-1] ** -0.5
         drop = dropout if getattr(module, "training", False) else 0.0
-        if query.shape[2] == 1 and attention_mask is None and not drop:
+        q_len = query.shape[2]
+        cols = q_len * (query.shape[1] // key.shape[1])
+        if not drop and ((q_len == 1 and attention_mask is None) or
+                         (1 < q_len and cache.causal_chunks and cols <= 16)):
             return cache.attend(layer_idx, query, scaling), None
         key, value = cache.history(layer_idx)
     return sdpa_attention_forward(module, query, key, value, attention_mask, dropout=dropout,

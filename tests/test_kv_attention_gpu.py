@@ -165,3 +165,47 @@ def test_model_decode_fused_vs_reference_behaviour(cuda, head_dim):
     assert fused._kv[0].groups == plain._kv[0].groups >= 3
     assert worst <= 2e-2, worst
     assert checked >= 100        # most steps are decisive
+
+
+CHUNK_CASES = [
+    # b, heads, kv_heads, head_dim, prefill, q_len
+    (1, 32, 8, 128, 189, 4),     # the chunk flushes a group; the window ends 1 token into a chunk
+    (2, 8, 8, 128, 330, 8),      # one head per kv head, 8 positions
+    (3, 16, 2, 64, 500, 2),      # 8 heads per kv head x 2 positions = 16 columns
+    (1, 8, 2, 128, 17000, 3),    # a cluster of 8 CTAs per head slot
+]
+
+
+@pytest.mark.parametrize("b,h,kvh,d,prefill,q_len", CHUNK_CASES)
+def test_kv_attention_chunk_matches_causal_oracle(cuda, b, h, kvh, d, prefill, q_len):
+    """q_len query positions that are the window's last tokens attend causally over the packed
+    history and the window (a speculative verify pass)."""
+    from rocketllm_b200 import kernels
+    from rocketllm_b200.kv_cache import RW4KVCache
+    cache = RW4KVCache(fused=True, causal_chunks=True)
+    _fill(cache, b, kvh, d, prefill, 0, seed=prefill + q_len, dev=cuda)
+    g = torch.Generator().manual_seed(11)
+    k = torch.randn(b, kvh, q_len, d, generator=g).to(torch.bfloat16)
+    v = torch.randn(b, kvh, q_len, d, generator=g).to(torch.bfloat16)
+    cache.update(k.to(cuda), v.to(cuda), 0)
+    hk, hv = cache.history(0)
+    q = torch.randn(b, h, q_len, d, generator=g).to(torch.bfloat16)
+    out = cache.attend(0, q.to(cuda), d ** -0.5)          # [b, q_len, h, d]
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    ref = O.attention_causal(q.float().numpy(), hk.float().cpu().numpy(),
+                             hv.float().cpu().numpy(), d ** -0.5)
+    err = np.abs(out.transpose(1, 2).float().cpu().numpy() - ref).max()
+    assert err <= ATOL, f"max abs error {err}"
+
+
+def test_kv_attention_chunk_column_limit(cuda):
+    from rocketllm_b200 import _lib, kernels
+    from rocketllm_b200.kv_cache import RW4KVCache
+    cache = RW4KVCache(fused=True, causal_chunks=True)
+    _fill(cache, 1, 2, 128, 20, 0, seed=2, dev=cuda)
+    layer = cache._kv[0]
+    q = torch.zeros(1, 8, 5, 128, dtype=torch.bfloat16, device=cuda)   # 5 x 4 = 20 columns
+    with pytest.raises(_lib.RW4Error):
+        kernels.kv_attention_decode(q, layer.k_codes, layer.k_sz, layer.v_codes, layer.v_sz,
+                                    layer.groups, layer.k_res, layer.v_res, layer.rlen, 1.0)

@@ -61,8 +61,8 @@ class CpuKVOps:
         vr = layer.v_res[:, :, :layer.rlen].float().numpy()
         k = np.concatenate([kq, kr], axis=2)
         v = np.concatenate([vq, vr], axis=2)
-        out = O.attention_decode(query[:, :, 0].float().numpy(), k, v, scaling)
-        return torch.from_numpy(out).to(torch.bfloat16).unsqueeze(1)
+        out = O.attention_causal(query.float().numpy(), k, v, scaling)   # [b, h, q, d]
+        return torch.from_numpy(out).to(torch.bfloat16).transpose(1, 2)
 
 
 @pytest.fixture(scope="module")
@@ -178,4 +178,29 @@ def test_model_decode_through_fused_attention():
             tok = b.argmax(-1, keepdim=True)
     assert ops.attends == 110 * 2                         # every decode step, every layer
     assert fused._kv[0].groups >= 2
+    assert worst <= 2e-2
+
+
+def test_chunked_queries_run_on_the_packed_history():
+    """A ``causal_chunks`` cache hands 3-token chunks (a verify pass) to the packed attention too;
+    the logits follow the reference behaviour (expanded history + masked SDPA) chunk by chunk,
+    across flushes."""
+    model = _tiny_llama()
+    enable_kv_attention(model)
+    ops = CpuKVOps()
+    chunked = RW4KVCache(ops=ops, fused=True, causal_chunks=True)
+    plain = RW4KVCache(ops=CpuKVOps(), fused=False)
+    ids = torch.randint(0, 512, (1, 150), generator=torch.Generator().manual_seed(7))
+    worst = 0.0
+    with torch.no_grad():
+        model(ids, past_key_values=chunked, use_cache=True)
+        model(ids, past_key_values=plain, use_cache=True)
+        g = torch.Generator().manual_seed(8)
+        for _ in range(40):                       # 270 tokens: two groups flushed meanwhile
+            chunk = torch.randint(0, 512, (1, 3), generator=g)
+            a = model(chunk, past_key_values=chunked, use_cache=True).logits
+            b = model(chunk, past_key_values=plain, use_cache=True).logits
+            worst = max(worst, (a.float() - b.float()).abs().max().item())
+    assert ops.attends == 40 * 2                  # every chunk, every layer, on the packed path
+    assert chunked._kv[0].groups >= 2
     assert worst <= 2e-2

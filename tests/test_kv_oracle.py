@@ -77,3 +77,23 @@ def test_window_never_flushes_a_partial_group():
     x = O.f32_to_bf16_bits(rng.standard_normal((1, 1, 1, 64)).astype(np.float32))
     hk, _ = cache.update(x, x)
     assert cache.quantized_tokens() == 64 and cache.k.shape[2] == 128 and hk.shape[2] == 192
+
+
+def test_causal_attention_matches_sdpa_with_a_cache_mask():
+    """``attention_causal``: Q query positions that are the last Q of T keys, each seeing keys up to
+    its own position -- torch SDPA with the bottom-right aligned causal mask, in fp64."""
+    import torch
+    rng = np.random.default_rng(3)
+    b, h, kvh, q_len, t, d = 2, 8, 2, 4, 37, 64
+    q = rng.standard_normal((b, h, q_len, d)).astype(np.float32)
+    k = rng.standard_normal((b, kvh, t, d)).astype(np.float32)
+    v = rng.standard_normal((b, kvh, t, d)).astype(np.float32)
+    out = O.attention_causal(q, k, v, d ** -0.5)
+    mask = torch.arange(t)[None, :] <= (t - q_len + torch.arange(q_len))[:, None]
+    kk = torch.from_numpy(k).double().repeat_interleave(h // kvh, dim=1)
+    vv = torch.from_numpy(v).double().repeat_interleave(h // kvh, dim=1)
+    ref = torch.nn.functional.scaled_dot_product_attention(
+        torch.from_numpy(q).double(), kk, vv, attn_mask=mask, scale=d ** -0.5)
+    np.testing.assert_allclose(out, ref.numpy(), rtol=0, atol=1e-6)
+    np.testing.assert_allclose(O.attention_causal(q[:, :, -1:], k, v, d ** -0.5)[:, :, 0],
+                               O.attention_decode(q[:, :, -1], k, v, d ** -0.5), atol=1e-7)

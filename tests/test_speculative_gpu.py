@@ -61,8 +61,11 @@ def test_streamed_speculation_matches_greedy(checkpoint, kv):
         ref = plain.generate(ids, max_new_tokens=n, do_sample=False,
                              return_dict_in_generate=True, output_logits=True)
     plain.close()
+    # lookahead 3 with the int4 cache: 4 positions x 4 heads per kv head = 16 columns, so every
+    # verify pass runs on the packed history (rw4_kv_attention); the fp16 cache takes 4
     spec = RocketModel(checkpoint, vram_budget=1, window=1, kv_cache=kv,
-                       draft_model=_draft(checkpoint), speculative="auto", lookahead=4)
+                       draft_model=_draft(checkpoint), speculative="auto",
+                       lookahead=4 if kv == "fp16" else 3, max_lookahead=4 if kv == "fp16" else 3)
     spec.model.generation_config.eos_token_id = None
     assert spec.speculation_enabled()[0]          # streamed weights: "auto" speculates
     out = spec.generate(ids, max_new_tokens=n, do_sample=False)
