@@ -838,25 +838,31 @@ def kv_attn_bench(args):
         cache.update(torch.randn(bsz, kvh, 1, d, device=device, generator=g).to(torch.bfloat16),
                      torch.randn(bsz, kvh, 1, d, device=device, generator=g).to(torch.bfloat16), 0)
         layer = cache._kv[0]
-        q = torch.randn(bsz, h, 1, d, device=device, generator=g).to(torch.bfloat16)
+        nq = args.kv_q
+        q = torch.randn(bsz, h, nq, d, device=device, generator=g).to(torch.bfloat16)
         scaling = d ** -0.5
         ms = timed(lambda: cache.attend(0, q, scaling))
+        # the query positions are the last nq of the ctx tokens (causal, aligned to the cache end)
+        mask = None if nq == 1 else (torch.arange(ctx, device=device)[None, :] <=
+                                     (ctx - nq + torch.arange(nq, device=device))[:, None])
 
         def reference_step():
             hk, hv = cache.history(0)
-            F.scaled_dot_product_attention(q, hk, hv, scale=scaling, enable_gqa=True)
+            F.scaled_dot_product_attention(q, hk, hv, attn_mask=mask, scale=scaling,
+                                           enable_gqa=True)
 
         ms_ref = timed(reference_step)
         hk, hv = cache.history(0)
-        ms_bf16 = timed(lambda: F.scaled_dot_product_attention(q, hk, hv, scale=scaling,
-                                                               enable_gqa=True))
+        ms_bf16 = timed(lambda: F.scaled_dot_product_attention(q, hk, hv, attn_mask=mask,
+                                                               scale=scaling, enable_gqa=True))
         vg = d // 64
         alg = bsz * kvh * (layer.groups * (36 * d + 32 * d + 64 * vg * 4) + layer.rlen * 4 * d) \
-            + 2 * bsz * h * d * 2
+            + 2 * bsz * h * nq * d * 2
         bf16_bytes = 2 * hk.numel() * 2
         gbs = alg / (ms * 1e-3) / 1e9
         print(json.dumps({
             "kv_attention": name, "batch": bsz, "heads": h, "kv_heads": kvh, "head_dim": d,
+            "query_positions": nq,
             "context": ctx, "quantized_tokens": layer.groups * 64, "window_tokens": layer.rlen,
             "us": round(ms * 1e3, 2), "alg_bytes": alg, "gbs": round(gbs, 1),
             "hbm_frac": round(gbs / peak, 4), "peak": peak_kind,
@@ -1026,6 +1032,8 @@ def main():
     ap.add_argument("--kv-attn", action="store_true",
                     help="decode attention over the int4 KV cache (one JSON line per case)")
     ap.add_argument("--kv-cases", default="all", help="'all' or indices into KV_CASES")
+    ap.add_argument("--kv-q", type=int, default=1,
+                    help="query positions per call (a speculative verify chunk when > 1)")
     ap.add_argument("--spec-decode", action="store_true",
                     help="speculative decoding on the streamed 8B (one JSON line per lookahead)")
     ap.add_argument("--spec-tokens", type=int, default=48)
