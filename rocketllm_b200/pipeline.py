@@ -25,10 +25,13 @@ class PipelineDecoder:
     """Greedy decode of a ``*ForCausalLM`` whose decoder layers are split over ``group``.
 
     ``model`` is this rank's copy; layers outside the rank's range (and the embedding / head on
-    ranks that do not use them) are dropped to free their memory.
+    ranks that do not use them) are dropped to free their memory.  ``cache`` is the key/value cache
+    of this rank's layers (default: transformers' ``DynamicCache``; an
+    :class:`~rocketllm_b200.kv_cache.RW4KVCache` keeps them in int4).
     """
 
-    def __init__(self, model, group=None, device="cuda", drop_remote=True, local=False):
+    def __init__(self, model, group=None, device="cuda", drop_remote=True, local=False,
+                 cache=None):
         from transformers import DynamicCache
         self.group = group
         self.local = local or not dist.is_initialized()   # one rank, no communication
@@ -52,7 +55,7 @@ class PipelineDecoder:
                 inner.norm = None
         self.rotary = inner.rotary_emb
         self.embed = inner.embed_tokens
-        self.cache = DynamicCache(config=model.config)
+        self.cache = cache if cache is not None else DynamicCache(config=model.config)
         self.hidden_size = model.config.hidden_size
         self.dtype = next(p.dtype for p in model.parameters() if p.is_floating_point()
                           and p.dtype != torch.float16)

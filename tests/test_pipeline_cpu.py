@@ -89,3 +89,50 @@ def test_pipeline_matches_single_rank(world):
         out = mgr.dict()
         mp.spawn(_worker, args=(world, 29711 + world, out), nprocs=world, join=True)
         assert all(out[r] for r in range(world)), dict(out)
+
+
+def _int4_model():
+    """A bf16 Llama with head_dim 64 (the int4 cache's layout) and room for a flushed group."""
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(0)
+    cfg = LlamaConfig(hidden_size=256, intermediate_size=256, num_hidden_layers=4,
+                      num_attention_heads=4, num_key_value_heads=2, vocab_size=97,
+                      max_position_embeddings=256, tie_word_embeddings=False)
+    m = LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+    with torch.no_grad():
+        for n, p in m.named_parameters():
+            if "norm" not in n:
+                p.normal_(0, 0.2)
+    return m
+
+
+def _int4_decoder(local):
+    from test_kv_cache_cpu import CpuKVOps
+
+    from rocketllm_b200.kv_cache import RW4KVCache, enable_kv_attention
+    from rocketllm_b200.pipeline import PipelineDecoder
+    m = enable_kv_attention(_int4_model())
+    return PipelineDecoder(m, device="cpu", local=local,
+                           cache=RW4KVCache(ops=CpuKVOps(), fused=True))
+
+
+def _int4_worker(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ids = torch.randint(0, 97, (1, 189), generator=torch.Generator().manual_seed(5))
+    ref = _int4_decoder(local=True).generate(ids, 8)     # crosses the first flush at 192 tokens
+    dec = _int4_decoder(local=False)
+    got = dec.generate(ids, 8)
+    own = [i for i in range(dec.start, dec.stop)]
+    out[rank] = bool(torch.equal(ref, got)) and all(dec.cache._kv[i].groups == 1 for i in own)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_pipeline_with_the_int4_kv_cache_matches_single_rank():
+    """Each rank keeps its own layers' int4 cache (fused decode attention, a group flushed during
+    the run); the tokens are the single-rank run's."""
+    with mp.Manager() as mgr:
+        out = mgr.dict()
+        mp.spawn(_int4_worker, args=(2, 29731, out), nprocs=2, join=True)
+        assert all(out[r] for r in range(2)), dict(out)
