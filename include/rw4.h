@@ -273,6 +273,26 @@ int rw4_xfer_sync(rw4_xfer* x, uint64_t ticket, int64_t timeout_ms);
 int rw4_xfer_stats(rw4_xfer* x, uint64_t* sends, uint64_t* bytes, uint64_t* chunks,
                    int32_t* in_flight);
 
+/*
+ * rw4_ring_*: a fixed ring of `slots` pinned staging slots of slot_bytes each in front of a
+ * transfer engine with `copy_streams` copy streams on the current device -- the slot-ring form of
+ * the pool + engine above, for callers that stage layer bytes from I/O worker threads.  Workers
+ * fill a slot with rw4_ring_stage (a host memcpy; or read into the address from rw4_ring_slot);
+ * the forward thread sends it with rw4_ring_submit (chunked over the copy streams; `done_event`,
+ * a cudaEvent_t or NULL, is recorded behind the copies) and makes compute wait on the device with
+ * rw4_ring_wait_compute (every slot's last submit).  A slot whose last submit is still in flight
+ * is refused for staging and submitting (RW4_EBUSY): the reference's lease rule
+ * (rocketllm/streaming/staging.py:33-66) per slot.  rw4_ring_destroy waits for copies in flight.
+ * slots 1..64, copy_streams 1..8.
+ */
+typedef struct rw4_ring rw4_ring;
+int rw4_ring_create(size_t slot_bytes, int32_t slots, int32_t copy_streams, rw4_ring** out);
+int rw4_ring_destroy(rw4_ring* ring);
+int rw4_ring_slot(rw4_ring* ring, int32_t slot, void** host);
+int rw4_ring_stage(rw4_ring* ring, int32_t slot, size_t offset, const void* src, size_t n);
+int rw4_ring_submit(rw4_ring* ring, int32_t slot, void* dst, size_t n, void* done_event);
+int rw4_ring_wait_compute(rw4_ring* ring, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -73,6 +73,12 @@ SIGNATURES = {
                                                _c_void_p, _c_void_p, _c_void_p, _c_void_p, _i64,
                                                _i64, _c_void_p, _c_void_p, _i64, _i64,
                                                ctypes.c_float, _c_void_p, _i64, _i64, _c_void_p]),
+    "rw4_ring_create": (ctypes.c_int, [_size, _i32, _i32, ctypes.POINTER(_c_void_p)]),
+    "rw4_ring_destroy": (ctypes.c_int, [_c_void_p]),
+    "rw4_ring_slot": (ctypes.c_int, [_c_void_p, _i32, ctypes.POINTER(_c_void_p)]),
+    "rw4_ring_stage": (ctypes.c_int, [_c_void_p, _i32, _size, _c_void_p, _size]),
+    "rw4_ring_submit": (ctypes.c_int, [_c_void_p, _i32, _c_void_p, _size, _c_void_p]),
+    "rw4_ring_wait_compute": (ctypes.c_int, [_c_void_p, _c_void_p]),
     "rw4_pool_create": (ctypes.c_int, [_size, ctypes.POINTER(_c_void_p)]),
     "rw4_pool_destroy": (ctypes.c_int, [_c_void_p]),
     "rw4_pool_lease": (ctypes.c_int, [_c_void_p, _size, ctypes.POINTER(_i32),

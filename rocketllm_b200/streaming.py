@@ -336,3 +336,57 @@ class WeightTransfer:
 
 
 __all__ = ["BufferLease", "HostStagingPool", "TransferHandle", "WeightTransfer"]
+
+
+class StagingRing:
+    """A fixed ring of pinned staging slots feeding the device (``rw4_ring_*``).
+
+    I/O workers fill slots (:meth:`stage`, or :meth:`slot` for a CPU tensor view to read into);
+    the forward thread sends a slot to a device buffer (:meth:`submit`) and makes compute wait on
+    the device (:meth:`wait_compute`).  A slot whose last send is still in flight raises
+    :class:`~rocketllm_b200._lib.RW4Error` (``RW4_EBUSY``) on stage / submit.
+    """
+
+    def __init__(self, slot_bytes, slots, copy_streams=2, device=None):
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None \
+            else torch.device(device)
+        self.slot_bytes, self.slots = int(slot_bytes), int(slots)
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.call("rw4_ring_create", self.slot_bytes, self.slots, int(copy_streams),
+                      ctypes.byref(handle))
+        self._h = handle
+
+    def slot(self, i):
+        """Slot ``i`` as a CPU uint8 tensor view (no copy)."""
+        ptr = ctypes.c_void_p()
+        _lib.call("rw4_ring_slot", self._h, int(i), ctypes.byref(ptr))
+        return _host_tensor(ptr.value, self.slot_bytes, torch.uint8, self.slot_bytes)
+
+    def stage(self, i, src, offset=0):
+        """Copy the bytes of CPU tensor ``src`` into slot ``i`` at ``offset``."""
+        src = src.contiguous()
+        _lib.call("rw4_ring_stage", self._h, int(i), int(offset), src.data_ptr(),
+                  src.numel() * src.element_size())
+
+    def submit(self, i, dst, nbytes=None, done=None):
+        """Send slot ``i``'s first ``nbytes`` (default: ``dst``'s size) into CUDA tensor ``dst``;
+        ``done`` (a recorded-before ``torch.cuda.Event``) is recorded behind the copies."""
+        n = dst.numel() * dst.element_size() if nbytes is None else int(nbytes)
+        _lib.call("rw4_ring_submit", self._h, int(i), dst.data_ptr(), n,
+                  ctypes.c_void_p(done.cuda_event) if done is not None else None)
+
+    def wait_compute(self, stream=None):
+        stream = torch.cuda.current_stream(self.device) if stream is None else stream
+        _lib.call("rw4_ring_wait_compute", self._h, ctypes.c_void_p(stream.cuda_stream))
+
+    def close(self):
+        if self._h:
+            _lib.call("rw4_ring_destroy", self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass

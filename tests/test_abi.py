@@ -100,3 +100,18 @@ def test_kv_and_expert_routing_entry_points_reject_bad_arguments():
         == _lib.RW4_EINVAL
     dev = ctypes.c_void_p()
     assert lib.rw4_host_ptr_device(None, ctypes.byref(dev)) == _lib.RW4_EINVAL
+
+
+def test_ring_rejects_bad_arguments_before_touching_the_device():
+    lib = _lib.lib()
+    out = ctypes.c_void_p()
+    assert lib.rw4_ring_create(0, 2, 1, ctypes.byref(out)) == _lib.RW4_EINVAL
+    assert lib.rw4_ring_create(1 << 20, 0, 1, ctypes.byref(out)) == _lib.RW4_EINVAL
+    assert lib.rw4_ring_create(1 << 20, 65, 1, ctypes.byref(out)) == _lib.RW4_EINVAL
+    assert lib.rw4_ring_create(1 << 20, 2, 9, ctypes.byref(out)) == _lib.RW4_EINVAL
+    assert lib.rw4_ring_create(1 << 20, 2, 1, None) == _lib.RW4_EINVAL
+    assert out.value is None
+    assert lib.rw4_ring_stage(None, 0, 0, None, 0) == _lib.RW4_EINVAL
+    assert lib.rw4_ring_submit(None, 0, None, 0, None) == _lib.RW4_EINVAL
+    assert lib.rw4_ring_wait_compute(None, None) == _lib.RW4_EINVAL
+    assert lib.rw4_ring_destroy(None) == _lib.RW4_OK

@@ -77,3 +77,34 @@ def test_after_stream_keeps_a_slot_from_being_overwritten(cuda):
     assert int(seen.min()) == 7 and int(seen.max()) == 7
     assert int(slot.min()) == 9
     xfer.close()
+
+
+def test_staging_ring_round_trip_and_busy_slot(cuda):
+    """Slots staged on the host land byte-exact in device buffers; the done event and the device-
+    side wait both cover the copies; a slot in flight refuses new bytes."""
+    from rocketllm_b200._lib import RW4Error
+    from rocketllm_b200.streaming import StagingRing
+    ring = StagingRing(1 << 20, 3, copy_streams=2)
+    src = [torch.randint(0, 256, (1 << 20,), dtype=torch.uint8) for _ in range(3)]
+    dst = [torch.empty(1 << 20, dtype=torch.uint8, device=cuda) for _ in range(3)]
+    done = torch.cuda.Event()
+    done.record()                                   # creates the event the ring records into
+    for i in range(3):
+        ring.stage(i, src[i])
+    ring.slot(2)[:16].fill_(7)                      # a worker writing straight into a slot
+    src[2][:16] = 7
+    for i in range(3):
+        ring.submit(i, dst[i], done=done if i == 0 else None)
+    done.synchronize()
+    assert torch.equal(dst[0].cpu(), src[0])
+    ring.wait_compute()
+    for i in range(3):
+        assert torch.equal(dst[i].cpu(), src[i])
+    big = torch.empty(1 << 20, dtype=torch.uint8, device=cuda)
+    ring.submit(1, big)
+    try:                                            # either refused while in flight, or done
+        ring.stage(1, src[0])
+    except RW4Error as e:
+        assert "RW4_EBUSY" in str(e)
+    torch.cuda.synchronize()
+    ring.close()
