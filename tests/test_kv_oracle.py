@@ -97,3 +97,67 @@ def test_causal_attention_matches_sdpa_with_a_cache_mask():
     np.testing.assert_allclose(out, ref.numpy(), rtol=0, atol=1e-6)
     np.testing.assert_allclose(O.attention_causal(q[:, :, -1:], k, v, d ** -0.5)[:, :, 0],
                                O.attention_decode(q[:, :, -1], k, v, d ** -0.5), atol=1e-7)
+
+
+# -- codec properties the reference's own suite asserts (tests/test_kv_cache.py:38-138), stated
+#    here for the oracle codec on bf16 keys / values --------------------------------------------
+
+def _kv_bits(shape, seed, scale=1.0):
+    rng = np.random.default_rng(seed)
+    return O.f32_to_bf16_bits((rng.standard_normal(shape) * scale).astype(np.float32))
+
+
+def _round_trip(bits, axis):
+    length = bits.shape[axis]
+    p, s, z, _ = O.kv_quantize(bits, axis, 64)
+    return O.kv_dequantize(p, s, z, axis, length, out="f32")
+
+
+@pytest.mark.parametrize("axis", [2, 3])
+def test_round_trip_within_half_a_step(axis):
+    """Every value comes back within half its group's step ((max - min) / 15), plus a little for
+    the scale and zero being stored in fp16."""
+    bits = _kv_bits((1, 2, 256, 128), seed=axis)
+    x = O.bf16_bits_to_f32(bits)
+    back = _round_trip(bits, axis)
+    moved = np.moveaxis(x, axis, -1)
+    grouped = moved.reshape(moved.shape[:-1] + (-1, 64))
+    spread = grouped.max(-1) - grouped.min(-1)
+    err = np.abs(np.moveaxis(back, axis, -1).reshape(grouped.shape) - grouped).max(-1)
+    assert np.all(err <= spread / 30 + spread * 1e-3 + 1e-4)
+
+
+def test_constant_and_ragged_groups_are_exact():
+    const = O.f32_to_bf16_bits(np.full((1, 1, 64, 64), 0.375, np.float32))
+    assert np.array_equal(_round_trip(const, 2), O.bf16_bits_to_f32(const))
+    # 100 tokens: the last group is padded by repeating its last value, which cannot widen it
+    ragged = O.f32_to_bf16_bits(np.full((1, 1, 100, 8), 5.0, np.float32))
+    assert np.array_equal(_round_trip(ragged, 2), O.bf16_bits_to_f32(ragged))
+
+
+def test_an_axis_shorter_than_a_group():
+    bits = _kv_bits((1, 2, 8, 16), seed=4)
+    p, s, z, pad = O.kv_quantize(bits, 3, 64)
+    assert s.shape[-1] == 1 and pad == 0              # one group of 16
+    back = O.kv_dequantize(p, s, z, 3, 16, out="f32")
+    assert back.shape == bits.shape
+    assert np.abs(back - O.bf16_bits_to_f32(bits)).max() < 1.0
+
+
+def test_four_bits_per_value():
+    bits = _kv_bits((1, 2, 1024, 64), seed=5)
+    p, s, z, _ = O.kv_quantize(bits, 2, 64)
+    assert p.dtype == np.uint8 and p.nbytes + s.nbytes + z.nbytes < bits.size * 2 / 3
+
+
+def test_keys_need_per_channel_groups():
+    """With one outlier channel, grouping keys along tokens (a scale per channel) keeps the other
+    channels accurate; grouping along channels (the value layout) would not."""
+    x = np.random.default_rng(3).standard_normal((1, 2, 256, 64)).astype(np.float32)
+    x[..., 7] *= 30.0
+    bits = O.f32_to_bf16_bits(x)
+    xf = O.bf16_bits_to_f32(bits)
+    others = [c for c in range(64) if c != 7]
+    good = np.abs(_round_trip(bits, 2)[..., others] - xf[..., others]).mean()
+    bad = np.abs(_round_trip(bits, 3)[..., others] - xf[..., others]).mean()
+    assert good * 3 < bad
