@@ -46,6 +46,10 @@ def test_rw4_weight_groups_and_sizes():
     assert w.needs_scratch is False and w.scratch_bytes == 0
     bias = weights[1]
     assert bias.bits == 16 and bias.packed_bytes == N * 2
+    # an fp32 compute dtype is what the expanded size expands into (the packed size is unchanged)
+    wide = detect_backend({"quant_method": "rw4", "bits": 4}, compute_dtype=torch.float32)
+    ww = wide.plan(rw4_shard())[0]
+    assert ww.expanded_bytes == N * K * 4 and ww.packed_bytes == w.packed_bytes
 
 
 def test_sizes_from_header_match_sizes_from_data():
