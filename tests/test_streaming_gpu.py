@@ -108,3 +108,31 @@ def test_staging_ring_round_trip_and_busy_slot(cuda):
         assert "RW4_EBUSY" in str(e)
     torch.cuda.synchronize()
     ring.close()
+
+
+def test_pool_buffers_pack_losslessly_cast_on_the_way_in_and_do_not_leak(cuda):
+    """The reference pool's packing properties (tests/test_staging_pool.py:137-174): several
+    tensors packed into one buffer read back exactly, a reused buffer carries nothing of the
+    previous layer once rewritten, and packing in a narrower dtype casts on the way in."""
+    pool = HostStagingPool(None, 64 << 20)
+    g = torch.Generator().manual_seed(0)
+    tensors = [torch.randn(shape, generator=g) for shape in ((16, 32), (32,), (8, 8, 4), (100,))]
+    buf = pool.buffer(sum(t.numel() for t in tensors), torch.float32)
+    off = 0
+    for t in tensors:
+        buf.narrow(0, off, t.numel()).copy_(t.reshape(-1))
+        off += t.numel()
+    off = 0
+    for t in tensors:
+        assert torch.equal(buf.narrow(0, off, t.numel()).view(t.shape), t)
+        off += t.numel()
+    first = pool.buffer(1000, torch.float32)
+    first.fill_(7.0)
+    second = pool.buffer(1000, torch.float32)
+    second.copy_(torch.zeros(1000))
+    assert torch.equal(second, torch.zeros(1000))
+    src = torch.randn(64, generator=g)
+    narrow = pool.buffer(64, torch.bfloat16)
+    narrow.copy_(src)
+    assert narrow.dtype == torch.bfloat16 and torch.allclose(narrow.float(), src, atol=1e-2)
+    pool.close()
