@@ -204,6 +204,50 @@ class LayerShardReader:
         self.direct_reads += int(direct)
         return buffer
 
+    def read_tensor(self, i, key, rows=None, out=None):
+        """One tensor of layer ``i`` -- ``key`` is ``"<module path>.<leaf>"`` as in the index -- or
+        the rows ``[start, stop)`` of its leading dimension (one expert of a stacked tensor), read
+        with one positioned read of exactly those bytes (``loader.py:161-236``: a subset of a
+        layer costs only its own bytes).  Returns a CPU tensor of the entry's dtype (``out``, a CPU
+        tensor of that shape and dtype, is filled instead of allocating)."""
+        rec = self.layers[i]
+        for m, leaf, kind, dt, shape, off in rec["entries"]:
+            if (f"{m}.{leaf}" if m else leaf) == key:
+                break
+        else:
+            raise KeyError(f"layer {i} has no tensor {key!r}")
+        dtype = getattr(torch, dt)
+        shape = list(shape)
+        item = torch.empty((), dtype=dtype).element_size()
+        row_elems = 1
+        for d in shape[1:]:
+            row_elems *= d
+        start, stop = (0, shape[0]) if rows is None else (int(rows[0]), int(rows[1]))
+        if not shape or not 0 <= start <= stop <= shape[0]:
+            raise ValueError(f"rows {rows} outside {key!r} of shape {tuple(shape)}")
+        shape[0] = stop - start
+        nbytes = (stop - start) * row_elems * item
+        if out is None:
+            out = torch.empty(shape, dtype=dtype)
+        elif (tuple(out.shape) != tuple(shape) or out.dtype != dtype or out.is_cuda
+              or not out.is_contiguous()):
+            raise ValueError(f"out must be a contiguous CPU {dtype} tensor of shape {shape}")
+        view = memoryview(out.view(-1).view(torch.uint8).numpy()).cast("B")
+        fd = os.open(os.path.join(self.root, rec["file"]), os.O_RDONLY)
+        try:
+            done = 0
+            pos = rec["data_start"] + off + start * row_elems * item
+            while done < nbytes:
+                got = os.preadv(fd, [view[done:nbytes]], pos + done)
+                if got <= 0:
+                    raise IOError(f"{rec['file']}: short read at {pos + done}")
+                done += got
+        finally:
+            os.close(fd)
+        self.reads += 1
+        self.bytes_read += nbytes
+        return out
+
     def stats(self):
         return {"layers": len(self.layers), "reads": self.reads, "bytes_read": self.bytes_read,
                 "direct_reads": self.direct_reads}

@@ -78,3 +78,28 @@ def test_done_layers_are_not_rewritten(tmp_path):
     split_rw4_layers(model, root)
     assert os.stat(path).st_mtime_ns == before
     assert os.path.exists(os.path.join(root, INDEX))
+
+
+def test_a_subset_or_row_slice_costs_only_its_bytes(tmp_path):
+    """One tensor of a layer, or a row range of it, is one positioned read of exactly those bytes
+    (the reference loader's subset and per-expert row reads, streaming/loader.py:161-236)."""
+    model = tiny_rw4_model(2)
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    reader = LayerShardReader(root)
+    mlp = model.model.layers[1].mlp
+    key = "mlp.up_proj.weight_packed"
+    got = reader.read_tensor(1, key)
+    assert torch.equal(got, mlp.up_proj.weight_packed)
+    assert reader.stats()["bytes_read"] == got.numel()
+    before = reader.stats()["bytes_read"]
+    rows = reader.read_tensor(1, "mlp.up_proj.weight_scale", rows=(5, 9))
+    assert torch.equal(rows, mlp.up_proj.weight_scale[5:9])
+    assert reader.stats()["bytes_read"] - before == rows.numel() * rows.element_size()
+    out = torch.empty_like(mlp.down_proj.weight_zero_point[:3])
+    assert reader.read_tensor(1, "mlp.down_proj.weight_zero_point", rows=(0, 3), out=out) is out
+    assert torch.equal(out, mlp.down_proj.weight_zero_point[:3])
+    import pytest
+    with pytest.raises(KeyError):
+        reader.read_tensor(1, "mlp.no_such.weight")
+    with pytest.raises(ValueError):
+        reader.read_tensor(1, key, rows=(0, 10 ** 6))
