@@ -97,6 +97,12 @@ int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, const uint8_t* 
  * the word.  No reference counterpart: the reference has no device kernels that can wait. */
 int rw4_device_status(uint32_t* word, int32_t clear, void* stream);
 
+/* Diagnostic (no reference counterpart): one block runs the library's bounded mbarrier wait on a
+ * barrier that completes (arrive != 0) or that nothing completes (arrive == 0).  In the second case
+ * the wait gives up after its limit (1 s), sets bit 1 of the device status word and the kernel
+ * returns -- how every kernel here reports a copy that never landed, without trapping or hanging. */
+int rw4_wait_selftest(int32_t arrive, void* stream);
+
 /* ---------------------------------------------------------------------------------------------
  * MoE routed experts.  Together these replace the experts forward the reference streams
  * (transformers models/mixtral/modeling_mixtral.py:62-98, reached through rocketllm/base.py's
