@@ -147,3 +147,26 @@ def test_speculation_over_int4_cache_crops_the_window():
     assert cache.get_seq_length(0) == 239                 # every token but the last emitted
     assert cache._kv[0].groups >= 1 and cache.flushes >= 1
     assert dec.stats.passes <= 60 and dec.stats.emitted == 60
+
+
+def test_warps_and_greedy_verdicts_match_the_reference():
+    """Pinned to the reference's own ``SamplingParams.distribution`` and ``verify``
+    (``tests/golden/reference_spec.npz``, written by ``tests/golden/make_spec_golden.py``)."""
+    import os
+
+    import numpy as np
+    gold = dict(np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                                     "reference_spec.npz")))
+    logits = torch.from_numpy(gold["logits"])
+    warps = {"greedy": dict(do_sample=False), "t07": dict(do_sample=True, temperature=0.7),
+             "k5": dict(do_sample=True, temperature=1.3, top_k=5),
+             "p08": dict(do_sample=True, temperature=0.9, top_p=0.8)}
+    for name, kw in warps.items():
+        got = SamplingParams(**kw).distribution(logits).numpy()
+        np.testing.assert_allclose(got, gold[f"dist.{name}"], rtol=0, atol=1e-7, err_msg=name)
+    greedy = SamplingParams()
+    for c in gold["cases"].tolist():
+        target = greedy.distribution(torch.from_numpy(gold[f"case{c}.target_logits"]))
+        props = torch.from_numpy(gold[f"case{c}.proposals"])
+        dq = torch.nn.functional.one_hot(props, target.shape[-1]).float()
+        assert verify(props, dq, target) == tuple(gold[f"case{c}.result"].tolist()), c
