@@ -341,7 +341,8 @@ def moe_decode(args):
     model = build_rw4_causal_lm(cfg, device=device, seed=0)
     weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
     streamed = RocketModel(model, device=device, vram_budget=int(args.moe_budget_gb * 1e9),
-                           window=2, kv_cache="fp16", expert_routing=args.moe_routing)
+                           window=2, kv_cache="fp16", expert_routing=args.moe_routing,
+                           expert_policy=args.expert_policy)
     del model
     torch.cuda.empty_cache()
     setup_s = time.time() - t0
@@ -352,6 +353,7 @@ def moe_decode(args):
            "vram_budget_bytes": int(args.moe_budget_gb * 1e9),
            "pinned_layers": st.pinned, "streamed_layers": st.streamed,
            "expert_routing": args.moe_routing,
+           "expert_policy": st.experts.stats()["policy"] if st.experts else None,
            "expert_slots": st.experts.stats()["expert_slots"] if st.experts else 0,
            "expert_blob_bytes": st.experts.stats()["slot_bytes"] if st.experts else 0,
            "prompt_tokens": args.moe_prompt, "setup_s": round(setup_s, 1)}
@@ -1029,6 +1031,8 @@ def main():
     ap.add_argument("--moe-tokens", type=int, default=16)
     ap.add_argument("--moe-routing", choices=("host", "device"), default="host",
                     help="routed-set read back to the host per MoE layer, or decided on the device")
+    ap.add_argument("--expert-policy", choices=("lfu", "lru"), default=None,
+                    help="expert cache eviction (default: lfu with host routing, lru with device)")
     ap.add_argument("--kv-attn", action="store_true",
                     help="decode attention over the int4 KV cache (one JSON line per case)")
     ap.add_argument("--kv-cases", default="all", help="'all' or indices into KV_CASES")

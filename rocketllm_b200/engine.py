@@ -92,7 +92,7 @@ class LayerStreamer:
 
     def __init__(self, layers, device, window=2, copy_streams=2, chunk_bytes=16 << 20,
                  prefetching=True, expert_slots=None, blobs=None, pinned=0,
-                 expert_routing="host"):
+                 expert_routing="host", expert_policy="lfu"):
         if window < 1:
             raise ValueError("window must be >= 1")
         self.layers = list(layers)
@@ -128,7 +128,8 @@ class LayerStreamer:
             if moe and expert_routing == "device":
                 self.experts = DeviceExpertStreamer(moe, self.device, expert_slots)
             elif moe:
-                self.experts = ExpertStreamer(moe, self.device, expert_slots, self.xfer)
+                self.experts = ExpertStreamer(moe, self.device, expert_slots, self.xfer,
+                                              policy=expert_policy)
         self.tickets = [None] * len(self.layers)
         self.resident_slot = [None] * self.window   # which layer's bytes a slot holds (issued)
         self.fetches = 0
@@ -231,6 +232,9 @@ class RocketModel:
     ``"host"`` reads the routed set back per MoE layer and issues the sends from the host (the
     reference's scheme); ``"device"`` decides residency and copies on the device
     (:class:`~rocketllm_b200.expert_stream.DeviceExpertStreamer`, at most 80 expert slots).
+    ``expert_policy``: which resident expert gives way, ``"lfu"`` (the reference's LFU with aging;
+    host routing only) or ``"lru"``; None takes ``"lfu"`` with host routing and ``"lru"`` (the only
+    one it has) with device routing.
 
     ``kv_cache`` (``rocketllm/base.py:208-411``, ``quant/kv_cache.py:449-503``): ``"int4"`` gives
     every ``generate`` an :class:`~rocketllm_b200.kv_cache.RW4KVCache` whose decode attention reads
@@ -248,7 +252,8 @@ class RocketModel:
     def __init__(self, model_or_path, device="cuda", dtype=torch.bfloat16, vram_budget=None,
                  window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
                  expert_streaming=True, kv_cache="auto", draft_model=None, speculative="auto",
-                 lookahead=4, max_lookahead=8, expert_routing="host", **unused):
+                 lookahead=4, max_lookahead=8, expert_routing="host", expert_policy=None,
+                 **unused):
         from .kv_cache import KV_CHOICES
         from .shards import INDEX
         from .speculative import SPEC_CHOICES
@@ -256,6 +261,12 @@ class RocketModel:
             raise ValueError(f"kv_cache must be one of {', '.join(KV_CHOICES)}, not {kv_cache!r}")
         if expert_routing not in ("host", "device"):
             raise ValueError(f"expert_routing must be 'host' or 'device', not {expert_routing!r}")
+        if expert_policy is None:
+            expert_policy = "lru" if expert_routing == "device" else "lfu"
+        if expert_policy not in ("lfu", "lru") or (expert_routing, expert_policy) == ("device",
+                                                                                   "lfu"):
+            raise ValueError(f"expert_policy {expert_policy!r} with {expert_routing} routing: "
+                             "'lfu' or 'lru' with host routing, 'lru' with device routing")
         if speculative not in SPEC_CHOICES:
             raise ValueError(f"speculative must be one of {', '.join(SPEC_CHOICES)}, not "
                              f"{speculative!r}")
@@ -314,7 +325,8 @@ class RocketModel:
         self.streamer = LayerStreamer(layers, self.device, window=window,
                                       copy_streams=copy_streams, chunk_bytes=chunk_bytes,
                                       prefetching=prefetching, expert_slots=expert_slots,
-                                      pinned=pinned, expert_routing=expert_routing)
+                                      pinned=pinned, expert_routing=expert_routing,
+                                      expert_policy=expert_policy)
 
     @staticmethod
     def _plan_bytes(layer_bytes, window, pinned):

@@ -8,9 +8,10 @@ forward the routing is permuted on the device, the routed set is read back (one 
 per MoE layer, as the reference's ``.tolist()``), the sends of every routed expert that is not
 resident are issued together on the copy streams (``on_router``), the token gather runs meanwhile,
 and the grouped RW4 GEMV waits (device-side) for exactly those sends.  Experts no token routed to
-never cross PCIe.  Slots are recycled least-recently-used, never one holding an expert of the
-running layer; a send into a slot is ordered after all compute already queued, so the previous
-occupant's last reader has finished before its bytes are overwritten.
+never cross PCIe.  Which resident expert gives its slot up is the reference's expert policy, LFU
+with aging (:class:`ExpertSlotCache`), never one holding an expert of the running layer; a send
+into a slot is ordered after all compute already queued, so the previous occupant's last reader has
+finished before its bytes are overwritten.
 
 :class:`DeviceExpertStreamer` does the same with the routing decision on the device: nothing on the
 host reads the routed set (see its docstring).
@@ -70,11 +71,82 @@ def expert_blob_bytes(module):
     return (off + ALIGN - 1) // ALIGN * ALIGN
 
 
+class ExpertSlotCache:
+    """Which device slot holds which expert, and which resident expert gives way to a routed one.
+
+    ``policy="lfu"`` is the reference's expert policy (``rocketllm/memory/cache.py``: ``_touch``
+    434-441, ``_age`` 443-453, ``_expert_victims`` 484-493, ``acquire`` 201-250): each routed use
+    of an expert adds one to its count, every ``aging_interval``-th use halves every count, and the
+    victim is the resident expert with the smallest count, ties to the one admitted first.  The
+    victim is chosen before the incoming expert's use is counted, as ``acquire`` makes room before
+    it touches.  Counts and admission order outlive an eviction, because the expert's pinned host
+    blob stays, as an entry demoted to the reference's host tier keeps them (``cache.py:518-538``).
+    ``policy="lru"`` recycles the least recently used slot instead (the device-routed path's rule).
+    Either way a free slot goes first, lowest index first, and no slot holding an expert of
+    ``protect`` (the running layer's routed set, which one grouped launch reads at once, as the
+    reference's refcount keeps an acquired entry on the device) is ever recycled.
+    """
+
+    def __init__(self, num_slots, policy="lfu", aging_interval=4096):
+        if policy not in ("lfu", "lru"):
+            raise ValueError(f"expert cache policy {policy!r}: 'lfu' or 'lru'")
+        if num_slots < 1:
+            raise ValueError(f"{num_slots} expert slots")
+        self.policy = policy
+        self.aging_interval = max(1, int(aging_interval))
+        self.owner = [None] * num_slots    # slot -> key
+        self.where = {}                    # key -> slot
+        self.uses = {}                     # key -> aged use count (kept across evictions)
+        self.admitted = {}                 # key -> first-admission ordinal (kept likewise)
+        self.last_use = {}                 # key -> ordinal of its latest use
+        self.accesses = 0
+        self.agings = 0
+
+    def _touch(self, key):
+        self.accesses += 1
+        self.last_use[key] = self.accesses
+        self.uses[key] = self.uses.get(key, 0.0) + 1.0
+        if self.accesses % self.aging_interval == 0:
+            for k in self.uses:
+                self.uses[k] *= 0.5
+            self.agings += 1
+
+    def _victim_slot(self, protect):
+        for s, key in enumerate(self.owner):
+            if key is None:
+                return s
+        candidates = [k for k in self.where if k not in protect]
+        if not candidates:
+            raise RuntimeError("no expert slot can be recycled")
+        if self.policy == "lfu":
+            key = min(candidates, key=lambda k: (self.uses[k], self.admitted[k]))
+        else:
+            key = min(candidates, key=self.last_use.__getitem__)
+        return self.where[key]
+
+    def claim(self, key, protect=()):
+        """Count one use of ``key`` and give it a slot: ``(slot, hit, evicted)``.  ``hit`` is True
+        when it was resident already; ``evicted`` is the key that gave the slot up, or None."""
+        if key in self.where:
+            self._touch(key)
+            return self.where[key], True, None
+        s = self._victim_slot(protect)
+        old = self.owner[s]
+        if old is not None:
+            del self.where[old]
+        self.admitted.setdefault(key, len(self.admitted))
+        self.owner[s] = key
+        self.where[key] = s
+        self._touch(key)
+        return s, False, old
+
+
 class ExpertStreamer:
     """Routed experts of ``moe`` (a list of ``(layer_index, experts_module)``) streamed from pinned
-    host blobs into ``num_slots`` device slots through ``xfer`` (a ``WeightTransfer``)."""
+    host blobs into ``num_slots`` device slots through ``xfer`` (a ``WeightTransfer``); which
+    resident expert gives way follows ``policy`` (:class:`ExpertSlotCache`)."""
 
-    def __init__(self, moe, device, num_slots, xfer):
+    def __init__(self, moe, device, num_slots, xfer, policy="lfu", aging_interval=4096):
         self.device = torch.device(device)
         self.xfer = xfer
         self.blobs = {}
@@ -90,9 +162,8 @@ class ExpertStreamer:
         self.slot_bytes = max(b.nbytes for b in self.blobs.values())
         self.slots = [torch.empty(self.slot_bytes, dtype=torch.uint8, device=self.device)
                       for _ in range(min(num_slots, len(self.blobs)))]
-        self.owner = [None] * len(self.slots)     # slot -> (layer, expert)
-        self.where = {}                           # (layer, expert) -> slot
-        self.lru = collections.OrderedDict()      # resident keys, least recently used first
+        self.cache = ExpertSlotCache(len(self.slots), policy, aging_interval)
+        self.where = self.cache.where             # (layer, expert) -> slot
         self.tickets = {}
         self.frequency = collections.Counter()    # routed count per (layer, expert)
         self.fetches = 0
@@ -111,15 +182,6 @@ class ExpertStreamer:
 
     # -- residency ---------------------------------------------------------------------------------
 
-    def _slot_for(self, protect):
-        for s, key in enumerate(self.owner):
-            if key is None:
-                return s
-        for key in self.lru:
-            if key not in protect:
-                return self.where[key]
-        raise RuntimeError("no expert slot can be recycled")
-
     def on_router(self, layer, selected, compute):
         """The layer's router chose ``selected``: issue the sends of the ones not resident, all
         together, ordered after the compute queued on ``compute``.  Returns how many started."""
@@ -128,22 +190,15 @@ class ExpertStreamer:
         for e in selected:
             key = (layer, e)
             self.frequency[key] += 1
-            if key in self.where:
+            s, hit, old = self.cache.claim(key, protect)
+            if hit:
                 self.hits += 1
-                self.lru.move_to_end(key)
                 continue
-            s = self._slot_for(protect)
-            old = self.owner[s]
             if old is not None:
-                del self.where[old]
-                del self.lru[old]
                 self.tickets.pop(old, None)
             blob = self.blobs[key]
             self.tickets[key] = self.xfer.send_buffer(blob.host, out=self.slots[s][:blob.nbytes],
                                                       after=compute)
-            self.owner[s] = key
-            self.where[key] = s
-            self.lru[key] = None
             self.fetches += 1
             self.bytes += blob.nbytes
             started += 1
@@ -172,7 +227,8 @@ class ExpertStreamer:
     def stats(self):
         return {"expert_slots": len(self.slots), "slot_bytes": self.slot_bytes,
                 "fetches": self.fetches, "hits": self.hits, "bytes": self.bytes,
-                "resident": len(self.where)}
+                "resident": len(self.where), "policy": self.cache.policy,
+                "agings": self.cache.agings}
 
 
 def streamed_experts_forward(self, hidden_states, top_k_index, top_k_weights):
@@ -216,9 +272,11 @@ class DeviceExpertStreamer:
     stream without the host waiting: permute -> residency kernel (claims resident slots, assigns
     free / least-recently-used ones to the others, lists them) -> copy kernel (reads the listed
     blobs over PCIe into their slots) -> gather -> grouped GEMVs that reach each expert's weights
-    through its slot index -> combine.  Policy: the same least-recently-used cache as
-    :class:`ExpertStreamer` (a free slot first, never a slot the running layer's routed experts
-    hold); ties between slots last used in the same call go to the lower slot index.
+    through its slot index -> combine.  Policy: least recently used (``ExpertSlotCache``'s
+    ``"lru"``: a free slot first, never a slot the running layer's routed experts hold); ties
+    between slots last used in the same call go to the lower slot index.  This differs from the
+    host-routed :class:`ExpertStreamer`, whose default is the reference's LFU with aging: the
+    one-thread residency kernel keeps a last-use stamp per slot, not an aged count per expert.
     """
 
     MAX_SLOTS = 80
@@ -283,7 +341,7 @@ class DeviceExpertStreamer:
         hits, fetches = self.counters.tolist()
         return {"expert_slots": self.owner.numel(), "slot_bytes": self.blob_bytes,
                 "fetches": fetches, "hits": hits, "bytes": fetches * self.blob_bytes,
-                "resident": int((self.owner >= 0).sum()), "routing": "device"}
+                "resident": int((self.owner >= 0).sum()), "routing": "device", "policy": "lru"}
 
     def close(self):
         self.gate_up_maps.close()
