@@ -169,6 +169,18 @@ int rw4_moe_combine(const void* y_perm_bf16, const int32_t* inv, const int64_t* 
  * / copy_slot int32 [E], ncopy int32 [1]).  State: where int32 [layers*E], owner int32 [S],
  * stamp int32 [S], clock int32 [1] (all initialised to -1 / -1 / 0 / 0 by the caller), counters
  * uint64 [2] (hits, fetches).
+ * rw4_expert_residency_lfu: the same step under the reference's expert eviction, LFU with aging
+ * (rocketllm/memory/cache.py:434-493), where rw4_expert_residency recycles least recently used:
+ * routed experts in ascending order; a resident one is a hit; another takes a free slot, else the
+ * slot of the resident expert with the smallest aged use count (ties: admitted first), never one
+ * holding this layer's routed experts; then its use is counted and every aging_interval-th use
+ * halves every count.  State (keys = layers*E >= (layer+1)*E): where int32 [keys] (-1), owner
+ * int32 [S] (-1), uses double [keys] (0), admitted int32 [keys] (-1), state int64 [3] (0: uses
+ * counted, experts admitted, agings), counters uint64 [2].  A routed expert that finds no slot
+ * sets RW4_DEVERR_SLOT.
+ * rw4_expert_residency_lfu_host: that step on HOST tables, on the calling thread (a host-routed
+ * caller's form of the policy; the same compiled definition as the kernel's); RW4_EINVAL if a
+ * routed expert finds no slot.
  * rw4_expert_copy: copy every listed expert's blob (host_blobs uint64 [layers*E]: DEVICE-visible
  * addresses of mapped pinned host blobs, each blob_bytes long) into its slot (slots + s *
  * slot_bytes); grid ctas_per_expert x E.
@@ -187,6 +199,16 @@ int rw4_expert_residency(const int32_t* offsets, int32_t E, int32_t layer, int32
                          int32_t* owner, int32_t* stamp, int32_t S, int32_t* clock,
                          int32_t* slot_of, int32_t* copy_expert, int32_t* copy_slot,
                          int32_t* ncopy, uint64_t* counters, void* stream);
+int rw4_expert_residency_lfu(const int32_t* offsets, int32_t E, int32_t layer, int32_t keys,
+                             int32_t* where, int32_t* owner, int32_t S, double* uses,
+                             int32_t* admitted, int64_t* state, int64_t aging_interval,
+                             int32_t* slot_of, int32_t* copy_expert, int32_t* copy_slot,
+                             int32_t* ncopy, uint64_t* counters, void* stream);
+int rw4_expert_residency_lfu_host(const int32_t* offsets, int32_t E, int32_t layer, int32_t keys,
+                                  int32_t* where, int32_t* owner, int32_t S, double* uses,
+                                  int32_t* admitted, int64_t* state, int64_t aging_interval,
+                                  int32_t* slot_of, int32_t* copy_expert, int32_t* copy_slot,
+                                  int32_t* ncopy, uint64_t* counters);
 int rw4_expert_copy(const int32_t* copy_expert, const int32_t* copy_slot, const int32_t* ncopy,
                     int32_t layer, int32_t E, const uint64_t* host_blobs, int64_t blob_bytes,
                     uint8_t* slots, int64_t slot_bytes, int32_t S, int32_t ctas_per_expert,

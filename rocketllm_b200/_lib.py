@@ -63,6 +63,14 @@ SIGNATURES = {
     "rw4_expert_residency": (ctypes.c_int, [_c_void_p, _i32, _i32, _c_void_p, _c_void_p,
                                             _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p,
                                             _c_void_p, _c_void_p, _c_void_p, _c_void_p]),
+    "rw4_expert_residency_lfu": (ctypes.c_int, [_c_void_p, _i32, _i32, _i32, _c_void_p,
+                                                _c_void_p, _i32, _c_void_p, _c_void_p, _c_void_p,
+                                                _i64, _c_void_p, _c_void_p, _c_void_p, _c_void_p,
+                                                _c_void_p, _c_void_p]),
+    "rw4_expert_residency_lfu_host": (ctypes.c_int, [_c_void_p, _i32, _i32, _i32, _c_void_p,
+                                                     _c_void_p, _i32, _c_void_p, _c_void_p,
+                                                     _c_void_p, _i64, _c_void_p, _c_void_p,
+                                                     _c_void_p, _c_void_p, _c_void_p]),
     "rw4_expert_copy": (ctypes.c_int, [_c_void_p, _c_void_p, _c_void_p, _i32, _i32, _c_void_p,
                                        _i64, _c_void_p, _i64, _i32, _i32, _c_void_p]),
     "rw4_host_ptr_device": (ctypes.c_int, [_c_void_p, ctypes.POINTER(_c_void_p)]),

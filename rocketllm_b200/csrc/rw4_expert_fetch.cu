@@ -1,6 +1,7 @@
 // Device-side routing into the expert cache: after the router, a residency kernel decides which
-// routed experts are resident, assigns cache slots to the others (least recently used first, never
-// a slot this layer's routed experts hold) and lists them; a copy kernel then moves exactly those
+// routed experts are resident, assigns cache slots to the others (least recently used first, or by
+// the reference's LFU with aging in the _lfu form; never a slot this layer's routed experts hold)
+// and lists them; a copy kernel then moves exactly those
 // experts' blobs from mapped pinned host memory into their slots over PCIe.  The grouped GEMV finds
 // each expert through the slot index the residency kernel wrote (rw4_moe_grouped_slots), so no
 // host step waits for the routing -- the reference reads the routed set back to the host once per
@@ -9,10 +10,12 @@
 //
 // State (device, owned by the caller): where[L*E] (slot of layer l's expert e, or -1), owner[S]
 // (key l*E + e held by a slot, or -1), stamp[S] (use clock), clock[1], counters[2] (hits,
-// fetches).
+// fetches); the LFU form keeps uses[L*E], admitted[L*E] and state[3] instead of stamp and clock
+// (rw4_residency.cuh).
 #include <cuda_runtime.h>
 
 #include "rw4_common.cuh"
+#include "rw4_residency.cuh"
 #include "rw4_tma.cuh"
 
 namespace {
@@ -76,6 +79,25 @@ __global__ void expert_residency_kernel(const int32_t* __restrict__ offsets, int
   ncopy[0] = n;
   counters[0] += hits;
   counters[1] += fetches;
+}
+
+// The same step under the reference's LFU with aging (rw4_residency.cuh); one thread.
+__global__ void expert_residency_lfu_kernel(const int32_t* __restrict__ offsets, int E, int layer,
+                                            int keys, int32_t* __restrict__ where,
+                                            int32_t* __restrict__ owner, int S,
+                                            double* __restrict__ uses,
+                                            int32_t* __restrict__ admitted,
+                                            int64_t* __restrict__ state, int64_t aging_interval,
+                                            int32_t* __restrict__ slot_of,
+                                            int32_t* __restrict__ copy_expert,
+                                            int32_t* __restrict__ copy_slot,
+                                            int32_t* __restrict__ ncopy,
+                                            uint64_t* __restrict__ counters,
+                                            unsigned int* status) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  if (lfu_residency_step(offsets, E, layer, keys, where, owner, S, uses, admitted, state,
+                         aging_interval, slot_of, copy_expert, copy_slot, ncopy, counters))
+    atomicOr(status, RW4_DEVERR_SLOT);
 }
 
 // grid (chunks, E): block (c, i) copies chunk c of the i-th listed expert (if there is one);
@@ -142,6 +164,63 @@ extern "C" int rw4_expert_residency(const int32_t* offsets, int32_t E, int32_t l
       offsets, E, layer, where, owner, stamp, S, clock, slot_of, copy_expert, copy_slot, ncopy,
       reinterpret_cast<unsigned long long*>(counters), status);
   return launch_status("rw4_expert_residency launch");
+}
+
+namespace {
+
+int check_lfu_args(const char* who, const int32_t* offsets, int32_t E, int32_t layer, int32_t keys,
+                   const int32_t* where, const int32_t* owner, int32_t S, const double* uses,
+                   const int32_t* admitted, const int64_t* state, int64_t aging_interval,
+                   const int32_t* slot_of, const int32_t* copy_expert, const int32_t* copy_slot,
+                   const int32_t* ncopy, const uint64_t* counters) {
+  if (E < 1 || E > 4096 || S < 1 || layer < 0 || aging_interval < 1 ||
+      (int64_t)(layer + 1) * E > keys)
+    return fail(RW4_EINVAL, "%s: E=%d S=%d layer=%d keys=%d aging_interval=%lld", who, E, S, layer,
+                keys, (long long)aging_interval);
+  if (!offsets || !where || !owner || !uses || !admitted || !state || !slot_of || !copy_expert ||
+      !copy_slot || !ncopy || !counters)
+    return fail(RW4_EINVAL, "%s: null pointer", who);
+  return RW4_OK;
+}
+
+}  // namespace
+
+extern "C" int rw4_expert_residency_lfu(const int32_t* offsets, int32_t E, int32_t layer,
+                                        int32_t keys, int32_t* where, int32_t* owner, int32_t S,
+                                        double* uses, int32_t* admitted, int64_t* state,
+                                        int64_t aging_interval, int32_t* slot_of,
+                                        int32_t* copy_expert, int32_t* copy_slot, int32_t* ncopy,
+                                        uint64_t* counters, void* stream) {
+  const int st = check_lfu_args("rw4_expert_residency_lfu", offsets, E, layer, keys, where, owner,
+                                S, uses, admitted, state, aging_interval, slot_of, copy_expert,
+                                copy_slot, ncopy, counters);
+  if (st) return st;
+  unsigned int* status = device_status_ptr();
+  if (!status) return fail(RW4_ECUDA, "rw4_expert_residency_lfu: device status word unavailable");
+  expert_residency_lfu_kernel<<<1, 32, 0, as_stream(stream)>>>(
+      offsets, E, layer, keys, where, owner, S, uses, admitted, state, aging_interval, slot_of,
+      copy_expert, copy_slot, ncopy, counters, status);
+  return launch_status("rw4_expert_residency_lfu launch");
+}
+
+extern "C" int rw4_expert_residency_lfu_host(const int32_t* offsets, int32_t E, int32_t layer,
+                                             int32_t keys, int32_t* where, int32_t* owner,
+                                             int32_t S, double* uses, int32_t* admitted,
+                                             int64_t* state, int64_t aging_interval,
+                                             int32_t* slot_of, int32_t* copy_expert,
+                                             int32_t* copy_slot, int32_t* ncopy,
+                                             uint64_t* counters) {
+  const int st = check_lfu_args("rw4_expert_residency_lfu_host", offsets, E, layer, keys, where,
+                                owner, S, uses, admitted, state, aging_interval, slot_of,
+                                copy_expert, copy_slot, ncopy, counters);
+  if (st) return st;
+  const int unplaced = lfu_residency_step(offsets, E, layer, keys, where, owner, S, uses, admitted,
+                                          state, aging_interval, slot_of, copy_expert, copy_slot,
+                                          ncopy, counters);
+  if (unplaced)
+    return fail(RW4_EINVAL, "rw4_expert_residency_lfu_host: %d routed experts of layer %d found no "
+                "slot (%d slots, all held by the layer's routed experts)", unplaced, layer, S);
+  return RW4_OK;
 }
 
 extern "C" int rw4_expert_copy(const int32_t* copy_expert, const int32_t* copy_slot,

@@ -92,7 +92,7 @@ class LayerStreamer:
 
     def __init__(self, layers, device, window=2, copy_streams=2, chunk_bytes=16 << 20,
                  prefetching=True, expert_slots=None, blobs=None, pinned=0,
-                 expert_routing="host", expert_policy="lfu"):
+                 expert_routing="host", expert_policy=None):
         if window < 1:
             raise ValueError("window must be >= 1")
         self.layers = list(layers)
@@ -126,10 +126,11 @@ class LayerStreamer:
             moe = [(i, m) for i, layer in enumerate(self.layers) for m in layer.modules()
                    if is_rw4_experts(m)]
             if moe and expert_routing == "device":
-                self.experts = DeviceExpertStreamer(moe, self.device, expert_slots)
+                self.experts = DeviceExpertStreamer(moe, self.device, expert_slots,
+                                                    policy=expert_policy or "lru")
             elif moe:
                 self.experts = ExpertStreamer(moe, self.device, expert_slots, self.xfer,
-                                              policy=expert_policy)
+                                              policy=expert_policy or "lfu")
         self.tickets = [None] * len(self.layers)
         self.resident_slot = [None] * self.window   # which layer's bytes a slot holds (issued)
         self.fetches = 0
@@ -232,9 +233,8 @@ class RocketModel:
     ``"host"`` reads the routed set back per MoE layer and issues the sends from the host (the
     reference's scheme); ``"device"`` decides residency and copies on the device
     (:class:`~rocketllm_b200.expert_stream.DeviceExpertStreamer`, at most 80 expert slots).
-    ``expert_policy``: which resident expert gives way, ``"lfu"`` (the reference's LFU with aging;
-    host routing only) or ``"lru"``; None takes ``"lfu"`` with host routing and ``"lru"`` (the only
-    one it has) with device routing.
+    ``expert_policy``: which resident expert gives way, ``"lfu"`` (the reference's LFU with aging)
+    or ``"lru"``; None takes ``"lfu"`` with host routing and ``"lru"`` with device routing.
 
     ``kv_cache`` (``rocketllm/base.py:208-411``, ``quant/kv_cache.py:449-503``): ``"int4"`` gives
     every ``generate`` an :class:`~rocketllm_b200.kv_cache.RW4KVCache` whose decode attention reads
@@ -263,10 +263,8 @@ class RocketModel:
             raise ValueError(f"expert_routing must be 'host' or 'device', not {expert_routing!r}")
         if expert_policy is None:
             expert_policy = "lru" if expert_routing == "device" else "lfu"
-        if expert_policy not in ("lfu", "lru") or (expert_routing, expert_policy) == ("device",
-                                                                                   "lfu"):
-            raise ValueError(f"expert_policy {expert_policy!r} with {expert_routing} routing: "
-                             "'lfu' or 'lru' with host routing, 'lru' with device routing")
+        if expert_policy not in ("lfu", "lru"):
+            raise ValueError(f"expert_policy must be 'lfu' or 'lru', not {expert_policy!r}")
         if speculative not in SPEC_CHOICES:
             raise ValueError(f"speculative must be one of {', '.join(SPEC_CHOICES)}, not "
                              f"{speculative!r}")

@@ -81,7 +81,7 @@ class ExpertSlotCache:
     victim is chosen before the incoming expert's use is counted, as ``acquire`` makes room before
     it touches.  Counts and admission order outlive an eviction, because the expert's pinned host
     blob stays, as an entry demoted to the reference's host tier keeps them (``cache.py:518-538``).
-    ``policy="lru"`` recycles the least recently used slot instead (the device-routed path's rule).
+    ``policy="lru"`` recycles the least recently used slot instead (the device-routed default).
     Either way a free slot goes first, lowest index first, and no slot holding an expert of
     ``protect`` (the running layer's routed set, which one grouped launch reads at once, as the
     reference's refcount keeps an acquired entry on the device) is ever recycled.
@@ -272,16 +272,21 @@ class DeviceExpertStreamer:
     stream without the host waiting: permute -> residency kernel (claims resident slots, assigns
     free / least-recently-used ones to the others, lists them) -> copy kernel (reads the listed
     blobs over PCIe into their slots) -> gather -> grouped GEMVs that reach each expert's weights
-    through its slot index -> combine.  Policy: least recently used (``ExpertSlotCache``'s
-    ``"lru"``: a free slot first, never a slot the running layer's routed experts hold); ties
-    between slots last used in the same call go to the lower slot index.  This differs from the
-    host-routed :class:`ExpertStreamer`, whose default is the reference's LFU with aging: the
-    one-thread residency kernel keeps a last-use stamp per slot, not an aged count per expert.
+    through its slot index -> combine.  ``policy``: ``"lru"`` (least recently used: a free slot
+    first, never a slot the running layer's routed experts hold; ties between slots last used in
+    the same call go to the lower slot index) or ``"lfu"``, the reference's LFU with aging, the
+    same decisions as :class:`ExpertSlotCache` with whole-set protection (an aged count and an
+    admission ordinal per expert in device tables, ``rw4_expert_residency_lfu``).
     """
 
     MAX_SLOTS = 80
 
-    def __init__(self, moe, device, num_slots, ctas_per_expert=64):
+    def __init__(self, moe, device, num_slots, ctas_per_expert=64, policy="lru",
+                 aging_interval=4096):
+        if policy not in ("lfu", "lru"):
+            raise ValueError(f"expert cache policy {policy!r}: 'lfu' or 'lru'")
+        self.policy = policy
+        self.aging_interval = max(1, int(aging_interval))
         self.device = torch.device(device)
         counts = {m.gate_up_proj_packed.shape[0] for _, m in moe}
         shapes = {(tuple(m.gate_up_proj_packed.shape[1:]), tuple(m.down_proj_packed.shape[1:]))
@@ -320,6 +325,11 @@ class DeviceExpertStreamer:
         self.owner = torch.full((slots,), -1, **i32)
         self.stamp = torch.zeros(slots, **i32)
         self.clock = torch.zeros(1, **i32)
+        keys = len(moe) * e_count
+        self.uses = torch.zeros(keys if policy == "lfu" else 0, dtype=torch.float64,
+                                device=self.device)
+        self.admitted = torch.full((keys if policy == "lfu" else 0,), -1, **i32)
+        self.lfu_state = torch.zeros(3, dtype=torch.int64, device=self.device)
         self.counters = torch.zeros(2, dtype=torch.int64, device=self.device)
         self.slot_of = torch.empty(e_count, **i32)
         self.copy_expert = torch.empty(e_count, **i32)
@@ -341,7 +351,8 @@ class DeviceExpertStreamer:
         hits, fetches = self.counters.tolist()
         return {"expert_slots": self.owner.numel(), "slot_bytes": self.blob_bytes,
                 "fetches": fetches, "hits": hits, "bytes": fetches * self.blob_bytes,
-                "resident": int((self.owner >= 0).sum()), "routing": "device", "policy": "lru"}
+                "resident": int((self.owner >= 0).sum()), "routing": "device",
+                "policy": self.policy, "agings": int(self.lfu_state[2])}
 
     def close(self):
         self.gate_up_maps.close()
@@ -361,8 +372,13 @@ def device_streamed_experts_forward(self, hidden_states, top_k_index, top_k_weig
     if w.dtype not in (torch.float32, torch.bfloat16):
         w = w.float()
     perm, inv, offsets = kernels.moe_permute(idx, st.num_experts)
-    kernels.expert_residency(offsets, li, st.where, st.owner, st.stamp, st.clock, st.slot_of,
-                             st.copy_expert, st.copy_slot, st.ncopy, st.counters)
+    if st.policy == "lfu":
+        kernels.expert_residency_lfu(offsets, li, st.where, st.owner, st.uses, st.admitted,
+                                     st.lfu_state, st.aging_interval, st.slot_of, st.copy_expert,
+                                     st.copy_slot, st.ncopy, st.counters)
+    else:
+        kernels.expert_residency(offsets, li, st.where, st.owner, st.stamp, st.clock, st.slot_of,
+                                 st.copy_expert, st.copy_slot, st.ncopy, st.counters)
     kernels.expert_copy(st.copy_expert, st.copy_slot, st.ncopy, li, st.num_experts, st.host_ptrs,
                         st.blob_bytes, st.slots, st.blob_bytes, st.ctas_per_expert)
     rows = 1 if t == 1 else t * k

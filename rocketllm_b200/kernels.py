@@ -263,6 +263,21 @@ def expert_residency(offsets, layer, where, owner, stamp, clock, slot_of, copy_e
               ncopy.data_ptr(), counters.data_ptr(), _stream())
 
 
+def expert_residency_lfu(offsets, layer, where, owner, uses, admitted, state, aging_interval,
+                         slot_of, copy_expert, copy_slot, ncopy, counters):
+    """Device-side residency step of one MoE layer under LFU with aging
+    (``rw4_expert_residency_lfu``); ``uses`` float64, ``state`` int64 [3]."""
+    _require_cuda(offsets, where, owner, uses, admitted, state, slot_of, copy_expert, copy_slot,
+                  ncopy, counters)
+    if uses.dtype != torch.float64 or state.dtype != torch.int64 or state.numel() != 3:
+        raise TypeError("uses must be float64 and state int64 [3]")
+    _lib.call("rw4_expert_residency_lfu", offsets.data_ptr(), offsets.numel() - 1, int(layer),
+              where.numel(), where.data_ptr(), owner.data_ptr(), owner.numel(), uses.data_ptr(),
+              admitted.data_ptr(), state.data_ptr(), int(aging_interval), slot_of.data_ptr(),
+              copy_expert.data_ptr(), copy_slot.data_ptr(), ncopy.data_ptr(), counters.data_ptr(),
+              _stream())
+
+
 def expert_copy(copy_expert, copy_slot, ncopy, layer, num_experts, host_blobs, blob_bytes, slots,
                 slot_bytes, ctas_per_expert=64):
     """Copy the listed experts' mapped host blobs into their slots (``rw4_expert_copy``)."""

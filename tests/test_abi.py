@@ -93,6 +93,13 @@ def test_kv_and_expert_routing_entry_points_reject_bad_arguments():
     assert lib.rw4_moe_grouped_slots(p, p, 8, 1, None, p, p, None) == _lib.RW4_EINVAL
     assert lib.rw4_expert_residency(p, 0, 0, p, p, p, 8, p, p, p, p, p, p, None) \
         == _lib.RW4_EINVAL
+    lfu = lib.rw4_expert_residency_lfu
+    assert lfu(p, 8, 3, 24, p, p, 8, p, p, p, 4096, p, p, p, p, p, None) \
+        == _lib.RW4_EINVAL                                    # layer 3 of a 3-layer table
+    assert lfu(p, 8, 0, 24, p, p, 8, p, p, p, 0, p, p, p, p, p, None) \
+        == _lib.RW4_EINVAL                                    # aging interval 0
+    assert lfu(p, 8, 0, 24, p, p, 8, None, p, p, 4096, p, p, p, p, p, None) \
+        == _lib.RW4_EINVAL                                    # no count table
     # a blob larger than a slot, a blob that is not whole 16-byte vectors
     assert lib.rw4_expert_copy(p, p, p, 0, 8, p, 1 << 21, p, 1 << 20, 4, 8, None) \
         == _lib.RW4_EINVAL

@@ -193,3 +193,103 @@ def test_on_router_sends_only_what_is_missing_into_the_slot_it_was_given():
     assert s.where[(1, 1)] == sent[1 * 4 + 1] and s.where[(0, 2)] == sent[2]
     assert (0, 0) not in s.tickets and s.fetches == 4 and s.bytes == 4 * 64
     assert s.frequency[(0, 0)] == 2
+
+
+class _LfuTables:
+    """Host tables for ``rw4_expert_residency_lfu_host``: the residency kernel's own step compiled
+    for the host (one definition, ``csrc/rw4_residency.cuh``)."""
+
+    def __init__(self, layers, experts, slots, aging):
+        keys = layers * experts
+        self.E, self.aging = experts, aging
+        self.where = torch.full((keys,), -1, dtype=torch.int32)
+        self.owner = torch.full((slots,), -1, dtype=torch.int32)
+        self.uses = torch.zeros(keys, dtype=torch.float64)
+        self.admitted = torch.full((keys,), -1, dtype=torch.int32)
+        self.state = torch.zeros(3, dtype=torch.int64)
+        self.counters = torch.zeros(2, dtype=torch.int64)
+        self.slot_of = torch.empty(experts, dtype=torch.int32)
+        self.copy_expert = torch.empty(experts, dtype=torch.int32)
+        self.copy_slot = torch.empty(experts, dtype=torch.int32)
+        self.ncopy = torch.zeros(1, dtype=torch.int32)
+
+    def step(self, layer, routed):
+        from rocketllm_b200 import _lib
+        counts = torch.zeros(self.E, dtype=torch.int32)
+        counts[list(routed)] = 1
+        offsets = torch.zeros(self.E + 1, dtype=torch.int32)
+        offsets[1:] = torch.cumsum(counts, 0)
+        _lib.call("rw4_expert_residency_lfu_host", offsets.data_ptr(), self.E, int(layer),
+                  self.where.numel(), self.where.data_ptr(), self.owner.data_ptr(),
+                  self.owner.numel(), self.uses.data_ptr(), self.admitted.data_ptr(),
+                  self.state.data_ptr(), self.aging, self.slot_of.data_ptr(),
+                  self.copy_expert.data_ptr(), self.copy_slot.data_ptr(), self.ncopy.data_ptr(),
+                  self.counters.data_ptr())
+        n = int(self.ncopy[0])
+        return (self.slot_of.tolist(),
+                list(zip(self.copy_expert.tolist()[:n], self.copy_slot.tolist()[:n])))
+
+
+def _same_step(t, cache, layer, routed):
+    """One firing through the compiled step and through ExpertSlotCache: same slots, same copies,
+    bit-identical counts and admission order."""
+    slot_of, copies = t.step(layer, routed)
+    protect = {(layer, e) for e in routed}
+    want_copies = []
+    for e in routed:
+        s, hit, _ = cache.claim((layer, e), protect)
+        if not hit:
+            want_copies.append((e, s))
+    assert copies == want_copies
+    assert [slot_of[e] for e in routed] == [cache.where[(layer, e)] for e in routed]
+    assert all(slot_of[e] == -1 for e in range(t.E) if e not in routed)
+    keys = t.where.numel()
+    assert t.owner.tolist() == [-1 if k is None else k[0] * t.E + k[1] for k in cache.owner]
+    uses = [cache.uses.get((k // t.E, k % t.E), 0.0) for k in range(keys)]
+    assert t.uses.tolist() == uses                                  # exact: same halvings
+    assert t.admitted.tolist() == [cache.admitted.get((k // t.E, k % t.E), -1)
+                                   for k in range(keys)]
+    assert t.state.tolist() == [cache.accesses, len(cache.admitted), cache.agings]
+
+
+def test_the_residency_kernels_lfu_step_is_the_policy_on_the_golden_traces(golden):
+    for name in golden["cases"]:
+        layers, experts, top_k, slots, aging = (int(x) for x in golden[f"{name}.params"])
+        t = _LfuTables(layers, experts, slots, aging)
+        cache = ExpertSlotCache(slots, "lfu", aging)
+        hits = 0
+        for layer, sel in zip(golden[f"{name}.layer"], golden[f"{name}.selected"]):
+            before = int(t.counters[0])
+            _same_step(t, cache, int(layer), [int(e) for e in sel])
+            hits += int(t.counters[0]) - before
+        _, resident, _ = replay(golden, str(name), "lfu", whole_set=True)
+        rows = np.zeros(layers * experts, dtype=np.uint8)
+        rows[[k for k in t.owner.tolist() if k >= 0]] = 1
+        np.testing.assert_array_equal(rows, resident[-1])
+        assert hits >= int(golden[f"{name}.hits"].sum())
+
+
+@pytest.mark.parametrize("seed", range(4))
+def test_the_residency_kernels_lfu_step_is_the_policy_on_random_routings(seed):
+    rng = np.random.default_rng(seed)
+    layers, experts = 3, int(rng.integers(4, 17))
+    slots = int(rng.integers(experts, layers * experts + 3))
+    aging = int(rng.integers(1, 40))
+    t = _LfuTables(layers, experts, slots, aging)
+    cache = ExpertSlotCache(slots, "lfu", aging)
+    for _ in range(120):
+        layer = int(rng.integers(0, layers))
+        k = int(rng.integers(1, experts + 1))
+        routed = sorted(rng.choice(experts, size=k, replace=False).tolist())
+        _same_step(t, cache, layer, routed)
+
+
+def test_the_host_lfu_step_rejects_what_it_cannot_place():
+    """Three slots, all held by the layer's routed experts, and a fourth routed expert: no slot."""
+    from rocketllm_b200 import _lib
+    t = _LfuTables(2, 4, 3, 16)
+    t.step(1, [0, 1, 2])
+    with pytest.raises(_lib.RW4Error, match="found no slot"):
+        t.step(1, [0, 1, 2, 3])
+    with pytest.raises(_lib.RW4Error, match="RW4_EINVAL"):
+        t.step(2, [0])                                   # layer 2 of a 2-layer table

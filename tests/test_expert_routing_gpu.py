@@ -89,6 +89,55 @@ def test_residency_kernel_follows_the_policy(cuda, slots):
     assert kernels.device_status() == 0
 
 
+@pytest.mark.parametrize("slots,aging", [(8, 5), (13, 4096), (24, 3)])
+def test_lfu_residency_kernel_follows_the_policy(cuda, slots, aging):
+    """The LFU-with-aging step on the device makes the host cache's decisions (whole routed set
+    protected), with bit-identical aged counts."""
+    from rocketllm_b200.expert_stream import ExpertSlotCache
+    n_exp, layers, steps = 8, 4, 60
+    rng = np.random.default_rng(100 + slots)
+    i32 = dict(dtype=torch.int32, device=cuda)
+    keys = layers * n_exp
+    where = torch.full((keys,), -1, **i32)
+    owner = torch.full((slots,), -1, **i32)
+    uses = torch.zeros(keys, dtype=torch.float64, device=cuda)
+    admitted = torch.full((keys,), -1, **i32)
+    state = torch.zeros(3, dtype=torch.int64, device=cuda)
+    counters = torch.zeros(2, dtype=torch.int64, device=cuda)
+    slot_of = torch.empty(n_exp, **i32)
+    ce = torch.empty(n_exp, **i32)
+    cs = torch.empty(n_exp, **i32)
+    nc = torch.zeros(1, **i32)
+    cache = ExpertSlotCache(slots, "lfu", aging)
+    r_hits = r_fetch = 0
+    for step in range(steps):
+        layer = int(rng.integers(0, layers))
+        t = int(rng.integers(1, 4))
+        idx = np.stack([rng.choice(n_exp, 2, replace=False) for _ in range(t)])
+        counts = np.bincount(idx.reshape(-1), minlength=n_exp)
+        offsets = torch.tensor(np.concatenate([[0], np.cumsum(counts)]), **i32)
+        kernels.expert_residency_lfu(offsets, layer, where, owner, uses, admitted, state, aging,
+                                     slot_of, ce, cs, nc, counters)
+        routed = [e for e in range(n_exp) if counts[e]]
+        protect = {(layer, e) for e in routed}
+        ref_copies = []
+        for e in routed:
+            s, hit, _ = cache.claim((layer, e), protect)
+            r_hits += hit
+            if not hit:
+                ref_copies.append((e, s))
+        r_fetch += len(ref_copies)
+        n = int(nc.item())
+        got = [s if counts[e] else -1 for e, s in enumerate(slot_of.tolist())]
+        assert got == [cache.where[(layer, e)] if counts[e] else -1 for e in range(n_exp)], step
+        assert list(zip(ce.tolist()[:n], cs.tolist()[:n])) == ref_copies, step
+    assert owner.tolist() == [-1 if k is None else k[0] * n_exp + k[1] for k in cache.owner]
+    assert uses.tolist() == [cache.uses.get((k // n_exp, k % n_exp), 0.0) for k in range(keys)]
+    assert state.tolist() == [cache.accesses, len(cache.admitted), cache.agings]
+    assert counters.tolist() == [r_hits, r_fetch]
+    assert kernels.device_status() == 0
+
+
 def test_copy_kernel_lands_listed_blobs(cuda):
     n_exp, blob = 4, 1 << 20
     host = [torch.randint(0, 256, (blob,), dtype=torch.uint8).pin_memory() for _ in range(n_exp)]
@@ -108,13 +157,13 @@ def test_copy_kernel_lands_listed_blobs(cuda):
         kernels.host_ptr_device(torch.zeros(16, dtype=torch.uint8).data_ptr())  # pageable
 
 
-@pytest.mark.parametrize("slots", [E, 2 * E])
-def test_device_routed_experts_equal_resident(checkpoint, slots):  # noqa: F811
+@pytest.mark.parametrize("slots,policy", [(E, "lru"), (2 * E, "lru"), (2 * E, "lfu")])
+def test_device_routed_experts_equal_resident(checkpoint, slots, policy):  # noqa: F811
     ids = torch.randint(0, 2048, (1, 12), generator=torch.Generator().manual_seed(4)).cuda()
     resident = AutoModel.from_pretrained(checkpoint)
     budget = budget_for(resident.model, slots)
     streamed = RocketModel(checkpoint, vram_budget=budget, window=1, kv_cache="fp16",
-                           expert_routing="device")
+                           expert_routing="device", expert_policy=policy)
     ex = streamed.streamer.experts
     assert type(ex).__name__ == "DeviceExpertStreamer"
     with torch.no_grad():
@@ -124,5 +173,6 @@ def test_device_routed_experts_equal_resident(checkpoint, slots):  # noqa: F811
     assert torch.equal(a, b)
     st = ex.stats()
     assert st["routing"] == "device" and st["fetches"] > 0 and st["resident"] <= st["expert_slots"]
+    assert st["policy"] == policy
     assert kernels.device_status() == 0
     streamed.close()
