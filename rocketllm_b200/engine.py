@@ -235,6 +235,8 @@ class RocketModel:
     (:class:`~rocketllm_b200.expert_stream.DeviceExpertStreamer`, at most 80 expert slots).
     ``expert_policy``: which resident expert gives way, ``"lfu"`` (the reference's LFU with aging)
     or ``"lru"``; None takes ``"lfu"`` with host routing and ``"lru"`` with device routing.
+    ``io_workers``: threads that read each layer's blob from a layer-shard directory (adjacent,
+    byte-balanced stretches of the blob: the reference loader's ``io_workers``).
 
     ``kv_cache`` (``rocketllm/base.py:208-411``, ``quant/kv_cache.py:449-503``): ``"int4"`` gives
     every ``generate`` an :class:`~rocketllm_b200.kv_cache.RW4KVCache` whose decode attention reads
@@ -253,7 +255,7 @@ class RocketModel:
                  window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
                  expert_streaming=True, kv_cache="auto", draft_model=None, speculative="auto",
                  lookahead=4, max_lookahead=8, expert_routing="host", expert_policy=None,
-                 **unused):
+                 io_workers=4, **unused):
         from .kv_cache import KV_CHOICES
         from .shards import INDEX
         from .speculative import SPEC_CHOICES
@@ -278,7 +280,7 @@ class RocketModel:
         if isinstance(model_or_path, (str, os.PathLike)) and \
                 os.path.exists(os.path.join(str(model_or_path), INDEX)):
             self._init_from_shards(str(model_or_path), device, dtype, vram_budget, window,
-                                   prefetching, copy_streams, chunk_bytes)
+                                   prefetching, copy_streams, chunk_bytes, io_workers)
             return
         if isinstance(model_or_path, (str, os.PathLike)):
             from transformers import AutoModelForCausalLM
@@ -343,14 +345,15 @@ class RocketModel:
         return pinned
 
     def _init_from_shards(self, root, device, dtype, vram_budget, window, prefetching,
-                          copy_streams, chunk_bytes):
+                          copy_streams, chunk_bytes, io_workers=1):
         """Layer shards written by ``shards.split_rw4_layers``: the model is built on the meta
         device, the non-layer tensors come from ``rest.safetensors`` straight to the device, and
-        each layer's blob is read from its file into pinned memory in one positioned read (no
-        CPU copy of the model ever exists).  Routed experts stream with their layer."""
+        each layer's blob is read from its file into pinned memory by positioned reads over
+        ``io_workers`` threads (no CPU copy of the model ever exists).  Routed experts stream with
+        their layer."""
         from .shards import LayerShardReader, _materialize_rest, build_skeleton
         self.device = torch.device(device)
-        reader = LayerShardReader(root)
+        reader = LayerShardReader(root, io_workers=io_workers)
         self.shards = reader
         model = build_skeleton(root, dtype).eval()
         self.model = model
@@ -375,6 +378,7 @@ class RocketModel:
                 slot = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
                 slot.copy_(staging[:nbytes])   # synchronous: the staging buffer is reused
                 _bind(_LayerBlob(None, resolve(layer, entries), nbytes), slot)
+            reader.close()
             return
         blobs = []
         for i, layer in enumerate(layers):
@@ -382,6 +386,7 @@ class RocketModel:
             host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
             reader.read_into(i, host)
             blobs.append(_LayerBlob(host, resolve(layer, entries), nbytes))
+        reader.close()
         left = max(0, vram_budget - rest)
         window = max(1, min(window, int(left // max(layer_bytes))))
         self.streamer = LayerStreamer(layers, self.device, window=window,

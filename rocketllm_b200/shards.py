@@ -135,16 +135,28 @@ def split_rw4_layers(model, out_dir):
 
 
 class LayerShardReader:
-    """Reads layer blobs of a directory written by :func:`split_rw4_layers`."""
+    """Reads layer blobs of a directory written by :func:`split_rw4_layers`.
 
-    def __init__(self, root):
+    ``io_workers`` > 1 reads a layer of at least ``io_workers`` x ``MIN_STRETCH`` bytes as that
+    many adjacent, byte-balanced stretches on as many threads (positioned reads release the
+    interpreter lock): the reference loader's ``io_workers`` partition (``streaming/loader.py:
+    214-236``, ``streaming/shards.py:664-700``: batches balanced by bytes, each one a contiguous
+    sweep of the file, the submitting thread taking the first).  A layer here is one blob, so the
+    stretches are cut at 4096-byte boundaries of the blob itself rather than between tensors."""
+
+    MIN_STRETCH = 4 << 20
+
+    def __init__(self, root, io_workers=1):
         self.root = str(root)
         with open(os.path.join(self.root, INDEX)) as f:
             self.index = json.load(f)
         self.layers = self.index["layers"]
+        self.io_workers = max(1, int(io_workers))
+        self._executor = None
         self.reads = 0
         self.bytes_read = 0
         self.direct_reads = 0
+        self.parallel_reads = 0
 
     def __len__(self):
         return len(self.layers)
@@ -156,19 +168,23 @@ class LayerShardReader:
                    for m, leaf, kind, dt, shape, off in rec["entries"]]
         return entries, rec["nbytes"]
 
-    def read_into(self, i, buffer):
-        """Read layer ``i``'s blob into ``buffer`` (a CPU uint8 tensor of at least ``nbytes``,
-        pinned or not) with positioned reads; ``O_DIRECT`` when the buffer, size and file
-        offset are 4096-aligned and the file system accepts it."""
-        rec = self.layers[i]
-        nbytes, start = rec["nbytes"], rec["data_start"]
-        if buffer.dtype != torch.uint8 or buffer.numel() < nbytes or buffer.is_cuda:
-            raise ValueError("read_into needs a CPU uint8 buffer of at least the blob's size")
-        path = os.path.join(self.root, rec["file"])
-        view = memoryview(buffer[:nbytes].numpy()).cast("B")
+    def stretches(self, nbytes, ways=None):
+        """``[(lo, hi), ...]``: ``[0, nbytes)`` cut into at most ``ways`` adjacent stretches of
+        nearly equal bytes, every cut on a 4096-byte boundary, none under ``MIN_STRETCH``."""
+        if nbytes <= 0:
+            return [(0, 0)]
+        ways = self.io_workers if ways is None else max(1, int(ways))
+        ways = max(1, min(ways, nbytes // self.MIN_STRETCH))
+        step = -(-nbytes // ways)
+        step = -(-step // DATA_ALIGN) * DATA_ALIGN
+        return [(lo, min(nbytes, lo + step)) for lo in range(0, nbytes, step)]
+
+    def _read_stretch(self, path, view, start, lo, hi, direct_ok):
+        """Positioned reads of blob bytes ``[lo, hi)`` (file offset ``start + lo``) into
+        ``view[lo:hi]``; ``O_DIRECT`` while the remaining size stays 4096-aligned and the file
+        system accepts it.  Returns whether any of it bypassed the page cache."""
         fd, direct = None, False
-        if hasattr(os, "O_DIRECT") and buffer.data_ptr() % DATA_ALIGN == 0 \
-                and start % DATA_ALIGN == 0:
+        if direct_ok:
             try:
                 fd = os.open(path, os.O_RDONLY | os.O_DIRECT)
                 direct = True
@@ -176,10 +192,11 @@ class LayerShardReader:
                 fd = None
         if fd is None:
             fd = os.open(path, os.O_RDONLY)
+        used_direct = False
         try:
-            done = 0
-            while done < nbytes:
-                want = nbytes - done
+            done = lo
+            while done < hi:
+                want = hi - done
                 if direct:
                     if want % DATA_ALIGN:   # the tail of an O_DIRECT read must stay aligned
                         os.close(fd)
@@ -196,13 +213,57 @@ class LayerShardReader:
                     continue
                 if got <= 0:
                     raise IOError(f"{path}: short read at {start + done}")
+                used_direct |= direct
                 done += got
         finally:
             os.close(fd)
+        return used_direct
+
+    def read_into(self, i, buffer):
+        """Read layer ``i``'s blob into ``buffer`` (a CPU uint8 tensor of at least ``nbytes``,
+        pinned or not) with positioned reads, over ``io_workers`` threads for a large layer;
+        ``O_DIRECT`` when the buffer, size and file offset are 4096-aligned and the file system
+        accepts it.  A short file raises ``IOError``."""
+        rec = self.layers[i]
+        nbytes, start = rec["nbytes"], rec["data_start"]
+        if buffer.dtype != torch.uint8 or buffer.numel() < nbytes or buffer.is_cuda:
+            raise ValueError("read_into needs a CPU uint8 buffer of at least the blob's size")
+        path = os.path.join(self.root, rec["file"])
+        view = memoryview(buffer[:nbytes].numpy()).cast("B")
+        direct_ok = (hasattr(os, "O_DIRECT") and buffer.data_ptr() % DATA_ALIGN == 0
+                     and start % DATA_ALIGN == 0)
+        parts = self.stretches(nbytes)
+        if len(parts) == 1:
+            direct = self._read_stretch(path, view, start, 0, nbytes, direct_ok)
+        else:
+            if self._executor is None:
+                from concurrent.futures import ThreadPoolExecutor
+                self._executor = ThreadPoolExecutor(max_workers=self.io_workers - 1,
+                                                    thread_name_prefix="rw4-shard-read")
+            futures = [self._executor.submit(self._read_stretch, path, view, start, lo, hi,
+                                             direct_ok) for lo, hi in parts[1:]]
+            first_error = None
+            try:
+                direct = self._read_stretch(path, view, start, *parts[0], direct_ok)
+            except BaseException as e:  # noqa: BLE001 - re-raised once the others are done
+                first_error, direct = e, False
+            for f in futures:              # every stretch finishes before the buffer is handed on
+                try:
+                    direct |= f.result()
+                except BaseException as e:  # noqa: BLE001
+                    first_error = first_error or e
+            if first_error is not None:
+                raise first_error
+            self.parallel_reads += 1
         self.reads += 1
         self.bytes_read += nbytes
         self.direct_reads += int(direct)
         return buffer
+
+    def close(self):
+        if self._executor is not None:
+            self._executor.shutdown(wait=True)
+            self._executor = None
 
     def read_tensor(self, i, key, rows=None, out=None):
         """One tensor of layer ``i`` -- ``key`` is ``"<module path>.<leaf>"`` as in the index -- or
@@ -250,7 +311,8 @@ class LayerShardReader:
 
     def stats(self):
         return {"layers": len(self.layers), "reads": self.reads, "bytes_read": self.bytes_read,
-                "direct_reads": self.direct_reads}
+                "direct_reads": self.direct_reads, "parallel_reads": self.parallel_reads,
+                "io_workers": self.io_workers}
 
 
 def build_skeleton(root, dtype=torch.bfloat16):

@@ -103,3 +103,44 @@ def test_a_subset_or_row_slice_costs_only_its_bytes(tmp_path):
         reader.read_tensor(1, "mlp.no_such.weight")
     with pytest.raises(ValueError):
         reader.read_tensor(1, key, rows=(0, 10 ** 6))
+
+
+def test_stretches_are_adjacent_aligned_and_byte_balanced():
+    """The io-worker partition (the reference's ``partition``, streaming/shards.py:664-700):
+    adjacent stretches covering the blob, cut on 4096-byte boundaries, balanced by bytes."""
+    reader = object.__new__(LayerShardReader)
+    reader.io_workers = 4
+    mb = LayerShardReader.MIN_STRETCH
+    for n in (0, 1, mb - 1, 3 * mb, 4 * mb + 12345, 10 * mb + 1, 1 << 31):
+        parts = reader.stretches(n)
+        assert parts[0][0] == 0 and parts[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(parts, parts[1:]))
+        assert all(hi % 4096 == 0 for _, hi in parts[:-1])
+        assert len(parts) <= max(1, min(4, n // mb))
+        sizes = [hi - lo for lo, hi in parts]
+        assert max(sizes) - min(sizes) <= 4096 * len(parts) or len(parts) == 1
+    assert len(reader.stretches(1 << 31)) == 4 and len(reader.stretches(mb)) == 1
+    assert len(reader.stretches(1 << 31, ways=2)) == 2
+
+
+def test_parallel_reads_give_the_same_blob_and_fail_loudly(tmp_path):
+    model = tiny_rw4_model(3)
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    one = LayerShardReader(root)
+    many = LayerShardReader(root, io_workers=3)
+    many.MIN_STRETCH = 4096                 # force several stretches on these small layers
+    for i in range(len(one)):
+        n = one.layers[i]["nbytes"]
+        assert len(many.stretches(n)) > 1
+        a = torch.zeros(n + 4096, dtype=torch.uint8)
+        b = torch.full((n + 4096,), 7, dtype=torch.uint8)
+        one.read_into(i, a)
+        many.read_into(i, b)
+        assert torch.equal(a[:n], b[:n]) and int((b[n:] != 7).sum()) == 0
+    assert many.stats()["parallel_reads"] == len(one) and many.stats()["io_workers"] == 3
+    rec = many.layers[2]
+    with open(os.path.join(root, rec["file"]), "r+b") as f:        # lose the last stretch's tail
+        f.truncate(rec["data_start"] + rec["nbytes"] - 100)
+    with __import__("pytest").raises(IOError, match="short read"):
+        many.read_into(2, torch.zeros(rec["nbytes"], dtype=torch.uint8))
+    many.close()
