@@ -469,10 +469,34 @@ def ep_decode(args):
     return 0
 
 
-def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget):
+def _timed_streamed_decode(streamed, vocab, gen, device, tokens):
+    """ms per token and streamed bytes per token of ``tokens`` greedy steps at batch 1 after a
+    128-token prompt (eager steps: the streaming hooks run every token)."""
+    from rocketllm_b200.decode import GraphedDecoder
+    ids = torch.randint(0, vocab, (1, 128), generator=gen).to(device)
+    dec = GraphedDecoder(streamed.model, 1, 128 + tokens + 8, device=device, use_graph=False)
+    dec.prefill(ids)
+    dec.step()
+    torch.cuda.synchronize()
+    st0 = streamed.stats()["streaming"]
+    a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(tokens):
+        dec.step()
+    c.record()
+    torch.cuda.synchronize()
+    st1 = streamed.stats()["streaming"]
+    del dec
+    return a.elapsed_time(c) / tokens, st0, st1
+
+
+def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget,
+                 storage_dir=None, host_budget=None):
     """Greedy decode tok/s of a Llama-3.1-8B-architecture RW4 model (random init N(0, 0.02),
     every Linear incl. lm_head in RW4): resident with a CUDA-graphed step, then streamed from
-    pinned host memory under a VRAM budget."""
+    pinned host memory under a VRAM budget, then (with ``storage_dir``) from layer shards written
+    there, with only ``host_budget`` bytes of layer blobs in host memory and the rest read from
+    the files every token (the storage tier)."""
     from transformers import LlamaConfig
 
     from rocketllm_b200.decode import GraphedDecoder
@@ -514,21 +538,8 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
     # streamed: the decoder layers leave HBM and stream from pinned host RAM every token
     streamed = RocketModel(model, device=device, vram_budget=vram_budget, window=2,
                            kv_cache="fp16")
-    ids = torch.randint(0, cfg.vocab_size, (1, 128), generator=gen).to(device)
-    dec = GraphedDecoder(streamed.model, 1, 128 + stream_tokens + 8, device=device,
-                         use_graph=False)
-    dec.prefill(ids)
-    dec.step()
-    torch.cuda.synchronize()
-    st0 = streamed.stats()["streaming"]["bytes"]
-    a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(stream_tokens):
-        dec.step()
-    c.record()
-    torch.cuda.synchronize()
-    ms = a.elapsed_time(c) / stream_tokens
-    nbytes = (streamed.stats()["streaming"]["bytes"] - st0) / stream_tokens
+    ms, st0, st1 = _timed_streamed_decode(streamed, cfg.vocab_size, gen, device, stream_tokens)
+    nbytes = (st1["bytes"] - st0["bytes"]) / stream_tokens
     out["streamed_b1"] = {"tok_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 3),
                           "vram_budget_bytes": vram_budget, "window": streamed.streamer.window,
                           "pinned_layers": streamed.streamer.pinned,
@@ -537,7 +548,33 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
                           "h2d_gbs": round(nbytes / (ms * 1e-3) / 1e9, 2),
                           "decode_tokens": stream_tokens}
     streamed.close()
-    del model, streamed, dec
+    del streamed
+    if storage_dir is not None:
+        from rocketllm_b200.shards import split_rw4_layers
+        split_rw4_layers(model, storage_dir)
+        del model
+        torch.cuda.empty_cache()
+        stored = RocketModel(storage_dir, device=device, vram_budget=vram_budget, window=2,
+                             kv_cache="fp16", host_budget=host_budget)
+        ms, st0, st1 = _timed_streamed_decode(stored, cfg.vocab_size, gen, device,
+                                              stream_tokens)
+        s0, s1 = st0["storage"] or {}, st1["storage"] or {}
+        disk = (s1.get("bytes", 0) - s0.get("bytes", 0)) / stream_tokens
+        h2d = (st1["bytes"] - st0["bytes"]) / stream_tokens
+        out["storage_b1"] = {"tok_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 3),
+                             "host_budget_bytes": host_budget,
+                             "storage_layers": len(stored.streamer.storage.order)
+                             if stored.streamer.storage else 0,
+                             "storage_bytes_per_token": int(disk),
+                             "storage_gbs": round(disk / (ms * 1e-3) / 1e9, 2),
+                             "h2d_bytes_per_token": int(h2d),
+                             "reads_waited": s1.get("waits", 0) - s0.get("waits", 0),
+                             "io_workers": stored.shards.io_workers,
+                             "decode_tokens": stream_tokens}
+        stored.close()
+        del stored
+    else:
+        del model
     torch.cuda.empty_cache()
     return out
 
@@ -1016,6 +1053,10 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="only the model decode section (one JSON line)")
     ap.add_argument("--decode-batches", default="1,16")
+    ap.add_argument("--storage-dir", default=None,
+                    help="with --decode-only: also write the model as layer shards here and "
+                         "decode from them with --host-budget-gb of layer blobs in host memory")
+    ap.add_argument("--host-budget-gb", type=float, default=1.0)
     ap.add_argument("--pp-decode", action="store_true",
                     help="pipeline-parallel decode over the torchrun ranks (one JSON line)")
     ap.add_argument("--pp-model", choices=("405b", "8b"), default="405b")
@@ -1064,8 +1105,11 @@ def main():
         device = torch.device("cuda", 0)
         torch.cuda.set_device(device)
         batches = tuple(int(b) for b in args.decode_batches.split(","))
-        print(json.dumps(decode_bench(device, args.decode_prompt, args.decode_tokens, batches,
-                                      args.stream_tokens, int(4e9))), flush=True)
+        print(json.dumps(decode_bench(
+            device, args.decode_prompt, args.decode_tokens, batches, args.stream_tokens,
+            int(4e9), storage_dir=args.storage_dir,
+            host_budget=int(args.host_budget_gb * 1e9) if args.storage_dir else None)),
+            flush=True)
         return 0
     if args.impl == "reference":
         return reference_arm(args)

@@ -92,7 +92,7 @@ class LayerStreamer:
 
     def __init__(self, layers, device, window=2, copy_streams=2, chunk_bytes=16 << 20,
                  prefetching=True, expert_slots=None, blobs=None, pinned=0,
-                 expert_routing="host", expert_policy=None):
+                 expert_routing="host", expert_policy=None, storage=None):
         if window < 1:
             raise ValueError("window must be >= 1")
         self.layers = list(layers)
@@ -119,8 +119,15 @@ class LayerStreamer:
             _bind(blob, dev)
             self.resident.append(dev)
             self.blobs[i] = _LayerBlob(None, blob.entries, blob.nbytes)  # host copy released
+        # storage tier (shards.LayerStager): streamed layers with no host blob are read from their
+        # shard files ahead of use into leases of the stager's pool; the transfer engine releases
+        # a lease once its copy has finished (and reclaims finished ones when the pool runs dry)
+        self.storage = storage
+        if any(self.blobs[i].host is None for i in range(self.streamed)) and storage is None:
+            raise ValueError("streamed layers without a host blob need a storage tier")
         self.xfer = WeightTransfer(device=self.device, copy_streams=copy_streams,
-                                   chunk_bytes=chunk_bytes)
+                                   chunk_bytes=chunk_bytes,
+                                   pool=storage.pool if storage is not None else None)
         self.experts = None
         if stream_experts:
             moe = [(i, m) for i, layer in enumerate(self.layers) for m in layer.modules()
@@ -144,7 +151,13 @@ class LayerStreamer:
         if self.resident_slot[s] == i:
             return
         blob = self.blobs[i]
-        handle = self.xfer.send_buffer(blob.host, out=self.slots[s][:blob.nbytes], after=compute)
+        if blob.host is None:
+            lease = self.storage.take(i)
+            handle = self.xfer.send_buffer(lease.view, lease=lease,
+                                           out=self.slots[s][:blob.nbytes], after=compute)
+        else:
+            handle = self.xfer.send_buffer(blob.host, out=self.slots[s][:blob.nbytes],
+                                           after=compute)
         self.tickets[i] = handle
         self.resident_slot[s] = i
         self.fetches += 1
@@ -177,6 +190,7 @@ class LayerStreamer:
                 "window": self.window, "slot_bytes": self.slot_bytes,
                 "fetches": self.fetches, "bytes": self.bytes, "slot_hits": self.hits,
                 "experts": self.experts.stats() if self.experts else None,
+                "storage": self.storage.stats() if self.storage else None,
                 "transfer": self.xfer.stats()}
 
     def close(self):
@@ -186,6 +200,10 @@ class LayerStreamer:
         if hasattr(self.experts, "close"):
             self.experts.close()
         self.xfer.close()
+        if self.storage is not None:
+            self.storage.close()
+            self.storage.pool.close()
+            self.storage = None
 
 
 def _layers_path(model):
@@ -237,6 +255,10 @@ class RocketModel:
     or ``"lru"``; None takes ``"lfu"`` with host routing and ``"lru"`` with device routing.
     ``io_workers``: threads that read each layer's blob from a layer-shard directory (adjacent,
     byte-balanced stretches of the blob: the reference loader's ``io_workers``).
+    ``host_budget`` (bytes; layer-shard directories only): pinned host memory for streamed layer
+    blobs.  Streamed layers past it form the storage tier: they stay in their files and are read
+    ``storage_depth`` layers ahead of use into leased staging buffers on every pass
+    (:class:`~rocketllm_b200.shards.LayerStager`).  None keeps every blob in host memory.
 
     ``kv_cache`` (``rocketllm/base.py:208-411``, ``quant/kv_cache.py:449-503``): ``"int4"`` gives
     every ``generate`` an :class:`~rocketllm_b200.kv_cache.RW4KVCache` whose decode attention reads
@@ -255,7 +277,7 @@ class RocketModel:
                  window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
                  expert_streaming=True, kv_cache="auto", draft_model=None, speculative="auto",
                  lookahead=4, max_lookahead=8, expert_routing="host", expert_policy=None,
-                 io_workers=4, **unused):
+                 io_workers=4, host_budget=None, storage_depth=2, **unused):
         from .kv_cache import KV_CHOICES
         from .shards import INDEX
         from .speculative import SPEC_CHOICES
@@ -280,7 +302,8 @@ class RocketModel:
         if isinstance(model_or_path, (str, os.PathLike)) and \
                 os.path.exists(os.path.join(str(model_or_path), INDEX)):
             self._init_from_shards(str(model_or_path), device, dtype, vram_budget, window,
-                                   prefetching, copy_streams, chunk_bytes, io_workers)
+                                   prefetching, copy_streams, chunk_bytes, io_workers,
+                                   host_budget, storage_depth)
             return
         if isinstance(model_or_path, (str, os.PathLike)):
             from transformers import AutoModelForCausalLM
@@ -345,7 +368,8 @@ class RocketModel:
         return pinned
 
     def _init_from_shards(self, root, device, dtype, vram_budget, window, prefetching,
-                          copy_streams, chunk_bytes, io_workers=1):
+                          copy_streams, chunk_bytes, io_workers=1, host_budget=None,
+                          storage_depth=2):
         """Layer shards written by ``shards.split_rw4_layers``: the model is built on the meta
         device, the non-layer tensors come from ``rest.safetensors`` straight to the device, and
         each layer's blob is read from its file into pinned memory by positioned reads over
@@ -380,19 +404,40 @@ class RocketModel:
                 _bind(_LayerBlob(None, resolve(layer, entries), nbytes), slot)
             reader.close()
             return
-        blobs = []
-        for i, layer in enumerate(layers):
-            entries, nbytes = plans[i]
-            host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
-            reader.read_into(i, host)
-            blobs.append(_LayerBlob(host, resolve(layer, entries), nbytes))
-        reader.close()
         left = max(0, vram_budget - rest)
         window = max(1, min(window, int(left // max(layer_bytes))))
+        pinned = self._pin_count(layer_bytes, left, window)
+        streamed = len(layers) - pinned
+        # host tier: streamed blobs in pinned host memory while host_budget lasts (in scan order);
+        # the storage tier takes the rest, read from their files on every pass
+        host_left = float("inf") if host_budget is None else max(0, int(host_budget))
+        blobs, storage_layers = [], []
+        for i, layer in enumerate(layers):
+            entries, nbytes = plans[i]
+            if i < streamed and (storage_layers or nbytes > host_left):
+                blobs.append(_LayerBlob(None, resolve(layer, entries), nbytes))
+                storage_layers.append(i)
+                continue
+            host = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+            reader.read_into(i, host)
+            if i < streamed:
+                host_left -= nbytes
+            blobs.append(_LayerBlob(host, resolve(layer, entries), nbytes))
+        storage = None
+        if storage_layers:
+            from .shards import LayerStager
+            from .streaming import HostStagingPool
+            cls = HostStagingPool._size_class(max(layer_bytes[i] for i in storage_layers))
+            pool = HostStagingPool(budget_bytes=(storage_depth + window + 1) * cls)
+            storage = LayerStager(reader, storage_layers, pool, depth=storage_depth)
+            for i in storage_layers[:storage_depth]:
+                storage.request(i)
+        else:
+            reader.close()
         self.streamer = LayerStreamer(layers, self.device, window=window,
                                       copy_streams=copy_streams, chunk_bytes=chunk_bytes,
-                                      prefetching=prefetching, blobs=blobs,
-                                      pinned=self._pin_count(layer_bytes, left, window))
+                                      prefetching=prefetching, blobs=blobs, pinned=pinned,
+                                      storage=storage)
 
     @property
     def config(self):

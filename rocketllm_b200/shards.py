@@ -19,6 +19,7 @@ layers, ``config.json`` the model config with its ``quantization_config``.
 """
 import json
 import os
+import threading
 
 import torch
 
@@ -153,6 +154,7 @@ class LayerShardReader:
         self.layers = self.index["layers"]
         self.io_workers = max(1, int(io_workers))
         self._executor = None
+        self._lock = threading.Lock()   # reads may come from several I/O threads
         self.reads = 0
         self.bytes_read = 0
         self.direct_reads = 0
@@ -236,11 +238,13 @@ class LayerShardReader:
         if len(parts) == 1:
             direct = self._read_stretch(path, view, start, 0, nbytes, direct_ok)
         else:
-            if self._executor is None:
-                from concurrent.futures import ThreadPoolExecutor
-                self._executor = ThreadPoolExecutor(max_workers=self.io_workers - 1,
-                                                    thread_name_prefix="rw4-shard-read")
-            futures = [self._executor.submit(self._read_stretch, path, view, start, lo, hi,
+            with self._lock:
+                if self._executor is None:
+                    from concurrent.futures import ThreadPoolExecutor
+                    self._executor = ThreadPoolExecutor(max_workers=self.io_workers - 1,
+                                                        thread_name_prefix="rw4-shard-read")
+                executor = self._executor
+            futures = [executor.submit(self._read_stretch, path, view, start, lo, hi,
                                              direct_ok) for lo, hi in parts[1:]]
             first_error = None
             try:
@@ -254,16 +258,19 @@ class LayerShardReader:
                     first_error = first_error or e
             if first_error is not None:
                 raise first_error
-            self.parallel_reads += 1
-        self.reads += 1
-        self.bytes_read += nbytes
-        self.direct_reads += int(direct)
+            with self._lock:
+                self.parallel_reads += 1
+        with self._lock:
+            self.reads += 1
+            self.bytes_read += nbytes
+            self.direct_reads += int(direct)
         return buffer
 
     def close(self):
-        if self._executor is not None:
-            self._executor.shutdown(wait=True)
-            self._executor = None
+        with self._lock:
+            executor, self._executor = self._executor, None
+        if executor is not None:
+            executor.shutdown(wait=True)
 
     def read_tensor(self, i, key, rows=None, out=None):
         """One tensor of layer ``i`` -- ``key`` is ``"<module path>.<leaf>"`` as in the index -- or
@@ -305,14 +312,97 @@ class LayerShardReader:
                 done += got
         finally:
             os.close(fd)
-        self.reads += 1
-        self.bytes_read += nbytes
+        with self._lock:
+            self.reads += 1
+            self.bytes_read += nbytes
         return out
 
     def stats(self):
         return {"layers": len(self.layers), "reads": self.reads, "bytes_read": self.bytes_read,
                 "direct_reads": self.direct_reads, "parallel_reads": self.parallel_reads,
                 "io_workers": self.io_workers}
+
+
+class LayerStager:
+    """The storage tier: streamed layers whose blobs stay in their shard files and are read, ahead
+    of use, into leased staging buffers -- the reference cache's miss path (``memory/cache.py:
+    236-250`` ``_fetch``, run ahead on prefetch workers by ``prefetch_window`` ``:254-272``; the
+    loader's ``load`` into one leased buffer, ``streaming/loader.py:196-207``).
+
+    ``order`` lists the storage-tier layers in the order the forward visits them (cyclically).
+    ``take(i)`` returns layer ``i``'s blob in a :class:`~rocketllm_b200.streaming.BufferLease`,
+    waiting for its read if it is still running, and starts the reads of the next ``depth``
+    storage layers in that order on the I/O threads.  The caller hands the lease to
+    ``WeightTransfer.send_buffer``, which releases it only once the copy has finished, so a staging
+    buffer is never refilled while a copy still reads it.  A read that fails releases its lease and
+    raises from ``take``.  Leases come from ``pool`` (a ``HostStagingPool``): pinned while its
+    budget lasts, a transient pageable buffer after that.
+    """
+
+    def __init__(self, reader, order, pool, depth=2):
+        from concurrent.futures import ThreadPoolExecutor
+        self.reader = reader
+        self.order = list(order)
+        if not self.order:
+            raise ValueError("a storage tier needs at least one layer")
+        self.pos = {layer: k for k, layer in enumerate(self.order)}
+        self.pool = pool
+        self.depth = max(1, int(depth))
+        self._executor = ThreadPoolExecutor(max_workers=self.depth,
+                                            thread_name_prefix="rw4-storage")
+        self._pending = {}
+        self._lock = threading.Lock()
+        self.reads = 0
+        self.bytes = 0
+        self.waits = 0
+
+    def _load(self, i):
+        lease = self.pool.lease(self.reader.layers[i]["nbytes"], torch.uint8)
+        try:
+            self.reader.read_into(i, lease.view)
+        except BaseException:
+            lease.release()
+            raise
+        return lease
+
+    def request(self, i):
+        """Start reading layer ``i`` unless its read is already pending."""
+        if i not in self.pos:
+            raise KeyError(f"layer {i} is not in the storage tier")
+        with self._lock:
+            if i not in self._pending:
+                self._pending[i] = self._executor.submit(self._load, i)
+
+    def take(self, i):
+        """Layer ``i``'s blob in a lease (the caller owns it), then read ahead ``depth`` layers."""
+        self.request(i)
+        with self._lock:
+            future = self._pending.pop(i)
+        if not future.done():
+            self.waits += 1
+        lease = future.result()
+        self.reads += 1
+        self.bytes += self.reader.layers[i]["nbytes"]
+        k = self.pos[i]
+        for d in range(1, self.depth + 1):
+            self.request(self.order[(k + d) % len(self.order)])
+        return lease
+
+    def stats(self):
+        return {"layers": len(self.order), "depth": self.depth, "reads": self.reads,
+                "bytes": self.bytes, "waits": self.waits}
+
+    def close(self):
+        """Wait for the reads in flight and release what nobody took."""
+        with self._lock:
+            pending, self._pending = list(self._pending.values()), {}
+        for future in pending:
+            try:
+                future.result().release()
+            except BaseException:  # noqa: BLE001 - a failed read already released its lease
+                pass
+        self._executor.shutdown(wait=True)
+        self.reader.close()
 
 
 def build_skeleton(root, dtype=torch.bfloat16):

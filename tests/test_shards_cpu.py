@@ -5,6 +5,7 @@ every tensor at the engine's aligned offset, the index alone plans a layer, and 
 (.done marker) is not rewritten."""
 import os
 
+import pytest
 import torch
 
 from rocketllm_b200.engine import _layer_tensors, _pack_layer
@@ -141,6 +142,63 @@ def test_parallel_reads_give_the_same_blob_and_fail_loudly(tmp_path):
     rec = many.layers[2]
     with open(os.path.join(root, rec["file"]), "r+b") as f:        # lose the last stretch's tail
         f.truncate(rec["data_start"] + rec["nbytes"] - 100)
-    with __import__("pytest").raises(IOError, match="short read"):
+    with pytest.raises(IOError, match="short read"):
         many.read_into(2, torch.zeros(rec["nbytes"], dtype=torch.uint8))
     many.close()
+
+
+class _CountingPool:
+    """A staging pool that hands out plain CPU buffers and records what comes back."""
+
+    def __init__(self):
+        self.leased, self.returned = 0, []
+
+    def lease(self, count, dtype):
+        from rocketllm_b200.streaming import BufferLease
+        self.leased += 1
+        return BufferLease(torch.zeros(count, dtype=dtype), self, self.leased)
+
+    def _return(self, slot):
+        self.returned.append(slot)
+
+
+def test_the_storage_tier_reads_ahead_in_scan_order(tmp_path):
+    """``LayerStager``: each take hands over the layer's blob (== a direct read) and starts the
+    next ``depth`` storage layers' reads, wrapping around the scan."""
+    from rocketllm_b200.shards import LayerStager
+    model = tiny_rw4_model(4)
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    direct = LayerShardReader(root)
+    pool = _CountingPool()
+    st = LayerStager(LayerShardReader(root), [0, 2], pool, depth=1)
+    for rnd in range(3):
+        for i in (0, 2):
+            lease = st.take(i)
+            want = direct.read_into(i, torch.zeros(direct.layers[i]["nbytes"], dtype=torch.uint8))
+            assert torch.equal(lease.view, want)
+            assert set(st._pending) == {2 if i == 0 else 0}     # the next one, wrapping
+            lease.release()
+    with pytest.raises(KeyError):
+        st.take(1)                                           # not a storage layer
+    assert st.stats()["reads"] == 6 and st.stats()["bytes"] == 3 * (
+        direct.layers[0]["nbytes"] + direct.layers[2]["nbytes"])
+    st.close()
+    assert len(pool.returned) == pool.leased                # the pending read-ahead came back too
+
+
+def test_a_failed_storage_read_releases_its_lease_and_raises(tmp_path):
+    from rocketllm_b200.shards import LayerStager
+    model = tiny_rw4_model(5)
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    reader = LayerShardReader(root)
+    rec = reader.layers[1]
+    with open(os.path.join(root, rec["file"]), "r+b") as f:
+        f.truncate(rec["data_start"] + rec["nbytes"] // 2)
+    pool = _CountingPool()
+    st = LayerStager(reader, [0, 1], pool, depth=1)
+    st.take(0).release()
+    with pytest.raises(IOError, match="short read"):
+        st.take(1)
+    assert pool.returned.count(2) == 1                      # the failed read's own lease
+    st.close()
+    assert sorted(pool.returned) == list(range(1, pool.leased + 1))

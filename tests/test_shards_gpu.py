@@ -52,3 +52,26 @@ def test_shards_equal_checkpoint(tmp_path, kind):
     assert torch.equal(a, b)
     assert from_shards.shards.stats()["bytes_read"] == sum(layers)
     streamed.close()
+
+
+def test_storage_tier_equals_checkpoint(tmp_path):
+    """Streamed layers past the host budget stay in their files and are read ahead of use on
+    every pass (the storage tier); logits and greedy tokens equal the resident model's."""
+    ckpt = save_rw4_checkpoint(dense_model("llama"), str(tmp_path / "rw4"), device="cuda")
+    resident = AutoModel.from_pretrained(ckpt)
+    root = split_rw4_layers(resident.model, str(tmp_path / "shards"))
+    ids = torch.randint(0, 2048, (1, 16), generator=torch.Generator().manual_seed(6)).cuda()
+    rest, layers = footprint(resident.model)
+    streamed = RocketModel(root, vram_budget=rest + 2 * max(layers) + 1000, window=2,
+                           kv_cache="fp16", host_budget=layers[0] + 1, storage_depth=2)
+    st = streamed.streamer
+    assert st.storage is not None and st.storage.order == list(range(1, st.streamed))
+    with torch.no_grad():
+        assert torch.equal(streamed(ids).logits, resident(ids).logits)
+        a = resident.generate(ids, max_new_tokens=6, do_sample=False, min_new_tokens=6)
+        b = streamed.generate(ids, max_new_tokens=6, do_sample=False, min_new_tokens=6)
+    assert torch.equal(a, b)
+    stats = streamed.stats()["streaming"]
+    assert stats["storage"]["reads"] >= 7 * len(st.storage.order)   # every pass re-reads them
+    assert stats["fetches"] >= 7 * st.streamed
+    streamed.close()
