@@ -1,0 +1,115 @@
+"""The engine's layer streaming and its storage tier, run on the CPU.
+
+The copy mechanism is the only GPU part of the layer path, so here it is a fake transfer engine
+that copies at once and releases the lease it was given (as the real one does when a copy has
+finished); pinning is the identity and there are no CUDA streams.  Everything else -- the host and
+storage tier split under ``host_budget``, ``LayerStager``'s read-ahead into leases, the layer
+pre-hooks with their window prefetch, the binding of parameters into the slots -- is the
+engine's own code, driving a plain fp32 Llama written as layer shards.  Logits and greedy tokens
+must equal the model's own, and every pass must read the storage layers from their files again.
+"""
+import pytest
+import torch
+
+from rocketllm_b200 import engine
+from rocketllm_b200.shards import split_rw4_layers
+
+
+class _Handle:
+    def resolve(self, stream=None):
+        return None
+
+
+class _FakeTransfer:
+    def __init__(self, device_caps=None, pool=None, device=None, copy_streams=2,
+                 chunk_bytes=1 << 24):
+        self.pool = pool
+        self.sent = 0
+        self.leases = 0
+        if pool is not None:
+            pool.set_reclaim_hook(self.reclaim)
+
+    def send_buffer(self, host, lease=None, out=None, after=None):
+        n = host.numel() * host.element_size()
+        out.view(-1)[:n].copy_(host.reshape(-1).view(torch.uint8)[:n])
+        if lease is not None:
+            self.leases += 1
+            lease.release()
+        self.sent += 1
+        return _Handle()
+
+    def reclaim(self):
+        return 0
+
+    def drain(self):
+        return 0
+
+    def stats(self):
+        return {"transfers": self.sent, "leased_sends": self.leases}
+
+    def close(self):
+        pass
+
+
+def _plain_llama():
+    from transformers import LlamaConfig, LlamaForCausalLM
+    torch.manual_seed(0)
+    cfg = LlamaConfig(hidden_size=64, intermediate_size=160, num_hidden_layers=5,
+                      num_attention_heads=4, num_key_value_heads=2, vocab_size=96,
+                      max_position_embeddings=64, tie_word_embeddings=False)
+    return LlamaForCausalLM(cfg).float().eval()
+
+
+@pytest.fixture
+def cpu_engine(monkeypatch):
+    import rocketllm_b200.quant.hf as hf
+    monkeypatch.setattr(hf, "convert_modules", lambda model, skip=(): [])   # a plain model
+    monkeypatch.setattr(torch.Tensor, "pin_memory", lambda self, *a, **k: self)
+    monkeypatch.setattr(torch.cuda, "current_stream", lambda device=None: None)
+    monkeypatch.setattr(engine, "WeightTransfer", _FakeTransfer)
+
+
+@pytest.mark.parametrize("host_layers,depth", [(0, 1), (1, 2), (2, 3)])
+def test_storage_tier_streams_the_models_own_logits(tmp_path, cpu_engine, host_layers, depth):
+    model = _plain_llama()
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    rest, layers = engine.footprint(model)
+    blob = max(layers)
+    rm = engine.RocketModel(root, device="cpu", dtype=torch.float32,
+                            vram_budget=rest + 2 * blob + 64 * 1024, window=2, kv_cache="fp16",
+                            host_budget=sum(layers[:host_layers]) + 4096 * host_layers,
+                            storage_depth=depth)
+    st = rm.streamer
+    assert st is not None and st.window == 2 and st.pinned == 0
+    assert st.storage is not None and st.storage.order == list(range(host_layers, st.streamed))
+    assert all(st.blobs[i].host is None for i in st.storage.order)
+    assert all(st.blobs[i].host is not None for i in range(host_layers))
+    ids = torch.randint(0, 96, (1, 9), generator=torch.Generator().manual_seed(3))
+    with torch.no_grad():
+        want = model(ids).logits
+        assert torch.equal(rm(ids).logits, want)
+        a = model.generate(ids, max_new_tokens=5, do_sample=False, min_new_tokens=5)
+        b = rm.generate(ids, max_new_tokens=5, do_sample=False, min_new_tokens=5)
+    assert torch.equal(a, b)
+    stats = rm.stats()["streaming"]
+    n_store = len(st.storage.order)
+    assert stats["storage"]["reads"] >= 6 * n_store          # re-read from the files every pass
+    assert stats["transfer"]["leased_sends"] == stats["storage"]["reads"]
+    ahead = list(st.storage._pending.values())              # read-ahead nobody took
+    assert ahead
+    rm.close()
+    assert all(f.result().released for f in ahead)          # released by close
+
+
+def test_without_a_host_budget_every_blob_stays_in_host_memory(tmp_path, cpu_engine):
+    model = _plain_llama()
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    rest, layers = engine.footprint(model)
+    rm = engine.RocketModel(root, device="cpu", dtype=torch.float32,
+                            vram_budget=rest + 2 * max(layers) + 64 * 1024, window=2,
+                            kv_cache="fp16")
+    assert rm.streamer.storage is None
+    ids = torch.randint(0, 96, (1, 7), generator=torch.Generator().manual_seed(4))
+    with torch.no_grad():
+        assert torch.equal(rm(ids).logits, model(ids).logits)
+    rm.close()
