@@ -69,18 +69,20 @@ def cpu_engine(monkeypatch):
     monkeypatch.setattr(engine, "WeightTransfer", _FakeTransfer)
 
 
-@pytest.mark.parametrize("host_layers,depth", [(0, 1), (1, 2), (2, 3)])
-def test_storage_tier_streams_the_models_own_logits(tmp_path, cpu_engine, host_layers, depth):
+@pytest.mark.parametrize("host_layers,depth,pinned", [(0, 1, 0), (1, 2, 0), (2, 3, 0), (1, 2, 1)])
+def test_storage_tier_streams_the_models_own_logits(tmp_path, cpu_engine, host_layers, depth,
+                                                    pinned):
     model = _plain_llama()
     root = split_rw4_layers(model, str(tmp_path / "shards"))
     rest, layers = engine.footprint(model)
     blob = max(layers)
     rm = engine.RocketModel(root, device="cpu", dtype=torch.float32,
-                            vram_budget=rest + 2 * blob + 64 * 1024, window=2, kv_cache="fp16",
+                            vram_budget=rest + (2 + pinned) * blob + 64 * 1024, window=2,
+                            kv_cache="fp16",
                             host_budget=sum(layers[:host_layers]) + 4096 * host_layers,
                             storage_depth=depth)
     st = rm.streamer
-    assert st is not None and st.window == 2 and st.pinned == 0
+    assert st is not None and st.window == 2 and st.pinned == pinned
     assert st.storage is not None and st.storage.order == list(range(host_layers, st.streamed))
     assert all(st.blobs[i].host is None for i in st.storage.order)
     assert all(st.blobs[i].host is not None for i in range(host_layers))
