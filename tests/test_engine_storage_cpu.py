@@ -93,7 +93,15 @@ def test_storage_tier_streams_the_models_own_logits(tmp_path, cpu_engine, host_l
         a = model.generate(ids, max_new_tokens=5, do_sample=False, min_new_tokens=5)
         b = rm.generate(ids, max_new_tokens=5, do_sample=False, min_new_tokens=5)
     assert torch.equal(a, b)
-    stats = rm.stats()["streaming"]
+    before = rm.stats()["streaming"]
+    with torch.no_grad():
+        rm(ids)
+    after = rm.stats()["streaming"]
+    # a pass over the layers in steady state sends each streamed layer exactly once and reads
+    # each storage layer exactly once (the window is a FIFO pipeline over the cyclic scan)
+    assert after["fetches"] - before["fetches"] == st.streamed
+    assert after["storage"]["reads"] - before["storage"]["reads"] == len(st.storage.order)
+    stats = after
     n_store = len(st.storage.order)
     assert stats["storage"]["reads"] >= 6 * n_store          # re-read from the files every pass
     assert stats["transfer"]["leased_sends"] == stats["storage"]["reads"]
