@@ -390,6 +390,10 @@ def moe_decode(args):
         del dec
         torch.cuda.empty_cache()
     out["h2d_probe_gbs"] = round(h2d_probe(device), 2)
+    if st.experts is not None and "routing" in st.experts.stats():
+        # lifetime routing skew over the whole run (prefills included)
+        out["routing"] = {k: round(v, 4) if isinstance(v, float) else v
+                          for k, v in st.experts.stats()["routing"].items()}
     print(json.dumps(out), flush=True)
     streamed.close()
     return 0

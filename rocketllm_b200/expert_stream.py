@@ -166,6 +166,7 @@ class ExpertStreamer:
         self.where = self.cache.where             # (layer, expert) -> slot
         self.tickets = {}
         self.frequency = collections.Counter()    # routed count per (layer, expert)
+        self.firings = 0                          # on_router calls (one per MoE layer call)
         self.fetches = 0
         self.hits = 0
         self.bytes = 0
@@ -187,6 +188,7 @@ class ExpertStreamer:
         together, ordered after the compute queued on ``compute``.  Returns how many started."""
         protect = {(layer, e) for e in selected}
         started = 0
+        self.firings += 1
         for e in selected:
             key = (layer, e)
             self.frequency[key] += 1
@@ -228,7 +230,36 @@ class ExpertStreamer:
         return {"expert_slots": len(self.slots), "slot_bytes": self.slot_bytes,
                 "fetches": self.fetches, "hits": self.hits, "bytes": self.bytes,
                 "resident": len(self.where), "policy": self.cache.policy,
-                "agings": self.cache.agings}
+                "agings": self.cache.agings,
+                "routing": routing_distribution(self.frequency, len(self.blobs), self.firings)}
+
+
+def routing_distribution(frequency, experts, firings):
+    """How skewed the routing was -- what an expert cache's hit rate rests on -- from lifetime
+    selection counts (``frequency``: key -> count over ``experts`` keys in all; ``firings``: router
+    calls).  The reference's benchmark reports the same figures (``rocketllm/moe/expert_cache.py:
+    171-200``): the share of selections taken by the most popular expert and by the most popular
+    tenth (beside the tenth's share under uniform routing), and the Gini coefficient of the counts
+    (0: uniform; (n-1)/n: one expert takes everything), here by its sorted-rank formula
+    G = 2 * sum_i(i * x_i) / (n * sum(x)) - (n + 1) / n over the ascending counts x_1..x_n."""
+    counts = sorted(frequency.values(), reverse=True)
+    counts += [0] * max(0, experts - len(counts))
+    total = sum(counts)
+    n = len(counts)
+    out = {"experts": n, "touched": sum(1 for c in counts if c), "firings": firings,
+           "selections": total,
+           "distinct_per_firing": total / firings if firings else 0.0}
+    if not total:
+        out.update(top_1_share=0.0, top_10pct_share=0.0, uniform_share=0.0, gini=0.0)
+        return out
+    head = max(1, n // 10)
+    ascending = counts[::-1]
+    out["top_1_share"] = counts[0] / total
+    out["top_10pct_share"] = sum(counts[:head]) / total
+    out["uniform_share"] = head / n
+    out["gini"] = 2.0 * sum((i + 1) * x for i, x in enumerate(ascending)) / (n * total) \
+        - (n + 1) / n
+    return out
 
 
 def streamed_experts_forward(self, hidden_states, top_k_index, top_k_weights):

@@ -176,7 +176,7 @@ def _streamer(num_slots, layers=2, experts=4, policy="lfu", aging=4096):
     s.cache = ExpertSlotCache(num_slots, policy, aging)
     s.where = s.cache.where
     s.tickets, s.frequency = {}, collections.Counter()
-    s.fetches = s.hits = s.bytes = 0
+    s.fetches = s.hits = s.bytes = s.firings = 0
     return s
 
 
@@ -293,3 +293,23 @@ def test_the_host_lfu_step_rejects_what_it_cannot_place():
         t.step(1, [0, 1, 2, 3])
     with pytest.raises(_lib.RW4Error, match="RW4_EINVAL"):
         t.step(2, [0])                                   # layer 2 of a 2-layer table
+
+
+def test_routing_distribution_figures():
+    """The skew report (the reference's ``ExpertStats.distribution``): uniform routing has Gini 0
+    and the top tenth at its uniform share; one expert taking everything has Gini (n-1)/n."""
+    from rocketllm_b200.expert_stream import routing_distribution
+    flat = routing_distribution(collections.Counter({(0, e): 5 for e in range(20)}), 20, 50)
+    assert flat["gini"] == pytest.approx(0.0, abs=1e-12)
+    assert flat["top_10pct_share"] == pytest.approx(flat["uniform_share"]) == pytest.approx(0.1)
+    assert flat["distinct_per_firing"] == 2.0 and flat["touched"] == 20
+    one = routing_distribution(collections.Counter({(1, 3): 7}), 20, 7)
+    assert one["gini"] == pytest.approx(19 / 20) and one["top_1_share"] == 1.0
+    assert one["touched"] == 1 and one["experts"] == 20
+    empty = routing_distribution(collections.Counter(), 8, 0)
+    assert empty["gini"] == 0.0 and empty["selections"] == 0
+    s = _streamer(3)
+    s.on_router(0, [0, 2], None)
+    s.on_router(1, [2], None)
+    got = routing_distribution(s.frequency, len(s.blobs), s.firings)
+    assert got["firings"] == 2 and got["selections"] == 3 and got["experts"] == 8
