@@ -183,8 +183,8 @@ class LayerShardReader:
 
     def _read_stretch(self, path, view, start, lo, hi, direct_ok):
         """Positioned reads of blob bytes ``[lo, hi)`` (file offset ``start + lo``) into
-        ``view[lo:hi]``; ``O_DIRECT`` while the remaining size stays 4096-aligned and the file
-        system accepts it.  Returns whether any of it bypassed the page cache."""
+        ``view[lo:hi]``; ``O_DIRECT`` for the whole 4096-byte blocks when the file system accepts
+        it, the ragged tail buffered.  Returns whether any of it bypassed the page cache."""
         fd, direct = None, False
         if direct_ok:
             try:
@@ -200,7 +200,10 @@ class LayerShardReader:
             while done < hi:
                 want = hi - done
                 if direct:
-                    if want % DATA_ALIGN:   # the tail of an O_DIRECT read must stay aligned
+                    # O_DIRECT moves whole 4096-byte blocks: the aligned part goes direct, a ragged
+                    # tail through the page cache
+                    want -= want % DATA_ALIGN
+                    if not want:
                         os.close(fd)
                         fd, direct = os.open(path, os.O_RDONLY), False
                         continue
