@@ -1,6 +1,6 @@
 """CPU oracle for the RW4 4-bit hot path.  TEST INFRASTRUCTURE ONLY.
 
-This module is the checker, never the product.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
+This module checks the product and is never part of it.  Only ``tests/``, ``__graft_entry__.smoke()`` and the
 ``cpu_baseline`` / ``--impl reference`` legs of ``bench.py`` may import it.  The shipped package
 (``rocketllm_b200``) never imports anything under ``oracle/`` and raises when its CUDA library is
 missing instead of falling back here.

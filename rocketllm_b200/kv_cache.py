@@ -416,7 +416,7 @@ def resolve_kv_cache(setting, weight_bytes=None, device_bytes=None, headroom=0.1
 def build_kv_cache(choice, config=None, fused=True):
     """The cache a resolved choice names, or ``None`` for the stock cache (``kv_cache.py:489-503``).
     ``hqq`` / ``quanto`` (transformers' own quantized caches on optional packages) are not part of
-    this build and fall back to the stock cache, as the reference does when they are missing."""
+    this package and fall back to the stock cache, as the reference does when they are missing."""
     if choice == KV_INT4:
         return RW4KVCache(config, fused=fused)
     return None

@@ -394,7 +394,7 @@ def registered_backends():
 def detect_backend(quantization_config=None, **context):
     """The backend for what the checkpoint declares about itself (``registry.py:656-675``).
 
-    A declared method nothing here recognises raises: this build computes RW4 only and has no
+    A declared method nothing here recognises raises: this package computes RW4 only and has no
     delegating fallback path.
     """
     _load_backends()
@@ -403,7 +403,7 @@ def detect_backend(quantization_config=None, **context):
         if cls.matches(method, quantization_config):
             return cls(config=quantization_config, **context)
     if method is not None:
-        raise ValueError(f"quant_method {method!r} is not served by this build "
+        raise ValueError(f"quant_method {method!r} is not served by rocketllm_b200 "
                          f"(known: {[c.quant_methods for c in _BACKENDS]})")
     return QuantBackend(config=quantization_config, **context)
 

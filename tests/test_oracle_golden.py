@@ -2,7 +2,7 @@
 
 Pins the CPU restatement in oracle/rw4_oracle.py bit for bit to RocketLLM's int4 codec
 (rocketllm/quant/kv_cache.py:190-272) and to transformers' Mixtral router, which the GPU parity
-tests then use as their checker.  Also restates the reference's own known-answer tests for the codec
+tests then compare against.  Also restates the reference's own known-answer tests for the codec
 (tests/test_kv_cache.py:39-111): half-step round-trip bound, constant groups exact, ragged tails.
 """
 import numpy as np
