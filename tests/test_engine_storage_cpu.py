@@ -123,3 +123,31 @@ def test_without_a_host_budget_every_blob_stays_in_host_memory(tmp_path, cpu_eng
     with torch.no_grad():
         assert torch.equal(rm(ids).logits, model(ids).logits)
     rm.close()
+
+
+@pytest.mark.parametrize("window,pinned", [(1, 0), (2, 1), (3, 0), (2, 2)])
+def test_in_memory_streaming_windows_and_pins(cpu_engine, window, pinned):
+    """A model already in host memory streams through ``window`` slots with the last ``pinned``
+    layers resident: the model's own logits, and each streamed layer that shares its slot crosses
+    once per pass (also when the layer count is not a multiple of the window and the prefetch
+    wraps); a layer alone in its slot crosses once."""
+    model = _plain_llama()
+    ref = _plain_llama()                    # the same seed: RocketModel takes over ``model``
+    rest, layers = engine.footprint(model)
+    budget = rest + window * max(layers) + sum(layers[len(layers) - pinned:]) + 64 * 1024
+    rm = engine.RocketModel(model, device="cpu", dtype=torch.float32, vram_budget=budget,
+                            window=window, kv_cache="fp16")
+    st = rm.streamer
+    assert (st.window, st.pinned, st.streamed) == (window, pinned, 5 - pinned)
+    ids = torch.randint(0, 96, (2, 6), generator=torch.Generator().manual_seed(5))
+    with torch.no_grad():
+        want = ref(ids).logits
+        assert torch.equal(rm(ids).logits, want)
+        before = rm.stats()["streaming"]["fetches"]
+        assert torch.equal(rm(ids).logits, want)
+    per_pass = rm.stats()["streaming"]["fetches"] - before
+    # layer i lives in slot i % window; a layer alone in its slot stays there between passes
+    sharing = [sum(1 for j in range(st.streamed) if j % window == i % window)
+               for i in range(st.streamed)]
+    assert per_pass == sum(1 for n in sharing if n > 1)
+    rm.close()
