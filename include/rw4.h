@@ -62,9 +62,10 @@ int rw4_dequant(const uint8_t* packed, const void* scale_f16, const void* zero_f
                 int64_t K, int32_t group, void* out, int32_t out_dtype, void* stream);
 
 /*
- * rw4_quantize: encode w[N, K] (dtype w_dtype: RW4_F32 or RW4_BF16) into packed/scale/zero,
- * bit-exact with quantize(w, axis=1, group_size=group) (rocketllm/quant/kv_cache.py:190-221),
- * including the bf16 scale arithmetic and the repeat-last-value padding of a ragged K.
+ * rw4_quantize: encode w[N, K] (dtype w_dtype: RW4_F32, RW4_BF16 or RW4_F16) into
+ * packed/scale/zero, bit-exact with quantize(w, axis=1, group_size=group)
+ * (rocketllm/quant/kv_cache.py:190-221), including the scale arithmetic in the input dtype and
+ * the repeat-last-value padding of a ragged K.
  * Output rows have ceil(K/group) groups.
  */
 int rw4_quantize(const void* w, int32_t w_dtype, int64_t N, int64_t K, int32_t group,

@@ -101,10 +101,11 @@ def _pad_rows_to_group(w, group):
 def quantize(w, group=64, dtype="f32"):
     """Quantize a 2-D weight ``[N, K]`` along its last axis, as the reference ``quantize(W, 1, g)``.
 
-    ``dtype`` is the dtype the reference tensor has: ``"f32"`` (``w`` is float32) or ``"bf16"``
-    (``w`` is the uint16 bit pattern of a bf16 tensor).  It matters because the reference computes
-    ``(hi - lo) / 15`` in the tensor's own dtype (``kv_cache.py:208``) and only then widens to fp32
-    for the code computation (``:213``).
+    ``dtype`` is the dtype the reference tensor has: ``"f32"`` (``w`` is float32), ``"bf16"``
+    (``w`` is the uint16 bit pattern of a bf16 tensor) or ``"f16"`` (``w`` is float16).  It
+    matters because the reference computes ``(hi - lo) / 15`` in the tensor's own dtype
+    (``kv_cache.py:208``), each op rounded to that dtype, and only then widens to fp32 for the code
+    computation (``:213``).
 
     Returns ``(packed u8 [N, Kp/2], scale f16 [N, Kp/g], zero f16 [N, Kp/g], padding)`` where
     ``Kp`` is ``K`` rounded up to the group.
@@ -113,6 +114,8 @@ def quantize(w, group=64, dtype="f32"):
         wf = bf16_bits_to_f32(w)
     elif dtype == "f32":
         wf = np.asarray(w, dtype=np.float32)
+    elif dtype == "f16":
+        wf = np.asarray(w, dtype=np.float16).astype(np.float32)
     else:
         raise ValueError(dtype)
     n, k = wf.shape
@@ -125,6 +128,9 @@ def quantize(w, group=64, dtype="f32"):
     if dtype == "bf16":
         diff = round_bf16(hi - lo)
         scale = round_bf16(diff / np.float32(LEVELS))
+    elif dtype == "f16":
+        diff = (hi - lo).astype(np.float16).astype(np.float32)
+        scale = (diff / np.float32(LEVELS)).astype(np.float16).astype(np.float32)
     else:
         scale = (hi - lo) / np.float32(LEVELS)
     scale = scale.astype(np.float32)
@@ -137,7 +143,8 @@ def quantize(w, group=64, dtype="f32"):
 def dequantize(packed, scale, zero, k=None, out="f32"):
     """``codes * scale + zero`` in fp32, narrowed to ``k`` columns, then cast (``kv_cache.py:249-257``).
 
-    ``out`` is ``"f32"`` (returns float32) or ``"bf16"`` (returns uint16 bf16 bit patterns).
+    ``out`` is ``"f32"`` (returns float32), ``"bf16"`` (returns uint16 bf16 bit patterns) or
+    ``"f16"`` (returns float16).
     The fp32 product is exact (a 4-bit code times an fp16 scale needs at most 15 significant
     bits), so a fused multiply-add on the device gives the same fp32 value before the cast.
     """

@@ -1,11 +1,14 @@
-// RW4 codec kernels: dequantize (packed -> fp32/bf16/fp16) and quantize (fp32/bf16 -> packed).
+// RW4 codec kernels: dequantize (packed -> fp32/bf16/fp16) and quantize (fp32/bf16/fp16 ->
+// packed).
 //
 // Both are bit-exact restatements of RocketLLM's int4 codec (rocketllm/quant/kv_cache.py):
 //   dequantize  (:249-257)  v = fp32(code) * fp32(scale) + fp32(zero), narrowed, then cast RNE.
 //               The product of a 4-bit code and an fp16 scale is exact in fp32, so one fused
 //               multiply-add rounds exactly where the reference's multiply-then-add does.
 //   quantize    (:190-221)  per group: lo = min, hi = max, scale = (hi - lo) / 15 computed in the
-//               INPUT dtype (bf16 arithmetic rounds after each op), scale = 1 where it is not
+//               INPUT dtype (bf16 / fp16 arithmetic rounds after each op; an fp32 op rounded once
+//               to the narrow type is that type's correctly rounded op, since fp32 carries more
+//               than twice its significand bits plus two), scale = 1 where it is not
 //               positive, code = clamp(rint((x - lo) / scale), 0, 15) in fp32 (rint = round half to
 //               even, as torch.round), scale and lo stored as fp16; a ragged last group repeats the
 //               row's last value (:160-187).
@@ -93,6 +96,26 @@ template <>
 __device__ __forceinline__ float load_f32<__nv_bfloat16>(const __nv_bfloat16* p) {
   return __bfloat162float(*p);
 }
+template <>
+__device__ __forceinline__ float load_f32<__half>(const __half* p) {
+  return __half2float(*p);
+}
+
+// One arithmetic result of the input dtype: fp32 as it is, bf16 / fp16 rounded to that type.
+template <typename InT>
+__device__ __forceinline__ float round_in(float v);
+template <>
+__device__ __forceinline__ float round_in<float>(float v) {
+  return v;
+}
+template <>
+__device__ __forceinline__ float round_in<__nv_bfloat16>(float v) {
+  return __bfloat162float(__float2bfloat16_rn(v));
+}
+template <>
+__device__ __forceinline__ float round_in<__half>(float v) {
+  return __half2float(__float2half_rn(v));
+}
 
 // One warp per (row, group).  Each lane owns the code pairs (2l, 2l+1), (2l+64, 2l+65), ...
 template <typename InT>
@@ -122,14 +145,8 @@ __global__ void __launch_bounds__(256)
       lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, off));
       hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, off));
     }
-    float s;
-    if (sizeof(InT) == 2) {
-      // bf16 tensor arithmetic: each op computed in fp32 and rounded back to bf16.
-      const float diff = __bfloat162float(__float2bfloat16_rn(hi - lo));
-      s = __bfloat162float(__float2bfloat16_rn(__fdiv_rn(diff, 15.0f)));
-    } else {
-      s = __fdiv_rn(hi - lo, 15.0f);
-    }
+    // tensor arithmetic in the input dtype: each op computed in fp32, rounded back to that type
+    float s = round_in<InT>(__fdiv_rn(round_in<InT>(hi - lo), 15.0f));
     if (!(s > 0.0f)) s = 1.0f;
     for (int i = 2 * lane; i < group; i += 64) {
       uint32_t pair = 0;
@@ -217,8 +234,12 @@ extern "C" int rw4_quantize(const void* w, int32_t w_dtype, int64_t N, int64_t K
     quantize_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>((const __nv_bfloat16*)w, N, K, g, groups,
                                                           packed, (__half*)scale_f16,
                                                           (__half*)zero_f16);
+  } else if (w_dtype == RW4_F16) {
+    quantize_kernel<__half><<<blocks, 256, 0, s>>>((const __half*)w, N, K, g, groups, packed,
+                                                   (__half*)scale_f16, (__half*)zero_f16);
   } else {
-    return fail(RW4_EINVAL, "rw4_quantize: w_dtype %d (want RW4_F32 or RW4_BF16)", w_dtype);
+    return fail(RW4_EINVAL, "rw4_quantize: w_dtype %d (want RW4_F32, RW4_BF16 or RW4_F16)",
+                w_dtype);
   }
   return launch_status("rw4_quantize launch");
 }

@@ -59,13 +59,14 @@ def dequantize(packed, scale, zero, k=None, dtype=torch.bfloat16, out=None):
 
 
 def quantize(w, group=64):
-    """Encode ``w[N, K]`` (fp32 or bf16, CUDA) as ``(packed, scale, zero, padding)``.
+    """Encode ``w[N, K]`` (fp32, bf16 or fp16, CUDA) as ``(packed, scale, zero, padding)``.
 
-    Bit-exact with the reference ``quantize(w, 1, group)``.
+    Bit-exact with the reference ``quantize(w, 1, group)``, whose scale arithmetic runs in the
+    tensor's own dtype.
     """
     _require_cuda(w)
-    if w.dtype not in (torch.float32, torch.bfloat16):
-        raise TypeError(f"quantize takes float32 or bfloat16, not {w.dtype}")
+    if w.dtype not in (torch.float32, torch.bfloat16, torch.float16):
+        raise TypeError(f"quantize takes float32, bfloat16 or float16, not {w.dtype}")
     n, k = w.shape
     g = min(group, k) if k else group
     groups = (k + g - 1) // g if k else 0

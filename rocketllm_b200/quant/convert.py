@@ -19,7 +19,7 @@ from .hf import QUANT_METHOD, RW4Config, _is_stacked_experts
 
 def _quantize(w, device):
     w = w.detach().to(device)
-    if w.dtype not in (torch.float32, torch.bfloat16):
+    if w.dtype not in (torch.float32, torch.bfloat16, torch.float16):
         w = w.float()
     packed, scale, zero, padding = kernels.quantize(w.contiguous(), 64)
     if padding:

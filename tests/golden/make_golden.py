@@ -71,6 +71,16 @@ def main(root):
         for key, val in codec_case(kv_cache, w).items():
             out[f"{name}.{key}"] = val
 
+    # 2b. fp16 weights: the scale is computed in fp16 arithmetic (own generator, so the cases above
+    # keep their values).  The last case spreads values wide enough that fp16 rounding of the
+    # range matters.
+    g16 = torch.Generator().manual_seed(7)
+    for name, (n, k, sd) in {"f16_aligned": (8, 256, 0.02), "f16_ragged": (5, 100, 0.02),
+                             "f16_wide": (6, 192, 300.0)}.items():
+        w = (torch.randn(n, k, generator=g16) * sd).to(torch.float16)
+        for key, val in codec_case(kv_cache, w).items():
+            out[f"{name}.{key}"] = val
+
     # 3. constant groups take the scale-1 path and round-trip exactly.
     w = torch.full((4, 128), 0.375, dtype=torch.float32)
     w[2, 64:] = -1.25

@@ -8,7 +8,8 @@ from rocketllm_b200 import kernels
 
 pytestmark = pytest.mark.gpu
 
-CODEC_CASES = ["f32_aligned", "f32_ragged", "bf16_aligned", "bf16_ragged", "const"]
+CODEC_CASES = ["f32_aligned", "f32_ragged", "bf16_aligned", "bf16_ragged", "f16_aligned",
+               "f16_ragged", "f16_wide", "const"]
 
 
 def to_dev(a, dev):
@@ -40,12 +41,14 @@ def test_quantize_bit_exact_with_reference(golden, cuda, case):
 @pytest.mark.parametrize("case", CODEC_CASES)
 def test_dequantize_bit_exact_with_reference(golden, cuda, case):
     w = golden[f"{case}.w"]
-    dtype = torch.bfloat16 if w.dtype == np.uint16 else torch.float32
+    # the reference dequantizes to the weight's own dtype (bf16 is stored as its uint16 bits)
+    dtype = {np.dtype(np.uint16): torch.bfloat16, np.dtype(np.float16): torch.float16}.get(
+        w.dtype, torch.float32)
     out = kernels.dequantize(to_dev(golden[f"{case}.packed"], cuda),
                              to_dev(golden[f"{case}.scale"], cuda),
                              to_dev(golden[f"{case}.zero"], cuda), k=w.shape[1], dtype=dtype)
     ref = golden[f"{case}.deq"]
-    assert np.array_equal(bits(out), ref.view(np.uint16 if ref.dtype == np.uint16 else np.uint32))
+    assert np.array_equal(bits(out), ref.view({2: np.uint16, 4: np.uint32}[ref.dtype.itemsize]))
 
 
 def test_sweep_format_dequant_bit_exact(golden, cuda):

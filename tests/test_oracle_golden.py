@@ -10,7 +10,13 @@ import pytest
 
 from oracle import rw4_oracle as o
 
-CODEC_CASES = ["f32_aligned", "f32_ragged", "bf16_aligned", "bf16_ragged", "const"]
+CODEC_CASES = ["f32_aligned", "f32_ragged", "bf16_aligned", "bf16_ragged", "f16_aligned",
+               "f16_ragged", "f16_wide", "const"]
+
+
+def _dtype(w):
+    """The reference tensor's dtype from its stored form (bf16 is kept as its uint16 bits)."""
+    return {np.dtype(np.uint16): "bf16", np.dtype(np.float16): "f16"}.get(w.dtype, "f32")
 
 
 def _u(a):
@@ -21,8 +27,7 @@ def _u(a):
 @pytest.mark.parametrize("case", CODEC_CASES)
 def test_quantize_matches_reference(golden, case):
     w = golden[f"{case}.w"]
-    dtype = "bf16" if w.dtype == np.uint16 else "f32"
-    packed, scale, zero, padding = o.quantize(w, 64, dtype)
+    packed, scale, zero, padding = o.quantize(w, 64, _dtype(w))
     assert np.array_equal(packed, golden[f"{case}.packed"])
     assert np.array_equal(_u(scale), _u(golden[f"{case}.scale"]))
     assert np.array_equal(_u(zero), _u(golden[f"{case}.zero"]))
@@ -32,9 +37,8 @@ def test_quantize_matches_reference(golden, case):
 @pytest.mark.parametrize("case", CODEC_CASES)
 def test_dequantize_matches_reference(golden, case):
     w = golden[f"{case}.w"]
-    dtype = "bf16" if w.dtype == np.uint16 else "f32"
     deq = o.dequantize(golden[f"{case}.packed"], golden[f"{case}.scale"], golden[f"{case}.zero"],
-                       k=w.shape[1], out=dtype)
+                       k=w.shape[1], out=_dtype(w))
     assert np.array_equal(_u(deq), _u(golden[f"{case}.deq"]))
 
 
