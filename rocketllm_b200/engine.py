@@ -305,6 +305,10 @@ class RocketModel:
                                    prefetching, copy_streams, chunk_bytes, io_workers,
                                    host_budget, storage_depth)
             return
+        if host_budget is not None:
+            raise ValueError("host_budget applies to a layer-shard directory "
+                             "(shards.split_rw4_layers): a checkpoint or model loads whole into "
+                             "host memory")
         if isinstance(model_or_path, (str, os.PathLike)):
             from transformers import AutoModelForCausalLM
             model = AutoModelForCausalLM.from_pretrained(str(model_or_path), dtype=dtype)

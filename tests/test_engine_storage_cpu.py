@@ -151,3 +151,8 @@ def test_in_memory_streaming_windows_and_pins(cpu_engine, window, pinned):
                for i in range(st.streamed)]
     assert per_pass == sum(1 for n in sharing if n > 1)
     rm.close()
+
+
+def test_host_budget_needs_a_shard_directory():
+    with pytest.raises(ValueError, match="layer-shard directory"):
+        engine.RocketModel(_plain_llama(), device="cpu", vram_budget=1, host_budget=1)
