@@ -135,6 +135,16 @@ def split_rw4_layers(model, out_dir):
     return out_dir
 
 
+def _faults_from_env():
+    """Read ordinals to fail from ``RW4_FAULT`` (``read:N`` items, comma-separated)."""
+    out = set()
+    for item in os.environ.get("RW4_FAULT", "").split(","):
+        kind, _, n = item.strip().partition(":")
+        if kind == "read" and n.isdigit():
+            out.add(int(n))
+    return out
+
+
 class LayerShardReader:
     """Reads layer blobs of a directory written by :func:`split_rw4_layers`.
 
@@ -147,8 +157,13 @@ class LayerShardReader:
 
     MIN_STRETCH = 4 << 20
 
-    def __init__(self, root, io_workers=1):
+    def __init__(self, root, io_workers=1, faults=None):
         self.root = str(root)
+        # host-side fault injection: the listed reads (1-based, in issue order, read_into and
+        # read_tensor alike) raise IOError instead of reading; ``RW4_FAULT=read:3[,read:7...]``
+        # in the environment sets them when ``faults`` is not given
+        self.faults = set(faults) if faults is not None else _faults_from_env()
+        self._issued = 0
         with open(os.path.join(self.root, INDEX)) as f:
             self.index = json.load(f)
         self.layers = self.index["layers"]
@@ -234,6 +249,7 @@ class LayerShardReader:
         if buffer.dtype != torch.uint8 or buffer.numel() < nbytes or buffer.is_cuda:
             raise ValueError("read_into needs a CPU uint8 buffer of at least the blob's size")
         path = os.path.join(self.root, rec["file"])
+        self._maybe_fault(path)
         view = memoryview(buffer[:nbytes].numpy()).cast("B")
         direct_ok = (hasattr(os, "O_DIRECT") and buffer.data_ptr() % DATA_ALIGN == 0
                      and start % DATA_ALIGN == 0)
@@ -304,6 +320,7 @@ class LayerShardReader:
               or not out.is_contiguous()):
             raise ValueError(f"out must be a contiguous CPU {dtype} tensor of shape {shape}")
         view = memoryview(out.view(-1).view(torch.uint8).numpy()).cast("B")
+        self._maybe_fault(os.path.join(self.root, rec["file"]))
         fd = os.open(os.path.join(self.root, rec["file"]), os.O_RDONLY)
         try:
             done = 0
@@ -319,6 +336,13 @@ class LayerShardReader:
             self.reads += 1
             self.bytes_read += nbytes
         return out
+
+    def _maybe_fault(self, path):
+        with self._lock:
+            self._issued += 1
+            n = self._issued
+        if n in self.faults:
+            raise IOError(f"{path}: injected read fault (read {n})")
 
     def stats(self):
         return {"layers": len(self.layers), "reads": self.reads, "bytes_read": self.bytes_read,

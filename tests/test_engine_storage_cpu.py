@@ -156,3 +156,36 @@ def test_in_memory_streaming_windows_and_pins(cpu_engine, window, pinned):
 def test_host_budget_needs_a_shard_directory():
     with pytest.raises(ValueError, match="layer-shard directory"):
         engine.RocketModel(_plain_llama(), device="cpu", vram_budget=1, host_budget=1)
+
+
+def test_an_injected_storage_read_fault_fails_one_pass_and_the_next_reads_again(
+        tmp_path, cpu_engine, monkeypatch):
+    """``RW4_FAULT=read:8``: the eighth shard read raises (host-side injection, nothing on a
+    device).  The pass that needs it ends with that IOError, no lease is left behind, and the
+    next pass reads the layer again and gives the model's own logits."""
+    model = _plain_llama()
+    root = split_rw4_layers(model, str(tmp_path / "shards"))
+    rest, layers = engine.footprint(model)
+    monkeypatch.setenv("RW4_FAULT", "read:8")
+    rm = engine.RocketModel(root, device="cpu", dtype=torch.float32,
+                            vram_budget=rest + 2 * max(layers) + 64 * 1024, window=2,
+                            kv_cache="fp16", host_budget=0, storage_depth=2)
+    st = rm.streamer
+    assert st.storage.reader.faults == {8}
+    ids = torch.randint(0, 96, (1, 7), generator=torch.Generator().manual_seed(8))
+    with torch.no_grad():
+        want = model(ids).logits
+        failed = 0
+        for _ in range(4):
+            try:
+                got = rm(ids).logits
+            except IOError as e:
+                assert "injected read fault" in str(e)
+                failed += 1
+                continue
+            assert torch.equal(got, want)
+        assert failed == 1
+    assert st.storage.reader.stats()["reads"] >= 3 * 5          # three whole passes read
+    ahead = list(st.storage._pending.values())
+    rm.close()
+    assert all(f.result().released for f in ahead)

@@ -114,3 +114,25 @@ def test_a_failed_expert_parallel_rank_ends_the_exchange_with_an_error():
         mp.spawn(_ep_worker, args=(2, 29751, out), nprocs=2, join=True)
         assert out[1][0].startswith("RuntimeError: injected failure"), dict(out)
         assert out[0][0] != "finished" and out[0][1] < 6 * TIMEOUT_S, dict(out)
+
+
+def test_injected_read_faults_raise_and_the_reader_carries_on(tmp_path, monkeypatch):
+    """Host-side fault injection (``faults=`` or ``RW4_FAULT=read:N``): the listed reads raise
+    IOError, the others read normally."""
+    from test_shards_cpu import tiny_rw4_model
+
+    from rocketllm_b200.shards import LayerShardReader, split_rw4_layers
+    root = split_rw4_layers(tiny_rw4_model(6), str(tmp_path / "shards"))
+    reader = LayerShardReader(root, faults={2})
+    buf = torch.empty(max(l["nbytes"] for l in reader.layers), dtype=torch.uint8)
+    reader.read_into(0, buf)
+    with pytest.raises(IOError, match="injected read fault"):
+        reader.read_into(0, buf)
+    reader.read_into(1, buf)
+    assert reader.stats()["reads"] == 2
+    monkeypatch.setenv("RW4_FAULT", "read:1, read:3")
+    env = LayerShardReader(root)
+    assert env.faults == {1, 3}
+    with pytest.raises(IOError, match="injected read fault"):
+        env.read_tensor(0, "mlp.up_proj.weight_packed")
+    env.read_tensor(0, "mlp.up_proj.weight_packed")
