@@ -70,8 +70,8 @@ def test_linear_golden_reference_output(golden, cuda):
 @pytest.mark.parametrize("m", [17, 64, 255, 256, 300, 512])
 @pytest.mark.parametrize("k,n", [(4096, 4096), (1024, 200)])
 def test_gemm_matches_oracle(cuda, m, k, n):
-    """The tcgen05 GEMM itself (forced: the dispatcher sends most of these sizes to the GEMV),
-    all three token-tile widths and ragged N."""
+    """The tcgen05 GEMM itself (forced with path=2, so the test holds whatever the dispatcher
+    picks for these sizes), all three token-tile widths and ragged N."""
     packed, scale, zero = make_weight(n, k, device=cuda, seed=m + n)
     x = make_activation(m, k, device=cuda, seed=k + m)
     y = kernels.linear(x, packed, scale, zero, path=2)
