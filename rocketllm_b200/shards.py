@@ -6,9 +6,9 @@ byte-range reader (``rocketllm/streaming/shards.py``, ``streaming/loader.py:161-
 ``LayerLoader.plan`` reads only the header, ``load``/``_fill`` read the tensors into one leased
 buffer).  Here a layer file's data section IS the layer's host blob: every tensor sits at the
 256-byte aligned offset the engine binds device views at, so loading a layer is one positioned
-read straight into pinned memory -- no per-tensor copy, no repacking -- and the data section starts
-on a 4096-byte boundary so the read can bypass the page cache (``O_DIRECT``) where the file system
-allows it.
+read (or a few adjacent ones on I/O threads, for a large layer) straight into pinned memory -- no
+per-tensor copy, no repacking -- and the data section starts on a 4096-byte boundary so the read
+can bypass the page cache (``O_DIRECT``) where the file system allows it.
 
 Each file is still a valid safetensors container: the JSON header names every tensor with its
 dtype, shape and data offsets, gaps between aligned tensors are covered by ``__rw4_pad_<n>`` uint8

@@ -1,8 +1,9 @@
 """RW4 layer shards (the reference's per-layer split + byte-range reader, rocketllm/utils.py:470-621,
 streaming/shards.py, streaming/loader.py:161-236), on the CPU: every file is a valid safetensors
-container whose tensors equal the model's, a layer's blob read with one positioned read holds
-every tensor at the engine's aligned offset, the index alone plans a layer, and a finished layer
-(.done marker) is not rewritten."""
+container whose tensors equal the model's, a layer's blob read by positioned reads (one, or
+byte-balanced stretches on I/O threads) holds every tensor at the engine's aligned offset, the
+index alone plans a layer, a finished layer (.done marker) is not rewritten, and the storage tier
+reads ahead in scan order into leases it gives back."""
 import os
 
 import pytest
