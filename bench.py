@@ -798,15 +798,18 @@ def sweep(args):
         for m in ms_list:
             x = make_activation(m, k, device=device, seed=100 + i)
             y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
+            path = args.sweep_path or None
+            if path == 2 and m <= 16:
+                continue
             for _ in range(args.warmup):
                 for w in ws:
-                    kernels.linear(x, *w, out=y)
+                    kernels.linear(x, *w, out=y, path=path)
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             reps = max(args.steps, copies)
             with torch.cuda.graph(g):
                 for r in range(reps):
-                    kernels.linear(x, *ws[r % copies], out=y)
+                    kernels.linear(x, *ws[r % copies], out=y, path=path)
             g.replay()
             torch.cuda.synchronize()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -817,7 +820,8 @@ def sweep(args):
             ms = a.elapsed_time(b) / reps
             gbs = alg_bytes(m, k, n) / (ms * 1e-3) / 1e9
             tfl = 2 * m * n * k / (ms * 1e-3) / 1e12
-            print(json.dumps({"K": k, "N": n, "M": m, "path": kernels.linear_path(m, k, n),
+            print(json.dumps({"K": k, "N": n, "M": m,
+                              "path": path or kernels.linear_path(m, k, n),
                               "us": round(ms * 1e3, 2), "gbs": round(gbs, 1),
                               "hbm_frac": round(gbs / peak, 4), "tflops": round(tfl, 1),
                               "tensor_frac": round(tfl / tflops_peak, 4),
@@ -1054,6 +1058,9 @@ def main():
                     help="kernel sweep over the sweep shapes x --sweep-m (one JSON line each)")
     ap.add_argument("--sweep-m", default="1,4,16,64,512,2048")
     ap.add_argument("--sweep-shapes", default="all", help="'all' or KxN[,KxN...]")
+    ap.add_argument("--sweep-path", type=int, default=0,
+                    help="force a kernel in --sweep: 2 tcgen05 GEMM, 3 GEMV slices (0 = the "
+                         "library's choice)")
     ap.add_argument("--decode-only", action="store_true",
                     help="only the model decode section (one JSON line)")
     ap.add_argument("--decode-batches", default="1,16")

@@ -75,8 +75,14 @@ int rw4_quantize(const void* w, int32_t w_dtype, int64_t N, int64_t K, int32_t g
  * rw4_linear: y[M, N] = x[M, K] . W[N, K]^T, bf16 in and out, fp32 accumulation, W in RW4.
  * Replaces the nn.Linear / F.linear call a transformers module makes on a dequantized weight
  * (transformers models/llama/modeling_llama.py:171-184 via rocketllm/base.py:848-855).
- * M <= 16 runs the dequant-GEMV; larger M the tensor-core GEMM (rw4_linear_path).  group must be 64 and K a multiple of 64; x, y and packed
- * must be 16-byte aligned, scale and zero 8-byte aligned.
+ * M <= 64 runs the dequant-GEMV (16-row batch slices above 16 rows), larger M the tensor-core GEMM
+ * (rw4_linear_path).  The GEMV multiplies by the exact fp32 weight code * scale + zero and gives
+ * each row of y the same bits at every M <= 64 (a row's output does not depend on the rows beside
+ * it); the GEMM multiplies by the reference's bf16-rounded weight (dequantize().to(bfloat16),
+ * rocketllm/quant/kv_cache.py:257).  group must be 64 and K a multiple of 64; x, y and packed
+ * must be 16-byte aligned, scale and zero 8-byte aligned.  Most GEMV calls need a workspace
+ * (rw4_linear_workspace_size); this entry point takes it from the device's stream-ordered memory
+ * pool on `stream` and returns it there (rw4_linear_ws takes a caller-owned one instead).
  */
 int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
@@ -91,6 +97,21 @@ int rw4_linear_path(int64_t M, int64_t K, int64_t N);
 int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                        const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
                        void* y_bf16, int32_t path, void* stream);
+
+/* Bytes of device workspace rw4_linear_ws needs for (M, K, N) on `path` (0 = the path
+ * rw4_linear_path picks): the GEMV's converted activations (about 2*M*K bytes; 0 for one row
+ * that the GEMV converts itself, and for the GEMM).  Host-only.  No reference counterpart: the
+ * reference's F.linear takes no workspace. */
+int rw4_linear_workspace_size(int64_t M, int64_t K, int64_t N, int32_t path, size_t* bytes);
+
+/* rw4_linear with a caller-owned device workspace of workspace_bytes (>= the size above, 256-byte
+ * aligned; may be NULL when that size is 0) on `path` (0 = rw4_linear_path's choice).  The
+ * workspace is written and read by the work queued on `stream`; it must not be shared with work
+ * that can run at the same time.  Same replacement as rw4_linear. */
+int rw4_linear_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                  const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
+                  void* y_bf16, int32_t path, void* workspace, size_t workspace_bytes,
+                  void* stream);
 
 /* Reads the library's device status word on the current device after the work queued on `stream`
  * (synchronises that stream): bit 1 = a bounded wait inside a kernel gave up (the kernel returned

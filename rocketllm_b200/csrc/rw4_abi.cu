@@ -32,7 +32,8 @@ int sm_count() {
 }
 
 int gemv_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
-                const void* zr, int64_t N, void* y, cudaStream_t s);
+                const void* zr, int64_t N, void* y, cudaStream_t s, void* ws, size_t ws_bytes);
+size_t gemv_workspace(int64_t M, int64_t K, int64_t N);
 int gemm_tc_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                    const void* zr, int64_t N, void* y, cudaStream_t s);
 bool gemm_tc_supported(int64_t M, int64_t K, int64_t N);
@@ -71,25 +72,42 @@ extern "C" int rw4_last_error(char* buf, size_t n) {
   return (int)e.size();
 }
 
-// Above 16 rows the tensor-core GEMM runs whenever it applies: it multiplies by the reference's
-// bf16-rounded dequantized weight, as the reference does, while the GEMV multiplies by the exact
-// weight.  (Measured: GEMV batch slices would be faster up to M = 32 on every sweep shape and up to
-// M = 128 on small weights, but mixing the two roundings inside one prefill moved a Mixtral
-// model's logits past the 2e-2 parity bar; rw4_linear_on_path runs either kernel on request.)
+// Up to 64 rows the GEMV runs (16-row batch slices above 16 rows), above that the tensor-core GEMM
+// whenever it applies.  The GEMV multiplies by the exact fp32 weight and gives a row the same bits
+// at every M <= 64, so decode batches and speculative verify passes round like a one-token step;
+// the GEMM (prefill-sized M) multiplies by the reference's bf16-rounded dequantized weight, as the
+// reference's F.linear over dequantize().to(bf16) does.
+constexpr int64_t kGemvMaxRows = 64;
+
 extern "C" int rw4_linear_path(int64_t M, int64_t K, int64_t N) {
   if (M < 0 || K <= 0 || N < 0 || K % 64) return RW4_EINVAL;
   if (M <= 16) return 1;
-  if (rw4::gemm_tc_supported(M, K, N)) return 2;
+  if (M > kGemvMaxRows && rw4::gemm_tc_supported(M, K, N)) return 2;
   return 3;
 }
 
-extern "C" int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
-                                  const void* scale_f16, const void* zero_f16, int64_t N,
-                                  int32_t group, void* y_bf16, int32_t path, void* stream) {
+extern "C" int rw4_linear_workspace_size(int64_t M, int64_t K, int64_t N, int32_t path,
+                                         size_t* bytes) {
+  using namespace rw4;
+  if (!bytes) return fail(RW4_EINVAL, "rw4_linear_workspace_size: null output");
+  *bytes = 0;
+  if (M < 0 || K <= 0 || N < 0 || K % 64)
+    return fail(RW4_EINVAL, "rw4_linear_workspace_size: bad shape M=%lld K=%lld N=%lld",
+                (long long)M, (long long)K, (long long)N);
+  if (path == 0) path = rw4_linear_path(M, K, N);
+  if (M > 0 && N > 0 && (path == 1 || path == 3)) *bytes = gemv_workspace(M, K, N);
+  return RW4_OK;
+}
+
+extern "C" int rw4_linear_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                             const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
+                             void* y_bf16, int32_t path, void* workspace, size_t workspace_bytes,
+                             void* stream) {
   using namespace rw4;
   int st = check_linear_args("rw4_linear", x_bf16, M, K, packed, scale_f16, zero_f16, N, group,
                              y_bf16);
   if (st != RW4_OK || M == 0 || N == 0) return st;
+  if (path == 0) path = rw4_linear_path(M, K, N);
   if (path == 2 && !gemm_tc_supported(M, K, N))
     return fail(RW4_EINVAL, "rw4_linear: the tensor-core GEMM needs M > 16 (M=%lld)",
                 (long long)M);
@@ -97,7 +115,8 @@ extern "C" int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, cons
   switch (path) {
     case 1:
     case 3:
-      return gemv_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s);
+      return gemv_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s, workspace,
+                         workspace_bytes);
     case 2:
       return gemm_tc_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s);
     default:
@@ -106,12 +125,38 @@ extern "C" int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, cons
   }
 }
 
+// The entry points without a workspace argument take one, when the call needs one, from the
+// device's stream-ordered pool (cudaMallocAsync / cudaFreeAsync on the caller's stream).
+extern "C" int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                                  const void* scale_f16, const void* zero_f16, int64_t N,
+                                  int32_t group, void* y_bf16, int32_t path, void* stream) {
+  using namespace rw4;
+  int st = check_linear_args("rw4_linear", x_bf16, M, K, packed, scale_f16, zero_f16, N, group,
+                             y_bf16);
+  if (st != RW4_OK || M == 0 || N == 0) return st;
+  size_t bytes = 0;
+  st = rw4_linear_workspace_size(M, K, N, path, &bytes);
+  if (st != RW4_OK) return st;
+  cudaStream_t s = as_stream(stream);
+  void* ws = nullptr;
+  if (bytes) {
+    st = cuda_status(cudaMallocAsync(&ws, bytes, s), "rw4_linear workspace");
+    if (st != RW4_OK) return st;
+  }
+  st = rw4_linear_ws(x_bf16, M, K, packed, scale_f16, zero_f16, N, group, y_bf16, path, ws,
+                     bytes, stream);
+  if (ws) {
+    const int fst = cuda_status(cudaFreeAsync(ws, s), "rw4_linear workspace release");
+    if (st == RW4_OK) st = fst;
+  }
+  return st;
+}
+
 extern "C" int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                           const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
                           void* y_bf16, void* stream) {
-  const int path = rw4_linear_path(M, K, N);
-  return rw4_linear_on_path(x_bf16, M, K, packed, scale_f16, zero_f16, N, group, y_bf16,
-                            path < 0 ? 1 : path, stream);
+  return rw4_linear_on_path(x_bf16, M, K, packed, scale_f16, zero_f16, N, group, y_bf16, 0,
+                            stream);
 }
 
 // ---- device status word and TMA descriptors ---------------------------------------------------

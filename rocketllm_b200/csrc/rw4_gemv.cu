@@ -255,17 +255,26 @@ namespace rw4 {
 
 // y = x W^T for any M via 16-row batch slices (M <= 16: one slice).
 bool gemv_tma_supported(int64_t K);
+size_t gemv_tma_workspace(int64_t M, int64_t K, int64_t N);
 int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
-                    const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles);
+                    const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
+                    size_t ws_bytes);
+
+// Workspace bytes the GEMV needs for (M, K, N): the TMA kernel's x-prep arrays (none for a row it
+// converts itself); the register-staged kernel needs none.
+size_t gemv_workspace(int64_t M, int64_t K, int64_t N) {
+  static const bool no_tma = getenv("RW4_GEMV_NO_TMA") != nullptr;
+  return (!no_tma && gemv_tma_supported(K)) ? gemv_tma_workspace(M, K, N) : 0;
+}
 
 int gemv_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
-                const void* zr, int64_t N, void* y, cudaStream_t s) {
+                const void* zr, int64_t N, void* y, cudaStream_t s, void* ws, size_t ws_bytes) {
   const int nt = (M <= 8) ? 1 : 2;
   const int forced = rows_per_cta_override();
   static const bool no_tma = getenv("RW4_GEMV_NO_TMA") != nullptr;
   // the TMA kernel picks its own CTA shape (gemv_tma_policy) unless RW4_GEMV_ROW_TILES forces one
   if (!no_tma && gemv_tma_supported(K))
-    return gemv_tma_launch(x, M, K, wq, sc, zr, N, y, s, forced);
+    return gemv_tma_launch(x, M, K, wq, sc, zr, N, y, s, forced, ws, ws_bytes);
   // register-staged kernel (K % 512 != 0): 32-row CTAs from N >= 18944, else 16
   const int R = (forced == 1 || forced == 2) ? forced : (N >= 16 * 2 * 148 * 4) ? 2 : 1;
   const auto* xb = static_cast<const __nv_bfloat16*>(x);

@@ -57,15 +57,14 @@ __device__ __forceinline__ void a_frag(uint2 wa, uint2 wb, int j, uint32_t (&a)[
 }
 
 
-// ---- fp16 variant for one activation row ------------------------------------------------------
+// ---- fp16 variant (dense path: activations converted per row, rw4_gemv_tma.cu) -------------
 // The two nibbles of a byte feed the tensor cores without a shift between them: under the fp16
 // pattern 0x6400 (1024, ulp 1) the low nibble gives 1024 + c and the high nibble, masked in place,
-// 1024 + 16 c.  The activation of every high-nibble (odd-k) slot is pre-scaled by 2^-12 and every
-// low-nibble (even-k) slot by 2^-8, so both classes contribute 2^-8 * c * x; one shift by 8
-// serves the two nibbles of the byte above.  Four codes per shift instead of two per shift.
+// 1024 + 16 c.  The activation of every high-nibble (odd-k) slot therefore carries an extra 2^-4
+// relative to the low-nibble (even-k) slots, so both classes contribute c * x times the row's
+// common power of two; one shift by 8 serves the two nibbles of the byte above.  Four codes per
+// shift instead of two per shift.
 constexpr uint32_t kMagicF16 = 0x64006400u;   // f16 pair (1024, 1024)
-constexpr uint32_t kF16_1 = 0x3C003C00u;      // f16 pair (1, 1): 1 * x 2^-8 = 2^-8 x
-constexpr uint32_t kF16_16 = 0x4C004C00u;     // f16 pair (16, 16): 16 * x 2^-12 = 2^-8 x
 
 __device__ __forceinline__ uint32_t nib_lo_f16(uint32_t v) {
   uint32_t r;
@@ -93,18 +92,25 @@ __device__ __forceinline__ void a_frag_f16(uint2 wa, uint2 wb, int j, uint32_t (
   a[3] = nib_hi_f16(xb);
 }
 
-// 16 bf16 activations -> the 8 f16 pair registers b[j][0..1] in the K order above, even-k values
-// times 2^-8, odd-k values times 2^-12 (exact for |x| >= 2^-6 resp. 2^-2; smaller values keep
-// fp16's subnormal spacing 2^-24, i.e. an absolute error below 2^-12 resp. 2^-16).
 __device__ __forceinline__ uint32_t f16_pair(float lo, float hi) {
   uint32_t r;
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
-__device__ __forceinline__ void x16_to_f16_frag(uint4 lo, uint4 hi, uint32_t (&o)[8]) {
+
+// 16 bf16 activations (natural order, two 16-byte words) -> the 8 fp16 pair registers
+// o[2j], o[2j+1] = B operand of MMA step j in the K order of a_frag_f16, even-k values times
+// 2^e and odd-k values times 2^(e-4).  The power of two is applied as two exact multiplications
+// (p1 * p2 = 2^e, p1 and p2 normal fp32 for any exponent a bf16 row can need), so the result is
+// x * 2^e rounded once to fp16 -- exact whenever that value is an fp16 normal.
+// Also returns the chunk's two sums, each added in natural order: xs = sum of x * 2^e (exact
+// products) and hs = sum of the 16 fp16 values as the tensor cores will see them.
+__device__ __forceinline__ void x16_to_f16_frag(uint4 lo, uint4 hi, float p1, float p2,
+                                                uint32_t (&o)[8], float& xs, float& hs) {
   const uint32_t w[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
-  auto ev = [](uint32_t v) { return __uint_as_float(v << 16) * 0.00390625f; };       // 2^-8
-  auto od = [](uint32_t v) { return __uint_as_float(v & 0xFFFF0000u) * 0.000244140625f; };
+  const float p2o = p2 * 0.0625f;  // odd slots: 2^(e-4)
+  auto ev = [&](uint32_t v) { return (__uint_as_float(v << 16) * p1) * p2; };
+  auto od = [&](uint32_t v) { return (__uint_as_float(v & 0xFFFF0000u) * p1) * p2o; };
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     // values 8h .. 8h+7 sit in w[4h .. 4h+3] as (x0 x1)(x2 x3)(x4 x5)(x6 x7)
@@ -113,6 +119,49 @@ __device__ __forceinline__ void x16_to_f16_frag(uint4 lo, uint4 hi, uint32_t (&o
     o[4 * h + 2] = f16_pair(ev(w[4 * h + 1]), ev(w[4 * h + 3]));  // (x2, x6)
     o[4 * h + 3] = f16_pair(od(w[4 * h + 1]), od(w[4 * h + 3]));  // (x3, x7)
   }
+  xs = 0.f;
+  hs = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {  // 2^e * x exactly (power-of-two scaling of a bf16 value)
+    xs += ev(w[i]);
+    xs += (__uint_as_float(w[i] & 0xFFFF0000u) * p1) * p2;
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const __half2 h2 = *reinterpret_cast<const __half2*>(&o[i]);
+    hs += __low2float(h2);
+    hs += __high2float(h2);
+  }
+}
+
+// Sums of a group of 64 from its four chunks, held by lanes 4j .. 4j+3 of a warp (every lane of the
+// warp must call this): one butterfly, the same order on every lane and in every kernel.
+__device__ __forceinline__ void group_sums(float& xs, float& hs) {
+  xs += __shfl_xor_sync(0xFFFFFFFFu, xs, 1);
+  xs += __shfl_xor_sync(0xFFFFFFFFu, xs, 2);
+  hs += __shfl_xor_sync(0xFFFFFFFFu, hs, 1);
+  hs += __shfl_xor_sync(0xFFFFFFFFu, hs, 2);
+}
+
+// Largest |x| of 8 bf16 values as a bit pattern (bf16 magnitudes order like their bit patterns).
+__device__ __forceinline__ uint32_t absmax8(uint4 v) {
+  const uint32_t m2 = __vmaxu2(__vmaxu2(v.x & 0x7FFF7FFFu, v.y & 0x7FFF7FFFu),
+                               __vmaxu2(v.z & 0x7FFF7FFFu, v.w & 0x7FFF7FFFu));
+  return max(m2 & 0xFFFFu, m2 >> 16);
+}
+
+// The row's exponent e: its largest magnitude (bf16 bits) times 2^e lies in [2^14, 2^15), so every
+// even-k value x 2^e and odd-k value x 2^(e-4) fits fp16.  An all-zero row, or one holding inf or
+// NaN, keeps e = 0.
+__device__ __forceinline__ int row_exponent(uint32_t maxbits) {
+  return (maxbits != 0 && maxbits < 0x7F80u) ? 14 - ilogbf(__uint_as_float(maxbits << 16)) : 0;
+}
+
+// 2^e as two fp32 normals (|e| <= 147 for any bf16 row).
+__device__ __forceinline__ void exp_factors(int e, float& p1, float& p2) {
+  const int e1 = e >> 1, e2 = e - e1;
+  p1 = __int_as_float((127 + e1) << 23);
+  p2 = __int_as_float((127 + e2) << 23);
 }
 
 }  // namespace frag

@@ -1,36 +1,129 @@
 // RW4 dequant-GEMV, TMA-fed (K a multiple of 512): y[M, N] = x[M, K] . W[N, K]^T for decode
 // batches, one 16-row batch slice per grid row.  The pipeline itself lives in
-// rw4_gemv_tma_body.cuh; this file encodes the tensor maps and launches it.
+// rw4_gemv_tma_body.cuh; this file converts the activations and launches it.
+//
+// The activations are multiplied as fp16 values of x * 2^e, one power of two per row chosen from
+// the row's largest magnitude, so that a row's conversion depends on that row alone: the GEMV then
+// gives every row the same bits whether it runs alone (M = 1), in a decode batch or in a 16-row
+// slice of a larger M, and x scaled by a power of two gives y scaled by exactly that power.
+//
+//  * one row whose CTA K range fits 32 KB of shared memory: the GEMV converts it in its own
+//    prologue (XQ) -- one launch, no workspace;
+//  * otherwise two launches: the x-prep kernel (rw4_xprep_kernel, one CTA per activation row)
+//    writes the converted rows in MMA fragment order, per group of 64 the sum of x times 2^e and
+//    minus 1024 times the sum of the fp16 values, and e, into a caller-provided workspace
+//    (xprep_layout); the GEMV (XP) reads them through its TMA ring.  The pass reads and writes
+//    M*K*2 bytes once per call; the GEMV is launched with programmatic dependent launch, so its
+//    weight prefetch overlaps the pass.
+// Both paths use the same conversion helpers in the same order (rw4_gemv_frag.cuh), so they give
+// the same bits.
 #include <atomic>
 
 #include "rw4_gemv_tma_body.cuh"
+
+namespace rw4 {
+
+// Byte offsets of the x-prep arrays inside a workspace (each 256-byte aligned).
+struct XPrepLayout {
+  int64_t Mpad = 0;         // rows padded to even (the side box is 16 bytes wide per row pair)
+  size_t xf = 0;            // fp16 [M, K], fragment order within each 16-value chunk
+  size_t side = 0;          // fp32 pairs [K/64][Mpad]: (2^e * sum x, -1024 * sum fp16(x 2^e))
+  size_t row_exp = 0;       // int32 [Mpad]: e per row
+  size_t bytes = 0;         // total
+};
+
+inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+XPrepLayout xprep_layout(int64_t M, int64_t K) {
+  XPrepLayout l;
+  l.Mpad = (M + 1) & ~int64_t(1);
+  l.xf = 0;
+  l.side = align256((size_t)M * K * 2);
+  l.row_exp = l.side + align256((size_t)(K / 64) * l.Mpad * 8);
+  l.bytes = l.row_exp + align256((size_t)l.Mpad * 4);
+  return l;
+}
+
+}  // namespace rw4
 
 namespace {
 
 using namespace rw4;
 using namespace rw4::gemv_tma;
 
+constexpr int kPrepThreads = 256;
+
+// One CTA per row m < Mpad; rows M..Mpad-1 only zero their side pairs and exponent.
+__global__ void __launch_bounds__(kPrepThreads)
+    rw4_xprep_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, int Mpad,
+                     uint4* __restrict__ xf, float2* __restrict__ side, int* __restrict__ row_exp) {
+  const int m = blockIdx.x;
+  const int G = K / 64;
+  // x comes from the previous kernel on the stream; the GEMV after us may start launching now (it
+  // reads nothing of ours before its own griddepcontrol.wait, which waits for this grid)
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (m >= M) {
+    for (int g = threadIdx.x; g < G; g += kPrepThreads)
+      side[(int64_t)g * Mpad + m] = make_float2(0.f, 0.f);
+    if (threadIdx.x == 0) row_exp[m] = 0;
+    return;
+  }
+  const __nv_bfloat16* xr = x + (int64_t)m * K;
+  // 1. largest magnitude
+  uint32_t mx = 0;
+  for (int i = threadIdx.x; i < K / 8; i += kPrepThreads)
+    mx = max(mx, frag::absmax8(ldg_u4(xr + 8 * i)));
+  mx = __reduce_max_sync(0xFFFFFFFFu, mx);
+  __shared__ uint32_t wmax[kPrepThreads / 32];
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  uint32_t a = 0;
+#pragma unroll
+  for (int w = 0; w < kPrepThreads / 32; ++w) a = max(a, wmax[w]);
+  const int e = frag::row_exponent(a);
+  if (threadIdx.x == 0) row_exp[m] = e;
+  float p1, p2;
+  frag::exp_factors(e, p1, p2);
+  // 2. convert, 16 values per thread; the 4 chunks of a group sit on 4 consecutive lanes
+  const int chunks = K / 16;
+  for (int base = 0; base < chunks; base += kPrepThreads) {
+    const int c = base + threadIdx.x;
+    float xs = 0.f, hs = 0.f;
+    if (c < chunks) {
+      uint32_t o[8];
+      frag::x16_to_f16_frag(ldg_u4(xr + 16 * c), ldg_u4(xr + 16 * c + 8), p1, p2, o, xs, hs);
+      uint4* dst = xf + ((int64_t)m * K + 16 * c) / 8;
+      dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+      dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+    }
+    frag::group_sums(xs, hs);
+    if (c < chunks && (c & 3) == 0)
+      side[(int64_t)(c >> 2) * Mpad + m] = make_float2(xs, -1024.f * hs);
+  }
+}
+
 // Two CTAs per SM: the register cap this implies (<= 113 per thread) measurably improves the
 // schedule (16 consumer warps per SM sharing the ALU pipe with the producers).  KS > 1 splits K
 // over a (1, 1, KS) thread-block cluster (grid.z = KS) reduced through distributed shared memory.
-// XT: activations through the TMA ring (default); otherwise the consumers load them from global
-// memory (RW4_GEMV_X_GLOBAL=1, kept for comparison).  M1: one activation row.  XF: one row, in
-// fp16 from shared memory (rw4_gemv_frag.cuh), the default for M = 1 when the CTA's K range fits
-// 32 KB of shared memory (RW4_GEMV_NO_F16=1 keeps bf16).
-template <int NT, int R, int S, int KS, bool XT, bool M1, bool XF = false>
+// M1: one activation row.  XQ (with M1): the CTA converts that row itself (no x-prep launch, no
+// workspace); otherwise the x-prep output arrives through the TMA ring.
+template <int NT, int R, int S, int KS, bool M1, bool XQ>
 __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
     rw4_gemv_tma_kernel(const __grid_constant__ CUtensorMap tm_codes,
                         const __grid_constant__ CUtensorMap tm_scale,
                         const __grid_constant__ CUtensorMap tm_zero,
                         const __grid_constant__ CUtensorMap tm_x,
+                        const __grid_constant__ CUtensorMap tm_side, const int* row_exp,
                         const __nv_bfloat16* __restrict__ x, int bm, int M, int K, int N,
                         __nv_bfloat16* __restrict__ y, unsigned int* status) {
   // batch slices are the fastest grid dimension: the CTAs of all slices of one row tile run
   // together, so the slices after the first find the tile's weights in L2
   const int m0 = blockIdx.x * 16;
-  body<NT, R, S, false, KS, XT, M1, XF>(&tm_codes, &tm_scale, &tm_zero, &tm_x, x, m0, bm,
-                                        min(16, M - m0), K, y + (int64_t)m0 * N, N,
-                                        blockIdx.y * Layout<R, S>::BR, N, 0, status);
+  body<NT, R, S, false, KS, !XQ, M1, !XQ, XQ>(&tm_codes, &tm_scale, &tm_zero, &tm_x, &tm_side,
+                                              row_exp, x, m0, bm, min(16, M - m0), K,
+                                              y + (int64_t)m0 * N, N,
+                                              blockIdx.y * Layout<R, S>::BR, N, 0, status);
 }
 
 bool pdl_enabled() {
@@ -42,29 +135,48 @@ bool pdl_enabled() {
 // reserved per CTA).
 constexpr int kTwoPerSmSmem = 228 * 1024 / 3 + 1024;
 
-constexpr int kF16MaxStages = 32;  // fp16 activation row in shared memory: 1 KB per stage
-
-bool no_f16() {
-  static const bool on = getenv("RW4_GEMV_NO_F16") != nullptr;
-  return on;
+cudaLaunchAttribute pdl_attr() {
+  cudaLaunchAttribute a;
+  a.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  a.val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  return a;
 }
 
-bool x_global() {
-  static const bool on = getenv("RW4_GEMV_X_GLOBAL") != nullptr;
-  return on;
+int launch_xprep(const void* x, int M, int K, const XPrepLayout& l, uint8_t* ws,
+                 cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)l.Mpad);
+  cfg.blockDim = dim3(kPrepThreads);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1] = {pdl_attr()};
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t err = cudaLaunchKernelEx(
+      &cfg, rw4_xprep_kernel, static_cast<const __nv_bfloat16*>(x), M, K, (int)l.Mpad,
+      reinterpret_cast<uint4*>(ws + l.xf), reinterpret_cast<float2*>(ws + l.side),
+      reinterpret_cast<int*>(ws + l.row_exp));
+  if (err != cudaSuccess) return cuda_status(err, "rw4 x-prep launch");
+  return launch_status("rw4 x-prep launch");
+}
+
+// One activation row whose CTA K range fits the in-kernel conversion's shared memory: the GEMV
+// converts it itself (XQ).  Everything else goes through the x-prep pass.
+bool one_row_in_kernel(int64_t M, int64_t K, int ks) {
+  return M == 1 && ((K / kStageK) + ks - 1) / ks <= Layout<1, 1>::kXQMaxStages;
 }
 
 template <int NT, int R, int S, int KS = 1>
 int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, const void* zr,
-               int N, void* y, cudaStream_t stream) {
+               int N, void* y, const XPrepLayout& l, uint8_t* ws, cudaStream_t stream) {
   using L = Layout<R, S>;
   static_assert(L::kBars >= kConsumers * L::BR * (16 * NT + 1) * 4,
                 "reduction buffer must fit in the ring below the barriers");
-  CUtensorMap tc, ts, tz, tx;
+  CUtensorMap tc, ts, tz, tx, tside;
   const int G = K / 64;
   // activation rows per slice: the whole batch for M <= 8 (NT = 1), 16-row slices above
   const int bm = M < 16 ? M : 16;
   if (bm > 8 * NT) return fail(RW4_EINVAL, "gemv_tma: %d activation rows for NT=%d", M, NT);
+  const bool xq = NT == 1 && one_row_in_kernel(M, K, KS);
   int st = make_tensor_map_2d(&tc, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K / 2, K / 2, L::BR,
                               128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st == RW4_OK)
@@ -73,28 +185,32 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   if (st == RW4_OK)
     st = make_tensor_map_2d(&tz, zr, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, N, G, (uint64_t)G * 2,
                             L::BR, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
-  if (st == RW4_OK)
-    st = make_tensor_map_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, K, (uint64_t)K * 2,
-                            bm, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st != RW4_OK) return st;
-  const bool xt = !x_global();
+  if (xq) {
+    tx = tz;  // not read by the in-kernel conversion
+    tside = tz;
+  } else {
+    st = make_tensor_map_2d(&tx, ws + l.xf, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, M, K,
+                            (uint64_t)K * 2, bm, 256, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st == RW4_OK)
+      st = make_tensor_map_2d(&tside, ws + l.side, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, G,
+                              2 * l.Mpad, (uint64_t)l.Mpad * 8, 8, 2 * L::side_rows(bm),
+                              CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (st != RW4_OK) return st;
+  }
   const bool m1 = NT == 1 && M == 1;
-  const int cta_stages = ((K / kStageK) + KS - 1) / KS;
-  const bool xf = m1 && xt && !no_f16() && cta_stages <= kF16MaxStages;
-  const int variant = xf ? 4 : (xt ? 0 : 1) + (m1 ? 2 : 0);
-  auto kern = xf ? rw4_gemv_tma_kernel<NT, R, S, KS, false, NT == 1, NT == 1>
-              : xt ? (m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, true, NT == 1>
-                         : rw4_gemv_tma_kernel<NT, R, S, KS, true, false>)
-                   : (m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, false, NT == 1>
-                         : rw4_gemv_tma_kernel<NT, R, S, KS, false, false>);
+  const int variant = xq ? 2 : m1 ? 1 : 0;
+  auto kern = xq ? rw4_gemv_tma_kernel<NT, R, S, KS, NT == 1, NT == 1>
+              : m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, NT == 1, false>
+                   : rw4_gemv_tma_kernel<NT, R, S, KS, false, false>;
   // The dynamic shared memory limit is a per-device function attribute: set it once per device
-  // and kernel variant.
-  static std::atomic<uint32_t> attr_set[5];
+  // and kernel variant (this function is instantiated once per launch shape).
+  static std::atomic<uint32_t> attr_set[3];
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_set[variant].load() & (1u << dev))) {
-    const int need = xf ? L::kX + kF16MaxStages * 1024 + 1024 : L::dyn_smem(8 * NT);
-    const int most = need > kTwoPerSmSmem ? need : kTwoPerSmSmem;
+    const int largest = xq ? L::dyn_smem_xq(L::kXQMaxStages) : L::dyn_smem_xp(8 * NT);
+    const int most = largest > kTwoPerSmSmem ? largest : kTwoPerSmSmem;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most) !=
         cudaSuccess)
       return fail(RW4_ECUDA, "gemv_tma: cannot set dynamic shared memory size");
@@ -105,24 +221,24 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   const int64_t tiles = (N + L::BR - 1) / L::BR;
   if (tiles > 65535) return fail(RW4_EINVAL, "gemv_tma: N=%d needs more than 65535 row tiles", N);
   dim3 grid((M + 15) / 16, (unsigned)tiles, KS);
-  // Programmatic dependent launch: this grid may start while the previous kernel on the stream
-  // drains; it streams its weights at once and waits (griddepcontrol.wait) only before it reads x.
+  // Programmatic dependent launch: this grid may start while the kernel before it (the x-prep pass,
+  // or whatever produced x) runs; it streams its weights at once and waits (griddepcontrol.wait)
+  // only before it reads x.
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
   // At most two CTAs per SM: with smaller rings the block scheduler may stack three or four CTAs
   // of a one-wave grid on some SMs and leave others idle (measured: M=1 slower than M=8 on the
   // 4096-row shapes until the shared-memory request made a third CTA impossible).
-  const int smem_need = xf ? L::kX + cta_stages * 1024 + 1024
-                        : xt ? L::dyn_smem(bm) : L::kX + 1024;
+  const int cta_stages = ((K / kStageK) + KS - 1) / KS;
+  const int smem_need = xq ? L::dyn_smem_xq(cta_stages) : L::dyn_smem_xp(bm);
   cfg.dynamicSmemBytes = smem_need > kTwoPerSmSmem ? smem_need : kTwoPerSmSmem;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cudaLaunchAttribute attr[1] = {pdl_attr()};
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tc, ts, tz, tx,
+  cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tc, ts, tz, tx, tside,
+                                       reinterpret_cast<const int*>(ws + l.row_exp),
                                        static_cast<const __nv_bfloat16*>(x), bm, M, K, N,
                                        static_cast<__nv_bfloat16*>(y), status);
   if (err != cudaSuccess) return cuda_status(err, "rw4 gemv_tma launch");
@@ -135,89 +251,93 @@ namespace rw4 {
 
 bool gemv_tma_supported(int64_t K) { return K % kStageK == 0; }
 
-// Launch shape policy (measured on the isolated sweep and the Llama / Mixtral projection shapes,
-// decode M = 1 and 16).  Wider CTAs amortise the per-stage work (x fragment, barrier, all-ones
-// MMA) over more weight rows and win whenever they still give about 1.5 CTAs per SM (>= 222 of
-// the 296 two-per-SM slots): 64-row CTAs (M <= 8 only) from N >= 14208, then 32-row CTAs, then
-// 16-row CTAs, each with K split over a cluster of up to 4 CTAs (keeping >= 2 stages per CTA) to
-// reach that count.  9..16 activation rows always use 32-row CTAs; their K loops are twice as
-// costly, so long-K weights (>= 64 stages) also split K in two.
+// Launch shape policy (measured on the isolated sweep and the Llama / Mixtral projection shapes).
+// The K split is a function of the weight's shape alone, taken from the one-row launch: every
+// batch size then adds a row's partial sums in the same order, so a row's output has the same bits
+// at every M.  Wider CTAs amortise the per-stage work (x fragment, barrier) over more weight rows
+// and win whenever they still give about 1.5 CTAs per SM (>= 222 of the 296 two-per-SM slots):
+// 64-row CTAs from N >= 14208, then 32-row CTAs, then 16-row CTAs, each with K split over a
+// cluster of up to 4 CTAs (keeping >= 2 stages per CTA) to reach that count.  More than 8
+// activation rows (two MMA column tiles) use at most 32-row CTAs.
 void gemv_tma_policy(int64_t M, int64_t K, int64_t N, int* row_tiles, int* ksplit) {
   constexpr int64_t kTarget = 222;
-  const int64_t slices = (M + 15) / 16;
   const int64_t nst = K / kStageK;
-  auto ctas = [&](int r) { return (N + 16 * r - 1) / (16 * r) * slices; };
+  auto ctas = [&](int r) { return (N + 16 * r - 1) / (16 * r); };
   auto split_for = [&](int r) {
     int ks = 1;
     while (ks < 4 && ctas(r) * ks < kTarget && nst / (ks * 2) >= 2) ks *= 2;
     return ks;
   };
-  if (M > 8) {
-    *row_tiles = 2;
-    int ks = split_for(2);
-    if (ks == 1 && nst >= 64 && ctas(2) * 2 <= 1200) ks = 2;
-    *ksplit = ks;
-    return;
-  }
+  int r1 = 1, ks = 1;
   if (ctas(4) >= kTarget) {
-    *row_tiles = 4;
-    *ksplit = 1;
-    return;
-  }
-  for (int r : {2, 1}) {
-    const int ks = split_for(r);
-    if (ctas(r) * ks >= kTarget || r == 1) {
-      *row_tiles = r;
-      *ksplit = ks;
-      return;
+    r1 = 4;
+  } else {
+    for (int r : {2, 1}) {
+      ks = split_for(r);
+      if (ctas(r) * ks >= kTarget || r == 1) {
+        r1 = r;
+        break;
+      }
     }
   }
+  *ksplit = ks;
+  *row_tiles = M > 8 && r1 > 2 ? 2 : r1;
+}
+
+// Workspace the call needs: none when the one-row kernel converts x itself.
+size_t gemv_tma_workspace(int64_t M, int64_t K, int64_t N) {
+  int rt = 1, ks = 1;
+  gemv_tma_policy(M, K, N, &rt, &ks);
+  return one_row_in_kernel(M, K, ks) ? 0 : xprep_layout(M, K).bytes;
 }
 
 int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
-                    const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles) {
+                    const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
+                    size_t ws_bytes) {
   const int Mi = (int)M, Ki = (int)K, Ni = (int)N;
   static const int forced_ks = [] {
     const char* e = getenv("RW4_GEMV_KSPLIT");
     return e ? atoi(e) : 0;
   }();
+  if ((M + 15) / 16 > 65535) return fail(RW4_EINVAL, "rw4_linear: M=%lld too large", (long long)M);
   int policy_rt = 1, ks = 1;
   gemv_tma_policy(M, K, N, &policy_rt, &ks);
+  // RW4_GEMV_ROW_TILES / RW4_GEMV_KSPLIT force a launch shape (measurements only: a forced K
+  // split changes the order in which a row's sums are added)
   if (row_tiles != 1 && row_tiles != 2 && row_tiles != 4) row_tiles = policy_rt;
-  if (row_tiles == 4 && M > 8) row_tiles = 2;
   if (forced_ks == 1 || forced_ks == 2 || forced_ks == 4) ks = forced_ks;
-  if (row_tiles >= 4) ks = 1;
-  if (M == 1 && !no_f16()) {
-    // the fp16 one-row path holds the CTA's activation row in shared memory (<= 32 stages):
-    // split a longer K over a cluster, 64-row CTAs included
-    int need = 1;
-    while (need < 4 && (K / kStageK + need - 1) / need > kF16MaxStages) need *= 2;
-    if (need > ks) ks = need;
+  if (row_tiles == 4 && (M > 8 || ks > 1)) row_tiles = 2;
+  const XPrepLayout l = xprep_layout(M, K);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  if (!one_row_in_kernel(M, K, ks)) {
+    if (!ws || ws_bytes < l.bytes)
+      return fail(RW4_EINVAL, "rw4_linear: the GEMV needs a %zu-byte workspace (got %zu)",
+                  l.bytes, ws_bytes);
+    if (!aligned(ws, 256))
+      return fail(RW4_EINVAL, "rw4_linear: workspace must be 256-byte aligned");
+    const int st = launch_xprep(x, Mi, Ki, l, w, s);
+    if (st != RW4_OK) return st;
   }
   if (M <= 8) {
-    if (row_tiles == 4) {
-      if (ks == 4) return launch_tma<1, 4, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-      if (ks == 2) return launch_tma<1, 4, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-      return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-    }
+    if (row_tiles == 4) return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
     if (row_tiles == 2) {
-      if (ks == 4) return launch_tma<1, 2, 6, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-      if (ks == 2) return launch_tma<1, 2, 6, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-      return launch_tma<1, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+      if (ks == 4) return launch_tma<1, 2, 6, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+      if (ks == 2) return launch_tma<1, 2, 6, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+      return launch_tma<1, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
     }
-    if (ks == 4) return launch_tma<1, 1, 8, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-    if (ks == 2) return launch_tma<1, 1, 8, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-    return launch_tma<1, 1, 8>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+    if (ks == 4) return launch_tma<1, 1, 8, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+    if (ks == 2) return launch_tma<1, 1, 8, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+    return launch_tma<1, 1, 8>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
   }
-  // 9..16 activation rows: 16 KB of x per stage, so shallower rings keep two CTAs per SM
+  // 9..16 activation rows per slice: 16 KB of x per stage, so shallower rings keep two CTAs per SM
   if (row_tiles >= 2) {
-    if (ks == 4) return launch_tma<2, 2, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-    if (ks == 2) return launch_tma<2, 2, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-    return launch_tma<2, 2, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+    if (ks == 4) return launch_tma<2, 2, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+    if (ks == 2) return launch_tma<2, 2, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+    return launch_tma<2, 2, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
   }
-  if (ks == 4) return launch_tma<2, 1, 5, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-  if (ks == 2) return launch_tma<2, 1, 5, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
-  return launch_tma<2, 1, 5>(x, Mi, Ki, wq, sc, zr, Ni, y, s);
+  if (ks == 4) return launch_tma<2, 1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+  if (ks == 2) return launch_tma<2, 1, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+  return launch_tma<2, 1, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
 }
 
 }  // namespace rw4

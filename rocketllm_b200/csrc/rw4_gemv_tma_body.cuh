@@ -11,10 +11,12 @@
 //
 // A stage is 512 values of K (8 groups) of the CTA's 16R rows together with the same 512 values of
 // the slice's BM activation rows (x travels in the ring with the weights, so no consumer ever
-// waits on a global load); consumer warp w always takes group w of the stage, accumulates over all stages, and the 8 partial sums are combined in shared memory
-// at the end (deterministic, no atomics, no scratch memory).  Arithmetic: codes enter the tensor
-// cores as bf16 (128 + c) (rw4_gemv_frag.cuh), each group's fp32 accumulator is scaled by its
-// fp16 scale and the zero term uses the group's sum of x from an all-ones MMA.  The code boxes use
+// waits on a global load); consumer warp w always takes group w of the stage, accumulates over all
+// stages, and the 8 partial sums are combined in shared memory at the end (deterministic, no
+// atomics).  Arithmetic of the routed-expert path (bf16 activations): codes enter the tensor cores
+// as bf16 (128 + c) (rw4_gemv_frag.cuh), each group's fp32 accumulator is scaled by its fp16 scale
+// and the zero term uses the group's sum of x from an all-ones MMA.  The dense path (XP / XQ,
+// below) multiplies fp16 codes by pre-converted activations instead.  The code boxes use
 // the 128-byte TMA swizzle (16-byte chunk index XOR row % 8), which keeps the consumers' 8-byte
 // shared loads within the two wavefronts 256 bytes need.  Rows past the weight's end are
 // zero-filled by the TMA unit and never stored.
@@ -30,6 +32,18 @@
 // cluster's distributed shared memory, and after one cluster barrier rank 0 adds them and stores.
 // More CTAs (and shorter K loops) for short, narrow projections, with no global scratch and no
 // atomics.
+//
+// XP (the dense decode path): the activations arrive already converted by the x-prep kernel
+// (rw4_gemv_tma.cu) -- fp16, each row scaled by its own power of two 2^e so that its largest
+// magnitude lies in [2^14, 2^15), even-k values by 2^e and odd-k values by 2^(e-4), every 16-value
+// chunk permuted into MMA fragment order -- together with two fp32 numbers per (group, row): the
+// group's sum of x times 2^e and minus 1024 times the sum of its fp16 values (the code offset).
+// The codes then enter the tensor cores as fp16 (1024 + c) and (1024 + 16 c) straight from one LOP3
+// each (a_frag_f16), the accumulator starts from the offset, and the row's 2^-e is applied once
+// when the output is stored.  Every row is converted the same way whatever the batch, so a row's
+// output does not depend on the rows beside it or on the launch's M, and scaling x by a power of
+// two scales the output by exactly that power (no fixed pre-scale, no fp16 underflow of small
+// activations).  XQ does the same conversion inside the GEMV for a one-row launch.
 //
 // Every mbarrier wait is bounded (rw4_tma.cuh); on a timeout the CTA drains its own copies, writes
 // nothing and sets the library's device status word.
@@ -64,6 +78,20 @@ struct Layout {
   static constexpr int kX = (kBytes + 1023) / 1024 * 1024;
   __host__ __device__ static constexpr int x_stage(int bm) { return bm * 1024; }
   __host__ __device__ static constexpr int dyn_smem(int bm) { return kX + S * x_stage(bm) + 1024; }
+  // XP: per-(group, row) fp32 pairs of the stage's 8 groups for the slice's rows padded to even
+  __host__ __device__ static constexpr int side_rows(int bm) { return (bm + 1) & ~1; }
+  __host__ __device__ static constexpr int side_stage(int bm) { return 64 * side_rows(bm); }
+  __host__ __device__ static constexpr int side_base(int bm) { return kX + S * x_stage(bm); }
+  __host__ __device__ static constexpr int dyn_smem_xp(int bm) {
+    return kX + S * (x_stage(bm) + side_stage(bm)) + 1024;
+  }
+  // XQ: the CTA's converted activation row (1 KB per stage) and its (sum, -offset) pairs (64 B per
+  // stage) for up to kXQMaxStages stages
+  static constexpr int kXQMaxStages = 32;
+  static constexpr int kXQSide = kX + kXQMaxStages * 1024;
+  __host__ __device__ static constexpr int dyn_smem_xq(int nstages) {
+    return kXQSide + nstages * 64 + 1024;
+  }
 };
 
 // Shared-memory loads by shared-window address (always LDS, never a generic load).
@@ -106,17 +134,23 @@ __device__ __forceinline__ void x_frag_smem(uint32_t a, bool valid, uint32_t (&b
 // rows [x_row0, x_row0 + Ml) (Ml <= bm <= 16; box rows past the tensor's end arrive as zeros, rows
 // of the box past Ml are ignored).  Without XT (the routed-expert kernel, whose row count lives on
 // the device) the consumers read rows [x_row0, x_row0 + Ml) of x (row stride K) from global memory.
+// XP (implies the TMA ring): tm_x maps the x-prep output [rows, K] fp16 with the same box, tm_side
+// its per-(group, row) pairs [K/64, 2 * padded rows] fp32 with an [8, 2 * side_rows(bm)] box, and
+// row_exp[x_row0 + m] is row m's exponent e (the output is scaled by 2^-e).
+// XQ (one activation row, M1, without the ring): the consumers convert the row themselves before
+// the first stage -- its exponent from the whole row's largest magnitude, then this CTA's K range
+// into fp16 fragments and (sum, -offset) pairs in shared memory -- with the same helpers, in the
+// same order, as the x-prep kernel, so the output has the same bits as the XP path's.  x is the
+// bf16 activations (row x_row0, stride K).
 // y: output rows (stride ldy).
 // Plain: writes y[m, r0 + r] for r0 + r < n_out.  SWIGLU: writes y[m, r0 + r] for r0 + r < n_out
 // (= I) from weight rows r0 + r (gate) and r0 + I + r (up).
 // M1: the launch has exactly one activation row (NT == 1, M == 1).
-// XF (with M1, without XT): the consumers first convert the CTA's activation row into fp16 pair
-// registers in shared memory (x16_to_f16_frag, 1 KB per stage) and the MMAs run in fp16
-// (a_frag_f16: one shift per four codes); requires nstages * 1 KB of shared memory at kX.
 template <int NT, int R, int S, bool SWIGLU, int KS = 1, bool XT = true, bool M1 = false,
-          bool XF = false>
+          bool XP = false, bool XQ = false>
 __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensorMap* tm_scale,
                                      const CUtensorMap* tm_zero, const CUtensorMap* tm_x,
+                                     const CUtensorMap* tm_side, const int* __restrict__ row_exp,
                                      const __nv_bfloat16* __restrict__ x, int x_row0, int bm,
                                      int Ml, int K,
                                      __nv_bfloat16* __restrict__ y, int64_t ldy, int r0,
@@ -125,12 +159,14 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
   using L = Layout<R, S>;
   static_assert(!SWIGLU || R == 2, "the SwiGLU epilogue pairs one gate tile with one up tile");
   static_assert(!M1 || NT == 1, "one activation row fits one MMA column tile");
-  static_assert(!XF || (M1 && !XT), "the fp16 path is the one-row GEMV");
+  static_assert(!XP || (XT && !SWIGLU), "the pre-converted activations come through the ring");
+  static_assert(!XQ || (M1 && !XT && !XP && !SWIGLU), "XQ converts one activation row");
   if (M1) Ml = min(Ml, 1);  // a one-row launch never computes or stores a second row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   __shared__ int aborted;
+  __shared__ int xq_exp;  // XQ: the row's exponent, for every thread of the final store
   const uint32_t sbase = smem_addr(smem);
   const uint32_t full0 = sbase + L::kBars;
   const uint32_t empty0 = full0 + 8 * S;
@@ -147,6 +183,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
 
   if (threadIdx.x == 0) {
     aborted = 0;
+    xq_exp = 0;
     for (int s = 0; s < S; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, kConsumers);
@@ -172,6 +209,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       prefetch_tensormap(tm_scale);
       prefetch_tensormap(tm_zero);
       if (XT) prefetch_tensormap(tm_x);
+      if (XP) prefetch_tensormap(tm_side);
       const uint64_t pol = policy_evict_first();
       // Before the dependency on the previous kernel resolves, only pull the first stages' weights
       // into L2 (coherent: if that kernel wrote them, the loads below still see its writes).
@@ -194,7 +232,8 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
           break;
         }
         const uint32_t fb = full0 + 8 * st;
-        mbar_arrive_expect_tx(fb, L::kStageTx + (XT ? L::x_stage(bm) : 0));
+        mbar_arrive_expect_tx(fb, L::kStageTx + (XT ? L::x_stage(bm) : 0) +
+                                      (XP ? L::side_stage(bm) : 0));
         const uint32_t cdst = sbase + L::kCodes + st * L::kCodeStage;
         const uint32_t sdst = sbase + L::kScales + st * L::kScaleStage;
         const uint32_t zdst = sbase + L::kZeros + st * L::kScaleStage;
@@ -205,6 +244,9 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
           tma_load_2d(xdst, tm_x, (s_begin + s) * kStageK, x_row0, fb);
           tma_load_2d(xdst + bm * 512, tm_x, (s_begin + s) * kStageK + 256, x_row0, fb);
         }
+        if (XP)  // the stage's 8 groups x the slice's rows: (sum of x, -offset) pairs
+          tma_load_2d(sbase + L::side_base(bm) + st * L::side_stage(bm), tm_side, 2 * x_row0, gx,
+                      fb);
         if (SWIGLU) {
           // 16-row boxes: gate tile then up tile (2048 bytes apart, swizzle phase unchanged).
           const int ru = r0 + up_offset;
@@ -231,7 +273,8 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
   } else {
     // ---------------- consumers ----------------
     // The producer loads x only after the previous grid completed; waiting here as well keeps this
-    // warp's stores of y behind that grid too (a no-op without a programmatic dependency).
+    // warp's reads of x and stores of y behind that grid too (a no-op without a programmatic
+    // dependency).
     asm volatile("griddepcontrol.wait;" ::: "memory");
     const int g = lane >> 2, t = lane & 3;
     const int w = warp;              // group of the stage this warp owns
@@ -245,20 +288,48 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     const uint32_t scale_off = L::kScales + g * 16 + 2 * w;
     const uint32_t zero_off = L::kZeros + g * 16 + 2 * w;
     const uint32_t x_off = L::kX + half * bm * 512 + (64 * q + 16 * t) * 2;
-    if (XF) {
-      // the CTA's activation row -> fp16 pair registers, 32 bytes per 16 values, in shared memory
-      const __nv_bfloat16* xr = x + (int64_t)x_row0 * K + (int64_t)s_begin * kStageK;
-      const int chunks = nstages * (kStageK / 16);
-      for (int c = threadIdx.x; c < chunks; c += kConsumers * 32) {
-        uint32_t o[8];
-        x16_to_f16_frag(ldg_u4(xr + 16 * c), ldg_u4(xr + 16 * c + 8), o);
-        const uint32_t a = sbase + L::kX + 32 * c;
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a), "r"(o[0]), "r"(o[1]),
-                     "r"(o[2]), "r"(o[3]) : "memory");
-        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a + 16), "r"(o[4]),
-                     "r"(o[5]), "r"(o[6]), "r"(o[7]) : "memory");
-      }
+    const int srows = L::side_rows(bm);
+    const uint32_t side_off = L::side_base(bm) + w * srows * 8;
+    if (XQ) {
+      // 1. the row's exponent from its largest magnitude over the whole K (consumer threads only)
+      const __nv_bfloat16* xr = x + (int64_t)x_row0 * K;
+      const int tid = threadIdx.x;
+      uint32_t mx = 0;
+      for (int i = tid; i < K / 8; i += kConsumers * 32) mx = max(mx, absmax8(ldg_u4(xr + 8 * i)));
+      mx = __reduce_max_sync(0xFFFFFFFFu, mx);
+      __shared__ uint32_t wmax[kConsumers];
+      if (lane == 0) wmax[warp] = mx;
       asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");  // consumers only
+      uint32_t a = 0;
+#pragma unroll
+      for (int i = 0; i < kConsumers; ++i) a = max(a, wmax[i]);
+      const int e = row_exponent(a);
+      if (tid == 0) xq_exp = e;
+      float p1, p2;
+      exp_factors(e, p1, p2);
+      // 2. this CTA's K range -> fp16 fragments (32 bytes per 16 values) and per-group pairs
+      const __nv_bfloat16* xk = xr + (int64_t)s_begin * kStageK;
+      const int chunks = nstages * (kStageK / 16);
+      for (int base = 0; base < chunks; base += kConsumers * 32) {
+        const int c = base + tid;
+        float xs_c = 0.f, hs_c = 0.f;
+        if (c < chunks) {
+          uint32_t o[8];
+          x16_to_f16_frag(ldg_u4(xk + 16 * c), ldg_u4(xk + 16 * c + 8), p1, p2, o, xs_c, hs_c);
+          const uint32_t a0 = sbase + L::kX + 32 * c;
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a0), "r"(o[0]), "r"(o[1]),
+                       "r"(o[2]), "r"(o[3]) : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a0 + 16), "r"(o[4]),
+                       "r"(o[5]), "r"(o[6]), "r"(o[7]) : "memory");
+        }
+        group_sums(xs_c, hs_c);
+        if (c < chunks && (c & 3) == 0) {
+          float* sd = reinterpret_cast<float*>(smem + L::kXQSide) + 2 * (c >> 2);
+          sd[0] = xs_c;
+          sd[1] = -1024.f * hs_c;
+        }
+      }
+      asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
     }
     for (int s = 0; s < nstages; ++s) {
       const int st = s % S;
@@ -282,11 +353,50 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       }
       // x fragment of group (s * 8 + w) (box w / 4 of the stage), then release the slot
       uint32_t b[NT][4][2];
-      if (XF) {
-        const uint32_t xa = sbase + L::kX + 32 * (32 * s + 4 * w + t);
-        const uint4 v0 = lds_v4(xa), v1 = lds_v4(xa + 16);
+      float xs[NT][4], c0[NT][4];
+      if (XQ) {
+        // column 0 (g == 0) carries the row, the others zeros -- as the XP ring delivers it
+        uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
+        if (g == 0) {
+          const uint32_t xa = sbase + L::kX + 32 * (32 * s + 4 * w + t);
+          v0 = lds_v4(xa);
+          v1 = lds_v4(xa + 16);
+        }
         b[0][0][0] = v0.x; b[0][0][1] = v0.y; b[0][1][0] = v0.z; b[0][1][1] = v0.w;
         b[0][2][0] = v1.x; b[0][2][1] = v1.y; b[0][3][0] = v1.z; b[0][3][1] = v1.w;
+        float sx = 0.f, so = 0.f;
+        if (t == 0) {
+          const float* sd = reinterpret_cast<const float*>(smem + L::kXQSide) + 2 * (8 * s + w);
+          sx = sd[0];
+          so = sd[1];
+        }
+        xs[0][0] = xs[0][2] = sx;
+        xs[0][1] = xs[0][3] = 0.f;
+        c0[0][0] = c0[0][2] = so;
+        c0[0][1] = c0[0][3] = 0.f;
+      } else if (XP) {
+        const uint32_t xb = sbase + x_off + st * L::x_stage(bm);
+        const uint32_t sd = sbase + side_off + st * L::side_stage(bm);
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          // fp16 pairs already in fragment order: two 16-byte loads, no permutes
+          const int m = nt * 8 + g;
+          uint4 v0 = make_uint4(0, 0, 0, 0), v1 = make_uint4(0, 0, 0, 0);
+          if (m < Ml && m < bm) {
+            v0 = lds_v4(xb + m * 512);
+            v1 = lds_v4(xb + m * 512 + 16);
+          }
+          b[nt][0][0] = v0.x; b[nt][0][1] = v0.y; b[nt][1][0] = v0.z; b[nt][1][1] = v0.w;
+          b[nt][2][0] = v1.x; b[nt][2][1] = v1.y; b[nt][3][0] = v1.z; b[nt][3][1] = v1.w;
+          // (sum of x, -offset) of this group for accumulator columns 2t and 2t + 1
+          const int col = nt * 8 + 2 * t;
+          uint4 sv = make_uint4(0, 0, 0, 0);
+          if (col < srows) sv = lds_v4(sd + col * 8);
+          xs[nt][0] = xs[nt][2] = __uint_as_float(sv.x);
+          xs[nt][1] = xs[nt][3] = __uint_as_float(sv.z);
+          c0[nt][0] = c0[nt][2] = __uint_as_float(sv.y);
+          c0[nt][1] = c0[nt][3] = __uint_as_float(sv.w);
+        }
       } else if (XT) {
         const uint32_t xb = sbase + x_off + st * L::x_stage(bm);
 #pragma unroll
@@ -305,26 +415,9 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       __syncwarp();
       if (lane == 0) mbar_arrive(empty0 + 8 * st);
 
-      // sums of x over the group; the code MMAs start from -128 * sum(x), which removes the
-      // +128 of the bf16 code encoding: acc = sum(x * c)
-      float xs[NT][4], c0[NT][4];
-      if (XF) {
-        // 2^-8 sum(x) (A = 1 on even-k slots, 16 on odd-k slots) and the code offset
-        // sum(1024 * scaled x) that the code MMAs start from (negated); everything accumulated is
-        // then 2^-8 times the true value, undone once per output in the epilogue
-        const uint32_t unscale[4] = {kF16_1, kF16_1, kF16_16, kF16_16};
-        const uint32_t k1024[4] = {kMagicF16, kMagicF16, kMagicF16, kMagicF16};
-        float off[4];
-        mma_f16_16816(xs[0], unscale, b[0][0][0], b[0][0][1], zero4);
-        mma_f16_16816(off, k1024, b[0][0][0], b[0][0][1], zero4);
-#pragma unroll
-        for (int j = 1; j < 4; ++j) {
-          mma_f16_16816(xs[0], unscale, b[0][j][0], b[0][j][1], xs[0]);
-          mma_f16_16816(off, k1024, b[0][j][0], b[0][j][1], off);
-        }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) c0[0][e] = -off[e];
-      } else {
+      if (!XP && !XQ) {
+        // sums of x over the group; the code MMAs start from -128 * sum(x), which removes the
+        // +128 of the bf16 code encoding: acc = sum(x * c)
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           mma_bf16_16816(xs[nt], ones, b[nt][0][0], b[nt][0][1], zero4);
@@ -341,18 +434,16 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           uint32_t a[4];
-          if (XF) {
+          if (XP || XQ)
             a_frag_f16(wa[rt], wb[rt], j, a);
-            mma_f16_16816(acc[0], a, b[0][j][0], b[0][j][1], j == 0 ? c0[0] : acc[0]);
-            continue;
-          }
-          a_frag(wa[rt], wb[rt], j, a);
+          else
+            a_frag(wa[rt], wb[rt], j, a);
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt) {
-            if (j == 0)
-              mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], c0[nt]);
+            if (XP || XQ)
+              mma_f16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], j == 0 ? c0[nt] : acc[nt]);
             else
-              mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], acc[nt]);
+              mma_bf16_16816(acc[nt], a, b[nt][j][0], b[nt][j][1], j == 0 ? c0[nt] : acc[nt]);
           }
         }
 
@@ -439,6 +530,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     }
   }
   if (aborted) return;
+  const int xq_e = XQ ? xq_exp : 0;
 #pragma unroll
   for (int i = 0; i < kPer; ++i) {
     const int o = threadIdx.x + i * kThreads;
@@ -447,13 +539,15 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     if (o < kOut && n < n_out && m < Ml) {
       float v;
       if (SWIGLU) {
-        const float unit = XF ? 256.f : 1.f;
-        const float gb = __bfloat162float(__float2bfloat16_rn(part[i][0] * unit));
-        const float ub = __bfloat162float(__float2bfloat16_rn(part[i][SWIGLU ? 1 : 0] * unit));
+        const float gb = __bfloat162float(__float2bfloat16_rn(part[i][0]));
+        const float ub = __bfloat162float(__float2bfloat16_rn(part[i][SWIGLU ? 1 : 0]));
         const float act = __bfloat162float(__float2bfloat16_rn(gb / (1.f + expf(-gb))));
         v = act * ub;
+      } else if (XP || XQ) {
+        // undo the row's 2^e (exact)
+        v = ldexpf(part[i][0], XQ ? -xq_e : -row_exp[x_row0 + m]);
       } else {
-        v = XF ? part[i][0] * 256.f : part[i][0];
+        v = part[i][0];
       }
       y[(int64_t)m * ldy + n] = __float2bfloat16_rn(v);
     }

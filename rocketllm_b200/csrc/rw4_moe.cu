@@ -93,8 +93,9 @@ struct ExpertMaps {
   CUtensorMap zero[kMaxExperts];
 };
 
-// XF: every expert has at most one row (a one-token step): the fp16 one-row GEMV body.
-template <int NT, int R, int S, bool SWIGLU, bool XF = false>
+// Every routed row count runs the same bf16 body (one-token steps included), so an expert's output
+// for a token does not depend on how many other tokens it serves.
+template <int NT, int R, int S, bool SWIGLU>
 __global__ void __launch_bounds__(gemv_tma::kThreads)
     moe_grouped_kernel(const __grid_constant__ ExpertMaps maps, int e0,
                        const int32_t* __restrict__ offsets, const __nv_bfloat16* __restrict__ x,
@@ -109,14 +110,14 @@ __global__ void __launch_bounds__(gemv_tma::kThreads)
     atomicOr(status, RW4_DEVERR_ROWS);
   if (m0 >= rows) return;  // unrouted expert (or past its rows): no weight is read
   constexpr int kRowsPerCta = SWIGLU ? 16 : 16 * R;
-  gemv_tma::body<NT, R, S, SWIGLU, 1, false, XF, XF>(&maps.codes[z], &maps.scale[z],
-                                                     &maps.zero[z], nullptr, x, beg + m0, 16,
-                                                     min(16, rows - m0), K,
+  gemv_tma::body<NT, R, S, SWIGLU, 1, false>(&maps.codes[z], &maps.scale[z], &maps.zero[z],
+                                             nullptr, nullptr, nullptr, x, beg + m0, 16,
+                                             min(16, rows - m0), K,
                                    y + (int64_t)(beg + m0) * ldy, ldy, blockIdx.x * kRowsPerCta,
                                    n_out, up_offset, status);
 }
 
-template <int NT, int R, int S, bool SWIGLU, bool XF = false>
+template <int NT, int R, int S, bool SWIGLU>
 int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_rows,
                    const uint8_t* const* packed_e, const void* const* scale_e,
                    const void* const* zero_e, int K, int N, void* y, cudaStream_t stream) {
@@ -125,15 +126,13 @@ int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_row
   const int n_out = SWIGLU ? N / 2 : N;
   const int rows_per_cta = SWIGLU ? 16 : L::BR;
   const int G = K / 64;
-  auto kern = moe_grouped_kernel<NT, R, S, SWIGLU, XF>;
-  const int smem = L::kX + (XF ? K / 512 + 1 : 1) * 1024;  // + fp16 activation row (1 KB/stage)
+  auto kern = moe_grouped_kernel<NT, R, S, SWIGLU>;
+  const int smem = L::kX + 1024;
   static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!((attr_set.load() >> dev) & 1)) {
-    // the largest request this kernel can make (K / 512 <= 32 on the fp16 one-row path)
-    const int most = L::kX + (XF ? 33 : 1) * 1024;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most) !=
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return fail(RW4_ECUDA, "moe_grouped: cannot set dynamic shared memory size");
     attr_set.fetch_or(1ull << dev);
@@ -182,7 +181,7 @@ struct SlotMaps {
   CUtensorMap zero[kMaxSlots];
 };
 
-template <int NT, int R, int S, bool SWIGLU, bool XF = false>
+template <int NT, int R, int S, bool SWIGLU>
 __global__ void __launch_bounds__(gemv_tma::kThreads)
     moe_grouped_slots_kernel(const __grid_constant__ SlotMaps maps, int nslots,
                              const int32_t* __restrict__ slot_of,
@@ -203,8 +202,9 @@ __global__ void __launch_bounds__(gemv_tma::kThreads)
     return;
   }
   constexpr int kRowsPerCta = SWIGLU ? 16 : 16 * R;
-  gemv_tma::body<NT, R, S, SWIGLU, 1, false, XF, XF>(
-      &maps.codes[slot], &maps.scale[slot], &maps.zero[slot], nullptr, x, beg + m0, 16,
+  gemv_tma::body<NT, R, S, SWIGLU, 1, false>(
+      &maps.codes[slot], &maps.scale[slot], &maps.zero[slot], nullptr, nullptr, nullptr, x,
+      beg + m0, 16,
       min(16, rows - m0), K, y + (int64_t)(beg + m0) * ldy, ldy, blockIdx.x * kRowsPerCta, n_out,
       up_offset, status);
 }
@@ -219,7 +219,7 @@ struct rw4_slot_maps {
 
 namespace {
 
-template <int NT, int R, int S, bool SWIGLU, bool XF = false>
+template <int NT, int R, int S, bool SWIGLU>
 int launch_grouped_slots(const rw4_slot_maps* sm, const int32_t* slot_of, const void* x,
                          const int32_t* offsets, int E, int64_t max_rows, void* y,
                          cudaStream_t stream) {
@@ -227,14 +227,13 @@ int launch_grouped_slots(const rw4_slot_maps* sm, const int32_t* slot_of, const 
   const int K = sm->K, N = sm->N;
   const int n_out = SWIGLU ? N / 2 : N;
   const int rows_per_cta = SWIGLU ? 16 : L::BR;
-  auto kern = moe_grouped_slots_kernel<NT, R, S, SWIGLU, XF>;
-  const int smem = L::kX + (XF ? K / 512 + 1 : 1) * 1024;
+  auto kern = moe_grouped_slots_kernel<NT, R, S, SWIGLU>;
+  const int smem = L::kX + 1024;
   static std::atomic<uint64_t> attr_set{0};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!((attr_set.load() >> dev) & 1)) {
-    const int most = L::kX + (XF ? 33 : 1) * 1024;
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, most) !=
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
         cudaSuccess)
       return fail(RW4_ECUDA, "moe_grouped_slots: cannot set dynamic shared memory size");
     attr_set.fetch_or(1ull << dev);
@@ -357,16 +356,6 @@ extern "C" int rw4_moe_grouped(const void* x_perm_bf16, const int32_t* offsets, 
     return fail(RW4_EINVAL, "rw4_moe_grouped: activations must be 16-byte aligned");
   cudaStream_t s = rw4::as_stream(stream);
   const bool wide = max_rows > 8;
-  // one row per expert (a one-token step: a token's top-k experts are distinct) and a K range
-  // whose fp16 activation row fits 32 KB of shared memory: the fp16 one-row GEMV
-  const bool one = max_rows == 1 && K / 512 <= 32;
-  if (one) {
-    if (act == 1)
-      return launch_grouped<1, 2, 6, true, true>(x_perm_bf16, offsets, E, max_rows, packed_e,
-                                                 scale_e, zero_e, (int)K, (int)N, y_perm_bf16, s);
-    return launch_grouped<1, 2, 6, false, true>(x_perm_bf16, offsets, E, max_rows, packed_e,
-                                                scale_e, zero_e, (int)K, (int)N, y_perm_bf16, s);
-  }
   if (act == 1) {
     if (wide)
       return launch_grouped<2, 2, 6, true>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,
@@ -472,14 +461,7 @@ extern "C" int rw4_moe_grouped_slots(const void* x_perm_bf16, const int32_t* off
     return fail(RW4_EINVAL, "rw4_moe_grouped_slots: activations must be 16-byte aligned");
   cudaStream_t s = rw4::as_stream(stream);
   const bool wide = max_rows > 8;
-  const bool one = max_rows == 1 && maps->K / 512 <= 32;
   const int a = maps->act;
-  if (one)
-    return a == 1 ? launch_grouped_slots<1, 2, 6, true, true>(maps, slot_of, x_perm_bf16, offsets,
-                                                              E, max_rows, y_perm_bf16, s)
-                  : launch_grouped_slots<1, 2, 6, false, true>(maps, slot_of, x_perm_bf16,
-                                                               offsets, E, max_rows, y_perm_bf16,
-                                                               s);
   if (a == 1)
     return wide ? launch_grouped_slots<2, 2, 6, true>(maps, slot_of, x_perm_bf16, offsets, E,
                                                       max_rows, y_perm_bf16, s)

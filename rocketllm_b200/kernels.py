@@ -78,11 +78,28 @@ def quantize(w, group=64):
     return packed, scale, zero, groups * g - k
 
 
+_WS_BYTES = {}
+
+
+def linear_workspace_bytes(m, k, n, path=0):
+    """Device workspace bytes ``rw4_linear_ws`` needs for this call (0 for the tensor-core GEMM and
+    for one row that the GEMV converts itself)."""
+    key = (m, k, n, path)
+    b = _WS_BYTES.get(key)
+    if b is None:
+        v = ctypes.c_size_t()
+        _lib.call("rw4_linear_workspace_size", m, k, n, path, ctypes.byref(v))
+        b = _WS_BYTES[key] = v.value
+    return b
+
+
 def linear(x, packed, scale, zero, out=None, path=None):
     """``y = x . W^T`` with ``x`` bf16 ``[..., K]`` and W in RW4; returns bf16 ``[..., N]``.
 
     ``x`` may be a strided view (e.g. the last position of every sequence); it is compacted first.
-    ``path`` forces a kernel (1 / 3 GEMV, 2 tcgen05 GEMM) instead of the library's choice.
+    ``path`` forces a kernel (1 / 3 GEMV, 2 tcgen05 GEMM) instead of the library's choice.  The
+    GEMV's workspace (the converted activations) comes from torch's allocator on the current
+    stream, so the call also works inside a CUDA-graph capture.
     """
     if not x.is_cuda:
         raise ValueError("RW4 kernels take CUDA tensors only (there is no CPU path); got a "
@@ -101,12 +118,12 @@ def linear(x, packed, scale, zero, out=None, path=None):
     m = x2.shape[0]
     if out is None:
         out = torch.empty((*x.shape[:-1], n), dtype=torch.bfloat16, device=x.device)
-    if path is None:
-        _lib.call("rw4_linear", x2.data_ptr(), m, k, packed.data_ptr(), scale.data_ptr(),
-                  zero.data_ptr(), n, 64, out.data_ptr(), _stream())
-    else:
-        _lib.call("rw4_linear_on_path", x2.data_ptr(), m, k, packed.data_ptr(), scale.data_ptr(),
-                  zero.data_ptr(), n, 64, out.data_ptr(), int(path), _stream())
+    p = 0 if path is None else int(path)
+    wsb = linear_workspace_bytes(m, k, n, p) if m and n else 0
+    ws = torch.empty(wsb, dtype=torch.uint8, device=x.device) if wsb else None
+    _lib.call("rw4_linear_ws", x2.data_ptr(), m, k, packed.data_ptr(), scale.data_ptr(),
+              zero.data_ptr(), n, 64, out.data_ptr(), p, ws.data_ptr() if ws is not None else None,
+              wsb, _stream())
     return out
 
 

@@ -47,7 +47,8 @@ def test_linear_matches_oracle(cuda, m, k, n):
 
 @pytest.mark.parametrize("k,n", [(32768, 512), (53248, 1024), (53248, 16384)])
 def test_linear_long_k_one_row(cuda, k, n):
-    """One activation row with K beyond the fp16 row's 32 KB: K split over a cluster."""
+    """One activation row with a long K (converted in the GEMV, or by the x-prep pass when the CTA's
+    K range passes 32 stages)."""
     packed, scale, zero = make_weight(n, k, device=cuda, seed=k + n)
     x = make_activation(1, k, device=cuda, seed=5)
     y = kernels.linear(x, packed, scale, zero)
@@ -100,6 +101,51 @@ def test_linear_is_linear_in_x(cuda):
     y1 = kernels.linear(x1, packed, scale, zero).float()
     y2 = kernels.linear((2 * x1.float()).to(torch.bfloat16), packed, scale, zero).float()
     assert torch.allclose(y2, 2 * y1, rtol=1 / 64, atol=1e-2)
+
+
+@pytest.mark.parametrize("sigma", [1e-4, 1e-3, 1e-2, 1.0, 100.0])
+@pytest.mark.parametrize("m", [1, 3, 16])
+@pytest.mark.parametrize("k,n", [(4096, 1024), (16384, 512)])
+def test_linear_any_activation_scale(cuda, sigma, m, k, n):
+    """x ~ N(0, sigma^2) over six decades, plus one row whose channels 7, 700 and 3000 are outliers
+    (10^3 to 10^4 times sigma): within the bf16 tolerance of the oracle at every scale."""
+    packed, scale, zero = make_weight(n, k, device=cuda, seed=11)
+    x = make_activation(m, k, device=cuda, seed=12).float() * sigma
+    x[0, [7, 700, 3000]] = torch.tensor([1e3, -4e3, 1e4], device=cuda) * sigma
+    x = x.to(torch.bfloat16)
+    y = kernels.linear(x, packed, scale, zero)
+    torch.cuda.synchronize()
+    check_close(y, oracle_linear(x, packed, scale, zero))
+
+
+@pytest.mark.parametrize("m", [1, 5, 16, 40])
+def test_linear_power_of_two_scaling_is_exact(cuda, m):
+    """y(2^j x) = 2^j y(x) bit for bit: each row's fp16 conversion follows its own exponent."""
+    packed, scale, zero = make_weight(4096, 8192, device=cuda, seed=13)
+    x = make_activation(m, 8192, device=cuda, seed=14)
+    y = kernels.linear(x, packed, scale, zero)
+    for j in (-40, -12, -1, 3, 20):
+        ys = kernels.linear((x.float() * 2.0 ** j).to(torch.bfloat16), packed, scale, zero)
+        assert torch.equal(ys.float(), y.float() * 2.0 ** j), f"2^{j}"
+
+
+@pytest.mark.parametrize("k,n", [(4096, 4096), (14336, 4096), (4096, 14336), (53248, 1024)])
+def test_linear_row_independent_of_batch(cuda, k, n):
+    """A row's output has the same bits alone (M = 1), in a decode batch and in the 16-row slices of
+    a larger M (up to the GEMV's 64 rows): decode batches and speculative verify passes round
+    exactly like one-token steps.  (53248 x 1024: a one-row launch long enough to go through the
+    x-prep pass as well.)"""
+    packed, scale, zero = make_weight(n, k, device=cuda, seed=15)
+    x = make_activation(64, k, device=cuda, seed=16)
+    x[5] *= 1e-3  # rows of very different magnitude side by side
+    x[9] *= 300
+    alone = torch.cat([kernels.linear(x[i:i + 1], packed, scale, zero) for i in range(64)])
+    for m in (2, 4, 8, 9, 16, 17, 33, 64):
+        assert kernels.linear_path(m, k, n) in (1, 3)
+        y = kernels.linear(x[:m], packed, scale, zero)
+        assert torch.equal(y, alone[:m]), f"M={m}"
+    torch.cuda.synchronize()
+    check_close(alone, oracle_linear(x, packed, scale, zero))
 
 
 def test_linear_deterministic(cuda):

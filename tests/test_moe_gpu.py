@@ -99,13 +99,14 @@ def test_grouped_matches_oracle(cuda, t, act):
 
 @pytest.mark.parametrize("act", [0, 1])
 @pytest.mark.parametrize("hid", [1024, 4096])
-def test_grouped_one_token_fp16_path(cuda, act, hid):
-    """One token (each routed expert gets one row, max_rows=1): the fp16 one-row kernel."""
+@pytest.mark.parametrize("sigma", [1e-3, 1.0])
+def test_grouped_one_token(cuda, act, hid, sigma):
+    """One token (each routed expert gets one row, max_rows=1), small and unit activations."""
     e, k_top, inter = 8, 2, 512
     n = 2 * inter if act == 1 else hid
     weights = expert_weights(e, n, hid, cuda, seed=21 + act)
     idx = routing(1, k_top, e, 7).to(cuda)
-    x = torch.randn(1, hid, device=cuda).to(torch.bfloat16)
+    x = (torch.randn(1, hid, device=cuda) * sigma).to(torch.bfloat16)
     perm, inv, offsets = kernels.moe_permute(idx, e)
     xp = kernels.moe_gather(x, perm, k_top)
     y = kernels.moe_grouped(xp, offsets, weights, act=act, max_rows=1)
@@ -113,6 +114,26 @@ def test_grouped_one_token_fp16_path(cuda, act, hid):
     assert kernels.device_status() == 0
     for rows, ref in oracle_grouped(xp, offsets, weights, act, inter):
         close(y[rows], ref, rel=1 / 32 if act == 1 else 1 / 128)
+
+
+@pytest.mark.parametrize("act", [0, 1])
+def test_grouped_token_independent_of_batch(cuda, act):
+    """A token's expert outputs have the same bits alone (a one-token step) and among 24 tokens."""
+    e, k_top, hid, inter = 8, 2, 1024, 512
+    n = 2 * inter if act == 1 else hid
+    weights = expert_weights(e, n, hid, cuda, seed=31 + act)
+    idx = routing(24, k_top, e, 9).to(cuda)
+    x = torch.randn(24, hid, device=cuda).to(torch.bfloat16)
+
+    def run(xt, it):
+        perm, inv, offsets = kernels.moe_permute(it, e)
+        y = kernels.moe_grouped(kernels.moe_gather(xt, perm, k_top), offsets, weights, act=act,
+                                max_rows=xt.shape[0] * k_top)
+        return y[inv.long()].view(xt.shape[0], k_top, -1)   # per (token, slot)
+
+    together = run(x, idx)
+    for t in (0, 5, 23):
+        assert torch.equal(run(x[t:t + 1], idx[t:t + 1])[0], together[t]), f"token {t}"
 
 
 def test_grouped_flags_rows_beyond_max_rows(cuda):

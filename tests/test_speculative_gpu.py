@@ -2,10 +2,16 @@
 M = k+1 (the dequant-GEMV reads each weight once for all candidate positions), streamed or
 resident, with the stock or the int4 KV cache.
 
-Greedy speculation must reproduce the target's plain greedy decoding.  In bf16 a (k+1)-row pass can
-resolve a near-tie differently from a one-row step (the reference documents the same caveat,
-``rocketllm/spec/draft.py:45-64``), so the sequences must agree up to the first position where the
-plain run's top-1 margin is below 4e-2, and that position must exist only there.
+Greedy speculation must reproduce the target's plain greedy decoding.  The RW4 GEMV gives a row the
+same bits in a (k+1)-row verify pass as in a one-row step, but attention over a bf16 cache is a
+library kernel whose rounding may depend on the query count (the reference documents the caveat,
+``rocketllm/spec/draft.py:45-64``), so with the stock cache the sequences must agree up to the first
+position where the plain run's top-1 margin is below 4e-2, and that position must exist only there.
+With the int4 cache the two runs hold different caches from the first verify pass on: the pass
+appends k+1 tokens at once and flushes a whole group as soon as the window passes its limit, where
+one-token steps flush that group a few tokens later (the reference cache's rule, applied to the
+same appends, ``rocketllm/quant/kv_cache.py:322-346``), so some queries attend over quantized keys
+in one run and exact keys in the other; that case checks the first token and the pass statistics.
 """
 import pytest
 import torch
@@ -38,16 +44,17 @@ def _draft(checkpoint):
     return AutoModelForCausalLM.from_pretrained(checkpoint, dtype=torch.bfloat16).to("cuda")
 
 
-def _agree_up_to_near_tie(spec, plain, prompt):
+def _agree_up_to_near_tie(spec, plain, prompt, near_tie=True):
     seq, logits = plain.sequences, plain.logits
     n = min(spec.shape[1], seq.shape[1])
     diff = (spec[0, :n] != seq[0, :n]).nonzero()
     if diff.numel() == 0:
         return n
     j = int(diff[0, 0])
-    assert j >= prompt
-    top2 = logits[j - prompt][0].float().topk(2).values
-    assert float(top2[0] - top2[1]) < NEAR_TIE, f"diverged at {j} with margin {top2}"
+    assert j > prompt  # the first token comes from the shared prefill
+    if near_tie:
+        top2 = logits[j - prompt][0].float().topk(2).values
+        assert float(top2[0] - top2[1]) < NEAR_TIE, f"diverged at {j} with margin {top2}"
     return j
 
 
@@ -71,11 +78,9 @@ def test_streamed_speculation_matches_greedy(checkpoint, kv):
     out = spec.generate(ids, max_new_tokens=n, do_sample=False)
     assert out.shape == (1, 190 + n)
     st = spec.speculation
-    agree = _agree_up_to_near_tie(out, ref, 190)
+    agree = _agree_up_to_near_tie(out, ref, 190, near_tie=kv == "fp16")
     if kv == "fp16":
         assert agree >= 190 + 8
-    # (int4: the first verify pass writes 194 positions and flushes a group before the plain run
-    # does, so its first tokens attend over quantized keys -- the reference cache does the same)
     assert st.passes < n and st.tokens_per_pass > 2.0
     # the draft keeps exact keys while an int4 target attends over quantized ones, so near-ties
     # of this random-init model resolve differently more often
