@@ -112,3 +112,83 @@ def algorithmic_bytes(m, k, n, group=64):
 
 def flops(m, k, n):
     return 2 * m * n * k
+
+
+# ---- seeded Llama checkpoints built on the CPU ---------------------------------------------------
+
+# TinyLlama-1.1B architecture: the configuration the reference's CPU path is timed and compared on.
+TINYLLAMA = dict(hidden_size=2048, intermediate_size=5632, num_hidden_layers=22,
+                 num_attention_heads=32, num_key_value_heads=4, head_dim=64, vocab_size=32000,
+                 rms_norm_eps=1e-5, rope_theta=10000.0, max_position_embeddings=2048,
+                 tie_word_embeddings=False, bos_token_id=None, eos_token_id=None,
+                 pad_token_id=None)
+
+
+def llama_tensor_plan(cfg):
+    """``(name, shape, kind)`` of every tensor of a ``LlamaForCausalLM`` with config dict ``cfg`` in
+    a fixed order; ``kind`` is ``"linear"`` (an ``nn.Linear`` weight), ``"norm"`` or ``"embed"``."""
+    h, i, v = cfg["hidden_size"], cfg["intermediate_size"], cfg["vocab_size"]
+    hd = cfg.get("head_dim") or h // cfg["num_attention_heads"]
+    q, kv = cfg["num_attention_heads"] * hd, cfg["num_key_value_heads"] * hd
+    plan = [("model.embed_tokens.weight", (v, h), "embed")]
+    for layer in range(cfg["num_hidden_layers"]):
+        p = f"model.layers.{layer}."
+        plan += [(p + "self_attn.q_proj.weight", (q, h), "linear"),
+                 (p + "self_attn.k_proj.weight", (kv, h), "linear"),
+                 (p + "self_attn.v_proj.weight", (kv, h), "linear"),
+                 (p + "self_attn.o_proj.weight", (h, q), "linear"),
+                 (p + "mlp.gate_proj.weight", (i, h), "linear"),
+                 (p + "mlp.up_proj.weight", (i, h), "linear"),
+                 (p + "mlp.down_proj.weight", (h, i), "linear"),
+                 (p + "input_layernorm.weight", (h,), "norm"),
+                 (p + "post_attention_layernorm.weight", (h,), "norm")]
+    plan += [("model.norm.weight", (h,), "norm"), ("lm_head.weight", (v, h), "linear")]
+    return plan
+
+
+def seeded_llama_tensors(cfg, seed=0, std=0.02):
+    """Yield ``(name, kind, tensor)``: every matrix ~ N(0, std) in fp32, drawn in plan order from
+    one CPU ``torch.Generator(seed)`` (the same values on any machine with this torch), norms 1."""
+    gen = torch.Generator().manual_seed(seed)
+    for name, shape, kind in llama_tensor_plan(cfg):
+        if kind == "norm":
+            yield name, kind, torch.ones(shape, dtype=torch.float32)
+        else:
+            yield name, kind, torch.randn(shape, generator=gen, dtype=torch.float32) * std
+
+
+def write_rw4_llama(path, cfg, quantize_fn, seed=0, std=0.02):
+    """Write ``config.json`` + ``model.safetensors`` of a seeded Llama whose ``nn.Linear`` weights
+    are RW4 (``X.weight_packed`` / ``X.weight_scale`` / ``X.weight_zero_point`` from
+    ``quantize_fn(w fp32 [N, K]) -> (packed u8, scale f16, zero f16)``) and whose embedding and
+    norms stay fp32.  Returns ``{name: tensor}`` of what was written (CPU tensors)."""
+    import json
+    import os
+
+    from safetensors.torch import save_file
+    from transformers import LlamaConfig
+
+    os.makedirs(path, exist_ok=True)
+    sd = {}
+    for name, kind, t in seeded_llama_tensors(cfg, seed, std):
+        if kind == "linear":
+            packed, scale, zero = (a.contiguous().cpu() for a in quantize_fn(t))
+            base = name  # X.weight -> X.weight_packed / _scale / _zero_point
+            sd[base + "_packed"], sd[base + "_scale"], sd[base + "_zero_point"] = packed, scale, zero
+        else:
+            sd[name] = t
+    save_file(sd, os.path.join(path, "model.safetensors"), metadata={"format": "pt"})
+    conf = LlamaConfig(**cfg).to_dict()
+    conf["architectures"] = ["LlamaForCausalLM"]
+    conf["torch_dtype"] = "float32"
+    conf["quantization_config"] = {"quant_method": "rw4", "bits": 4, "group_size": 64,
+                                   "modules_to_not_convert": []}
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(conf, f, indent=1)
+    return sd
+
+
+def tinyllama_prompt(length=128, seed=1, vocab=32000):
+    """The reference configuration's prompt: ``length`` token ids uniform in [0, vocab) from
+    ``seed`` (CPU generator)."""
+    return torch.randint(0, vocab, (1, length), generator=torch.Generator().manual_seed(seed))
