@@ -113,6 +113,21 @@ int rw4_linear_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packe
                   void* y_bf16, int32_t path, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* rw4_linear_noalloc: rw4_linear for M <= 64 (the GEMV) that allocates nothing.  No counterpart in
+ * the reference.  For callers that cannot allocate device memory per call: a host that plans every
+ * byte of VRAM up front (a streaming engine sizing its layer slots from measured free memory, a
+ * serving process with a fixed memory plan) or a C caller with no allocator to hand a workspace
+ * from.  The scratch the GEMV needs for its converted activations is a fixed 4 MiB array in the
+ * library's device image, reserved on every GPU that loads the library until the process exits;
+ * a call needing more (about M*K > 2M values) or M > 64 is rejected with RW4_EINVAL.  The first
+ * call on a device looks up that array's device address (cudaGetSymbolAddress), so make it before
+ * any stream capture.  All calls share the array: calls whose work can overlap on the GPU race and
+ * must be serialised by the caller.  The array keeps the last call's contents; nothing has to be
+ * cleared between calls.  Same arithmetic and bits as rw4_linear for the same M. */
+int rw4_linear_noalloc(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                       const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
+                       void* y_bf16, void* stream);
+
 /* Reads the library's device status word on the current device after the work queued on `stream`
  * (synchronises that stream): bit 1 = a bounded wait inside a kernel gave up (the kernel returned
  * early and its outputs are invalid), bit 2 = a tensor-memory allocation failed.  clear != 0 resets
