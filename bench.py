@@ -130,21 +130,13 @@ class ClockSampler:
 # CPU: the oracle (test infrastructure) as the reported baseline and the reference arm
 # ----------------------------------------------------------------------------------------------
 
-def cpu_sample_step(pool, weights, x, threads):
-    """Dequantize-then-matmul (fp32) of the sampled rows of every shape on `threads` host threads:
-    the reference's dequant-to-scratch + F.linear, restated by the oracle."""
-    from oracle import rw4_oracle as o
-
-    def one(args):
-        xi, (p, s, z) = args
-        return xi @ o.dequantize(p, s, z).T
-
-    jobs = []
+def cpu_sample_step(weights, x):
+    """Dequantize-then-matmul (fp32) of the sampled rows of every shape: the reference's
+    dequant-to-scratch + F.linear, restated in torch on the CPU (``oracle/cpu_decode.py``), on the
+    thread count ``run_cpu`` fixed."""
+    from oracle import cpu_decode
     for xi, (p, s, z) in zip(x, weights):
-        for c in np.array_split(np.arange(p.shape[0]), threads):
-            if c.size:
-                jobs.append((xi, (p[c], s[c], z[c])))
-    list(pool.map(one, jobs))
+        cpu_decode.dequant_linear(xi, p, s, z)
 
 
 def cpu_workload(rows_per_shape, seed=0):
@@ -153,34 +145,41 @@ def cpu_workload(rows_per_shape, seed=0):
     rng = np.random.default_rng(seed)
     for k, n in SHAPES:
         rows = min(n, rows_per_shape)
-        weights.append(o.synthetic_weight(rows, k, GROUP, seed=seed + k + n))
-        xs.append(rng.standard_normal((M, k)).astype(np.float32))
+        p, s, z = o.synthetic_weight(rows, k, GROUP, seed=seed + k + n)
+        weights.append((torch.from_numpy(p), torch.from_numpy(s), torch.from_numpy(z)))
+        xs.append(torch.from_numpy(rng.standard_normal((M, k)).astype(np.float32)))
         nbytes += alg_bytes(M, k, rows)
     return weights, xs, nbytes
 
 
 def run_cpu(steps, warmup, rows_per_shape=None, budget_s=None):
-    """Time the CPU oracle.  With `budget_s`, the per-step row sample is sized from a calibration
+    """Time the CPU port on every host core.  The thread count is set explicitly (torch's intra-op
+    pool, whatever OMP_NUM_THREADS a launcher exported), so the figure is the same workload on the
+    same threads at every N.  With `budget_s`, the per-step row sample is sized from a calibration
     step so that warmup + steps take about `budget_s` seconds."""
-    from concurrent.futures import ThreadPoolExecutor
     threads = os.cpu_count() or 1
-    with ThreadPoolExecutor(threads) as pool:
+    before = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
         if budget_s is not None:
-            weights, xs, _ = cpu_workload(256)
+            weights, xs, _ = cpu_workload(512)
+            cpu_sample_step(weights, xs)
             t0 = time.perf_counter()
-            cpu_sample_step(pool, weights, xs, threads)
-            per_row = (time.perf_counter() - t0) / 256
-            rows_per_shape = int(max(8, min(8192, budget_s / max(1, steps + warmup) / per_row)))
+            cpu_sample_step(weights, xs)
+            per_row = (time.perf_counter() - t0) / 512
+            rows_per_shape = int(max(64, min(16384, budget_s / max(1, steps + warmup) / per_row)))
         weights, xs, nbytes = cpu_workload(rows_per_shape)
         for _ in range(warmup):
-            cpu_sample_step(pool, weights, xs, threads)
+            cpu_sample_step(weights, xs)
         t0 = time.perf_counter()
         for _ in range(steps):
-            cpu_sample_step(pool, weights, xs, threads)
+            cpu_sample_step(weights, xs)
         dt = (time.perf_counter() - t0) / steps
-    sample = (f"dequantize + fp32 matvec of {rows_per_shape} sampled rows of each of the five "
-              f"shapes at M=1 ({nbytes / 1e6:.2f} MB algorithmic per step), numpy oracle, "
-              f"{threads} threads")
+    finally:
+        torch.set_num_threads(before)
+    sample = (f"dequantize + fp32 F.linear of {rows_per_shape} sampled rows of each of the five "
+              f"shapes at M=1 ({nbytes / 1e6:.2f} MB algorithmic per step), torch port of the "
+              f"reference's dequant-to-scratch path, {threads} threads set explicitly")
     return nbytes / dt / 1e9, dt * 1e3, threads, sample
 
 
@@ -583,6 +582,166 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
     return out
 
 
+def partitioned_decode(device, dist, batch=32, prompt=512, tokens=32):
+    """Greedy decode of the Mixtral-8x7B architecture in RW4 (random init N(0, 0.02), router
+    N(0, 0.02): near-uniform routing) at ``batch`` sequences per GPU after a ``prompt``-token prompt,
+    every step a CUDA graph: one GPU holds the whole model (routed experts run by the grouped RW4
+    GEMV, no exchange); on G > 1 GPUs the 8 experts of every layer are split 8/G per rank and each
+    MoE layer exchanges its rows with a fixed-capacity NCCL all-to-all (out and back) inside the
+    graph, attention and the router replicated, every rank decoding its own batch.  Throughput is
+    summed over ranks, the step time is the slowest rank's (CUDA events)."""
+    from transformers import MixtralConfig
+
+    from rocketllm_b200.decode import GraphedDecoder
+    from rocketllm_b200.expert_parallel import enable_expert_parallel
+    from rocketllm_b200.synthetic import build_rw4_causal_lm
+
+    world = dist.get_world_size() if dist is not None else 1
+    rank = dist.get_rank() if dist is not None else 0
+    cfg = MixtralConfig(**MIXTRAL_8X7B)
+    model = build_rw4_causal_lm(cfg, device=device, seed=0)
+    if world > 1:
+        enable_expert_parallel(model, fixed_capacity=True)
+    torch.cuda.empty_cache()
+    ids = torch.randint(0, cfg.vocab_size, (batch, prompt),
+                        generator=torch.Generator().manual_seed(100 + rank))
+    if dist is not None:
+        dist.barrier()
+    dec = GraphedDecoder(model, batch, prompt + tokens + 8, device=device)
+    dec.prefill(ids)
+    for _ in range(3):   # capture (with the exchange's collectives inside) + warm-up replays
+        dec.step()
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(tokens):
+        dec.step()
+    c.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(c) / tokens
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del dec   # a graph holding NCCL calls goes before the process group
+    weight_bytes = sum(p.numel() * p.element_size() for p in model.parameters())
+    del model
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    h = cfg.hidden_size
+    rows = batch * cfg.num_experts_per_tok
+    return {"model": "Mixtral-8x7B architecture, RW4 group 64 (random init N(0,0.02))",
+            "mode": "resident, grouped RW4 GEMV" if world == 1 else
+                    "expert-parallel: 8/G experts per rank, fixed-capacity NCCL all-to-all out "
+                    "and back per MoE layer inside the CUDA-graphed step",
+            "n_gpus": world, "batch_per_gpu": batch, "prompt_tokens": prompt,
+            "decode_tokens": tokens, "tok_s": round(world * batch * 1000.0 / ms, 1),
+            "ms_per_token": round(ms, 3), "weight_bytes_per_gpu": weight_bytes,
+            "exchange_bytes_per_token_per_gpu": 0 if world == 1 else
+            2 * cfg.num_hidden_layers * (world - 1) * rows * h * 2,
+            "scaling": "weak (fixed batch per GPU)"}
+
+
+def tinyllama_bench(device, with_cpu, new_tokens=32):
+    """The TinyLlama-1.1B RW4 configuration (22 layers, prompt of 128 ids from CPU seed 1, greedy
+    decode with the KV cache): the configuration the reference's own CPU path is compared on.
+
+    The checkpoint is rebuilt from its seed (weights N(0, 0.02) from CPU seed 0, encoded by
+    ``rw4_quantize``).  GPU: the package's model (``AutoModel.from_pretrained``, bf16, resident),
+    timed as the reference's harness times decode -- logits-processor marks around ``generate``
+    (``tests/bench_streaming.py:474-502``) -- and as the CUDA-graphed step.  CPU (rank 0, one GPU):
+    the port of the reference's path (``oracle/cpu_decode.py``: the reference codec's fp32 weights
+    in transformers' Llama, every layer resident) on all of this host's cores.  Each run's greedy
+    tokens are compared with the reference's own (``tests/golden/reference_tinyllama.npz``, which
+    also records the reference's decode rate where it was made)."""
+    from transformers import LogitsProcessor, LogitsProcessorList
+
+    from rocketllm_b200 import kernels
+    from rocketllm_b200.decode import GraphedDecoder
+    from rocketllm_b200.engine import AutoModel
+    from rocketllm_b200.synthetic import TINYLLAMA, write_rw4_llama
+
+    golden = dict(np.load(os.path.join(ROOT, "tests", "golden", "reference_tinyllama.npz")))
+    ref_tokens = golden["tokens"][:new_tokens]
+    prompt = torch.from_numpy(golden["prompt"])
+
+    def agree(tokens):
+        diff = np.nonzero(np.asarray(tokens)[:len(ref_tokens)] != ref_tokens)[0]
+        return int(diff[0]) if diff.size else len(ref_tokens)
+
+    def quantize_on_gpu(w):
+        packed, scale, zero, _ = kernels.quantize(w.to(device), 64)
+        return packed.cpu(), scale.cpu(), zero.cpu()
+
+    class Marks(LogitsProcessor):
+        def __init__(self):
+            self.times = []
+
+        def __call__(self, input_ids, scores):
+            torch.cuda.synchronize()
+            self.times.append(time.perf_counter())
+            return scores
+
+    out = {"model": "TinyLlama-1.1B architecture, RW4 group 64 (random init N(0,0.02), seed 0)",
+           "prompt_tokens": int(prompt.shape[1]), "decode_tokens": new_tokens, "greedy": True,
+           "reference_tokens": "tests/golden/reference_tinyllama.npz"}
+    with tempfile.TemporaryDirectory() as tmp:
+        path = os.path.join(tmp, "tinyllama_rw4")
+        write_rw4_llama(path, TINYLLAMA, quantize_on_gpu)
+        model = AutoModel.from_pretrained(path)
+        ids = prompt.to(device)
+        with torch.no_grad():
+            model.generate(ids, max_new_tokens=4, do_sample=False, eos_token_id=None,
+                           pad_token_id=0)
+            marks = Marks()
+            seq = model.generate(ids, max_new_tokens=new_tokens, do_sample=False,
+                                 logits_processor=LogitsProcessorList([marks]),
+                                 eos_token_id=None, pad_token_id=0)
+        gpu_tokens = seq[0, prompt.shape[1]:].cpu().numpy()
+        eager = (len(marks.times) - 1) / (marks.times[-1] - marks.times[0])
+        dec = GraphedDecoder(model.model, 1, prompt.shape[1] + new_tokens + 8, device=device)
+        dec.prefill(ids)
+        dec.capture()
+        for _ in range(3):
+            dec.step()
+        a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(new_tokens):
+            dec.step()
+        c.record()
+        torch.cuda.synchronize()
+        graphed_ms = a.elapsed_time(c) / new_tokens
+        del dec
+        out["gpu"] = {"tok_s": round(eager, 2), "timing": "generate(), logits-processor marks",
+                      "graphed_tok_s": round(1000.0 / graphed_ms, 1),
+                      "graphed_ms_per_token": round(graphed_ms, 4),
+                      "tokens_equal_reference": agree(gpu_tokens)}
+        model.close()
+        del model
+        torch.cuda.empty_cache()
+        if with_cpu:
+            from oracle import cpu_decode
+            cores = os.cpu_count() or 1
+            cpu_model = cpu_decode.load_fp32_llama(path)
+            tokens, _, rate, prefill, threads = cpu_decode.greedy_decode(cpu_model, prompt,
+                                                                         new_tokens, cores)
+            out["cpu_port"] = {"tok_s": round(rate, 3), "cores": threads, "kind": "port",
+                               "prefill_s": round(prefill, 2),
+                               "tokens_equal_reference": agree(tokens),
+                               "sample": f"the whole {new_tokens}-token greedy decode after the "
+                                         f"128-token prompt, fp32, every layer resident"}
+            del cpu_model
+            out["gpu_over_cpu_port"] = round(eager / rate, 1)
+    out["reference_cpu_where_recorded"] = {
+        "tok_s": round(float(golden["decode_tok_s"]), 3), "threads": int(golden["threads"]),
+        "note": "the reference's own RocketModel(device='cpu', fp32) in the container that made "
+                "the fixture (its per-layer shards, streaming hooks and dequant-to-scratch seam); "
+                "its code does not travel to the GPU box"}
+    return out
+
+
 def rw4_arm(args):
     from rocketllm_b200 import kernels
     from rocketllm_b200.streaming import WeightTransfer
@@ -726,6 +885,14 @@ def rw4_arm(args):
                 decode[key]["max_ms_per_token"] = round(float(worst[1]), 4)
             decode["replicas"] = world
 
+    partitioned = None
+    if not args.no_decode and args.partitioned:
+        partitioned = partitioned_decode(device, dist)
+
+    if rank == 0 and world == 1 and not args.no_decode and args.tinyllama:
+        decode = decode if decode is not None else {}
+        decode["tinyllama"] = tinyllama_bench(device, with_cpu=not args.no_cpu)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         value, ms, threads, sample = run_cpu(max(1, args.cpu_steps), 1, budget_s=args.cpu_seconds)
@@ -758,6 +925,7 @@ def rw4_arm(args):
                     "h2d_frac": round(h2d / (e2e_ms * 1e-3) / 1e9 / h2d_peak, 4)
                     if h2d_peak else None},
             "decode": decode,
+            "partitioned_decode": partitioned,
             "gpu_launches": len(SHAPES) * args.steps,
             "clocks": clock,
             "device_status": status,
@@ -1048,6 +1216,14 @@ def main():
     ap.add_argument("--impl", choices=("rw4", "reference"), default="rw4")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-decode", action="store_true", help="skip the model decode section")
+    ap.add_argument("--tinyllama", type=int, default=1,
+                    help="1: include the TinyLlama configuration beside its reference (decode "
+                         "section, one GPU)")
+    ap.add_argument("--partitioned", type=int, default=1,
+                    help="1: include the Mixtral decode, resident on one GPU and expert-parallel "
+                         "(NCCL all-to-all) on several")
+    ap.add_argument("--tinyllama-only", action="store_true",
+                    help="only the TinyLlama GPU / CPU-port decode comparison, one JSON line")
     ap.add_argument("--decode-prompt", type=int, default=2048)
     ap.add_argument("--decode-tokens", type=int, default=256)
     ap.add_argument("--stream-tokens", type=int, default=16)
@@ -1121,6 +1297,11 @@ def main():
             int(4e9), storage_dir=args.storage_dir,
             host_budget=int(args.host_budget_gb * 1e9) if args.storage_dir else None)),
             flush=True)
+        return 0
+    if args.tinyllama_only:
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        print(json.dumps(tinyllama_bench(device, with_cpu=not args.no_cpu)), flush=True)
         return 0
     if args.impl == "reference":
         return reference_arm(args)

@@ -90,3 +90,24 @@ def greedy_decode(model, prompt, new_tokens, threads=None):
     rate = ((len(marker.times) - 1) / (marker.times[-1] - marker.times[0])
             if len(marker.times) > 1 else None)
     return tokens, scores, rate, marker.times[0] - t0, torch.get_num_threads()
+
+
+def dequantize_torch(packed, scale, zero):
+    """The reference's ``QuantizedTensor.dequantize`` to fp32 (``rocketllm/quant/kv_cache.py:
+    249-257``) for a ``[N, K/2]`` RW4 weight, in torch on the CPU: low nibble = even index
+    (``_unpack``, ``:269-272``), ``code * scale + zero`` per group of 64 in fp32 (two roundings
+    at most: the product is exact)."""
+    p = torch.as_tensor(packed)
+    codes = torch.stack([p & 0x0F, p >> 4], dim=-1).reshape(p.shape[0], -1).to(torch.float32)
+    n, k = codes.shape
+    grouped = codes.view(n, k // 64, 64)
+    restored = grouped * torch.as_tensor(scale).float().unsqueeze(-1)
+    restored = restored + torch.as_tensor(zero).float().unsqueeze(-1)
+    return restored.view(n, k)
+
+
+def dequant_linear(x, packed, scale, zero):
+    """``F.linear(x, dequantize(W))`` in fp32: the reference's dequant-to-scratch path for one
+    Linear (``rocketllm/base.py:848-855`` then ``nn.Linear``)."""
+    return torch.nn.functional.linear(torch.as_tensor(x, dtype=torch.float32),
+                                      dequantize_torch(packed, scale, zero))

@@ -234,10 +234,11 @@ def register_dequant_rw4():
         register_backend(DequantRW4Backend)
 
 
-def reference_cpu_model(path, threads=None):
-    """The reference's ``RocketModel`` on the CPU in fp32 over the checkpoint at ``path`` (its own
-    per-layer shard split, streaming and caching), without a tokenizer (token ids only, as the
-    reference's own CPU generation test builds it, ``tests/test_cpu_generation.py:37-45``)."""
+def reference_cpu_model(path, threads=None, dtype=torch.float32):
+    """The reference's ``RocketModel`` on the CPU in ``dtype`` (fp32 by default) over the checkpoint
+    at ``path`` (its own per-layer shard split, streaming and caching), without a tokenizer (token
+    ids only, as the reference's own CPU generation test builds it,
+    ``tests/test_cpu_generation.py:37-45``)."""
     rocketllm = import_reference()
     register_dequant_rw4()
     if threads:
@@ -247,13 +248,15 @@ def reference_cpu_model(path, threads=None):
         def get_tokenizer(self, hf_token=None):
             return None
 
-    return TokenIdModel(str(path), device="cpu", dtype=torch.float32)
+    return TokenIdModel(str(path), device="cpu", dtype=dtype)
 
 
-def phase_marker():
+def phase_marker(force=None):
     """A logits processor that records every step's scores and a timestamp: transformers calls it
     once per generated token, the first call at the end of prefill -- the reference harness's
-    decode-rate method (``tests/bench_streaming.py:474-502``)."""
+    decode-rate method (``tests/bench_streaming.py:474-502``).  With ``force`` (a token sequence)
+    it then leaves only that step's token, so the run follows ``force`` (teacher forcing) and its
+    recorded scores are comparable step by step with the run that produced ``force``."""
     import time
 
     from transformers import LogitsProcessor
@@ -265,7 +268,11 @@ def phase_marker():
         def __call__(self, input_ids, scores):
             self.times.append(time.perf_counter())
             self.scores.append(scores.detach().float().clone())
-            return scores
+            if force is None:
+                return scores
+            forced = torch.full_like(scores, float("-inf"))
+            forced[:, int(force[len(self.scores) - 1])] = 0
+            return forced
 
         def decode_tokens_per_second(self):
             if len(self.times) < 2:

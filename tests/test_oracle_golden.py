@@ -51,6 +51,18 @@ def test_sweep_format_dequant_and_linear(golden):
     assert np.abs(y - ref).max() <= 1e-5 * (1 + np.abs(ref).max())
 
 
+def test_torch_port_dequant_matches_reference(golden):
+    """The torch restatement the CPU baseline times (oracle/cpu_decode.py) gives the reference's
+    fp32 dequantization bit for bit."""
+    import torch
+
+    from oracle import cpu_decode
+    p, s, z = golden["sweep.packed"], golden["sweep.scale"], golden["sweep.zero"]
+    got = cpu_decode.dequantize_torch(torch.from_numpy(p), torch.from_numpy(s),
+                                      torch.from_numpy(z)).numpy()
+    assert np.array_equal(_u(got), _u(golden["sweep.deq_f32"]))
+
+
 def test_nibble_order_known_answer(golden):
     assert np.array_equal(o.pack(golden["pack.codes"]), golden["pack.packed"])
     assert o.pack(np.array([[1, 2]], np.uint8))[0, 0] == 0x21
