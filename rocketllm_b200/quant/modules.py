@@ -104,7 +104,7 @@ def rw4_experts_forward(self, hidden_states, top_k_index, top_k_weights):
     n_exp = getattr(self, "num_experts", None) or self.gate_up_proj_packed.shape[0]
     perm, inv, offsets = kernels.moe_permute(idx, n_exp)
     # rows per expert: a token's top-k experts are distinct, so one token gives each at most one
-    # row (the one-row fp16 kernel); otherwise bound by all of the token-slot pairs
+    # row; otherwise bound by all of the token-slot pairs (known on the host: no device read)
     rows = 1 if t == 1 else t * k
     xp = kernels.moe_gather(x, perm, k)
     act = kernels.moe_grouped(xp, offsets, _expert_triples(self, "gate_up_proj"), act=1,
