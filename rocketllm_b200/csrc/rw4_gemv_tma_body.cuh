@@ -291,11 +291,32 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     const int srows = L::side_rows(bm);
     const uint32_t side_off = L::side_base(bm) + w * srows * 8;
     if (XQ) {
-      // 1. the row's exponent from its largest magnitude over the whole K (consumer threads only)
-      const __nv_bfloat16* xr = x + (int64_t)x_row0 * K;
+      // One pass over the row: this CTA's K range is loaded once into registers (at most 4
+      // chunks of 16 per thread) and its largest magnitude taken there; with a K split the rest of
+      // the row is read only for its maximum.  Then the range is converted from the registers.
+      constexpr int kPer = L::kXQMaxStages * (kStageK / 16) / (kConsumers * 32);
       const int tid = threadIdx.x;
+      const __nv_bfloat16* xr = x + (int64_t)x_row0 * K;
+      const __nv_bfloat16* xk = xr + (int64_t)s_begin * kStageK;
+      const int chunks = nstages * (kStageK / 16);
+      uint4 lo[kPer], hi[kPer];
       uint32_t mx = 0;
-      for (int i = tid; i < K / 8; i += kConsumers * 32) mx = max(mx, absmax8(ldg_u4(xr + 8 * i)));
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int c = tid + kConsumers * 32 * i;
+        lo[i] = make_uint4(0, 0, 0, 0);
+        hi[i] = lo[i];
+        if (c < chunks) {
+          lo[i] = ldg_u4(xk + 16 * c);
+          hi[i] = ldg_u4(xk + 16 * c + 8);
+          mx = max(mx, max(absmax8(lo[i]), absmax8(hi[i])));
+        }
+      }
+      if (KS > 1) {
+        const int k0 = s_begin * kStageK, k1 = (s_begin + nstages) * kStageK;
+        for (int i = tid; i < K / 8; i += kConsumers * 32)
+          if (8 * i < k0 || 8 * i >= k1) mx = max(mx, absmax8(ldg_u4(xr + 8 * i)));
+      }
       mx = __reduce_max_sync(0xFFFFFFFFu, mx);
       __shared__ uint32_t wmax[kConsumers];
       if (lane == 0) wmax[warp] = mx;
@@ -307,15 +328,16 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       if (tid == 0) xq_exp = e;
       float p1, p2;
       exp_factors(e, p1, p2);
-      // 2. this CTA's K range -> fp16 fragments (32 bytes per 16 values) and per-group pairs
-      const __nv_bfloat16* xk = xr + (int64_t)s_begin * kStageK;
-      const int chunks = nstages * (kStageK / 16);
-      for (int base = 0; base < chunks; base += kConsumers * 32) {
-        const int c = base + tid;
+      // this CTA's K range -> fp16 fragments (32 bytes per 16 values) and per-group pairs; the
+      // 4 chunks of a group sit on 4 consecutive lanes, as in the x-prep kernel
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        if (kConsumers * 32 * i >= chunks) break;   // uniform over the CTA
+        const int c = tid + kConsumers * 32 * i;
         float xs_c = 0.f, hs_c = 0.f;
         if (c < chunks) {
           uint32_t o[8];
-          x16_to_f16_frag(ldg_u4(xk + 16 * c), ldg_u4(xk + 16 * c + 8), p1, p2, o, xs_c, hs_c);
+          x16_to_f16_frag(lo[i], hi[i], p1, p2, o, xs_c, hs_c);
           const uint32_t a0 = sbase + L::kX + 32 * c;
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(a0), "r"(o[0]), "r"(o[1]),
                        "r"(o[2]), "r"(o[3]) : "memory");
