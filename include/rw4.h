@@ -347,7 +347,10 @@ int rw4_xfer_stats(rw4_xfer* x, uint64_t* sends, uint64_t* bytes, uint64_t* chun
  * a cudaEvent_t or NULL, is recorded behind the copies) and makes compute wait on the device with
  * rw4_ring_wait_compute (every slot's last submit).  A slot whose last submit is still in flight
  * is refused for staging and submitting (RW4_EBUSY): the reference's lease rule
- * (rocketllm/streaming/staging.py:33-66) per slot.  rw4_ring_destroy waits for copies in flight.
+ * (rocketllm/streaming/staging.py:33-66) per slot; a slot that rw4_ring_stage is still copying
+ * into (another thread) is refused for submitting and for a second stage the same way.  The address
+ * rw4_ring_slot returns is for a caller that owns the slot until it submits it (no stage into it
+ * meanwhile).  rw4_ring_destroy waits for copies in flight.
  * slots 1..64, copy_streams 1..8.
  */
 typedef struct rw4_ring rw4_ring;

@@ -5,7 +5,10 @@
 // caller's event behind it) and makes compute wait for the copies on the device
 // (rw4_ring_wait_compute).  A slot is refused for staging while its last submit is in flight, so a
 // worker never overwrites bytes a copy is still reading -- the lease rule of the reference's
-// BufferLease (rocketllm/streaming/staging.py:33-66) applied per slot.  Built on rw4_pool_* (the
+// BufferLease (rocketllm/streaming/staging.py:33-66) applied per slot -- and refused for submitting
+// (and for a second stage) while a stage into it is still copying on the host, so a copy never
+// reads bytes a worker is still writing.  rw4_ring_slot hands out the slot's address for direct
+// reads: the caller owns that slot until it submits it, and must not stage into it meanwhile.  Built on rw4_pool_* (the
 // slots are leased once) and rw4_xfer_* (the copies).
 #include <cuda_runtime.h>
 
@@ -26,6 +29,7 @@ struct rw4_ring {
   std::vector<void*> host;
   std::vector<int32_t> lease;
   std::vector<uint64_t> ticket;  // last submit of each slot (0: none)
+  std::vector<uint8_t> staging;  // 1 while rw4_ring_stage copies into the slot (host memcpy)
 };
 
 namespace {
@@ -90,6 +94,7 @@ extern "C" int rw4_ring_create(size_t slot_bytes, int32_t slots, int32_t copy_st
     return st;
   }
   r->ticket.assign(slots, 0);
+  r->staging.assign(slots, 0);
   *out = r;
   return RW4_OK;
 }
@@ -120,8 +125,13 @@ extern "C" int rw4_ring_stage(rw4_ring* ring, int32_t slot, size_t offset, const
     const int f = slot_free(ring, slot);
     if (f < 0) return f;
     if (f == 0) return fail(RW4_EBUSY, "rw4_ring_stage: slot %d is still being copied", slot);
+    if (ring->staging[slot])
+      return fail(RW4_EBUSY, "rw4_ring_stage: slot %d is being staged by another caller", slot);
+    ring->staging[slot] = 1;   // the memcpy below runs without the lock
   }
   if (n) std::memcpy(static_cast<char*>(ring->host[slot]) + offset, src, n);
+  std::lock_guard<std::mutex> lock(ring->mu);
+  ring->staging[slot] = 0;
   return RW4_OK;
 }
 
@@ -134,6 +144,8 @@ extern "C" int rw4_ring_submit(rw4_ring* ring, int32_t slot, void* dst, size_t n
     return fail(RW4_EINVAL, "rw4_ring_submit: %zu bytes from a %zu-byte slot", n,
                 ring->slot_bytes);
   std::lock_guard<std::mutex> lock(ring->mu);
+  if (ring->staging[slot])
+    return fail(RW4_EBUSY, "rw4_ring_submit: slot %d is still being staged", slot);
   const int f = slot_free(ring, slot);
   if (f < 0) return f;
   if (f == 0) return fail(RW4_EBUSY, "rw4_ring_submit: slot %d is still being copied", slot);

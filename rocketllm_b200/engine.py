@@ -237,6 +237,15 @@ def footprint(model, skip_experts=False):
     return total - sum(layer_bytes), layer_bytes
 
 
+# Constructor knobs of the reference's RocketModel (rocketllm/base.py:203-208) that have no
+# counterpart here (its hardware-profile overrides, shard-path and tokenizer options): accepted so
+# that code written for the reference runs unchanged, and ignored.  Anything else is an error.
+REFERENCE_ONLY_KNOBS = ("max_seq_len", "layer_shards_saving_path", "profiling_mode",
+                        "compression", "hf_token", "delete_original", "vram_reserve",
+                        "host_cache_gb", "window_max", "shard_handle_limit", "pin_policy",
+                        "expert_residency")
+
+
 class RocketModel:
     """An RW4 ``*ForCausalLM`` with layer streaming (the reference's ``RocketModel`` surface:
     ``generate``, ``__call__``/``forward``, ``stats``, ``close``).
@@ -258,7 +267,12 @@ class RocketModel:
     ``host_budget`` (bytes; layer-shard directories only): pinned host memory for streamed layer
     blobs.  Streamed layers past it form the storage tier: they stay in their files and are read
     ``storage_depth`` layers ahead of use into leased staging buffers on every pass
-    (:class:`~rocketllm_b200.shards.LayerStager`).  None keeps every blob in host memory.
+    (:class:`~rocketllm_b200.shards.LayerStager`).  None keeps every blob in host memory.  The
+    staging pool those reads land in is pinned on top of ``host_budget``: ``storage_depth + window
+    + 1`` buffers of the largest layer blob's power-of-two size class (``stats()["staging_pool"]``).
+    ``read_faults`` (layer-shard directories; tests of failure handling): host-side injected read
+    failures, ``shards.parse_faults`` -- e.g. ``"read:layer=3:pass=2"``, or ``"env"`` for the
+    ``RW4_FAULT`` variable; None (default) injects nothing.
 
     ``kv_cache`` (``rocketllm/base.py:208-411``, ``quant/kv_cache.py:449-503``): ``"int4"`` gives
     every ``generate`` an :class:`~rocketllm_b200.kv_cache.RW4KVCache` whose decode attention reads
@@ -277,10 +291,21 @@ class RocketModel:
                  window=2, prefetching=True, copy_streams=2, chunk_bytes=16 << 20,
                  expert_streaming=True, kv_cache="auto", draft_model=None, speculative="auto",
                  lookahead=4, max_lookahead=8, expert_routing="host", expert_policy=None,
-                 io_workers=4, host_budget=None, storage_depth=2, **unused):
+                 io_workers=4, host_budget=None, storage_depth=2, read_faults=None,
+                 **reference_knobs):
         from .kv_cache import KV_CHOICES
         from .shards import INDEX
         from .speculative import SPEC_CHOICES
+        unknown = sorted(set(reference_knobs) - set(REFERENCE_ONLY_KNOBS))
+        if unknown:
+            raise TypeError(f"RocketModel got unknown argument(s) {', '.join(unknown)}; "
+                            f"the reference's other constructor knobs ("
+                            f"{', '.join(REFERENCE_ONLY_KNOBS)}) are accepted and have no effect "
+                            f"here")
+        if reference_knobs.get("compression") is not None:
+            raise ValueError("compression= is not supported: RocketLLM reads pre-quantized "
+                             "checkpoints only (rocketllm/utils.py:31-56); convert with "
+                             "rocketllm_b200.quant.convert.save_rw4_checkpoint")
         if kv_cache not in KV_CHOICES:
             raise ValueError(f"kv_cache must be one of {', '.join(KV_CHOICES)}, not {kv_cache!r}")
         if expert_routing not in ("host", "device"):
@@ -303,7 +328,7 @@ class RocketModel:
                 os.path.exists(os.path.join(str(model_or_path), INDEX)):
             self._init_from_shards(str(model_or_path), device, dtype, vram_budget, window,
                                    prefetching, copy_streams, chunk_bytes, io_workers,
-                                   host_budget, storage_depth)
+                                   host_budget, storage_depth, expert_streaming, read_faults)
             return
         if host_budget is not None:
             raise ValueError("host_budget applies to a layer-shard directory "
@@ -373,7 +398,7 @@ class RocketModel:
 
     def _init_from_shards(self, root, device, dtype, vram_budget, window, prefetching,
                           copy_streams, chunk_bytes, io_workers=1, host_budget=None,
-                          storage_depth=2):
+                          storage_depth=2, expert_streaming=True, read_faults=None):
         """Layer shards written by ``shards.split_rw4_layers``: the model is built on the meta
         device, the non-layer tensors come from ``rest.safetensors`` straight to the device, and
         each layer's blob is read from its file into pinned memory by positioned reads over
@@ -381,7 +406,7 @@ class RocketModel:
         their layer."""
         from .shards import LayerShardReader, _materialize_rest, build_skeleton
         self.device = torch.device(device)
-        reader = LayerShardReader(root, io_workers=io_workers)
+        reader = LayerShardReader(root, io_workers=io_workers, faults=read_faults)
         self.shards = reader
         model = build_skeleton(root, dtype).eval()
         self.model = model
@@ -408,6 +433,14 @@ class RocketModel:
                 _bind(_LayerBlob(None, resolve(layer, entries), nbytes), slot)
             reader.close()
             return
+        if expert_streaming and any(is_rw4_experts(m) for m in layers.modules()):
+            reader.close()
+            raise ValueError(
+                "this layer-shard directory holds routed experts and the layers do not fit the "
+                "VRAM budget: per-expert streaming (only the routed experts cross PCIe) is built "
+                "for a checkpoint directory or a loaded model, not yet from layer shards.  Load "
+                "the checkpoint directory instead, or pass expert_streaming=False to stream whole "
+                "layers (every expert) from the shards")
         left = max(0, vram_budget - rest)
         window = max(1, min(window, int(left // max(layer_bytes))))
         pinned = self._pin_count(layer_bytes, left, window)
@@ -514,7 +547,13 @@ class RocketModel:
     __call__ = forward
 
     def stats(self):
-        return {"streaming": self.streamer.stats() if self.streamer else None}
+        out = {"streaming": self.streamer.stats() if self.streamer else None,
+               "staging_pool": None}
+        storage = getattr(self.streamer, "storage", None) if self.streamer else None
+        if storage is not None and getattr(storage, "pool", None) is not None:
+            # pinned host memory of the storage tier's staging leases, beside host_budget
+            out["staging_pool"] = storage.pool.stats()
+        return out
 
     def close(self):
         if self.streamer is not None:

@@ -135,13 +135,28 @@ def split_rw4_layers(model, out_dir):
     return out_dir
 
 
-def _faults_from_env():
-    """Read ordinals to fail from ``RW4_FAULT`` (``read:N`` items, comma-separated)."""
+def parse_faults(spec):
+    """Injected read faults as a set of ``(layer, read)`` pairs: the ``read``-th read (1-based) of
+    ``layer``'s file fails.  ``spec`` is None (no faults), such a set, a string of
+    ``read:layer=L[:pass=P]`` items (comma-separated; ``pass`` defaults to 1), or ``"env"`` to take
+    that string from the ``RW4_FAULT`` environment variable (read only when asked for).  Counting
+    per layer makes a fault land on the same read whatever the I/O threads' timing."""
+    if spec is None:
+        return set()
+    if spec == "env":
+        spec = os.environ.get("RW4_FAULT", "")
+    if not isinstance(spec, str):
+        return {(int(a), int(b)) for a, b in spec}
     out = set()
-    for item in os.environ.get("RW4_FAULT", "").split(","):
-        kind, _, n = item.strip().partition(":")
-        if kind == "read" and n.isdigit():
-            out.add(int(n))
+    for item in spec.split(","):
+        item = item.strip()
+        if not item:
+            continue
+        kind, _, rest = item.partition(":")
+        fields = dict(f.split("=", 1) for f in rest.split(":") if "=" in f)
+        if kind != "read" or "layer" not in fields:
+            raise ValueError(f"fault {item!r}: expected read:layer=L[:pass=P]")
+        out.add((int(fields["layer"]), int(fields.get("pass", 1))))
     return out
 
 
@@ -159,11 +174,10 @@ class LayerShardReader:
 
     def __init__(self, root, io_workers=1, faults=None):
         self.root = str(root)
-        # host-side fault injection: the listed reads (1-based, in issue order, read_into and
-        # read_tensor alike) raise IOError instead of reading; ``RW4_FAULT=read:3[,read:7...]``
-        # in the environment sets them when ``faults`` is not given
-        self.faults = set(faults) if faults is not None else _faults_from_env()
-        self._issued = 0
+        # host-side fault injection (parse_faults): the listed (layer, read) pairs raise IOError
+        # instead of reading, read_into and read_tensor alike counting per layer
+        self.faults = parse_faults(faults)
+        self._layer_reads = {}
         with open(os.path.join(self.root, INDEX)) as f:
             self.index = json.load(f)
         self.layers = self.index["layers"]
@@ -249,7 +263,7 @@ class LayerShardReader:
         if buffer.dtype != torch.uint8 or buffer.numel() < nbytes or buffer.is_cuda:
             raise ValueError("read_into needs a CPU uint8 buffer of at least the blob's size")
         path = os.path.join(self.root, rec["file"])
-        self._maybe_fault(path)
+        self._maybe_fault(path, i)
         view = memoryview(buffer[:nbytes].numpy()).cast("B")
         direct_ok = (hasattr(os, "O_DIRECT") and buffer.data_ptr() % DATA_ALIGN == 0
                      and start % DATA_ALIGN == 0)
@@ -320,7 +334,7 @@ class LayerShardReader:
               or not out.is_contiguous()):
             raise ValueError(f"out must be a contiguous CPU {dtype} tensor of shape {shape}")
         view = memoryview(out.view(-1).view(torch.uint8).numpy()).cast("B")
-        self._maybe_fault(os.path.join(self.root, rec["file"]))
+        self._maybe_fault(os.path.join(self.root, rec["file"]), i)
         fd = os.open(os.path.join(self.root, rec["file"]), os.O_RDONLY)
         try:
             done = 0
@@ -337,12 +351,12 @@ class LayerShardReader:
             self.bytes_read += nbytes
         return out
 
-    def _maybe_fault(self, path):
+    def _maybe_fault(self, path, layer):
         with self._lock:
-            self._issued += 1
-            n = self._issued
-        if n in self.faults:
-            raise IOError(f"{path}: injected read fault (read {n})")
+            n = self._layer_reads.get(layer, 0) + 1
+            self._layer_reads[layer] = n
+        if (layer, n) in self.faults:
+            raise IOError(f"{path}: injected read fault (layer {layer}, read {n})")
 
     def stats(self):
         return {"layers": len(self.layers), "reads": self.reads, "bytes_read": self.bytes_read,

@@ -160,18 +160,19 @@ def test_host_budget_needs_a_shard_directory():
 
 def test_an_injected_storage_read_fault_fails_one_pass_and_the_next_reads_again(
         tmp_path, cpu_engine, monkeypatch):
-    """``RW4_FAULT=read:8``: the eighth shard read raises (host-side injection, nothing on a
-    device).  The pass that needs it ends with that IOError, no lease is left behind, and the
-    next pass reads the layer again and gives the model's own logits."""
+    """``RW4_FAULT=read:layer=1:pass=2`` (read because ``read_faults="env"``): the second read of
+    layer 1's shard raises (host-side injection, nothing on a device).  The pass that needs it ends
+    with that IOError, no lease is left behind, and the next pass reads the layer again and gives
+    the model's own logits."""
     model = _plain_llama()
     root = split_rw4_layers(model, str(tmp_path / "shards"))
     rest, layers = engine.footprint(model)
-    monkeypatch.setenv("RW4_FAULT", "read:8")
+    monkeypatch.setenv("RW4_FAULT", "read:layer=1:pass=2")
     rm = engine.RocketModel(root, device="cpu", dtype=torch.float32,
                             vram_budget=rest + 2 * max(layers) + 64 * 1024, window=2,
-                            kv_cache="fp16", host_budget=0, storage_depth=2)
+                            kv_cache="fp16", host_budget=0, storage_depth=2, read_faults="env")
     st = rm.streamer
-    assert st.storage.reader.faults == {8}
+    assert st.storage.reader.faults == {(1, 2)} and 1 in st.storage.order
     ids = torch.randint(0, 96, (1, 7), generator=torch.Generator().manual_seed(8))
     with torch.no_grad():
         want = model(ids).logits
@@ -189,3 +190,15 @@ def test_an_injected_storage_read_fault_fails_one_pass_and_the_next_reads_again(
     ahead = list(st.storage._pending.values())
     rm.close()
     assert all(f.result().released for f in ahead)
+
+
+def test_unknown_constructor_arguments_are_rejected():
+    """A misspelt knob is an error; the reference's own knobs that have no effect here are
+    accepted (code written for the reference runs unchanged); compression= raises as there."""
+    with pytest.raises(TypeError, match="windw"):
+        engine.RocketModel(_plain_llama(), device="cpu", windw=3)
+    rm = engine.RocketModel(_plain_llama(), device="cpu", dtype=torch.float32, max_seq_len=512,
+                            pin_policy="auto", vram_reserve=None)
+    assert rm.streamer is None
+    with pytest.raises(ValueError, match="pre-quantized"):
+        engine.RocketModel(_plain_llama(), device="cpu", compression="4bit")

@@ -117,22 +117,28 @@ def test_a_failed_expert_parallel_rank_ends_the_exchange_with_an_error():
 
 
 def test_injected_read_faults_raise_and_the_reader_carries_on(tmp_path, monkeypatch):
-    """Host-side fault injection (``faults=`` or ``RW4_FAULT=read:N``): the listed reads raise
-    IOError, the others read normally."""
+    """Host-side fault injection (``faults=`` pairs, a spec string, or ``"env"`` for
+    ``RW4_FAULT``): the listed (layer, read) pairs raise IOError, the others read normally; reads
+    are counted per layer, so a fault lands on the same read whatever the threads' timing; the
+    environment is read only when asked for."""
     from test_shards_cpu import tiny_rw4_model
 
     from rocketllm_b200.shards import LayerShardReader, split_rw4_layers
     root = split_rw4_layers(tiny_rw4_model(6), str(tmp_path / "shards"))
-    reader = LayerShardReader(root, faults={2})
+    reader = LayerShardReader(root, faults={(0, 2)})
     buf = torch.empty(max(l["nbytes"] for l in reader.layers), dtype=torch.uint8)
     reader.read_into(0, buf)
+    reader.read_into(1, buf)
     with pytest.raises(IOError, match="injected read fault"):
         reader.read_into(0, buf)
-    reader.read_into(1, buf)
-    assert reader.stats()["reads"] == 2
-    monkeypatch.setenv("RW4_FAULT", "read:1, read:3")
-    env = LayerShardReader(root)
-    assert env.faults == {1, 3}
+    reader.read_into(0, buf)
+    assert reader.stats()["reads"] == 3
+    monkeypatch.setenv("RW4_FAULT", "read:layer=0:pass=1, read:layer=2")
+    assert LayerShardReader(root).faults == set()          # not read unless asked for
+    env = LayerShardReader(root, faults="env")
+    assert env.faults == {(0, 1), (2, 1)}
     with pytest.raises(IOError, match="injected read fault"):
         env.read_tensor(0, "mlp.up_proj.weight_packed")
     env.read_tensor(0, "mlp.up_proj.weight_packed")
+    with pytest.raises(ValueError):
+        LayerShardReader(root, faults="read:8")

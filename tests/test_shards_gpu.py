@@ -40,8 +40,11 @@ def test_shards_equal_checkpoint(tmp_path, kind):
     from_shards = RocketModel(root)
     assert from_shards.streamer is None
     rest, layers = footprint(resident.model)
+    if kind == "mixtral":   # per-expert streaming is not built from layer shards: it says so
+        with pytest.raises(ValueError, match="expert_streaming=False"):
+            RocketModel(root, vram_budget=rest + 2 * max(layers) + 1000, window=2)
     streamed = RocketModel(root, vram_budget=rest + 2 * max(layers) + 1000, window=2,
-                           kv_cache="fp16")
+                           kv_cache="fp16", expert_streaming=False)
     assert streamed.streamer is not None and streamed.streamer.window == 2
     with torch.no_grad():
         ref = resident(ids).logits
