@@ -113,6 +113,37 @@ int rw4_linear_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packe
                   void* y_bf16, int32_t path, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* ---------------------------------------------------------------------------------------------
+ * Decode-step kernels around the projections of a Llama-family decoder layer, each replacing a
+ * chain of small transformers ops with one launch and the same bf16 rounding sequence
+ * (transformers models/llama/modeling_llama.py).  All bf16 unless stated.
+ *
+ * rw4_rmsnorm: y[r] = weight * bf16(x[r] * rsqrt(mean(x[r]^2) + eps)) (LlamaRMSNorm, :48-68);
+ *   rows <= 65535.
+ * rw4_rope_kv: rotary embedding of the q and k heads of `rows` token rows (one per sequence) with
+ *   bf16 cos / sin [rows, head_dim] (apply_rotary_pos_emb, :78-112), q written to q_out
+ *   [rows, heads, head_dim], k and v written into the static caches [rows, kv_heads, cache_len,
+ *   head_dim] at position *pos (DEVICE int64: a CUDA graph can replay it); q, k, v are row-major
+ *   with row stride ld elements (the slices of one concatenated q|k|v projection).  Replaces
+ *   apply_rotary_pos_emb + StaticCache.update's index_copy_.
+ * rw4_silu_mul: out[r, i] = bf16(bf16(silu(g)) * u), g = gate_up[r, i], u = gate_up[r, I + i]
+ *   (act_fn(gate_proj(x)) * up_proj(x) of a concatenated gate|up projection, :171-184).
+ * rw4_linear_residual_ws: y = bf16(residual + bf16(x . W^T)) for M <= 64 (the GEMV with the
+ *   decoder layer's residual add in its epilogue); residual [M, N] may be y itself (in place) when
+ *   K is a multiple of 512.  Workspace as rw4_linear_ws.
+ * ------------------------------------------------------------------------------------------- */
+int rw4_rmsnorm(const void* x, const void* weight, int64_t rows, int64_t H, float eps, void* y,
+                void* stream);
+int rw4_rope_kv(const void* q, const void* k, const void* v, int64_t ld, int32_t rows,
+                int32_t heads, int32_t kv_heads, int32_t head_dim, const void* cos_bf16,
+                const void* sin_bf16, const int64_t* pos, int64_t cache_len, void* q_out,
+                void* k_cache, void* v_cache, void* stream);
+int rw4_silu_mul(const void* gate_up, int64_t rows, int64_t I, void* out, void* stream);
+int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
+                           const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
+                           const void* residual, void* y_bf16, void* workspace,
+                           size_t workspace_bytes, void* stream);
+
 /* rw4_linear_noalloc: rw4_linear for M <= 64 (the GEMV) that allocates nothing.  No counterpart in
  * the reference.  For callers that cannot allocate device memory per call: a host that plans every
  * byte of VRAM up front (a streaming engine sizing its layer slots from measured free memory, a

@@ -1,0 +1,201 @@
+// Decode-step kernels around the RW4 GEMVs: the ops a Llama-family decoder layer runs between its
+// projections, each one launch, each reproducing the rounding sequence of the bf16 transformers
+// module it replaces (transformers models/llama/modeling_llama.py), so that a fused decode step
+// stays within rounding of the module-by-module one:
+//
+//   rw4_rmsnorm        LlamaRMSNorm: fp32 mean of squares, x * rsqrt(mean + eps) rounded to bf16,
+//                      times the bf16 weight (rounded again)                 [:48-68]
+//   rw4_rope_kv        apply_rotary_pos_emb on q and k with bf16 cos / sin (each product and the
+//                      sum rounded to bf16), k and v written into a static [B, KVH, T, D] cache at
+//                      the device-side position                            [:78-112, StaticCache]
+//   rw4_silu_mul       act_fn(gate) * up for a concatenated [gate | up] row: silu in fp32 rounded
+//                      to bf16, the product rounded to bf16                  [:171-184]
+//   rw4_linear_residual_ws   residual + linear(x): the GEMV with the residual added in its epilogue
+//                      (the product rounded to bf16 first, then the sum), as a decoder layer's
+//                      `hidden_states = residual + self_attn(...)` / `+ mlp(...)`.
+// All are memory-bound and tiny at decode batch sizes; their point is the launch count (about 1,600
+// small kernels per Llama-8B token through the modules, 8 per layer here).
+#include "rw4_common.cuh"
+
+namespace rw4 {
+int check_linear_args(const char* who, const void* x, int64_t M, int64_t K, const uint8_t* wq,
+                      const void* sc, const void* zr, int64_t N, int32_t group, const void* y);
+int gemv_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
+                const void* zr, int64_t N, void* y, cudaStream_t s, void* ws, size_t ws_bytes);
+bool gemv_tma_supported(int64_t K);
+int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
+                    const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
+                    size_t ws_bytes, const void* res);
+}  // namespace rw4
+
+namespace {
+
+using rw4::fail;
+
+__device__ __forceinline__ float bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+constexpr int kNormThreads = 256;
+
+// One CTA per row.
+__global__ void __launch_bounds__(kNormThreads)
+    rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
+                   int H, float eps, __nv_bfloat16* __restrict__ y) {
+  const __nv_bfloat16* xr = x + (int64_t)blockIdx.x * H;
+  __nv_bfloat16* yr = y + (int64_t)blockIdx.x * H;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += kNormThreads) {
+    const float v = __bfloat162float(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 16);
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 8);
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 4);
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 2);
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 1);
+  __shared__ float part[kNormThreads / 32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) tot += part[i];
+  const float r = rsqrtf(tot / (float)H + eps);
+  for (int i = threadIdx.x; i < H; i += kNormThreads)
+    yr[i] = __float2bfloat16_rn(__bfloat162float(w[i]) * bf(__bfloat162float(xr[i]) * r));
+}
+
+// One thread per (row, head, pair d < D/2) of q heads then k heads; v is copied by the k threads.
+// q/k/v rows have element strides ld (a concatenated q|k|v projection output); cos / sin [rows, D]
+// bf16; the cache is [B, KVH, T, D] with row b's token written at position *pos.
+__global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                               const __nv_bfloat16* __restrict__ v, int64_t ld, int rows, int Hq,
+                               int Hk, int D, const __nv_bfloat16* __restrict__ cosv,
+                               const __nv_bfloat16* __restrict__ sinv, const int64_t* __restrict__ pos,
+                               int64_t T, __nv_bfloat16* __restrict__ q_out,
+                               __nv_bfloat16* __restrict__ k_cache,
+                               __nv_bfloat16* __restrict__ v_cache) {
+  const int half = D / 2;
+  const int64_t total = (int64_t)rows * (Hq + Hk) * half;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int d = (int)(i % half);
+  const int h = (int)((i / half) % (Hq + Hk));
+  const int b = (int)(i / ((int64_t)half * (Hq + Hk)));
+  const __nv_bfloat16* cs = cosv + (int64_t)b * D;
+  const __nv_bfloat16* sn = sinv + (int64_t)b * D;
+  const float c0 = __bfloat162float(cs[d]), c1 = __bfloat162float(cs[d + half]);
+  const float s0 = __bfloat162float(sn[d]), s1 = __bfloat162float(sn[d + half]);
+  const bool is_q = h < Hq;
+  const int hh = is_q ? h : h - Hq;
+  const __nv_bfloat16* src = (is_q ? q : k) + (int64_t)b * ld + (int64_t)hh * D;
+  const float a = __bfloat162float(src[d]), bb = __bfloat162float(src[d + half]);
+  // x * cos + rotate_half(x) * sin, rotate_half(x) = cat(-x[half:], x[:half]); each op in bf16
+  const float o0 = bf(bf(a * c0) + bf(-bb * s0));
+  const float o1 = bf(bf(bb * c1) + bf(a * s1));
+  if (is_q) {
+    __nv_bfloat16* dst = q_out + ((int64_t)b * Hq + hh) * D;
+    dst[d] = __float2bfloat16_rn(o0);
+    dst[d + half] = __float2bfloat16_rn(o1);
+  } else {
+    const int64_t p = pos[0];
+    if (p < 0 || p >= T) return;  // the caller checks the position on the host
+    const int64_t off = (((int64_t)b * Hk + hh) * T + p) * D;
+    k_cache[off + d] = __float2bfloat16_rn(o0);
+    k_cache[off + d + half] = __float2bfloat16_rn(o1);
+    const __nv_bfloat16* vs = v + (int64_t)b * ld + (int64_t)hh * D;
+    v_cache[off + d] = vs[d];
+    v_cache[off + d + half] = vs[d + half];
+  }
+}
+
+// out[r, i] = bf16(bf16(silu(g)) * u) with g = gu[r, i], u = gu[r, I + i].
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int rows, int I,
+                                __nv_bfloat16* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (int64_t)rows * I) return;
+  const int64_t r = i / I, c = i % I;
+  const float g = __bfloat162float(gu[r * 2 * I + c]);
+  const float u = __bfloat162float(gu[r * 2 * I + I + c]);
+  out[i] = __float2bfloat16_rn(bf(g / (1.f + expf(-g))) * u);
+}
+
+// y = bf16(y + r) elementwise (the residual add after a GEMV that had no epilogue for it).
+__global__ void add_kernel(__nv_bfloat16* __restrict__ y, const __nv_bfloat16* __restrict__ r,
+                           int64_t n) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] = __float2bfloat16_rn(__bfloat162float(y[i]) + __bfloat162float(r[i]));
+}
+
+unsigned blocks(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
+
+}  // namespace
+
+extern "C" int rw4_rmsnorm(const void* x, const void* weight, int64_t rows, int64_t H, float eps,
+                           void* y, void* stream) {
+  if (rows < 0 || H <= 0 || H > (1 << 24)) return fail(RW4_EINVAL, "rw4_rmsnorm: bad shape");
+  if (rows == 0) return RW4_OK;
+  if (!x || !weight || !y) return fail(RW4_EINVAL, "rw4_rmsnorm: null pointer");
+  if (rows > 65535) return fail(RW4_EINVAL, "rw4_rmsnorm: more than 65535 rows");
+  rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, rw4::as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight), (int)H,
+      eps, static_cast<__nv_bfloat16*>(y));
+  return rw4::launch_status("rw4_rmsnorm launch");
+}
+
+extern "C" int rw4_rope_kv(const void* q, const void* k, const void* v, int64_t ld, int32_t rows,
+                           int32_t heads, int32_t kv_heads, int32_t head_dim, const void* cos_bf16,
+                           const void* sin_bf16, const int64_t* pos, int64_t cache_len,
+                           void* q_out, void* k_cache, void* v_cache, void* stream) {
+  if (rows < 0 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || head_dim % 2 || cache_len <= 0)
+    return fail(RW4_EINVAL, "rw4_rope_kv: bad shape");
+  if (rows == 0) return RW4_OK;
+  if (!q || !k || !v || !cos_bf16 || !sin_bf16 || !pos || !q_out || !k_cache || !v_cache)
+    return fail(RW4_EINVAL, "rw4_rope_kv: null pointer");
+  const int64_t n = (int64_t)rows * (heads + kv_heads) * (head_dim / 2);
+  rope_kv_kernel<<<blocks(n, 256), 256, 0, rw4::as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
+      static_cast<const __nv_bfloat16*>(v), ld, rows, heads, kv_heads, head_dim,
+      static_cast<const __nv_bfloat16*>(cos_bf16), static_cast<const __nv_bfloat16*>(sin_bf16),
+      pos, cache_len, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
+      static_cast<__nv_bfloat16*>(v_cache));
+  return rw4::launch_status("rw4_rope_kv launch");
+}
+
+extern "C" int rw4_silu_mul(const void* gate_up, int64_t rows, int64_t I, void* out, void* stream) {
+  if (rows < 0 || I <= 0) return fail(RW4_EINVAL, "rw4_silu_mul: bad shape");
+  if (rows == 0) return RW4_OK;
+  if (!gate_up || !out) return fail(RW4_EINVAL, "rw4_silu_mul: null pointer");
+  silu_mul_kernel<<<blocks(rows * I, 256), 256, 0, rw4::as_stream(stream)>>>(
+      static_cast<const __nv_bfloat16*>(gate_up), (int)rows, (int)I,
+      static_cast<__nv_bfloat16*>(out));
+  return rw4::launch_status("rw4_silu_mul launch");
+}
+
+extern "C" int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K,
+                                      const uint8_t* packed, const void* scale_f16,
+                                      const void* zero_f16, int64_t N, int32_t group,
+                                      const void* residual, void* y_bf16, void* workspace,
+                                      size_t workspace_bytes, void* stream) {
+  using namespace rw4;
+  int st = check_linear_args("rw4_linear_residual_ws", x_bf16, M, K, packed, scale_f16, zero_f16,
+                             N, group, y_bf16);
+  if (st != RW4_OK || M == 0 || N == 0) return st;
+  if (!residual) return fail(RW4_EINVAL, "rw4_linear_residual_ws: null residual");
+  if (M > 64)
+    return fail(RW4_EINVAL, "rw4_linear_residual_ws: M=%lld; the GEMV takes at most 64 rows",
+                (long long)M);
+  cudaStream_t s = as_stream(stream);
+  static const bool no_tma = getenv("RW4_GEMV_NO_TMA") != nullptr;
+  if (!no_tma && gemv_tma_supported(K))
+    return gemv_tma_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s, 0, workspace,
+                           workspace_bytes, residual);
+  if (residual == y_bf16)
+    return fail(RW4_EINVAL, "rw4_linear_residual_ws: K=%lld takes the register-staged GEMV, "
+                "which cannot add in place", (long long)K);
+  st = gemv_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s, workspace,
+                   workspace_bytes);
+  if (st != RW4_OK) return st;
+  add_kernel<<<blocks(M * N, 256), 256, 0, s>>>(static_cast<__nv_bfloat16*>(y_bf16),
+                                                static_cast<const __nv_bfloat16*>(residual),
+                                                M * N);
+  return launch_status("rw4_linear_residual_ws add");
+}

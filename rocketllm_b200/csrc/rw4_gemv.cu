@@ -258,7 +258,7 @@ bool gemv_tma_supported(int64_t K);
 size_t gemv_tma_workspace(int64_t M, int64_t K, int64_t N);
 int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                     const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
-                    size_t ws_bytes);
+                    size_t ws_bytes, const void* res = nullptr);
 
 // Workspace bytes the GEMV needs for (M, K, N): the TMA kernel's x-prep arrays (none for a row it
 // converts itself); the register-staged kernel needs none.

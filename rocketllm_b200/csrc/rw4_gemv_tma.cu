@@ -116,14 +116,16 @@ __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
                         const __grid_constant__ CUtensorMap tm_x,
                         const __grid_constant__ CUtensorMap tm_side, const int* row_exp,
                         const __nv_bfloat16* __restrict__ x, int bm, int M, int K, int N,
-                        __nv_bfloat16* __restrict__ y, unsigned int* status) {
+                        __nv_bfloat16* __restrict__ y, unsigned int* status,
+                        const __nv_bfloat16* __restrict__ res) {
   // batch slices are the fastest grid dimension: the CTAs of all slices of one row tile run
   // together, so the slices after the first find the tile's weights in L2
   const int m0 = blockIdx.x * 16;
   body<NT, R, S, false, KS, !XQ, M1, !XQ, XQ>(&tm_codes, &tm_scale, &tm_zero, &tm_x, &tm_side,
                                               row_exp, x, m0, bm, min(16, M - m0), K,
                                               y + (int64_t)m0 * N, N,
-                                              blockIdx.y * Layout<R, S>::BR, N, 0, status);
+                                              blockIdx.y * Layout<R, S>::BR, N, 0, status,
+                                              res ? res + (int64_t)m0 * N : nullptr);
 }
 
 bool pdl_enabled() {
@@ -167,7 +169,8 @@ bool one_row_in_kernel(int64_t M, int64_t K, int ks) {
 
 template <int NT, int R, int S, int KS = 1>
 int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, const void* zr,
-               int N, void* y, const XPrepLayout& l, uint8_t* ws, cudaStream_t stream) {
+               int N, void* y, const XPrepLayout& l, uint8_t* ws, cudaStream_t stream,
+               const void* res) {
   using L = Layout<R, S>;
   static_assert(L::kBars >= kConsumers * L::BR * (16 * NT + 1) * 4,
                 "reduction buffer must fit in the ring below the barriers");
@@ -240,7 +243,8 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   cudaError_t err = cudaLaunchKernelEx(&cfg, kern, tc, ts, tz, tx, tside,
                                        reinterpret_cast<const int*>(ws + l.row_exp),
                                        static_cast<const __nv_bfloat16*>(x), bm, M, K, N,
-                                       static_cast<__nv_bfloat16*>(y), status);
+                                       static_cast<__nv_bfloat16*>(y), status,
+                                       static_cast<const __nv_bfloat16*>(res));
   if (err != cudaSuccess) return cuda_status(err, "rw4 gemv_tma launch");
   return launch_status("rw4 gemv_tma launch");
 }
@@ -293,7 +297,7 @@ size_t gemv_tma_workspace(int64_t M, int64_t K, int64_t N) {
 
 int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                     const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
-                    size_t ws_bytes) {
+                    size_t ws_bytes, const void* res) {
   const int Mi = (int)M, Ki = (int)K, Ni = (int)N;
   static const int forced_ks = [] {
     const char* e = getenv("RW4_GEMV_KSPLIT");
@@ -319,25 +323,25 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
     if (st != RW4_OK) return st;
   }
   if (M <= 8) {
-    if (row_tiles == 4) return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+    if (row_tiles == 4) return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
     if (row_tiles == 2) {
-      if (ks == 4) return launch_tma<1, 2, 6, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
-      if (ks == 2) return launch_tma<1, 2, 6, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
-      return launch_tma<1, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+      if (ks == 4) return launch_tma<1, 2, 6, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+      if (ks == 2) return launch_tma<1, 2, 6, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+      return launch_tma<1, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
     }
-    if (ks == 4) return launch_tma<1, 1, 8, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
-    if (ks == 2) return launch_tma<1, 1, 8, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
-    return launch_tma<1, 1, 8>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+    if (ks == 4) return launch_tma<1, 1, 8, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+    if (ks == 2) return launch_tma<1, 1, 8, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+    return launch_tma<1, 1, 8>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
   }
   // 9..16 activation rows per slice: 16 KB of x per stage, so shallower rings keep two CTAs per SM
   if (row_tiles >= 2) {
-    if (ks == 4) return launch_tma<2, 2, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
-    if (ks == 2) return launch_tma<2, 2, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
-    return launch_tma<2, 2, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+    if (ks == 4) return launch_tma<2, 2, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+    if (ks == 2) return launch_tma<2, 2, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+    return launch_tma<2, 2, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
   }
-  if (ks == 4) return launch_tma<2, 1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
-  if (ks == 2) return launch_tma<2, 1, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
-  return launch_tma<2, 1, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s);
+  if (ks == 4) return launch_tma<2, 1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+  if (ks == 2) return launch_tma<2, 1, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+  return launch_tma<2, 1, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
 }
 
 }  // namespace rw4

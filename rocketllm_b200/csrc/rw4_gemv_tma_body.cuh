@@ -142,7 +142,8 @@ __device__ __forceinline__ void x_frag_smem(uint32_t a, bool valid, uint32_t (&b
 // into fp16 fragments and (sum, -offset) pairs in shared memory -- with the same helpers, in the
 // same order, as the x-prep kernel, so the output has the same bits as the XP path's.  x is the
 // bf16 activations (row x_row0, stride K).
-// y: output rows (stride ldy).
+// y: output rows (stride ldy); res (XP / XQ only, may be null): rows added to the output in the
+// model's bf16 order, bf16(bf16(x . W^T) + res) -- a decoder layer's residual connection.
 // Plain: writes y[m, r0 + r] for r0 + r < n_out.  SWIGLU: writes y[m, r0 + r] for r0 + r < n_out
 // (= I) from weight rows r0 + r (gate) and r0 + I + r (up).
 // M1: the launch has exactly one activation row (NT == 1, M == 1).
@@ -154,7 +155,8 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
                                      const __nv_bfloat16* __restrict__ x, int x_row0, int bm,
                                      int Ml, int K,
                                      __nv_bfloat16* __restrict__ y, int64_t ldy, int r0,
-                                     int n_out, int up_offset, unsigned int* status) {
+                                     int n_out, int up_offset, unsigned int* status,
+                                     const __nv_bfloat16* __restrict__ res = nullptr) {
   using namespace rw4::frag;
   using L = Layout<R, S>;
   static_assert(!SWIGLU || R == 2, "the SwiGLU epilogue pairs one gate tile with one up tile");
@@ -568,6 +570,10 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       } else if (XP || XQ) {
         // undo the row's 2^e (exact)
         v = ldexpf(part[i][0], XQ ? -xq_e : -row_exp[x_row0 + m]);
+        // residual (same layout as y): the model's bf16 `residual + linear(x)`, i.e. the product
+        // rounded to bf16 first, then the sum
+        if (res) v = __bfloat162float(__float2bfloat16_rn(v)) +
+                     __bfloat162float(res[(int64_t)m * ldy + n]);
       } else {
         v = part[i][0];
       }

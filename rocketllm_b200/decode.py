@@ -48,6 +48,7 @@ class GraphedDecoder:
     def _step(self):
         logits = self.model(self.ids, past_key_values=self.cache, cache_position=self.pos,
                             use_cache=True).logits[:, -1]
+        self.logits = logits   # the step's scores (a static tensor once captured)
         nxt = logits.argmax(-1, keepdim=True)
         self.ids.copy_(nxt)
         self.pos.add_(1)

@@ -1,0 +1,187 @@
+"""Fused decode step for resident RW4 Llama-architecture models (the decode-step op stream around
+the RW4 GEMVs, B200-first).
+
+Through the transformers modules one decode step of a Llama layer is about fifty small launches:
+RMSNorm as six elementwise kernels, q / k / v as three GEMVs, the rotary embedding as cat / neg /
+mul / add kernels, ``index_copy_`` into the static cache, the grouped-query key / value copies
+(``repeat_kv``), attention, o_proj, the residual add, RMSNorm again, gate, up, SiLU, the product,
+down, the residual add (transformers ``models/llama/modeling_llama.py``).  The step here is eight
+launches per layer, each reproducing the modules' bf16 rounding sequence:
+
+    rw4_rmsnorm                       input_layernorm
+    rw4_linear (q|k|v concatenated)   q_proj, k_proj, v_proj: one GEMV over one weight
+    rw4_rope_kv                       apply_rotary_pos_emb + StaticCache.update (device position)
+    SDPA with enable_gqa              attention over the static cache, no key / value copies
+    rw4_linear_residual_ws            o_proj + residual add in the GEMV epilogue
+    rw4_rmsnorm                       post_attention_layernorm
+    rw4_linear (gate|up concatenated) gate_proj, up_proj: one GEMV
+    rw4_silu_mul                      act_fn(gate) * up
+    rw4_linear_residual_ws            down_proj + residual add
+
+The q/k/v and gate/up weights are concatenated once at set-up and the original modules'
+parameters become views of the concatenated tensors, so nothing is duplicated and the
+transformers forward (prefill, or any other use) runs on the same bytes.  The prefill itself
+runs through the modules; only decode steps take the fused path, captured in a CUDA graph by
+:class:`~rocketllm_b200.decode.GraphedDecoder`'s machinery.
+"""
+import torch
+
+from . import _lib, kernels
+from .decode import GraphedDecoder
+from .quant.modules import RW4Linear
+
+
+def fusable(model):
+    """Whether ``model`` is a resident RW4 Llama-architecture ``*ForCausalLM`` the fused step
+    covers: every projection an ``RW4Linear`` without bias, no sliding window, no streaming hooks,
+    all on one CUDA device."""
+    cfg = model.config
+    if getattr(cfg, "model_type", None) != "llama" or getattr(cfg, "sliding_window", None):
+        return False
+    inner = getattr(model, "model", None)
+    if inner is None or not isinstance(getattr(model, "lm_head", None), RW4Linear):
+        return False
+    for layer in inner.layers:
+        a, m = layer.self_attn, layer.mlp
+        mods = (a.q_proj, a.k_proj, a.v_proj, a.o_proj, m.gate_proj, m.up_proj, m.down_proj)
+        if not all(isinstance(x, RW4Linear) and x.bias is None for x in mods):
+            return False
+        if layer._forward_pre_hooks or layer._forward_hooks:
+            return False
+        if getattr(m, "act_fn", None) is None or cfg.hidden_act not in ("silu", "swish"):
+            return False
+    return all(p.is_cuda for p in model.parameters())
+
+
+def _concat_rows(mods):
+    """One RW4 weight whose rows are the given modules' rows in order; each module's parameters
+    become views of it (the originals are released)."""
+    parts = {}
+    for leaf in ("weight_packed", "weight_scale", "weight_zero_point"):
+        tensors = [getattr(m, leaf) for m in mods]
+        fused = torch.cat([t.detach() for t in tensors], dim=0).contiguous()
+        parts[leaf] = fused
+        off = 0
+        for m, t in zip(mods, tensors):
+            n = t.shape[0]
+            m._parameters[leaf] = torch.nn.Parameter(fused[off:off + n], requires_grad=False)
+            off += n
+    return parts["weight_packed"], parts["weight_scale"], parts["weight_zero_point"]
+
+
+class _LayerWeights:
+    __slots__ = ("ln1", "ln2", "qkv", "o", "gate_up", "down", "eps1", "eps2")
+
+
+class FusedDecoder(GraphedDecoder):
+    """Greedy decode of a resident RW4 Llama model with the fused step (see the module docstring);
+    same interface as :class:`~rocketllm_b200.decode.GraphedDecoder` (``prefill``, ``step``,
+    ``generate``, ``capture``).  Raises ``ValueError`` for a model :func:`fusable` rejects."""
+
+    def __init__(self, model, batch, max_len, device="cuda", use_graph=True):
+        if not fusable(model):
+            raise ValueError("the fused decode step covers resident RW4 Llama-architecture models")
+        super().__init__(model, batch, max_len, device=device, use_graph=use_graph)
+        cfg = model.config
+        self.hq = cfg.num_attention_heads
+        self.hk = cfg.num_key_value_heads
+        self.hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.hq
+        self.hidden = cfg.hidden_size
+        self.inter = cfg.intermediate_size
+        self.layers = []
+        for layer in model.model.layers:
+            a, m = layer.self_attn, layer.mlp
+            w = _LayerWeights()
+            w.ln1, w.eps1 = layer.input_layernorm.weight, layer.input_layernorm.variance_epsilon
+            w.ln2 = layer.post_attention_layernorm.weight
+            w.eps2 = layer.post_attention_layernorm.variance_epsilon
+            w.qkv = _concat_rows([a.q_proj, a.k_proj, a.v_proj])
+            w.o = (a.o_proj.weight_packed, a.o_proj.weight_scale, a.o_proj.weight_zero_point)
+            w.gate_up = _concat_rows([m.gate_proj, m.up_proj])
+            w.down = (m.down_proj.weight_packed, m.down_proj.weight_scale,
+                      m.down_proj.weight_zero_point)
+            self.layers.append(w)
+        norm = model.model.norm
+        self.final_norm, self.final_eps = norm.weight, norm.variance_epsilon
+        head = model.lm_head
+        self.head = (head.weight_packed, head.weight_scale, head.weight_zero_point)
+        dev, b = self.device, batch
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        nqkv = (self.hq + 2 * self.hk) * self.hd
+        # static buffers of the step (a captured graph reads and writes these addresses)
+        self.h = [torch.empty(b, self.hidden, **bf) for _ in range(2)]
+        self.xn = torch.empty(b, self.hidden, **bf)
+        self.qkv_out = torch.empty(b, nqkv, **bf)
+        self.q_rot = torch.empty(b, self.hq, 1, self.hd, **bf)
+        self.gu = torch.empty(b, 2 * self.inter, **bf)
+        self.act = torch.empty(b, self.inter, **bf)
+        self.positions = torch.arange(max_len, device=dev)
+        wsb = max(kernels.linear_workspace_bytes(b, k, n) for k, n in (
+            (self.hidden, nqkv), (self.hq * self.hd, self.hidden), (self.hidden, 2 * self.inter),
+            (self.inter, self.hidden), (self.hidden, self.head[0].shape[0])))
+        self.ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
+
+    def _lin(self, x, w, out, residual=None):
+        m, k = x.shape
+        n = w[0].shape[0]
+        ws, wsb = self.ws.data_ptr(), self.ws.numel()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        if residual is None:
+            _lib.call("rw4_linear_ws", x.data_ptr(), m, k, w[0].data_ptr(), w[1].data_ptr(),
+                      w[2].data_ptr(), n, 64, out.data_ptr(), 0, ws, wsb, stream)
+        else:
+            _lib.call("rw4_linear_residual_ws", x.data_ptr(), m, k, w[0].data_ptr(),
+                      w[1].data_ptr(), w[2].data_ptr(), n, 64, residual.data_ptr(),
+                      out.data_ptr(), ws, wsb, stream)
+        return out
+
+    def _norm(self, x, weight, eps, out):
+        _lib.call("rw4_rmsnorm", x.data_ptr(), weight.data_ptr(), x.shape[0], x.shape[1],
+                  float(eps), out.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
+        return out
+
+    @torch.no_grad()
+    def _step(self):
+        model, b = self.model, self.batch
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        inner = model.model
+        h = inner.embed_tokens(self.ids).view(b, self.hidden)
+        if h.dtype != torch.bfloat16:
+            h = h.to(torch.bfloat16)
+        cur = self.h[0]
+        cur.copy_(h)
+        pos = self.pos
+        cos, sin = inner.rotary_emb(cur.view(b, 1, self.hidden), pos.view(1, 1).expand(b, 1))
+        cos = cos.reshape(b, self.hd).to(torch.bfloat16).contiguous()
+        sin = sin.reshape(b, self.hd).to(torch.bfloat16).contiguous()
+        mask = (self.positions <= pos).view(1, 1, 1, -1)
+        nq, nk = self.hq * self.hd, self.hk * self.hd
+        qkv = self.qkv_out
+        other = self.h[1]
+        for i, w in enumerate(self.layers):
+            layer = self.cache.layers[i]
+            self._lin(self._norm(cur, w.ln1, w.eps1, self.xn), w.qkv, qkv)
+            _lib.call("rw4_rope_kv", qkv.data_ptr(), qkv[:, nq:].data_ptr(),
+                      qkv[:, nq + nk:].data_ptr(), qkv.shape[1], b, self.hq, self.hk, self.hd,
+                      cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), layer.keys.shape[2],
+                      self.q_rot.data_ptr(), layer.keys.data_ptr(), layer.values.data_ptr(),
+                      stream)
+            attn = torch.nn.functional.scaled_dot_product_attention(
+                self.q_rot, layer.keys, layer.values, attn_mask=mask,
+                scale=self.hd ** -0.5, enable_gqa=True)
+            # residual stream: each add writes the other buffer (no in-place update)
+            self._lin(attn.reshape(b, nq), w.o, other, residual=cur)
+            cur, other = other, cur
+            self._lin(self._norm(cur, w.ln2, w.eps2, self.xn), w.gate_up, self.gu)
+            _lib.call("rw4_silu_mul", self.gu.data_ptr(), b, self.inter, self.act.data_ptr(),
+                      stream)
+            self._lin(self.act, w.down, other, residual=cur)
+            cur, other = other, cur
+            layer.cumulative_length.add_(1)
+        logits = kernels.linear(self._norm(cur, self.final_norm, self.final_eps, self.xn),
+                                *self.head)
+        self.logits = logits
+        nxt_tok = logits.argmax(-1, keepdim=True)
+        self.ids.copy_(nxt_tok)
+        self.pos.add_(1)
+        return nxt_tok

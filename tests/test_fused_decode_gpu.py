@@ -1,0 +1,106 @@
+"""The fused decode step (``rocketllm_b200.fused_decode``: eight launches per Llama layer) against
+the module-by-module step (``GraphedDecoder``: transformers' modules around the RW4 GEMVs) and
+against the reference's own CPU decode of the TinyLlama configuration.
+
+Both steps run the same arithmetic in the same bf16 rounding sequence, but not bit for bit: the
+concatenated q|k|v and gate|up weights may split K differently from the separate projections, and
+attention reads the static cache through SDPA's grouped-query path instead of copied keys and
+values.  So, with the module path's tokens fed back to both (teacher forcing), every step's logits
+must agree within the linear tests' bf16 tolerance scaled to the logits, and the greedy choice must
+agree wherever the module path's top-1 margin is at least 4e-2.
+"""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from rocketllm_b200 import kernels
+from rocketllm_b200.decode import GraphedDecoder
+from rocketllm_b200.engine import AutoModel
+from rocketllm_b200.fused_decode import FusedDecoder, fusable
+from rocketllm_b200.quant.convert import save_rw4_checkpoint
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def checkpoint(tmp_path_factory):
+    from transformers import LlamaConfig, LlamaForCausalLM
+    cfg = LlamaConfig(hidden_size=512, intermediate_size=1536, num_hidden_layers=4,
+                      num_attention_heads=8, num_key_value_heads=2, vocab_size=2048,
+                      max_position_embeddings=1024, tie_word_embeddings=False)
+    torch.manual_seed(0)
+    model = LlamaForCausalLM(cfg)
+    with torch.no_grad():
+        for n, p in model.named_parameters():
+            p.copy_(torch.ones_like(p) if "norm" in n else torch.randn_like(p) * 0.02)
+    return save_rw4_checkpoint(model, str(tmp_path_factory.mktemp("rw4")), device="cuda")
+
+
+def forced_steps(dec, prompt, tokens):
+    """Logits of each decode step with ``tokens`` fed back (the first comes from the prefill)."""
+    out = []
+    dec.prefill(prompt)
+    for t in tokens[:-1]:
+        dec.ids.copy_(t.view(-1, 1))
+        dec.step()
+        out.append(dec.logits.float().clone())
+    return torch.stack(out)
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_fused_step_matches_module_step(checkpoint, batch):
+    model = AutoModel.from_pretrained(checkpoint).model
+    assert fusable(model)
+    g = torch.Generator().manual_seed(batch)
+    prompt = torch.randint(0, 2048, (batch, 37), generator=g).cuda()
+    ref_dec = GraphedDecoder(model, batch, 37 + 24 + 8)
+    want = ref_dec.generate(prompt, 24)                      # module path, greedy
+    ref = forced_steps(GraphedDecoder(model, batch, 37 + 24 + 8), prompt, want.T)
+    fused = forced_steps(FusedDecoder(model, batch, 37 + 24 + 8), prompt, want.T)
+    assert kernels.device_status() == 0
+    scale = float(ref.abs().max())
+    err = float((fused - ref).abs().max())
+    print(f"batch {batch}: max |fused - modules| = {err:.4g} (logits up to {scale:.3g})")
+    assert err <= 2e-2 * max(1.0, scale)
+    top2 = ref.topk(2, dim=-1).values
+    clear = (top2[..., 0] - top2[..., 1]) >= 4e-2
+    assert torch.equal(fused.argmax(-1)[clear], ref.argmax(-1)[clear])
+    # free-running: the fused decoder's greedy tokens equal the module path's up to a near-tie
+    got = FusedDecoder(model, batch, 37 + 24 + 8).generate(prompt, 24)
+    for b in range(batch):
+        diff = (got[b] != want[b]).nonzero()
+        if diff.numel():
+            j = int(diff[0, 0])
+            assert j > 0 and float(top2[j - 1, b, 0] - top2[j - 1, b, 1]) < 4e-2
+
+
+def test_fused_step_on_the_reference_configuration():
+    """TinyLlama RW4: the fused step, fed the reference's tokens, stays within
+    the same 1.5x of the reference's own bf16 distance from its fp32 run as the module path."""
+    import tempfile
+
+    from rocketllm_b200.synthetic import TINYLLAMA, write_rw4_llama
+    golden = dict(np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden",
+                                       "reference_tinyllama.npz")))
+
+    def q(w):
+        p, s, z, _ = kernels.quantize(w.cuda(), 64)
+        return p.cpu(), s.cpu(), z.cpu()
+
+    with tempfile.TemporaryDirectory() as tmp:
+        write_rw4_llama(tmp, TINYLLAMA, q)
+        model = AutoModel.from_pretrained(tmp).model
+    prompt = torch.from_numpy(golden["prompt"]).cuda()
+    toks = torch.from_numpy(golden["tokens"]).cuda().view(-1, 1)
+    dec = FusedDecoder(model, 1, 128 + 32 + 8)
+    scores = forced_steps(dec, prompt, toks)[:, 0].cpu().numpy()     # steps 1..31
+    ids = golden["top_ids"].astype(np.int64)[1:]
+    err_top = float(np.abs(np.take_along_axis(scores, ids, 1) - golden["top_values"][1:]).max())
+    err_last = float(np.abs(scores[-1] - golden["last_scores"]).max())
+    floor_top = float(np.abs(golden["bf16_top_values"] - golden["top_values"]).max())
+    floor_last = float(np.abs(golden["bf16_last_scores"] - golden["last_scores"]).max())
+    print(f"fused step vs the reference's fp32 run: top-64 {err_top:.4g} (bf16 floor "
+          f"{floor_top:.4g}), last {err_last:.4g} (floor {floor_last:.4g})")
+    assert err_top <= 1.5 * floor_top and err_last <= 1.5 * floor_last
