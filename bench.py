@@ -506,14 +506,38 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
     from rocketllm_b200.engine import RocketModel
     from rocketllm_b200.synthetic import build_rw4_causal_lm
 
+    from rocketllm_b200.fused_decode import FusedDecoder, fusable
+
     cfg = LlamaConfig(**LLAMA_8B)
     model = build_rw4_causal_lm(cfg, device=device, seed=0)
+    step_cls = FusedDecoder if fusable(model) else GraphedDecoder
     out = {"model": "Llama-3.1-8B architecture, RW4 group 64 (random init N(0,0.02))",
-           "prompt_tokens": prompt, "greedy": True}
+           "prompt_tokens": prompt, "greedy": True,
+           "resident_step": "fused (rocketllm_b200.fused_decode), CUDA graph"
+           if step_cls is FusedDecoder else "transformers modules, CUDA graph"}
     gen = torch.Generator().manual_seed(1)
+    if step_cls is FusedDecoder:
+        # the module-by-module graphed step, for comparison (batch 1, 64 tokens)
+        ids = torch.randint(0, cfg.vocab_size, (1, prompt), generator=gen).to(device)
+        dec = GraphedDecoder(model, 1, prompt + 64 + 8, device=device)
+        dec.prefill(ids)
+        dec.capture()
+        for _ in range(3):
+            dec.step()
+        a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(64):
+            dec.step()
+        c.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(c) / 64
+        out["resident_b1_modules"] = {"tok_s": round(1000.0 / ms, 1), "ms_per_token": round(ms, 4),
+                                      "decode_tokens": 64}
+        del dec
+        torch.cuda.empty_cache()
     for b in batches:
         ids = torch.randint(0, cfg.vocab_size, (b, prompt), generator=gen).to(device)
-        dec = GraphedDecoder(model, b, prompt + new_tokens + 8, device=device)  # + 3 warm-up steps
+        dec = step_cls(model, b, prompt + new_tokens + 8, device=device)  # + 3 warm-up steps
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
@@ -653,7 +677,9 @@ def tinyllama_bench(device, with_cpu, new_tokens=32):
     timed as the reference's harness times decode -- logits-processor marks around ``generate``
     (``tests/bench_streaming.py:474-502``) -- and as the CUDA-graphed step.  CPU (rank 0, one GPU):
     the port of the reference's path (``oracle/cpu_decode.py``: the reference codec's fp32 weights
-    in transformers' Llama, every layer resident) on all of this host's cores.  Each run's greedy
+    in transformers' Llama, every layer resident) on all of this host's cores.  The GPU figures:
+    the fused decode step in a CUDA graph, the public ``generate()`` call as a whole (it takes
+    that step), and transformers' own loop over the modules (logits-processor marks).  Each run's greedy
     tokens are compared with the reference's own (``tests/golden/reference_tinyllama.npz``, which
     also records the reference's decode rate where it was made)."""
     from transformers import LogitsProcessor, LogitsProcessorList
@@ -693,15 +719,27 @@ def tinyllama_bench(device, with_cpu, new_tokens=32):
         model = AutoModel.from_pretrained(path)
         ids = prompt.to(device)
         with torch.no_grad():
+            # transformers' own loop over the modules, timed as the reference's harness times it
+            # (a logits processor, which also keeps generate() off the fused path)
+            model.generate(ids, max_new_tokens=4, do_sample=False, eos_token_id=None,
+                           pad_token_id=0, logits_processor=LogitsProcessorList([Marks()]))
+            marks = Marks()
+            model.generate(ids, max_new_tokens=new_tokens, do_sample=False,
+                           logits_processor=LogitsProcessorList([marks]),
+                           eos_token_id=None, pad_token_id=0)
+            eager = (len(marks.times) - 1) / (marks.times[-1] - marks.times[0])
+            # the public generate() (fused, graphed step): whole call, prefill and capture included
             model.generate(ids, max_new_tokens=4, do_sample=False, eos_token_id=None,
                            pad_token_id=0)
-            marks = Marks()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
             seq = model.generate(ids, max_new_tokens=new_tokens, do_sample=False,
-                                 logits_processor=LogitsProcessorList([marks]),
                                  eos_token_id=None, pad_token_id=0)
+            torch.cuda.synchronize()
+            call_s = time.perf_counter() - t0
         gpu_tokens = seq[0, prompt.shape[1]:].cpu().numpy()
-        eager = (len(marks.times) - 1) / (marks.times[-1] - marks.times[0])
-        dec = GraphedDecoder(model.model, 1, prompt.shape[1] + new_tokens + 8, device=device)
+        from rocketllm_b200.fused_decode import FusedDecoder
+        dec = FusedDecoder(model.model, 1, prompt.shape[1] + new_tokens + 8, device=device)
         dec.prefill(ids)
         dec.capture()
         for _ in range(3):
@@ -714,9 +752,16 @@ def tinyllama_bench(device, with_cpu, new_tokens=32):
         torch.cuda.synchronize()
         graphed_ms = a.elapsed_time(c) / new_tokens
         del dec
-        out["gpu"] = {"tok_s": round(eager, 2), "timing": "generate(), logits-processor marks",
-                      "graphed_tok_s": round(1000.0 / graphed_ms, 1),
-                      "graphed_ms_per_token": round(graphed_ms, 4),
+        out["gpu"] = {"tok_s": round(1000.0 / graphed_ms, 1),
+                      "timing": "fused decode step in a CUDA graph (CUDA events)",
+                      "ms_per_token": round(graphed_ms, 4),
+                      "generate_call_s": round(call_s, 4),
+                      "generate_tok_s": round(new_tokens / call_s, 1),
+                      "generate_note": "the public generate(): prefill, graph capture and all "
+                                       f"{new_tokens} steps in one call",
+                      "modules_eager_tok_s": round(eager, 2),
+                      "modules_eager_timing": "transformers' loop over the modules, "
+                                              "logits-processor marks",
                       "tokens_equal_reference": agree(gpu_tokens)}
         model.close()
         del model
@@ -733,7 +778,7 @@ def tinyllama_bench(device, with_cpu, new_tokens=32):
                                "sample": f"the whole {new_tokens}-token greedy decode after the "
                                          f"128-token prompt, fp32, every layer resident"}
             del cpu_model
-            out["gpu_over_cpu_port"] = round(eager / rate, 1)
+            out["gpu_over_cpu_port"] = round(1000.0 / graphed_ms / rate, 1)
     out["reference_cpu_where_recorded"] = {
         "tok_s": round(float(golden["decode_tok_s"]), 3), "threads": int(golden["threads"]),
         "note": "the reference's own RocketModel(device='cpu', fp32) in the container that made "

@@ -515,12 +515,62 @@ class RocketModel:
         ids = args[0] if args else kwargs.get("input_ids")
         if ids is not None and ids.shape[0] == 1 and self.speculation_enabled()[0]:
             return self._speculative_generate(ids, int4, **kwargs)
+        fast = self._fused_greedy(ids, int4, kwargs)
+        if fast is not None:
+            return fast
         # a quantized context has to be handed in (transformers builds its own cache otherwise);
         # a cache the caller passed is kept
         if kwargs.get("past_key_values") is None and int4:
             kwargs["past_key_values"] = RW4KVCache(fused=True)
             kwargs.setdefault("use_cache", True)
         return self.model.generate(*args, **kwargs)
+
+    # generate() arguments the fused greedy path honours; anything else goes to transformers
+    _FUSED_KWARGS = frozenset(("input_ids", "max_new_tokens", "do_sample", "eos_token_id",
+                               "pad_token_id", "min_new_tokens", "attention_mask", "use_cache"))
+
+    def _fused_greedy(self, ids, int4, kwargs):
+        """Greedy ``generate`` on the fused, CUDA-graphed decode step
+        (:class:`~rocketllm_b200.fused_decode.FusedDecoder`) when it applies: a resident RW4 Llama
+        model with the stock cache, greedy decoding, an explicit ``max_new_tokens`` and no
+        argument the fused path does not honour (no padding mask, logits processors, streamers,
+        dictionary outputs).  Returns the sequences as transformers does -- prompt, then the new
+        tokens, rows that produced an end-of-sequence token padded after it, and the output cut
+        where every row has ended -- or None to take transformers' loop."""
+        from .fused_decode import FusedDecoder, fusable
+        gc = self.model.generation_config
+        if ids is None or ids.dim() != 2 or self.streamer is not None or int4:
+            return None
+        if set(kwargs) - self._FUSED_KWARGS or not kwargs.get("max_new_tokens"):
+            return None
+        do_sample = kwargs.get("do_sample", getattr(gc, "do_sample", False))
+        if do_sample or getattr(gc, "num_beams", 1) not in (None, 1):
+            return None
+        mask = kwargs.get("attention_mask")
+        if mask is not None and not bool(torch.all(mask == 1)):
+            return None
+        eos = kwargs.get("eos_token_id", getattr(gc, "eos_token_id", None))
+        if eos is not None and kwargs.get("min_new_tokens"):
+            return None   # transformers masks the end token below min_new_tokens; this path does not
+        if not fusable(self.model):
+            return None
+        n = int(kwargs["max_new_tokens"])
+        ids = ids.to(self.device)
+        b, t = ids.shape
+        dec = FusedDecoder(self.model, b, t + n + 1, device=self.device, use_graph=n > 2)
+        new = dec.generate(ids, n)
+        if eos is not None:
+            eos = torch.tensor([eos] if isinstance(eos, int) else list(eos), device=self.device)
+            pad = kwargs.get("pad_token_id", getattr(gc, "pad_token_id", None))
+            pad = int(eos[0]) if pad is None else int(pad)
+            hit = torch.isin(new, eos)
+            done = hit.cumsum(1) > 0                    # at or after the first end token
+            after = done & ~hit.logical_and(hit.cumsum(1) == 1)
+            new = torch.where(after, torch.full_like(new, pad), new)
+            if bool(done[:, -1].all()):
+                last = int((~done).sum(1).max()) + 1   # every row has ended by here
+                new = new[:, :last]
+        return torch.cat([ids, new], dim=1)
 
     def _speculative_generate(self, ids, int4, max_new_tokens=None, generator=None,
                               past_key_values=None, **kwargs):

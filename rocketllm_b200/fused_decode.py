@@ -55,18 +55,30 @@ def fusable(model):
 
 def _concat_rows(mods):
     """One RW4 weight whose rows are the given modules' rows in order; each module's parameters
-    become views of it (the originals are released)."""
+    become views of it (the originals are released).  Done once: a later call finds the modules
+    already views of the same tensors and returns those."""
+    done = getattr(mods[0], "_rw4_rows_fused", None)
+    if done is not None and done[1] == tuple(id(m) for m in mods) and all(
+            getattr(m, leaf).data_ptr() == base.data_ptr() + off * base.stride(0) *
+            base.element_size()
+            for leaf, base in zip(("weight_packed", "weight_scale", "weight_zero_point"), done[0])
+            for m, off in zip(mods, done[2])):
+        return done[0]
     parts = {}
     for leaf in ("weight_packed", "weight_scale", "weight_zero_point"):
         tensors = [getattr(m, leaf) for m in mods]
         fused = torch.cat([t.detach() for t in tensors], dim=0).contiguous()
         parts[leaf] = fused
         off = 0
+        offsets = []
         for m, t in zip(mods, tensors):
             n = t.shape[0]
             m._parameters[leaf] = torch.nn.Parameter(fused[off:off + n], requires_grad=False)
+            offsets.append(off)
             off += n
-    return parts["weight_packed"], parts["weight_scale"], parts["weight_zero_point"]
+    out = (parts["weight_packed"], parts["weight_scale"], parts["weight_zero_point"])
+    mods[0]._rw4_rows_fused = (out, tuple(id(m) for m in mods), tuple(offsets))
+    return out
 
 
 class _LayerWeights:

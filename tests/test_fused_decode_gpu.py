@@ -104,3 +104,36 @@ def test_fused_step_on_the_reference_configuration():
     print(f"fused step vs the reference's fp32 run: top-64 {err_top:.4g} (bf16 floor "
           f"{floor_top:.4g}), last {err_last:.4g} (floor {floor_last:.4g})")
     assert err_top <= 1.5 * floor_top and err_last <= 1.5 * floor_last
+
+
+def test_generate_takes_the_fused_path_and_matches_transformers(checkpoint):
+    """``RocketModel.generate`` for a plain greedy call runs the fused graphed step; its tokens equal
+    transformers' own greedy loop over the same model up to the first near-tie, end tokens stop a
+    row as there (padding after it), and calls the fused path does not honour fall back."""
+    from transformers import LogitsProcessorList
+    rm = AutoModel.from_pretrained(checkpoint)
+    prompt = torch.randint(0, 2048, (2, 21), generator=torch.Generator().manual_seed(9)).cuda()
+    with torch.no_grad():
+        fast = rm.generate(prompt, max_new_tokens=20, do_sample=False, eos_token_id=None,
+                           pad_token_id=0)
+        slow = rm.model.generate(prompt, max_new_tokens=20, do_sample=False, eos_token_id=None,
+                                 pad_token_id=0, return_dict_in_generate=True, output_logits=True)
+    assert fast.shape == slow.sequences.shape and torch.equal(fast[:, :21], prompt)
+    for b in range(2):
+        diff = (fast[b] != slow.sequences[b]).nonzero()
+        if diff.numel():
+            j = int(diff[0, 0]) - 21
+            top2 = slow.logits[j][b].float().topk(2).values
+            assert float(top2[0] - top2[1]) < 4e-2, f"row {b} diverged at {j}"
+    # an end token: make the row's third generated token the end token and rerun
+    eos = int(fast[0, 23])
+    with torch.no_grad():
+        stopped = rm.generate(prompt[:1], max_new_tokens=20, do_sample=False, eos_token_id=eos,
+                              pad_token_id=0)
+    first = int((stopped[0, 21:] == eos).nonzero()[0, 0])
+    assert stopped.shape[1] == 21 + first + 1      # one row: the output ends at its end token
+    with torch.no_grad():      # not honoured by the fused path: transformers' loop runs
+        out = rm.generate(prompt, max_new_tokens=5, do_sample=False,
+                          logits_processor=LogitsProcessorList([]), eos_token_id=None,
+                          pad_token_id=0)
+    assert out.shape == (2, 26)
