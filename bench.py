@@ -494,7 +494,7 @@ def _timed_streamed_decode(streamed, vocab, gen, device, tokens):
 
 
 def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget,
-                 storage_dir=None, host_budget=None):
+                 storage_dir=None, host_budget=None, profile_window=False):
     """Greedy decode tok/s of a Llama-3.1-8B-architecture RW4 model (random init N(0, 0.02),
     every Linear incl. lm_head in RW4): resident with a CUDA-graphed step, then streamed from
     pinned host memory under a VRAM budget, then (with ``storage_dir``) from layer shards written
@@ -546,12 +546,17 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
         dec.capture()
         for _ in range(3):
             dec.step()
+        if profile_window:   # the timed steps alone, for `ncu --profile-from-start off`
+            torch.cuda.synchronize()
+            torch.cuda.cudart().cudaProfilerStart()
         a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for _ in range(new_tokens):
             dec.step()
         c.record()
         torch.cuda.synchronize()
+        if profile_window:
+            torch.cuda.cudart().cudaProfilerStop()
         ms = a.elapsed_time(c) / new_tokens
         out[f"resident_b{b}"] = {"tok_s": round(b * 1000.0 / ms, 1), "ms_per_token": round(ms, 4),
                                  "prefill_ms": round(t0.elapsed_time(t1), 2),
@@ -1285,6 +1290,9 @@ def main():
     ap.add_argument("--decode-only", action="store_true",
                     help="only the model decode section (one JSON line)")
     ap.add_argument("--decode-batches", default="1,16")
+    ap.add_argument("--profile-window", action="store_true",
+                    help="with --decode-only: bracket each batch's timed resident steps with "
+                         "cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--storage-dir", default=None,
                     help="with --decode-only: also write the model as layer shards here and "
                          "decode from them with --host-budget-gb of layer blobs in host memory")
@@ -1340,8 +1348,8 @@ def main():
         print(json.dumps(decode_bench(
             device, args.decode_prompt, args.decode_tokens, batches, args.stream_tokens,
             int(4e9), storage_dir=args.storage_dir,
-            host_budget=int(args.host_budget_gb * 1e9) if args.storage_dir else None)),
-            flush=True)
+            host_budget=int(args.host_budget_gb * 1e9) if args.storage_dir else None,
+            profile_window=args.profile_window)), flush=True)
         return 0
     if args.tinyllama_only:
         device = torch.device("cuda", 0)

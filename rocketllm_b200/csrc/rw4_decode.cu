@@ -14,7 +14,10 @@
 //                      (the product rounded to bf16 first, then the sum), as a decoder layer's
 //                      `hidden_states = residual + self_attn(...)` / `+ mlp(...)`.
 // All are memory-bound and tiny at decode batch sizes; their point is the launch count (about 1,600
-// small kernels per Llama-8B token through the modules, 8 per layer here).
+// small kernels per Llama-8B token through the modules, 8 per layer here).  They are launched with
+// programmatic dependent launch: each waits for the kernel before it (griddepcontrol.wait) before it
+// touches memory, then lets the next one launch, so the following GEMV streams its first weight
+// stages while they run.
 #include "rw4_common.cuh"
 
 namespace rw4 {
@@ -34,12 +37,41 @@ using rw4::fail;
 
 __device__ __forceinline__ float bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
 
+// Start of every kernel here: wait for the previous grid's writes, then release the next grid.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+bool pdl_on() {
+  static const bool off = getenv("RW4_NO_PDL") != nullptr;
+  return !off;
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, cudaStream_t s, const char* what,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_on() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+  if (err != cudaSuccess) return rw4::cuda_status(err, what);
+  return rw4::launch_status(what);
+}
+
 constexpr int kNormThreads = 256;
 
 // One CTA per row.
 __global__ void __launch_bounds__(kNormThreads)
     rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w,
                    int H, float eps, __nv_bfloat16* __restrict__ y) {
+  pdl_enter();
   const __nv_bfloat16* xr = x + (int64_t)blockIdx.x * H;
   __nv_bfloat16* yr = y + (int64_t)blockIdx.x * H;
   float ss = 0.f;
@@ -73,6 +105,7 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ q, const __nv_b
                                int64_t T, __nv_bfloat16* __restrict__ q_out,
                                __nv_bfloat16* __restrict__ k_cache,
                                __nv_bfloat16* __restrict__ v_cache) {
+  pdl_enter();
   const int half = D / 2;
   const int64_t total = (int64_t)rows * (Hq + Hk) * half;
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -110,6 +143,7 @@ __global__ void rope_kv_kernel(const __nv_bfloat16* __restrict__ q, const __nv_b
 // out[r, i] = bf16(bf16(silu(g)) * u) with g = gu[r, i], u = gu[r, I + i].
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int rows, int I,
                                 __nv_bfloat16* __restrict__ out) {
+  pdl_enter();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)rows * I) return;
   const int64_t r = i / I, c = i % I;
@@ -135,10 +169,11 @@ extern "C" int rw4_rmsnorm(const void* x, const void* weight, int64_t rows, int6
   if (rows == 0) return RW4_OK;
   if (!x || !weight || !y) return fail(RW4_EINVAL, "rw4_rmsnorm: null pointer");
   if (rows > 65535) return fail(RW4_EINVAL, "rw4_rmsnorm: more than 65535 rows");
-  rmsnorm_kernel<<<(unsigned)rows, kNormThreads, 0, rw4::as_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight), (int)H,
-      eps, static_cast<__nv_bfloat16*>(y));
-  return rw4::launch_status("rw4_rmsnorm launch");
+  return launch_pdl(rmsnorm_kernel, dim3((unsigned)rows), dim3(kNormThreads),
+                    rw4::as_stream(stream), "rw4_rmsnorm launch",
+                    static_cast<const __nv_bfloat16*>(x),
+                    static_cast<const __nv_bfloat16*>(weight), (int)H, eps,
+                    static_cast<__nv_bfloat16*>(y));
 }
 
 extern "C" int rw4_rope_kv(const void* q, const void* k, const void* v, int64_t ld, int32_t rows,
@@ -151,23 +186,24 @@ extern "C" int rw4_rope_kv(const void* q, const void* k, const void* v, int64_t 
   if (!q || !k || !v || !cos_bf16 || !sin_bf16 || !pos || !q_out || !k_cache || !v_cache)
     return fail(RW4_EINVAL, "rw4_rope_kv: null pointer");
   const int64_t n = (int64_t)rows * (heads + kv_heads) * (head_dim / 2);
-  rope_kv_kernel<<<blocks(n, 256), 256, 0, rw4::as_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(q), static_cast<const __nv_bfloat16*>(k),
-      static_cast<const __nv_bfloat16*>(v), ld, rows, heads, kv_heads, head_dim,
-      static_cast<const __nv_bfloat16*>(cos_bf16), static_cast<const __nv_bfloat16*>(sin_bf16),
-      pos, cache_len, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
-      static_cast<__nv_bfloat16*>(v_cache));
-  return rw4::launch_status("rw4_rope_kv launch");
+  return launch_pdl(rope_kv_kernel, dim3(blocks(n, 256)), dim3(256), rw4::as_stream(stream),
+                    "rw4_rope_kv launch", static_cast<const __nv_bfloat16*>(q),
+                    static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
+                    ld, (int)rows, (int)heads, (int)kv_heads, (int)head_dim,
+                    static_cast<const __nv_bfloat16*>(cos_bf16),
+                    static_cast<const __nv_bfloat16*>(sin_bf16), pos, cache_len,
+                    static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_cache),
+                    static_cast<__nv_bfloat16*>(v_cache));
 }
 
 extern "C" int rw4_silu_mul(const void* gate_up, int64_t rows, int64_t I, void* out, void* stream) {
   if (rows < 0 || I <= 0) return fail(RW4_EINVAL, "rw4_silu_mul: bad shape");
   if (rows == 0) return RW4_OK;
   if (!gate_up || !out) return fail(RW4_EINVAL, "rw4_silu_mul: null pointer");
-  silu_mul_kernel<<<blocks(rows * I, 256), 256, 0, rw4::as_stream(stream)>>>(
-      static_cast<const __nv_bfloat16*>(gate_up), (int)rows, (int)I,
-      static_cast<__nv_bfloat16*>(out));
-  return rw4::launch_status("rw4_silu_mul launch");
+  return launch_pdl(silu_mul_kernel, dim3(blocks(rows * I, 256)), dim3(256),
+                    rw4::as_stream(stream), "rw4_silu_mul launch",
+                    static_cast<const __nv_bfloat16*>(gate_up), (int)rows, (int)I,
+                    static_cast<__nv_bfloat16*>(out));
 }
 
 extern "C" int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K,

@@ -128,6 +128,7 @@ class FusedDecoder(GraphedDecoder):
         self.gu = torch.empty(b, 2 * self.inter, **bf)
         self.act = torch.empty(b, self.inter, **bf)
         self.positions = torch.arange(max_len, device=dev)
+        self._counters = None
         wsb = max(kernels.linear_workspace_bytes(b, k, n) for k, n in (
             (self.hidden, nqkv), (self.hq * self.hd, self.hidden), (self.hidden, 2 * self.inter),
             (self.inter, self.hidden), (self.hidden, self.head[0].shape[0])))
@@ -153,6 +154,12 @@ class FusedDecoder(GraphedDecoder):
         return out
 
     @torch.no_grad()
+    def prefill(self, input_ids):
+        nxt = super().prefill(input_ids)
+        self._counters = [layer.cumulative_length for layer in self.cache.layers]
+        return nxt
+
+    @torch.no_grad()
     def _step(self):
         model, b = self.model, self.batch
         stream = torch.cuda.current_stream(self.device).cuda_stream
@@ -166,7 +173,9 @@ class FusedDecoder(GraphedDecoder):
         cos, sin = inner.rotary_emb(cur.view(b, 1, self.hidden), pos.view(1, 1).expand(b, 1))
         cos = cos.reshape(b, self.hd).to(torch.bfloat16).contiguous()
         sin = sin.reshape(b, self.hd).to(torch.bfloat16).contiguous()
-        mask = (self.positions <= pos).view(1, 1, 1, -1)
+        # one additive mask per step for every layer (0 up to the position, -inf after)
+        mask = torch.where(self.positions <= pos, 0.0, float("-inf")).to(torch.bfloat16)
+        mask = mask.view(1, 1, 1, -1)
         nq, nk = self.hq * self.hd, self.hk * self.hd
         qkv = self.qkv_out
         other = self.h[1]
@@ -189,7 +198,8 @@ class FusedDecoder(GraphedDecoder):
                       stream)
             self._lin(self.act, w.down, other, residual=cur)
             cur, other = other, cur
-            layer.cumulative_length.add_(1)
+        # the static cache's own write counters, kept in step for transformers (one launch)
+        torch._foreach_add_(self._counters, 1)
         logits = kernels.linear(self._norm(cur, self.final_norm, self.final_eps, self.xn),
                                 *self.head)
         self.logits = logits
