@@ -23,9 +23,10 @@ def main():
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
-    cfg = LlamaConfig(hidden_size=1024, intermediate_size=2816, num_hidden_layers=5,
-                      num_attention_heads=16, num_key_value_heads=4, vocab_size=4096,
-                      max_position_embeddings=256, tie_word_embeddings=False)
+    cfg = LlamaConfig(hidden_size=1024, intermediate_size=2816,
+                      num_hidden_layers=max(5, world + 1), num_attention_heads=16,
+                      num_key_value_heads=4, vocab_size=4096, max_position_embeddings=256,
+                      tie_word_embeddings=False)
     ids = torch.randint(0, cfg.vocab_size, (3, 19), generator=torch.Generator().manual_seed(5))
     ref = PipelineDecoder(build_rw4_causal_lm(cfg, device=dev, seed=0, std=0.05), device=dev,
                           local=True).generate(ids, 10)

@@ -1,4 +1,4 @@
-"""Pipeline parallelism over NCCL on 2+ GPUs (skipped with fewer): an RW4 model split layer-wise
+"""Pipeline parallelism over NCCL on 2, 4 and 8 GPUs (each case skipped with fewer): an RW4 model split layer-wise
 across the GPUs decodes exactly the tokens it decodes on one GPU."""
 import os
 import subprocess
@@ -12,12 +12,13 @@ pytestmark = pytest.mark.gpu
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                    reason="needs 2 GPUs")
-def test_pipeline_two_gpus():
+@pytest.mark.parametrize("n", [2, 4, 8])
+def test_pipeline(n):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < n:
+        pytest.skip(f"needs {n} GPUs")
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     cmd = ["timeout", "-k", "30", "240", sys.executable, "-m", "torch.distributed.run",
-           "--nnodes=1", "--nproc-per-node=2", "--master-addr", "127.0.0.1",
-           "--master-port", "29641", os.path.join(HERE, "pp_gpu_worker.py")]
+           "--nnodes=1", f"--nproc-per-node={n}", "--master-addr", "127.0.0.1",
+           "--master-port", str(29641 + n), os.path.join(HERE, "pp_gpu_worker.py")]
     res = subprocess.run(cmd, env=env, capture_output=True, text=True)
     assert res.returncode == 0 and "PP_OK" in res.stdout, res.stdout[-3000:] + res.stderr[-3000:]
