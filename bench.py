@@ -472,12 +472,13 @@ def ep_decode(args):
     return 0
 
 
-def _timed_streamed_decode(streamed, vocab, gen, device, tokens):
-    """ms per token and streamed bytes per token of ``tokens`` greedy steps at batch 1 after a
-    128-token prompt (eager steps: the streaming hooks run every token)."""
+def _timed_streamed_decode(streamed, vocab, gen, device, tokens, prompt=128, batch=1):
+    """ms per token and streamed bytes per token of ``tokens`` greedy steps at ``batch`` after a
+    ``prompt``-token prompt (eager steps: the streaming hooks run every token)."""
     from rocketllm_b200.decode import GraphedDecoder
-    ids = torch.randint(0, vocab, (1, 128), generator=gen).to(device)
-    dec = GraphedDecoder(streamed.model, 1, 128 + tokens + 8, device=device, use_graph=False)
+    ids = torch.randint(0, vocab, (batch, prompt), generator=gen).to(device)
+    dec = GraphedDecoder(streamed.model, batch, prompt + tokens + 8, device=device,
+                         use_graph=False)
     dec.prefill(ids)
     dec.step()
     torch.cuda.synchronize()
@@ -494,7 +495,8 @@ def _timed_streamed_decode(streamed, vocab, gen, device, tokens):
 
 
 def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget,
-                 storage_dir=None, host_budget=None, profile_window=False):
+                 storage_dir=None, host_budget=None, profile_window=False, stream_prompt=128,
+                 stream_batches=(1,)):
     """Greedy decode tok/s of a Llama-3.1-8B-architecture RW4 model (random init N(0, 0.02),
     every Linear incl. lm_head in RW4): resident with a CUDA-graphed step, then streamed from
     pinned host memory under a VRAM budget, then (with ``storage_dir``) from layer shards written
@@ -570,15 +572,18 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
     # streamed: the decoder layers leave HBM and stream from pinned host RAM every token
     streamed = RocketModel(model, device=device, vram_budget=vram_budget, window=2,
                            kv_cache="fp16")
-    ms, st0, st1 = _timed_streamed_decode(streamed, cfg.vocab_size, gen, device, stream_tokens)
-    nbytes = (st1["bytes"] - st0["bytes"]) / stream_tokens
-    out["streamed_b1"] = {"tok_s": round(1000.0 / ms, 2), "ms_per_token": round(ms, 3),
-                          "vram_budget_bytes": vram_budget, "window": streamed.streamer.window,
-                          "pinned_layers": streamed.streamer.pinned,
-                          "streamed_layers": streamed.streamer.streamed,
-                          "h2d_bytes_per_token": int(nbytes),
-                          "h2d_gbs": round(nbytes / (ms * 1e-3) / 1e9, 2),
-                          "decode_tokens": stream_tokens}
+    for b in stream_batches:
+        ms, st0, st1 = _timed_streamed_decode(streamed, cfg.vocab_size, gen, device,
+                                              stream_tokens, stream_prompt, b)
+        nbytes = (st1["bytes"] - st0["bytes"]) / stream_tokens
+        out[f"streamed_b{b}"] = {"tok_s": round(b * 1000.0 / ms, 2), "ms_per_token": round(ms, 3),
+                                 "vram_budget_bytes": vram_budget,
+                                 "window": streamed.streamer.window,
+                                 "pinned_layers": streamed.streamer.pinned,
+                                 "streamed_layers": streamed.streamer.streamed,
+                                 "h2d_bytes_per_token": int(nbytes),
+                                 "h2d_gbs": round(nbytes / (ms * 1e-3) / 1e9, 2),
+                                 "prompt_tokens": stream_prompt, "decode_tokens": stream_tokens}
     streamed.close()
     del streamed
     if storage_dir is not None:
@@ -611,7 +616,7 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
     return out
 
 
-def partitioned_decode(device, dist, batch=32, prompt=512, tokens=32):
+def partitioned_decode(device, dist, batch=32, prompt=512, tokens=32, profile_window=False):
     """Greedy decode of the Mixtral-8x7B architecture in RW4 (random init N(0, 0.02), router
     N(0, 0.02): near-uniform routing) at ``batch`` sequences per GPU after a ``prompt``-token prompt,
     every step a CUDA graph: one GPU holds the whole model (routed experts run by the grouped RW4
@@ -623,6 +628,7 @@ def partitioned_decode(device, dist, batch=32, prompt=512, tokens=32):
 
     from rocketllm_b200.decode import GraphedDecoder
     from rocketllm_b200.expert_parallel import enable_expert_parallel
+    from rocketllm_b200.fused_decode import FusedDecoder, fusable
     from rocketllm_b200.synthetic import build_rw4_causal_lm
 
     world = dist.get_world_size() if dist is not None else 1
@@ -636,7 +642,9 @@ def partitioned_decode(device, dist, batch=32, prompt=512, tokens=32):
                         generator=torch.Generator().manual_seed(100 + rank))
     if dist is not None:
         dist.barrier()
-    dec = GraphedDecoder(model, batch, prompt + tokens + 8, device=device)
+    fused = fusable(model)
+    dec = (FusedDecoder if fused else GraphedDecoder)(model, batch, prompt + tokens + 8,
+                                                      device=device)
     dec.prefill(ids)
     for _ in range(3):   # capture (with the exchange's collectives inside) + warm-up replays
         dec.step()
@@ -644,11 +652,15 @@ def partitioned_decode(device, dist, batch=32, prompt=512, tokens=32):
     if dist is not None:
         dist.barrier()
     a, c = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if profile_window:   # the timed steps alone, for `ncu --profile-from-start off`
+        torch.cuda.cudart().cudaProfilerStart()
     a.record()
     for _ in range(tokens):
         dec.step()
     c.record()
     torch.cuda.synchronize()
+    if profile_window:
+        torch.cuda.cudart().cudaProfilerStop()
     ms = a.elapsed_time(c) / tokens
     if dist is not None:
         t = torch.tensor([ms], dtype=torch.float64, device=device)
@@ -665,6 +677,8 @@ def partitioned_decode(device, dist, batch=32, prompt=512, tokens=32):
             "mode": "resident, grouped RW4 GEMV" if world == 1 else
                     "expert-parallel: 8/G experts per rank, fixed-capacity NCCL all-to-all out "
                     "and back per MoE layer inside the CUDA-graphed step",
+            "step": "fused attention half + the model's sparse-MoE block (rocketllm_b200."
+                    "fused_decode), CUDA graph" if fused else "transformers modules, CUDA graph",
             "n_gpus": world, "batch_per_gpu": batch, "prompt_tokens": prompt,
             "decode_tokens": tokens, "tok_s": round(world * batch * 1000.0 / ms, 1),
             "ms_per_token": round(ms, 3), "weight_bytes_per_gpu": weight_bytes,
@@ -1272,11 +1286,19 @@ def main():
     ap.add_argument("--partitioned", type=int, default=1,
                     help="1: include the Mixtral decode, resident on one GPU and expert-parallel "
                          "(NCCL all-to-all) on several")
+    ap.add_argument("--partitioned-only", action="store_true",
+                    help="only the Mixtral decode of --partitioned, one JSON line (one GPU)")
+    ap.add_argument("--partitioned-tokens", type=int, default=32)
     ap.add_argument("--tinyllama-only", action="store_true",
                     help="only the TinyLlama GPU / CPU-port decode comparison, one JSON line")
     ap.add_argument("--decode-prompt", type=int, default=2048)
     ap.add_argument("--decode-tokens", type=int, default=256)
     ap.add_argument("--stream-tokens", type=int, default=16)
+    ap.add_argument("--stream-prompt", type=int, default=128,
+                    help="prompt of the streamed decode (2048 for the streamed 8B configuration)")
+    ap.add_argument("--stream-batches", default="1",
+                    help="batch sizes of the streamed decode (1,16 for the streamed 8B "
+                         "configuration)")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="approximate CPU time of the CPU baseline leg")
     ap.add_argument("--cpu-steps", type=int, default=3)
@@ -1291,7 +1313,7 @@ def main():
                     help="only the model decode section (one JSON line)")
     ap.add_argument("--decode-batches", default="1,16")
     ap.add_argument("--profile-window", action="store_true",
-                    help="with --decode-only: bracket each batch's timed resident steps with "
+                    help="with --decode-only or --partitioned-only: bracket the timed steps with "
                          "cudaProfilerStart/Stop (for ncu --profile-from-start off)")
     ap.add_argument("--storage-dir", default=None,
                     help="with --decode-only: also write the model as layer shards here and "
@@ -1349,7 +1371,14 @@ def main():
             device, args.decode_prompt, args.decode_tokens, batches, args.stream_tokens,
             int(4e9), storage_dir=args.storage_dir,
             host_budget=int(args.host_budget_gb * 1e9) if args.storage_dir else None,
-            profile_window=args.profile_window)), flush=True)
+            profile_window=args.profile_window, stream_prompt=args.stream_prompt,
+            stream_batches=tuple(int(v) for v in args.stream_batches.split(",")))), flush=True)
+        return 0
+    if args.partitioned_only:
+        device = torch.device("cuda", 0)
+        torch.cuda.set_device(device)
+        print(json.dumps(partitioned_decode(device, None, tokens=args.partitioned_tokens,
+                                            profile_window=args.profile_window)), flush=True)
         return 0
     if args.tinyllama_only:
         device = torch.device("cuda", 0)

@@ -20,7 +20,8 @@
 //              32 (w % 4) .. +31, the two warps of a quarter split the columns) and store bf16 y.
 // The product equals a bf16 GEMM over the reference's dequantized weight up to fp32 accumulation
 // order.  CTAs sharing a weight tile are adjacent in the grid (tokens fastest), so a weight tile
-// is read from HBM about once and the activations stay in L2.
+// is read from HBM about once; the activations are loaded evict-last and stay in L2 across the
+// waves of weight tiles.
 //
 // Every TMA load is a plain per-CTA load.  Every mbarrier wait is bounded (rw4_tma.cuh); on a timeout the CTA
 // stops issuing, waits (bounded) for its own copies and MMAs, frees its TMEM and writes nothing.
@@ -233,6 +234,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- activation producer (shallow ring) ----------------
     if (lane == 0) {
       prefetch_tensormap(&tm_x);
+      // every weight-row tile streams against the same activations: keep them in L2 (evict-last)
+      // so that each wave of weight tiles finds them there
+      const uint64_t pol = policy_evict_last();
       int issued = 0;
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % S2;
@@ -241,7 +245,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         mbar_arrive_expect_tx(aready0 + 8 * s, C::kXBytes);
-        tma_load_2d(sb + C::kOffX + s * C::kXBytes, &tm_x, kb * BK, m0, aready0 + 8 * s);
+        tma_load_2d_hint(sb + C::kOffX + s * C::kXBytes, &tm_x, kb * BK, m0, aready0 + 8 * s,
+                         pol);
         issued = kb + 1;
       }
       for (int kb = max(0, issued - S2); kb < issued; ++kb)  // drain own copies

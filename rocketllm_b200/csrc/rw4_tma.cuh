@@ -120,6 +120,14 @@ __device__ __forceinline__ uint64_t policy_evict_first() {
   return p;
 }
 
+// For data many CTAs re-read over the kernel's life (an activation matrix that every weight tile
+// streams against): kept in L2 ahead of evict-first / normal lines.
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

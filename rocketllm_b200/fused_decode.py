@@ -1,5 +1,5 @@
-"""Fused decode step for resident RW4 Llama-architecture models (the decode-step op stream around
-the RW4 GEMVs, B200-first).
+"""Fused decode step for resident RW4 Llama- and Mixtral-architecture models (the decode-step op
+stream around the RW4 GEMVs, B200-first).
 
 Through the transformers modules one decode step of a Llama layer is about fifty small launches:
 RMSNorm as six elementwise kernels, q / k / v as three GEMVs, the rotary embedding as cat / neg /
@@ -23,6 +23,16 @@ parameters become views of the concatenated tensors, so nothing is duplicated an
 transformers forward (prefill, or any other use) runs on the same bytes.  The prefill itself
 runs through the modules; only decode steps take the fused path, captured in a CUDA graph by
 :class:`~rocketllm_b200.decode.GraphedDecoder`'s machinery.
+
+Mixtral-architecture models (transformers ``models/mixtral/modeling_mixtral.py``: the same
+attention and norms, a sparse-MoE block in place of the MLP) take the same attention half; the
+MoE half is the model's own block -- its top-k router, then its routed-experts module, which is
+the RW4 grouped path (``rw4_experts_forward``) or, after ``enable_expert_parallel``, the
+expert-parallel exchange -- followed by the residual add:
+
+    rw4_rmsnorm                       post_attention_layernorm
+    mlp (router + routed experts)     MixtralSparseMoeBlock, unchanged
+    residual add                      ``residual + hidden_states``
 """
 import torch
 
@@ -31,25 +41,39 @@ from .decode import GraphedDecoder
 from .quant.modules import RW4Linear
 
 
+def _rw4(mods):
+    return all(isinstance(x, RW4Linear) and x.bias is None for x in mods)
+
+
 def fusable(model):
-    """Whether ``model`` is a resident RW4 Llama-architecture ``*ForCausalLM`` the fused step
-    covers: every projection an ``RW4Linear`` without bias, no sliding window, no streaming hooks,
-    all on one CUDA device."""
+    """Whether ``model`` is a resident RW4 ``*ForCausalLM`` the fused step covers: a Llama
+    architecture whose projections are all ``RW4Linear`` without bias, or a Mixtral architecture
+    whose attention projections are and whose routed experts are RW4 (or expert-parallel over
+    them); no sliding window, no streaming hooks, all on one CUDA device."""
     cfg = model.config
-    if getattr(cfg, "model_type", None) != "llama" or getattr(cfg, "sliding_window", None):
+    kind = getattr(cfg, "model_type", None)
+    if kind not in ("llama", "mixtral") or getattr(cfg, "sliding_window", None):
         return False
     inner = getattr(model, "model", None)
     if inner is None or not isinstance(getattr(model, "lm_head", None), RW4Linear):
         return False
     for layer in inner.layers:
         a, m = layer.self_attn, layer.mlp
-        mods = (a.q_proj, a.k_proj, a.v_proj, a.o_proj, m.gate_proj, m.up_proj, m.down_proj)
-        if not all(isinstance(x, RW4Linear) and x.bias is None for x in mods):
+        if not _rw4((a.q_proj, a.k_proj, a.v_proj, a.o_proj)):
             return False
         if layer._forward_pre_hooks or layer._forward_hooks:
             return False
-        if getattr(m, "act_fn", None) is None or cfg.hidden_act not in ("silu", "swish"):
-            return False
+        if kind == "llama":
+            if not _rw4((m.gate_proj, m.up_proj, m.down_proj)):
+                return False
+            if getattr(m, "act_fn", None) is None or cfg.hidden_act not in ("silu", "swish"):
+                return False
+        else:
+            experts = getattr(m, "experts", None)
+            if getattr(m, "gate", None) is None or not getattr(experts, "rw4", False):
+                return False
+            if m._forward_pre_hooks or m._forward_hooks or experts._forward_pre_hooks:
+                return False
     return all(p.is_cuda for p in model.parameters())
 
 
@@ -82,17 +106,19 @@ def _concat_rows(mods):
 
 
 class _LayerWeights:
-    __slots__ = ("ln1", "ln2", "qkv", "o", "gate_up", "down", "eps1", "eps2")
+    __slots__ = ("ln1", "ln2", "qkv", "o", "gate_up", "down", "eps1", "eps2", "moe")
 
 
 class FusedDecoder(GraphedDecoder):
-    """Greedy decode of a resident RW4 Llama model with the fused step (see the module docstring);
-    same interface as :class:`~rocketllm_b200.decode.GraphedDecoder` (``prefill``, ``step``,
-    ``generate``, ``capture``).  Raises ``ValueError`` for a model :func:`fusable` rejects."""
+    """Greedy decode of a resident RW4 Llama or Mixtral model with the fused step (see the module
+    docstring); same interface as :class:`~rocketllm_b200.decode.GraphedDecoder` (``prefill``,
+    ``step``, ``generate``, ``capture``).  Raises ``ValueError`` for a model :func:`fusable`
+    rejects."""
 
     def __init__(self, model, batch, max_len, device="cuda", use_graph=True):
         if not fusable(model):
-            raise ValueError("the fused decode step covers resident RW4 Llama-architecture models")
+            raise ValueError("the fused decode step covers resident RW4 Llama- and "
+                             "Mixtral-architecture models")
         super().__init__(model, batch, max_len, device=device, use_graph=use_graph)
         cfg = model.config
         self.hq = cfg.num_attention_heads
@@ -100,6 +126,7 @@ class FusedDecoder(GraphedDecoder):
         self.hd = getattr(cfg, "head_dim", None) or cfg.hidden_size // self.hq
         self.hidden = cfg.hidden_size
         self.inter = cfg.intermediate_size
+        moe = cfg.model_type == "mixtral"
         self.layers = []
         for layer in model.model.layers:
             a, m = layer.self_attn, layer.mlp
@@ -109,9 +136,11 @@ class FusedDecoder(GraphedDecoder):
             w.eps2 = layer.post_attention_layernorm.variance_epsilon
             w.qkv = _concat_rows([a.q_proj, a.k_proj, a.v_proj])
             w.o = (a.o_proj.weight_packed, a.o_proj.weight_scale, a.o_proj.weight_zero_point)
-            w.gate_up = _concat_rows([m.gate_proj, m.up_proj])
-            w.down = (m.down_proj.weight_packed, m.down_proj.weight_scale,
-                      m.down_proj.weight_zero_point)
+            w.moe = m if moe else None
+            if not moe:
+                w.gate_up = _concat_rows([m.gate_proj, m.up_proj])
+                w.down = (m.down_proj.weight_packed, m.down_proj.weight_scale,
+                          m.down_proj.weight_zero_point)
             self.layers.append(w)
         norm = model.model.norm
         self.final_norm, self.final_eps = norm.weight, norm.variance_epsilon
@@ -125,13 +154,15 @@ class FusedDecoder(GraphedDecoder):
         self.xn = torch.empty(b, self.hidden, **bf)
         self.qkv_out = torch.empty(b, nqkv, **bf)
         self.q_rot = torch.empty(b, self.hq, 1, self.hd, **bf)
-        self.gu = torch.empty(b, 2 * self.inter, **bf)
-        self.act = torch.empty(b, self.inter, **bf)
+        shapes = [(self.hidden, nqkv), (self.hq * self.hd, self.hidden),
+                  (self.hidden, self.head[0].shape[0])]
+        if not moe:
+            self.gu = torch.empty(b, 2 * self.inter, **bf)
+            self.act = torch.empty(b, self.inter, **bf)
+            shapes += [(self.hidden, 2 * self.inter), (self.inter, self.hidden)]
         self.positions = torch.arange(max_len, device=dev)
         self._counters = None
-        wsb = max(kernels.linear_workspace_bytes(b, k, n) for k, n in (
-            (self.hidden, nqkv), (self.hq * self.hd, self.hidden), (self.hidden, 2 * self.inter),
-            (self.inter, self.hidden), (self.hidden, self.head[0].shape[0])))
+        wsb = max(kernels.linear_workspace_bytes(b, k, n) for k, n in shapes)
         self.ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
 
     def _lin(self, x, w, out, residual=None):
@@ -193,10 +224,16 @@ class FusedDecoder(GraphedDecoder):
             # residual stream: each add writes the other buffer (no in-place update)
             self._lin(attn.reshape(b, nq), w.o, other, residual=cur)
             cur, other = other, cur
-            self._lin(self._norm(cur, w.ln2, w.eps2, self.xn), w.gate_up, self.gu)
-            _lib.call("rw4_silu_mul", self.gu.data_ptr(), b, self.inter, self.act.data_ptr(),
-                      stream)
-            self._lin(self.act, w.down, other, residual=cur)
+            xn = self._norm(cur, w.ln2, w.eps2, self.xn)
+            if w.moe is not None:
+                # the model's own sparse-MoE block (router + routed experts), then the residual
+                y = w.moe(xn.view(b, 1, self.hidden)).view(b, self.hidden)
+                torch.add(cur, y, out=other)
+            else:
+                self._lin(xn, w.gate_up, self.gu)
+                _lib.call("rw4_silu_mul", self.gu.data_ptr(), b, self.inter,
+                          self.act.data_ptr(), stream)
+                self._lin(self.act, w.down, other, residual=cur)
             cur, other = other, cur
         # the static cache's own write counters, kept in step for transformers (one launch)
         torch._foreach_add_(self._counters, 1)

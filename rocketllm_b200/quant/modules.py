@@ -103,9 +103,9 @@ def rw4_experts_forward(self, hidden_states, top_k_index, top_k_weights):
         w = w.float()
     n_exp = getattr(self, "num_experts", None) or self.gate_up_proj_packed.shape[0]
     perm, inv, offsets = kernels.moe_permute(idx, n_exp)
-    # rows per expert: a token's top-k experts are distinct, so one token gives each at most one
-    # row; otherwise bound by all of the token-slot pairs (known on the host: no device read)
-    rows = 1 if t == 1 else t * k
+    # rows per expert: a token's top-k experts are distinct, so every expert gets at most one row
+    # per token (known on the host: no device read)
+    rows = t
     xp = kernels.moe_gather(x, perm, k)
     act = kernels.moe_grouped(xp, offsets, _expert_triples(self, "gate_up_proj"), act=1,
                               max_rows=rows)

@@ -1,6 +1,7 @@
-"""The fused decode step (``rocketllm_b200.fused_decode``: eight launches per Llama layer) against
-the module-by-module step (``GraphedDecoder``: transformers' modules around the RW4 GEMVs) and
-against the reference's own CPU decode of the TinyLlama configuration.
+"""The fused decode step (``rocketllm_b200.fused_decode``: eight launches per Llama layer; the same
+attention half before the model's own sparse-MoE block on a Mixtral) against the module-by-module
+step (``GraphedDecoder``: transformers' modules around the RW4 GEMVs) and against the reference's
+own CPU decode of the TinyLlama configuration.
 
 Both steps run the same arithmetic in the same bf16 rounding sequence, but not bit for bit: the
 concatenated q|k|v and gate|up weights may split K differently from the separate projections, and
@@ -74,6 +75,41 @@ def test_fused_step_matches_module_step(checkpoint, batch):
         if diff.numel():
             j = int(diff[0, 0])
             assert j > 0 and float(top2[j - 1, b, 0] - top2[j - 1, b, 1]) < 4e-2
+
+
+@pytest.mark.parametrize("batch", [1, 4])
+def test_fused_step_on_a_mixtral_model(batch):
+    """A Mixtral-architecture RW4 model: the fused attention half plus the model's own sparse-MoE
+    block against the module step, teacher-forced, with the Llama test's bounds.  The router is
+    drawn with std 0.5 so that its top-2 margins are wide: the attention half's rounding must not
+    flip an expert choice (a flip at a near-tie is legitimate, but it is not what is tested)."""
+    from transformers import MixtralConfig
+
+    from rocketllm_b200.synthetic import build_rw4_causal_lm
+    cfg = MixtralConfig(hidden_size=512, intermediate_size=1024, num_hidden_layers=3,
+                        num_attention_heads=8, num_key_value_heads=2, vocab_size=2048,
+                        num_local_experts=4, num_experts_per_tok=2, max_position_embeddings=256,
+                        tie_word_embeddings=False)
+    model = build_rw4_causal_lm(cfg, device="cuda", seed=4)
+    with torch.no_grad():
+        g = torch.Generator(device="cuda").manual_seed(9)
+        for layer in model.model.layers:
+            r = layer.mlp.gate.weight
+            r.copy_(torch.randn(r.shape, device="cuda", generator=g) * 0.5)
+    assert fusable(model)
+    prompt = torch.randint(0, 2048, (batch, 29), generator=torch.Generator().manual_seed(batch))
+    prompt = prompt.cuda()
+    want = GraphedDecoder(model, batch, 29 + 16 + 8).generate(prompt, 16)
+    ref = forced_steps(GraphedDecoder(model, batch, 29 + 16 + 8), prompt, want.T)
+    fused = forced_steps(FusedDecoder(model, batch, 29 + 16 + 8), prompt, want.T)
+    assert kernels.device_status() == 0
+    scale = float(ref.abs().max())
+    err = float((fused - ref).abs().max())
+    print(f"mixtral batch {batch}: max |fused - modules| = {err:.4g} (logits up to {scale:.3g})")
+    assert err <= 2e-2 * max(1.0, scale)
+    top2 = ref.topk(2, dim=-1).values
+    clear = (top2[..., 0] - top2[..., 1]) >= 4e-2
+    assert torch.equal(fused.argmax(-1)[clear], ref.argmax(-1)[clear])
 
 
 def test_fused_step_on_the_reference_configuration():
