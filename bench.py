@@ -1182,13 +1182,14 @@ def spec_decode(args):
     """Speculative decoding on the streamed Llama-3-8B architecture (the decode bench's 4 GB
     budget: 19 layers pinned, 13 streamed every pass).  A one-token step streams the 13 layers; a
     verify pass streams them once for k+1 positions (RW4 GEMV at M = k+1).  The draft replays the
-    target's greedy continuation; the acceptance rate is measured, not assumed -- with random
-    weights over a 128K vocabulary the top-2 logit margins sit below the rounding difference
-    between a one-row and a (k+1)-row pass, so most proposals are rejected and the end-to-end
-    tokens/s is that of a poor draft.  What the lines establish is the exchange rate:
-    ``verify_pass_ms`` (k+1 positions, measured in the speculative run) against ``step_ms`` (one
-    position); ``tok_s_per_accepted_pass`` = (k+1) / verify_pass_ms is what each fully accepted
-    pass delivers.  One JSON line per lookahead, each after its own warm-up run."""
+    target's greedy continuation (the plain run's tokens); the acceptance rate is measured, not
+    assumed.  Both runs start from the same prefilled cache (the prompt but its last token, one
+    pass), and a (k+1)-position pass gives each position the bits of a one-position step (RW4
+    rows do not depend on the batch, SDPA's rows do not depend on the query count), so the
+    replayed tokens are the target's own choices.  ``verify_pass_ms`` (k+1 positions) against
+    ``step_ms`` (one position) is the exchange rate; ``tok_s_per_accepted_pass`` = (k+1) /
+    verify_pass_ms is what each fully accepted pass delivers.  The timed regions exclude the
+    prefill.  One JSON line per lookahead, each after its own warm-up run."""
     from transformers import DynamicCache, LlamaConfig
 
     from rocketllm_b200.engine import RocketModel
@@ -1203,25 +1204,32 @@ def spec_decode(args):
     ids = torch.randint(0, cfg.vocab_size, (1, 128),
                         generator=torch.Generator().manual_seed(0)).to(device)
 
-    def plain():
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def prefilled():
+        """A cache holding the prompt but its last token, made by one pass (the same pass for the
+        plain and the speculative runs, so their caches hold the same bits)."""
         cache = DynamicCache()
         with torch.inference_mode():
-            tok = target(input_ids=ids, past_key_values=cache, use_cache=True).logits[:, -1:] \
-                .argmax(-1)
-            out = [tok]
-            for _ in range(n - 1):
+            target(input_ids=ids[:, :-1], past_key_values=cache, use_cache=True)
+        return cache
+
+    def plain():
+        cache = prefilled()
+        torch.cuda.synchronize()
+        a.record()
+        with torch.inference_mode():
+            tok, out = ids[:, -1:], []
+            for _ in range(n):
                 tok = target(input_ids=tok, past_key_values=cache, use_cache=True) \
                     .logits[:, -1:].argmax(-1)
                 out.append(tok)
-        return torch.cat(out, dim=1)[0]
+        b.record()
+        torch.cuda.synchronize()
+        return torch.cat(out, dim=1)[0], a.elapsed_time(b)
 
     plain()                                   # warm-up (first-touch of every slot and stream)
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    cont = plain()
-    b.record()
-    torch.cuda.synchronize()
-    plain_ms = a.elapsed_time(b)
+    cont, plain_ms = plain()
     base = {"spec_decode": "llama3-8b architecture, RW4, streamed (4 GB budget)",
             "prompt_tokens": 128, "new_tokens": n, "draft": "replay of the target's greedy tokens"}
     print(json.dumps({**base, "lookahead": 0, "tok_s": round(n / (plain_ms * 1e-3), 2),
@@ -1246,16 +1254,18 @@ def spec_decode(args):
         # warm-up: a whole untimed run (the first speculative run of a process measured 2.3x
         # slower per pass than the same run repeated)
         SpeculativeDecoder(target, _ReplayDraft(cont, 128, cfg.vocab_size), lookahead=k,
-                           max_lookahead=k).generate(ids, n)
+                           max_lookahead=k).generate(ids, n, past_key_values=prefilled())
         dec = SpeculativeDecoder(target, _ReplayDraft(cont, 128, cfg.vocab_size), lookahead=k,
                                  max_lookahead=k)
+        cache = prefilled()
+        torch.cuda.synchronize()
         a.record()
-        out = dec.generate(ids, n)
+        out = dec.generate(ids, n, past_key_values=cache)
         b.record()
         torch.cuda.synchronize()
         ms = a.elapsed_time(b)
         st = dec.stats
-        # the first pass carries the 128-token prompt; the rest carry the k+1 candidates
+        # every pass carries the last accepted token and k proposals
         verify_ms = 1e3 * st.target_seconds / max(1, st.passes)
         print(json.dumps({**base, "lookahead": k, "tok_s": round(n / (ms * 1e-3), 2),
                           "speedup_vs_plain": round(plain_ms / ms, 2), "passes": st.passes,

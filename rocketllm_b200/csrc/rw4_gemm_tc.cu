@@ -61,7 +61,7 @@ struct Cfg {
   static constexpr int kOffBars = kOffCodes + S1 * kCodeBytes;
   // codes_full[S1], codes_empty[S1], x_full[S2], a_ready[S2], stage_empty[S2], accum
   static constexpr int kNumBars = 2 * S1 + 3 * S2 + 1;
-  static constexpr int kOffTmemSlot = kOffBars + kNumBars * 8;
+  static constexpr int kOffTmemSlot = kOffBars + kNumBars * 8;  // + 8: the dequant scratch word
   static constexpr int kDynSmem = kOffTmemSlot + 16 + 1024;
   static constexpr uint32_t kTmemCols = BN < 32 ? 32 : BN;
   // UMMA instruction descriptor, kind::f16: D f32, A/B bf16, both K-major, M = 128, N = BN.
@@ -319,6 +319,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < kKbPerCodeStage; ++j)   // 128-byte swizzle: chunk c at c ^ (r % 8)
         cw[j] = *reinterpret_cast<const uint4*>(crow + (((2 * j + h) ^ (r & 7)) << 4));
+      // The TMA refill of this slot (async proxy) must not overtake these shared-memory reads
+      // (released right after them, outputs varied from run to run at some shapes): every thread
+      // stores a value computed from all 16 words it read into a scratch word, which it cannot
+      // issue before those reads have returned, and only then is the slot released.  (A
+      // fence.proxy.async here does the same but also waits for the scale prefetch in flight.)
+      {
+        const uint32_t v = cw[0].x ^ cw[0].y ^ cw[0].z ^ cw[0].w ^ cw[1].x ^ cw[1].y ^ cw[1].z ^
+                           cw[1].w ^ cw[2].x ^ cw[2].y ^ cw[2].z ^ cw[2].w ^ cw[3].x ^ cw[3].y ^
+                           cw[3].z ^ cw[3].w;
+        asm volatile("st.shared.b32 [%0], %1;" ::"r"(sb + C::kOffTmemSlot + 8), "r"(v) : "memory");
+      }
       __syncwarp();
       if (lane == 0) mbar_arrive(cempty0 + 8 * s1);  // codes slot may be refilled
 #pragma unroll

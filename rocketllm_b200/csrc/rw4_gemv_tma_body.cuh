@@ -375,7 +375,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
         z_a[rt] = lds_half(zb + rt * 256);
         z_b[rt] = lds_half(zb + rt * 256 + 128);
       }
-      // x fragment of group (s * 8 + w) (box w / 4 of the stage), then release the slot
+      // x fragment of group (s * 8 + w) (box w / 4 of the stage)
       uint32_t b[NT][4][2];
       float xs[NT][4], c0[NT][4];
       if (XQ) {
@@ -436,8 +436,6 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
           load_x_frag(x + (int64_t)(x_row0 + min(m, Ml - 1)) * K + kofs, m < Ml, b[nt]);
         }
       }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty0 + 8 * st);
 
       if (!XP && !XQ) {
         // sums of x over the group; the code MMAs start from -128 * sum(x), which removes the
@@ -482,6 +480,12 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
             out[rt][nt][3] = fmaf(s_b[rt], acc[nt][3], fmaf(z_b[rt], xs[nt][3], out[rt][nt][3]));
         }
       }
+      // Release the slot only now: every value this thread read from it has been consumed by the
+      // MMAs and FMAs above, so its shared-memory reads are complete before the producer's TMA
+      // (async proxy) can refill the slot.  (Released right after the reads, a refill could
+      // overtake reads still in flight -- the tcgen05 GEMM's codes ring showed exactly that.)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty0 + 8 * st);
     }
   }
 

@@ -435,12 +435,11 @@ __global__ void __launch_bounds__(kWarps * 32, 1) rw4_kv_attn_kernel(const KvArg
           }
         }
       }
+      // every lane orders its generic reads of the stage before the bulk refill (async proxy)
+      fence_proxy_async_smem();
       __syncwarp();
       const int64_t next = consumed + kStages;
-      if (lane == 0 && next < nq_w) {
-        fence_proxy_async_smem();
-        issue(next);
-      }
+      if (lane == 0 && next < nq_w) issue(next);
       ++consumed;
     } else {
       // ---------------- a 64-token chunk of the bf16 window ----------------

@@ -154,3 +154,19 @@ def test_linear_deterministic(cuda):
     a = kernels.linear(x, packed, scale, zero)
     b = kernels.linear(x, packed, scale, zero)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("k,n", [(4096, 6144), (4096, 14336), (14336, 4096)])
+@pytest.mark.parametrize("m", [1, 8, 32, 127, 128])
+def test_linear_repeats_bit_for_bit(cuda, k, n, m):
+    """Forty launches on the same inputs, each compared (a host sync between launches) with the
+    first: every path's ring protocol must leave no room for a slot being refilled while its last
+    reader is still on it.  Shapes with fewer weight tiles than SMs at M = 127-128 (one token tile
+    on the tcgen05 GEMM) are where a missing proxy fence between the consumers' generic reads of
+    a codes slot and its TMA refill showed as run-to-run differences in a prefill."""
+    w = make_weight(n, k, device=cuda, seed=11)
+    x = make_activation(m, k, device=cuda, seed=12)
+    first = kernels.linear(x, *w)
+    diffs = sum(int(not torch.equal(first, kernels.linear(x, *w))) for _ in range(40))
+    assert kernels.device_status() == 0
+    assert diffs == 0, f"{diffs} of 40 launches differ from the first"
