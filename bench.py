@@ -1001,6 +1001,67 @@ def rw4_arm(args):
     return 0
 
 
+def moe_sweep(args):
+    """Routed-experts kernel timing (not the driver's line): the grouped RW4 GEMV at the
+    Mixtral-8x7B expert shapes (8 experts, gate/up 2 x 14336 x 4096 with the SwiGLU epilogue, down
+    4096 x 14336) for ``--moe-tokens-list`` tokens routed top-2 (distinct random experts per token,
+    seeded), one JSON line per (tokens, projection) with the launch's CUDA-event time over
+    ``--steps`` graphed back-to-back launches and the routed experts' weight bytes per second
+    against the measured HBM peak."""
+    from rocketllm_b200 import kernels
+    from rocketllm_b200.synthetic import make_weight
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    peak, peak_kind = measured_peak()
+    n_exp, hid, inter, top = 8, 4096, 14336, 2
+    gate_up = [make_weight(2 * inter, hid, device=device, seed=e) for e in range(n_exp)]
+    down = [make_weight(hid, inter, device=device, seed=100 + e) for e in range(n_exp)]
+
+    def nbytes(trip):
+        return sum(t.numel() * t.element_size() for t in trip)
+
+    for t in (int(v) for v in args.moe_tokens_list.split(",")):
+        g = torch.Generator(device=device).manual_seed(t)
+        x = torch.randn(t, hid, device=device, generator=g).to(torch.bfloat16)
+        idx = torch.stack([torch.randperm(n_exp, device=device, generator=g)[:top]
+                           for _ in range(t)])
+        perm, inv, off = kernels.moe_permute(idx, n_exp)
+        routed = sorted(set(idx.flatten().tolist()))
+        xp = kernels.moe_gather(x, perm, top)
+        act = kernels.moe_grouped(xp, off, gate_up, act=1, max_rows=t)
+        yp = kernels.moe_grouped(act, off, down, act=0, max_rows=t)
+        for name, weights, fn in (
+                ("gate_up", gate_up,
+                 lambda: kernels.moe_grouped(xp, off, gate_up, act=1, max_rows=t, out=act)),
+                ("down", down,
+                 lambda: kernels.moe_grouped(act, off, down, act=0, max_rows=t, out=yp))):
+            for _ in range(args.warmup):
+                fn()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                for _ in range(args.steps):
+                    fn()
+            graph.replay()
+            torch.cuda.synchronize()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            graph.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ms = a.elapsed_time(b) / args.steps
+            wb = sum(nbytes(weights[e]) for e in routed)
+            gbs = wb / (ms * 1e-3) / 1e9
+            print(json.dumps({"moe": "Mixtral-8x7B experts, RW4 group 64", "tokens": t,
+                              "top_k": top, "projection": name, "routed_experts": len(routed),
+                              "us": round(ms * 1e3, 1), "weight_gbs": round(gbs, 1),
+                              "hbm_frac": round(gbs / peak, 4), "peaks": peak_kind,
+                              "launches": args.steps}), flush=True)
+            del graph
+    assert kernels.device_status() == 0
+    return 0
+
+
 def sweep(args):
     """Kernel sweep (not the driver's line): every (K, N) x M of the isolated sweep, one JSON line
     each with the launch's CUDA-event time over ``--steps`` graphed back-to-back launches (cycling
@@ -1315,6 +1376,9 @@ def main():
     ap.add_argument("--sweep", action="store_true",
                     help="kernel sweep over the sweep shapes x --sweep-m (one JSON line each)")
     ap.add_argument("--sweep-m", default="1,4,16,64,512,2048")
+    ap.add_argument("--moe-sweep", action="store_true",
+                    help="routed-experts grouped GEMV timing at the Mixtral expert shapes")
+    ap.add_argument("--moe-tokens-list", default="1,8,32,128")
     ap.add_argument("--sweep-shapes", default="all", help="'all' or KxN[,KxN...]")
     ap.add_argument("--sweep-path", type=int, default=0,
                     help="force a kernel in --sweep: 2 tcgen05 GEMM, 3 GEMV slices (0 = the "
@@ -1367,6 +1431,8 @@ def main():
         return spec_decode(args)
     if args.sweep:
         return sweep(args)
+    if args.moe_sweep:
+        return moe_sweep(args)
     if args.ep_decode:
         return ep_decode(args)
     if args.moe_decode:
