@@ -389,10 +389,11 @@ def moe_decode(args):
         del dec
         torch.cuda.empty_cache()
     out["h2d_probe_gbs"] = round(h2d_probe(device), 2)
-    if st.experts is not None and "routing" in st.experts.stats():
-        # lifetime routing skew over the whole run (prefills included)
+    routing = st.experts.stats().get("routing") if st.experts is not None else None
+    if isinstance(routing, dict):
+        # lifetime routing skew over the whole run (prefills included; host routing only)
         out["routing"] = {k: round(v, 4) if isinstance(v, float) else v
-                          for k, v in st.experts.stats()["routing"].items()}
+                          for k, v in routing.items()}
     print(json.dumps(out), flush=True)
     streamed.close()
     return 0
@@ -608,6 +609,21 @@ def decode_bench(device, prompt, new_tokens, batches, stream_tokens, vram_budget
                              "reads_waited": s1.get("waits", 0) - s0.get("waits", 0),
                              "io_workers": stored.shards.io_workers,
                              "decode_tokens": stream_tokens}
+        # the storage tier's roofline on this box: the same reader (positioned reads, O_DIRECT
+        # where the file system takes it, io_workers stretches) over the storage-tier layers'
+        # files, alone
+        order = stored.streamer.storage.order if stored.streamer.storage else []
+        if order:
+            sizes = [stored.shards.plan(i)[1] for i in order]
+            buf = torch.empty(max(sizes), dtype=torch.uint8).pin_memory()
+            t0 = time.perf_counter()
+            for i in order:
+                stored.shards.read_into(i, buf)
+            dt = time.perf_counter() - t0
+            out["storage_b1"]["read_probe_gbs"] = round(sum(sizes) / dt / 1e9, 2)
+            out["storage_b1"]["read_probe_note"] = (
+                "the storage-tier layers read once by the package's reader alone; the decode's "
+                "storage_gbs against it is the tier's fraction of this box's read rate")
         stored.close()
         del stored
     else:
@@ -1067,7 +1083,7 @@ def sweep(args):
     each with the launch's CUDA-event time over ``--steps`` graphed back-to-back launches (cycling
     through enough copies of the weight that none is still in L2), its algorithmic GB/s and
     TFLOP/s against the measured peaks, and which kernel ran (1 GEMV, 2 tcgen05 GEMM, 3 GEMV
-    slices)."""
+    slices, 4 tcgen05 decode GEMM)."""
     from rocketllm_b200 import kernels
     from rocketllm_b200.synthetic import make_activation, make_weight
     device = torch.device("cuda", 0)
@@ -1092,7 +1108,7 @@ def sweep(args):
             x = make_activation(m, k, device=device, seed=100 + i)
             y = torch.empty(m, n, dtype=torch.bfloat16, device=device)
             path = args.sweep_path or None
-            if path == 2 and m <= 16:
+            if (path == 2 and m <= 16) or (path == 4 and not 16 < m <= 64):
                 continue
             for _ in range(args.warmup):
                 for w in ws:
@@ -1381,7 +1397,8 @@ def main():
     ap.add_argument("--moe-tokens-list", default="1,8,32,128")
     ap.add_argument("--sweep-shapes", default="all", help="'all' or KxN[,KxN...]")
     ap.add_argument("--sweep-path", type=int, default=0,
-                    help="force a kernel in --sweep: 2 tcgen05 GEMM, 3 GEMV slices (0 = the "
+                    help="force a kernel in --sweep: 2 tcgen05 GEMM, 3 GEMV slices, 4 tcgen05 "
+                         "decode GEMM (0 = the "
                          "library's choice)")
     ap.add_argument("--decode-only", action="store_true",
                     help="only the model decode section (one JSON line)")

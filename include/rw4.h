@@ -75,10 +75,12 @@ int rw4_quantize(const void* w, int32_t w_dtype, int64_t N, int64_t K, int32_t g
  * rw4_linear: y[M, N] = x[M, K] . W[N, K]^T, bf16 in and out, fp32 accumulation, W in RW4.
  * Replaces the nn.Linear / F.linear call a transformers module makes on a dequantized weight
  * (transformers models/llama/modeling_llama.py:171-184 via rocketllm/base.py:848-855).
- * M <= 64 runs the dequant-GEMV (16-row batch slices above 16 rows), larger M the tensor-core GEMM
- * (rw4_linear_path).  The GEMV multiplies by the exact fp32 weight code * scale + zero and gives
- * each row of y the same bits at every M <= 64 (a row's output does not depend on the rows beside
- * it); the GEMM multiplies by the reference's bf16-rounded weight (dequantize().to(bfloat16),
+ * M <= 16 runs the dequant-GEMV; 17-64 rows the GEMV in 16-row batch slices, or for 49-64 rows
+ * the tcgen05 decode GEMM where the weight has enough 128-row tiles; larger M the tcgen05 GEMM
+ * (rw4_linear_path).  The GEMV and the decode GEMM multiply by the exact fp32 weight
+ * code * scale + zero; the GEMV gives each row of y the same bits at every M <= 16, the decode GEMM
+ * at every M of one column tile (17-32, 33-64) -- a row's output does not depend on the rows beside
+ * it; the GEMM multiplies by the reference's bf16-rounded weight (dequantize().to(bfloat16),
  * rocketllm/quant/kv_cache.py:257).  group must be 64 and K a multiple of 64; x, y and packed
  * must be 16-byte aligned, scale and zero 8-byte aligned.  Most GEMV calls need a workspace
  * (rw4_linear_workspace_size); this entry point takes it from the device's stream-ordered memory
@@ -89,18 +91,21 @@ int rw4_linear(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                void* y_bf16, void* stream);
 
 /* Which kernel rw4_linear would launch for (M, K, N): 1 = GEMV, 2 = tcgen05 GEMM,
- * 3 = GEMV over 16-row slices. Negative on invalid shapes. Host-only, launches nothing. */
+ * 3 = GEMV over 16-row slices, 4 = tcgen05 decode GEMM (picked for 49-64 rows; runs 17-64 rows
+ * with K % 512 == 0 and N >= 12288). Negative on invalid shapes. Host-only, launches nothing. */
 int rw4_linear_path(int64_t M, int64_t K, int64_t N);
 
-/* rw4_linear on a given path (1 or 3: GEMV / GEMV slices, 2: tcgen05 GEMM, which needs M > 16)
+/* rw4_linear on a given path (1 or 3: GEMV / GEMV slices, 2: tcgen05 GEMM, which needs M > 16,
+ * 4: tcgen05 decode GEMM, which needs the shapes above)
  * instead of the one rw4_linear_path picks; for tests and measurements of each kernel. */
 int rw4_linear_on_path(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                        const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
                        void* y_bf16, int32_t path, void* stream);
 
 /* Bytes of device workspace rw4_linear_ws needs for (M, K, N) on `path` (0 = the path
- * rw4_linear_path picks): the GEMV's converted activations (about 2*M*K bytes; 0 for one row
- * that the GEMV converts itself, and for the GEMM).  Host-only.  No reference counterpart: the
+ * rw4_linear_path picks): the converted activations of the GEMV and the decode GEMM (about
+ * 2*M*K bytes; 0 for one row that the GEMV converts itself, and for the GEMM).  Host-only.  No
+ * reference counterpart: the
  * reference's F.linear takes no workspace. */
 int rw4_linear_workspace_size(int64_t M, int64_t K, int64_t N, int32_t path, size_t* bytes);
 
@@ -128,9 +133,10 @@ int rw4_linear_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packe
  *   apply_rotary_pos_emb + StaticCache.update's index_copy_.
  * rw4_silu_mul: out[r, i] = bf16(bf16(silu(g)) * u), g = gate_up[r, i], u = gate_up[r, I + i]
  *   (act_fn(gate_proj(x)) * up_proj(x) of a concatenated gate|up projection, :171-184).
- * rw4_linear_residual_ws: y = bf16(residual + bf16(x . W^T)) for M <= 64 (the GEMV with the
- *   decoder layer's residual add in its epilogue); residual [M, N] may be y itself (in place) when
- *   K is a multiple of 512.  Workspace as rw4_linear_ws.
+ * rw4_linear_residual_ws: y = bf16(residual + bf16(x . W^T)) for M <= 64 (the kernel rw4_linear
+ *   would run -- the GEMV, or the decode GEMM -- with the decoder layer's residual add in its
+ *   epilogue); residual [M, N] may be y itself (in place) when K is a multiple of 512.
+ *   Workspace as rw4_linear_ws.
  * ------------------------------------------------------------------------------------------- */
 int rw4_rmsnorm(const void* x, const void* weight, int64_t rows, int64_t H, float eps, void* y,
                 void* stream);

@@ -37,6 +37,10 @@ size_t gemv_workspace(int64_t M, int64_t K, int64_t N);
 int gemm_tc_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                    const void* zr, int64_t N, void* y, cudaStream_t s);
 bool gemm_tc_supported(int64_t M, int64_t K, int64_t N);
+bool gemm_skinny_supported(int64_t M, int64_t K, int64_t N);
+int gemm_skinny_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
+                       const void* zr, int64_t N, void* y, cudaStream_t s, void* ws,
+                       size_t ws_bytes, const void* res);
 
 // Shape / pointer validation shared by every RW4 matmul entry point.
 int check_linear_args(const char* who, const void* x, int64_t M, int64_t K, const uint8_t* wq,
@@ -72,16 +76,23 @@ extern "C" int rw4_last_error(char* buf, size_t n) {
   return (int)e.size();
 }
 
-// Up to 64 rows the GEMV runs (16-row batch slices above 16 rows), above that the tensor-core GEMM
-// whenever it applies.  The GEMV multiplies by the exact fp32 weight and gives a row the same bits
-// at every M <= 64, so decode batches and speculative verify passes round like a one-token step;
-// the GEMM (prefill-sized M) multiplies by the reference's bf16-rounded dequantized weight, as the
-// reference's F.linear over dequantize().to(bf16) does.
+// Paths: 1 the dequant-GEMV (up to 16 rows); 3 the GEMV in 16-row batch slices (17-64 rows);
+// 4 the tcgen05 decode GEMM (17-64 rows, K % 512 == 0, N >= 12288), chosen for 49-64 rows, where it
+// measured faster than the slices (below that the slices win: its k-blocks advance at ~1,000 cycles
+// whatever the row count); 2 the bf16 tcgen05 GEMM (more rows).  Paths 1, 3 and 4 multiply by the
+// exact fp32 weight; the GEMV gives a row the same bits at every M <= 16 (and in every 16-row
+// slice), so decode steps and speculative verify passes round like a one-token step; the decode
+// GEMM gives a row the same bits at every M in 17-32 and in 33-64.  Path 2 (prefill-sized M)
+// multiplies by the reference's bf16-rounded dequantized weight, as the reference's F.linear over
+// dequantize().to(bf16) does.
 constexpr int64_t kGemvMaxRows = 64;
+constexpr int64_t kDecodeGemmMinRows = 49;
 
 extern "C" int rw4_linear_path(int64_t M, int64_t K, int64_t N) {
   if (M < 0 || K <= 0 || N < 0 || K % 64) return RW4_EINVAL;
   if (M <= 16) return 1;
+  if (M >= kDecodeGemmMinRows && M <= kGemvMaxRows && rw4::gemm_skinny_supported(M, K, N))
+    return 4;
   if (M > kGemvMaxRows && rw4::gemm_tc_supported(M, K, N)) return 2;
   return 3;
 }
@@ -95,7 +106,7 @@ extern "C" int rw4_linear_workspace_size(int64_t M, int64_t K, int64_t N, int32_
     return fail(RW4_EINVAL, "rw4_linear_workspace_size: bad shape M=%lld K=%lld N=%lld",
                 (long long)M, (long long)K, (long long)N);
   if (path == 0) path = rw4_linear_path(M, K, N);
-  if (M > 0 && N > 0 && (path == 1 || path == 3)) *bytes = gemv_workspace(M, K, N);
+  if (M > 0 && N > 0 && (path == 1 || path == 3 || path == 4)) *bytes = gemv_workspace(M, K, N);
   return RW4_OK;
 }
 
@@ -111,6 +122,9 @@ extern "C" int rw4_linear_ws(const void* x_bf16, int64_t M, int64_t K, const uin
   if (path == 2 && !gemm_tc_supported(M, K, N))
     return fail(RW4_EINVAL, "rw4_linear: the tensor-core GEMM needs M > 16 (M=%lld)",
                 (long long)M);
+  if (path == 4 && !gemm_skinny_supported(M, K, N))
+    return fail(RW4_EINVAL, "rw4_linear: the decode GEMM needs 17-64 rows, K %% 512 == 0 and "
+                "N >= 12288 (M=%lld K=%lld N=%lld)", (long long)M, (long long)K, (long long)N);
   cudaStream_t s = as_stream(stream);
   switch (path) {
     case 1:
@@ -119,6 +133,9 @@ extern "C" int rw4_linear_ws(const void* x_bf16, int64_t M, int64_t K, const uin
                          workspace_bytes);
     case 2:
       return gemm_tc_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s);
+    case 4:
+      return gemm_skinny_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s,
+                                workspace, workspace_bytes, nullptr);
     default:
       return fail(RW4_EINVAL, "rw4_linear: no path %d for M=%lld K=%lld N=%lld", path,
                   (long long)M, (long long)K, (long long)N);

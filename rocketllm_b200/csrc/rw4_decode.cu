@@ -29,6 +29,10 @@ bool gemv_tma_supported(int64_t K);
 int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                     const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
                     size_t ws_bytes, const void* res);
+bool gemm_skinny_supported(int64_t M, int64_t K, int64_t N);
+int gemm_skinny_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
+                       const void* zr, int64_t N, void* y, cudaStream_t s, void* ws,
+                       size_t ws_bytes, const void* res);
 }  // namespace rw4
 
 namespace {
@@ -220,6 +224,9 @@ extern "C" int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K,
     return fail(RW4_EINVAL, "rw4_linear_residual_ws: M=%lld; the GEMV takes at most 64 rows",
                 (long long)M);
   cudaStream_t s = as_stream(stream);
+  if (M >= 49 && gemm_skinny_supported(M, K, N))   // the path rw4_linear takes for these shapes
+    return gemm_skinny_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s, workspace,
+                              workspace_bytes, residual);
   static const bool no_tma = getenv("RW4_GEMV_NO_TMA") != nullptr;
   if (!no_tma && gemv_tma_supported(K))
     return gemv_tma_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s, 0, workspace,

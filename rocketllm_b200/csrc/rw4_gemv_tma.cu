@@ -20,17 +20,9 @@
 #include <atomic>
 
 #include "rw4_gemv_tma_body.cuh"
+#include "rw4_xprep.cuh"
 
 namespace rw4 {
-
-// Byte offsets of the x-prep arrays inside a workspace (each 256-byte aligned).
-struct XPrepLayout {
-  int64_t Mpad = 0;         // rows padded to even (the side box is 16 bytes wide per row pair)
-  size_t xf = 0;            // fp16 [M, K], fragment order within each 16-value chunk
-  size_t side = 0;          // fp32 pairs [K/64][Mpad]: (2^e * sum x, -1024 * sum fp16(x 2^e))
-  size_t row_exp = 0;       // int32 [Mpad]: e per row
-  size_t bytes = 0;         // total
-};
 
 inline size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 
@@ -160,6 +152,17 @@ int launch_xprep(const void* x, int M, int K, const XPrepLayout& l, uint8_t* ws,
   if (err != cudaSuccess) return cuda_status(err, "rw4 x-prep launch");
   return launch_status("rw4 x-prep launch");
 }
+
+}  // namespace
+
+namespace rw4 {
+int xprep_launch(const void* x, int M, int K, const XPrepLayout& l, uint8_t* ws,
+                 cudaStream_t stream) {
+  return launch_xprep(x, M, K, l, ws, stream);
+}
+}  // namespace rw4
+
+namespace {
 
 // One activation row whose CTA K range fits the in-kernel conversion's shared memory: the GEMV
 // converts it itself (XQ).  Everything else goes through the x-prep pass.

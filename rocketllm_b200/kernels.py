@@ -97,7 +97,8 @@ def linear(x, packed, scale, zero, out=None, path=None):
     """``y = x . W^T`` with ``x`` bf16 ``[..., K]`` and W in RW4; returns bf16 ``[..., N]``.
 
     ``x`` may be a strided view (e.g. the last position of every sequence); it is compacted first.
-    ``path`` forces a kernel (1 / 3 GEMV, 2 tcgen05 GEMM) instead of the library's choice.  The
+    ``path`` forces a kernel (1 / 3 GEMV, 2 tcgen05 GEMM, 4 tcgen05 decode GEMM for 17-64 rows)
+    instead of the library's choice.  The
     GEMV's workspace (the converted activations) comes from torch's allocator on the current
     stream, so the call also works inside a CUDA-graph capture.
     """
@@ -128,7 +129,8 @@ def linear(x, packed, scale, zero, out=None, path=None):
 
 
 def linear_path(m, k, n):
-    """Which kernel :func:`linear` launches: 1 GEMV, 2 tcgen05 GEMM, 3 GEMV slices."""
+    """Which kernel :func:`linear` launches: 1 GEMV, 2 tcgen05 GEMM, 3 GEMV slices, 4 tcgen05
+    decode GEMM (17-64 rows)."""
     return _lib.check(_lib.lib().rw4_linear_path(m, k, n), "rw4_linear_path")
 
 

@@ -141,11 +141,77 @@ def test_linear_row_independent_of_batch(cuda, k, n):
     x[9] *= 300
     alone = torch.cat([kernels.linear(x[i:i + 1], packed, scale, zero) for i in range(64)])
     for m in (2, 4, 8, 9, 16, 17, 33, 64):
-        assert kernels.linear_path(m, k, n) in (1, 3)
-        y = kernels.linear(x[:m], packed, scale, zero)
+        # past 16 rows the GEMV runs in 16-row slices (path 3; the default there may be the
+        # tcgen05 decode GEMM, tested below)
+        y = kernels.linear(x[:m], packed, scale, zero, path=1 if m <= 16 else 3)
         assert torch.equal(y, alone[:m]), f"M={m}"
     torch.cuda.synchronize()
     check_close(alone, oracle_linear(x, packed, scale, zero))
+
+
+@pytest.mark.parametrize("k,n", [(4096, 14336), (1024, 12288), (14336, 12416)])
+@pytest.mark.parametrize("m", [17, 24, 32, 33, 48, 64])
+def test_decode_gemm_matches_oracle(cuda, m, k, n):
+    """The tcgen05 decode GEMM (path 4, forced here for 17-64 rows; the library picks it for 49-64):
+    exact fp32 weights through fp16 code patterns and per-group scales applied from TMEM, against
+    the oracle's exact-weight linear; rows of very different magnitude side by side."""
+    assert kernels.linear_path(m, k, n) == (4 if m >= 49 else 3)
+    packed, scale, zero = make_weight(n, k, device=cuda, seed=m + 3 * k)
+    x = make_activation(m, k, device=cuda, seed=n + m)
+    x[1] *= 1e-3
+    x[m - 1] *= 300
+    y = kernels.linear(x, packed, scale, zero, path=4)
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    rows = np.arange(0, n, max(1, n // 512))
+    check_close(y[:, torch.from_numpy(rows).to(cuda)],
+                oracle_linear(x, packed, scale, zero, rows=rows, path=4))
+
+
+@pytest.mark.parametrize("k,n", [(4096, 14336), (14336, 12416)])
+def test_decode_gemm_rows_independent_of_batch(cuda, k, n):
+    """A row's output from the decode GEMM has the same bits at every M of one column tile
+    (17-32, 33-64), and a power-of-two scaling of x scales y exactly."""
+    packed, scale, zero = make_weight(n, k, device=cuda, seed=21)
+    x = make_activation(64, k, device=cuda, seed=22)
+    x[3] *= 1e-3
+    x[20] *= 300
+    y32 = kernels.linear(x[:32], packed, scale, zero, path=4)
+    for m in (17, 24, 31):
+        assert torch.equal(kernels.linear(x[:m], packed, scale, zero, path=4), y32[:m]), f"M={m}"
+    y64 = kernels.linear(x, packed, scale, zero, path=4)
+    for m in (33, 48, 63):
+        assert torch.equal(kernels.linear(x[:m], packed, scale, zero, path=4), y64[:m]), f"M={m}"
+    for j in (-20, 7):
+        ys = kernels.linear((x.float() * 2.0 ** j).to(torch.bfloat16), packed, scale, zero,
+                            path=4)
+        assert torch.equal(ys.float(), y64.float() * 2.0 ** j), f"2^{j}"
+    assert kernels.device_status() == 0
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 4096), (5, 4096, 6144), (40, 1024, 2048),
+                                   (56, 4096, 12288)])
+def test_linear_residual_epilogue(cuda, m, k, n):
+    """rw4_linear_residual_ws (a decoder layer's o_proj / down_proj with its residual add): the
+    GEMV's epilogue (one row, a decode batch), the 16-row slices, and the tcgen05 decode GEMM's
+    epilogue (56 rows) all give bf16(residual + bf16(x . W^T)) -- the module's two roundings --
+    bit for bit, also in place (the residual is the output buffer)."""
+    from rocketllm_b200 import _lib
+    w = make_weight(n, k, device=cuda, seed=31)
+    x = make_activation(m, k, device=cuda, seed=32)
+    res = make_activation(m, n, device=cuda, seed=33)
+    want = (kernels.linear(x, *w).float() + res.float()).to(torch.bfloat16)
+    wsb = kernels.linear_workspace_bytes(m, k, n)
+    ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=cuda)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    for in_place in (False, True):
+        y = res.clone() if in_place else torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+        _lib.call("rw4_linear_residual_ws", x.data_ptr(), m, k, w[0].data_ptr(), w[1].data_ptr(),
+                  w[2].data_ptr(), n, 64, y.data_ptr() if in_place else res.data_ptr(),
+                  y.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+        torch.cuda.synchronize()
+        assert torch.equal(y, want), f"in_place={in_place}"
+    assert kernels.device_status() == 0
 
 
 def test_linear_deterministic(cuda):
