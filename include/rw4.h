@@ -145,6 +145,17 @@ int rw4_rope_kv(const void* q, const void* k, const void* v, int64_t ld, int32_t
                 const void* sin_bf16, const int64_t* pos, int64_t cache_len, void* q_out,
                 void* k_cache, void* v_cache, void* stream);
 int rw4_silu_mul(const void* gate_up, int64_t rows, int64_t I, void* out, void* stream);
+/* rw4_linear_rmsnorm_ws: y = x_n . W^T with x_n = rw4_rmsnorm(x, norm_weight, eps) for M <= 64
+ *   (a decoder layer's input_layernorm / post_attention_layernorm followed by its first
+ *   projection); for two or more rows with K % 512 == 0 the norm runs inside the activation
+ *   conversion (no separate launch, the same bits as the two calls), otherwise rw4_rmsnorm first.
+ *   norm_weight bf16 [K], 16-byte aligned; workspace of rw4_linear_rmsnorm_workspace_size bytes,
+ *   256-byte aligned. */
+int rw4_linear_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes);
+int rw4_linear_rmsnorm_ws(const void* x_bf16, int64_t M, int64_t K, const void* norm_weight,
+                          float eps, const uint8_t* packed, const void* scale_f16,
+                          const void* zero_f16, int64_t N, int32_t group, void* y_bf16,
+                          void* workspace, size_t workspace_bytes, void* stream);
 int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                            const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
                            const void* residual, void* y_bf16, void* workspace,

@@ -6,6 +6,7 @@
 
 #include "rw4_common.cuh"
 #include "rw4_tma.cuh"
+#include "rw4_xprep.cuh"
 
 namespace rw4 {
 
@@ -40,7 +41,7 @@ bool gemm_tc_supported(int64_t M, int64_t K, int64_t N);
 bool gemm_skinny_supported(int64_t M, int64_t K, int64_t N);
 int gemm_skinny_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                        const void* zr, int64_t N, void* y, cudaStream_t s, void* ws,
-                       size_t ws_bytes, const void* res);
+                       size_t ws_bytes, const void* res, const XNorm* norm = nullptr);
 
 // Shape / pointer validation shared by every RW4 matmul entry point.
 int check_linear_args(const char* who, const void* x, int64_t M, int64_t K, const uint8_t* wq,

@@ -10,6 +10,8 @@
 //                      the device-side position                            [:78-112, StaticCache]
 //   rw4_silu_mul       act_fn(gate) * up for a concatenated [gate | up] row: silu in fp32 rounded
 //                      to bf16, the product rounded to bf16                  [:171-184]
+//   rw4_linear_rmsnorm_ws    linear(rmsnorm(x)): a projection after the layer's norm, the norm
+//                      folded into the activation conversion for two or more rows
 //   rw4_linear_residual_ws   residual + linear(x): the GEMV with the residual added in its epilogue
 //                      (the product rounded to bf16 first, then the sum), as a decoder layer's
 //                      `hidden_states = residual + self_attn(...)` / `+ mlp(...)`.
@@ -19,6 +21,7 @@
 // touches memory, then lets the next one launch, so the following GEMV streams its first weight
 // stages while they run.
 #include "rw4_common.cuh"
+#include "rw4_xprep.cuh"
 
 namespace rw4 {
 int check_linear_args(const char* who, const void* x, int64_t M, int64_t K, const uint8_t* wq,
@@ -28,11 +31,12 @@ int gemv_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const vo
 bool gemv_tma_supported(int64_t K);
 int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                     const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
-                    size_t ws_bytes, const void* res);
+                    size_t ws_bytes, const void* res, const XNorm* norm = nullptr);
+size_t gemv_workspace(int64_t M, int64_t K, int64_t N);
 bool gemm_skinny_supported(int64_t M, int64_t K, int64_t N);
 int gemm_skinny_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                        const void* zr, int64_t N, void* y, cudaStream_t s, void* ws,
-                       size_t ws_bytes, const void* res);
+                       size_t ws_bytes, const void* res, const XNorm* norm = nullptr);
 }  // namespace rw4
 
 namespace {
@@ -208,6 +212,64 @@ extern "C" int rw4_silu_mul(const void* gate_up, int64_t rows, int64_t I, void* 
                     rw4::as_stream(stream), "rw4_silu_mul launch",
                     static_cast<const __nv_bfloat16*>(gate_up), (int)rows, (int)I,
                     static_cast<__nv_bfloat16*>(out));
+}
+
+namespace {
+// Two or more rows on the TMA path normalise inside the activation conversion; otherwise the rows
+// are normalised by rw4_rmsnorm into the workspace first.
+bool norm_folded(int64_t M, int64_t K) {
+  static const bool no_tma = getenv("RW4_GEMV_NO_TMA") != nullptr;
+  return M >= 2 && !no_tma && rw4::gemv_tma_supported(K);
+}
+}  // namespace
+
+// Workspace of rw4_linear_rmsnorm_ws: the linear's own, plus room for the normalised rows when the
+// norm is not folded into the conversion.
+extern "C" int rw4_linear_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes) {
+  if (!bytes) return fail(RW4_EINVAL, "rw4_linear_rmsnorm_workspace_size: null output");
+  if (M < 0 || K <= 0 || N < 0 || K % 64)
+    return fail(RW4_EINVAL, "rw4_linear_rmsnorm_workspace_size: bad shape");
+  const size_t lin = (M > 0 && N > 0) ? rw4::gemv_workspace(M, K, N) : 0;
+  *bytes = norm_folded(M, K) ? lin : ((lin + 255) & ~size_t(255)) + (size_t)M * K * 2;
+  return RW4_OK;
+}
+
+extern "C" int rw4_linear_rmsnorm_ws(const void* x_bf16, int64_t M, int64_t K,
+                                     const void* norm_weight, float eps, const uint8_t* packed,
+                                     const void* scale_f16, const void* zero_f16, int64_t N,
+                                     int32_t group, void* y_bf16, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  using namespace rw4;
+  int st = check_linear_args("rw4_linear_rmsnorm_ws", x_bf16, M, K, packed, scale_f16, zero_f16,
+                             N, group, y_bf16);
+  if (st != RW4_OK || M == 0 || N == 0) return st;
+  if (!norm_weight || !aligned(norm_weight, 16))
+    return fail(RW4_EINVAL, "rw4_linear_rmsnorm_ws: norm weight null or not 16-byte aligned");
+  if (M > 64)
+    return fail(RW4_EINVAL, "rw4_linear_rmsnorm_ws: M=%lld; at most 64 rows", (long long)M);
+  size_t need = 0;
+  st = rw4_linear_rmsnorm_workspace_size(M, K, N, &need);
+  if (st != RW4_OK) return st;
+  if (need && (!workspace || workspace_bytes < need || !aligned(workspace, 256)))
+    return fail(RW4_EINVAL, "rw4_linear_rmsnorm_ws: needs a 256-byte aligned %zu-byte workspace",
+                need);
+  cudaStream_t s = as_stream(stream);
+  const XNorm norm{norm_weight, eps};
+  if (norm_folded(M, K)) {
+    // the norm runs inside the activation conversion that the multi-row kernels start with
+    if (M >= 49 && gemm_skinny_supported(M, K, N))
+      return gemm_skinny_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s,
+                                workspace, workspace_bytes, nullptr, &norm);
+    return gemv_tma_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s, 0,
+                           workspace, workspace_bytes, nullptr, &norm);
+  }
+  // one row (its GEMV converts the row itself) or no TMA path: normalise, then the linear
+  const size_t lin = (gemv_workspace(M, K, N) + 255) & ~size_t(255);
+  uint8_t* xn = static_cast<uint8_t*>(workspace) + lin;
+  st = rw4_rmsnorm(x_bf16, norm_weight, M, K, eps, xn, stream);
+  if (st != RW4_OK) return st;
+  return rw4_linear_ws(xn, M, K, packed, scale_f16, zero_f16, N, group, y_bf16, 0, workspace,
+                       lin, stream);
 }
 
 extern "C" int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K,

@@ -396,7 +396,7 @@ bool gemm_skinny_supported(int64_t M, int64_t K, int64_t N) {
 // The x-prep workspace of the same rows (xprep_layout(M, K).bytes) must be passed in `ws`.
 int gemm_skinny_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                        const void* zr, int64_t N, void* y, cudaStream_t s, void* ws,
-                       size_t ws_bytes, const void* res) {
+                       size_t ws_bytes, const void* res, const XNorm* norm) {
   const XPrepLayout l = xprep_layout(M, K);
   if (!ws || ws_bytes < l.bytes)
     return fail(RW4_EINVAL, "rw4_linear: the decode GEMM needs a %zu-byte workspace (got %zu)",
@@ -405,7 +405,7 @@ int gemm_skinny_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, c
   if (!aligned(sc, 16) || !aligned(zr, 16))
     return fail(RW4_EINVAL, "rw4_linear: scales and zeros must be 16-byte aligned");
   uint8_t* w = static_cast<uint8_t*>(ws);
-  int st = xprep_launch(x, (int)M, (int)K, l, w, s);
+  int st = xprep_launch(x, (int)M, (int)K, l, w, s, norm);
   if (st != RW4_OK) return st;
   if (M <= 32) return launch_bn<32>(x, (int)M, (int)K, wq, sc, zr, (int)N, y, l, w, res, s);
   return launch_bn<64>(x, (int)M, (int)K, wq, sc, zr, (int)N, y, l, w, res, s);

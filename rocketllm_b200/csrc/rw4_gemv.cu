@@ -31,6 +31,7 @@
 // subtraction of 128 * sum(x) cancels ~7 bits, leaving ~2^-17 relative error per group, far below
 // the bf16 output rounding (2^-9).
 #include "rw4_gemv_frag.cuh"
+#include "rw4_xprep.cuh"
 
 namespace {
 
@@ -258,7 +259,7 @@ bool gemv_tma_supported(int64_t K);
 size_t gemv_tma_workspace(int64_t M, int64_t K, int64_t N);
 int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                     const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
-                    size_t ws_bytes, const void* res = nullptr);
+                    size_t ws_bytes, const void* res = nullptr, const XNorm* norm = nullptr);
 
 // Workspace bytes the GEMV needs for (M, K, N): the TMA kernel's x-prep arrays (none for a row it
 // converts itself); the register-staged kernel needs none.

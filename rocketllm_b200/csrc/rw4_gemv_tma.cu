@@ -46,9 +46,25 @@ using namespace rw4::gemv_tma;
 constexpr int kPrepThreads = 256;
 
 // One CTA per row m < Mpad; rows M..Mpad-1 only zero their side pairs and exponent.
+// bf16(w * bf16(x * r)) for 8 values (RMSNorm's scaling, as rw4_rmsnorm rounds it).
+__device__ __forceinline__ uint4 norm8(uint4 xv, uint4 wv, float r) {
+  const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float a = __bfloat162float(__float2bfloat16_rn(__uint_as_float(xs[j] << 16) * r));
+    const float b = __bfloat162float(__float2bfloat16_rn(__uint_as_float(xs[j] & 0xFFFF0000u) * r));
+    const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(ws[j] << 16) * a,
+                                                  __uint_as_float(ws[j] & 0xFFFF0000u) * b);
+    o[j] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
 __global__ void __launch_bounds__(kPrepThreads)
     rw4_xprep_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, int Mpad,
-                     uint4* __restrict__ xf, float2* __restrict__ side, int* __restrict__ row_exp) {
+                     uint4* __restrict__ xf, float2* __restrict__ side, int* __restrict__ row_exp,
+                     const __nv_bfloat16* __restrict__ nw, float eps) {
   const int m = blockIdx.x;
   const int G = K / 64;
   // x comes from the previous kernel on the stream; the GEMV after us may start launching now (it
@@ -62,10 +78,36 @@ __global__ void __launch_bounds__(kPrepThreads)
     return;
   }
   const __nv_bfloat16* xr = x + (int64_t)m * K;
+  // 0. with a norm: the row's scale, summed in rw4_rmsnorm's order (strided per thread, the warp
+  //    butterfly, the warps in order)
+  float r = 1.f;
+  if (nw) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < K; i += kPrepThreads) {
+      const float v = __bfloat162float(xr[i]);
+      ss = fmaf(v, v, ss);
+    }
+    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 16);
+    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 8);
+    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 4);
+    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 2);
+    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 1);
+    __shared__ float wss[kPrepThreads / 32];
+    if ((threadIdx.x & 31) == 0) wss[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kPrepThreads / 32; ++w) tot += wss[w];
+    r = rsqrtf(tot / (float)K + eps);
+  }
+  auto load8 = [&](int i) {   // 8 values of the (normalised) row starting at 8 i
+    const uint4 v = ldg_u4(xr + 8 * i);
+    return nw ? norm8(v, ldg_u4(nw + 8 * i), r) : v;
+  };
   // 1. largest magnitude
   uint32_t mx = 0;
   for (int i = threadIdx.x; i < K / 8; i += kPrepThreads)
-    mx = max(mx, frag::absmax8(ldg_u4(xr + 8 * i)));
+    mx = max(mx, frag::absmax8(load8(i)));
   mx = __reduce_max_sync(0xFFFFFFFFu, mx);
   __shared__ uint32_t wmax[kPrepThreads / 32];
   if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = mx;
@@ -84,7 +126,7 @@ __global__ void __launch_bounds__(kPrepThreads)
     float xs = 0.f, hs = 0.f;
     if (c < chunks) {
       uint32_t o[8];
-      frag::x16_to_f16_frag(ldg_u4(xr + 16 * c), ldg_u4(xr + 16 * c + 8), p1, p2, o, xs, hs);
+      frag::x16_to_f16_frag(load8(2 * c), load8(2 * c + 1), p1, p2, o, xs, hs);
       uint4* dst = xf + ((int64_t)m * K + 16 * c) / 8;
       dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
       dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
@@ -137,7 +179,7 @@ cudaLaunchAttribute pdl_attr() {
 }
 
 int launch_xprep(const void* x, int M, int K, const XPrepLayout& l, uint8_t* ws,
-                 cudaStream_t stream) {
+                 cudaStream_t stream, const XNorm* norm = nullptr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)l.Mpad);
   cfg.blockDim = dim3(kPrepThreads);
@@ -148,7 +190,8 @@ int launch_xprep(const void* x, int M, int K, const XPrepLayout& l, uint8_t* ws,
   cudaError_t err = cudaLaunchKernelEx(
       &cfg, rw4_xprep_kernel, static_cast<const __nv_bfloat16*>(x), M, K, (int)l.Mpad,
       reinterpret_cast<uint4*>(ws + l.xf), reinterpret_cast<float2*>(ws + l.side),
-      reinterpret_cast<int*>(ws + l.row_exp));
+      reinterpret_cast<int*>(ws + l.row_exp),
+      norm ? static_cast<const __nv_bfloat16*>(norm->weight) : nullptr, norm ? norm->eps : 0.f);
   if (err != cudaSuccess) return cuda_status(err, "rw4 x-prep launch");
   return launch_status("rw4 x-prep launch");
 }
@@ -157,8 +200,8 @@ int launch_xprep(const void* x, int M, int K, const XPrepLayout& l, uint8_t* ws,
 
 namespace rw4 {
 int xprep_launch(const void* x, int M, int K, const XPrepLayout& l, uint8_t* ws,
-                 cudaStream_t stream) {
-  return launch_xprep(x, M, K, l, ws, stream);
+                 cudaStream_t stream, const XNorm* norm) {
+  return launch_xprep(x, M, K, l, ws, stream, norm);
 }
 }  // namespace rw4
 
@@ -300,7 +343,7 @@ size_t gemv_tma_workspace(int64_t M, int64_t K, int64_t N) {
 
 int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                     const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
-                    size_t ws_bytes, const void* res) {
+                    size_t ws_bytes, const void* res, const XNorm* norm) {
   const int Mi = (int)M, Ki = (int)K, Ni = (int)N;
   static const int forced_ks = [] {
     const char* e = getenv("RW4_GEMV_KSPLIT");
@@ -316,13 +359,15 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
   if (row_tiles == 4 && (M > 8 || ks > 1)) row_tiles = 2;
   const XPrepLayout l = xprep_layout(M, K);
   uint8_t* w = static_cast<uint8_t*>(ws);
+  if (norm && one_row_in_kernel(M, K, ks))
+    return fail(RW4_EINVAL, "gemv_tma: a normalised one-row call takes the x-prep path only");
   if (!one_row_in_kernel(M, K, ks)) {
     if (!ws || ws_bytes < l.bytes)
       return fail(RW4_EINVAL, "rw4_linear: the GEMV needs a %zu-byte workspace (got %zu)",
                   l.bytes, ws_bytes);
     if (!aligned(ws, 256))
       return fail(RW4_EINVAL, "rw4_linear: workspace must be 256-byte aligned");
-    const int st = launch_xprep(x, Mi, Ki, l, w, s);
+    const int st = launch_xprep(x, Mi, Ki, l, w, s, norm);
     if (st != RW4_OK) return st;
   }
   if (M <= 8) {

@@ -21,9 +21,17 @@ struct XPrepLayout {
 
 XPrepLayout xprep_layout(int64_t M, int64_t K);
 
-// Launch the conversion of x [M, K] bf16 into the workspace `ws` laid out as `l` (programmatic
-// dependent launch; the kernel after it may start and must wait before reading the workspace).
+// An RMSNorm applied to each row before its conversion: x -> bf16(w * bf16(x * rsqrt(mean(x^2) +
+// eps))), the rounding sequence (and summation order) of rw4_rmsnorm.
+struct XNorm {
+  const void* weight;   // bf16 [K], 16-byte aligned
+  float eps;
+};
+
+// Launch the conversion of x [M, K] bf16 (RMS-normalised first when `norm` is given) into the
+// workspace `ws` laid out as `l` (programmatic dependent launch; the kernel after it may start and
+// must wait before reading the workspace).
 int xprep_launch(const void* x, int M, int K, const XPrepLayout& l, uint8_t* ws,
-                 cudaStream_t stream);
+                 cudaStream_t stream, const XNorm* norm = nullptr);
 
 }  // namespace rw4

@@ -5,16 +5,18 @@ Through the transformers modules one decode step of a Llama layer is about fifty
 RMSNorm as six elementwise kernels, q / k / v as three GEMVs, the rotary embedding as cat / neg /
 mul / add kernels, ``index_copy_`` into the static cache, the grouped-query key / value copies
 (``repeat_kv``), attention, o_proj, the residual add, RMSNorm again, gate, up, SiLU, the product,
-down, the residual add (transformers ``models/llama/modeling_llama.py``).  The step here is eight
-launches per layer, each reproducing the modules' bf16 rounding sequence:
+down, the residual add (transformers ``models/llama/modeling_llama.py``).  The step here is about
+ten launches per layer (attention's two and the conversion passes included), each reproducing the
+modules' bf16 rounding sequence:
 
-    rw4_rmsnorm                       input_layernorm
-    rw4_linear (q|k|v concatenated)   q_proj, k_proj, v_proj: one GEMV over one weight
+    rw4_linear_rmsnorm_ws             input_layernorm, then q_proj, k_proj, v_proj as one GEMV
+                                      over the concatenated weight (from two rows on, the norm
+                                      runs inside the GEMV's activation conversion)
     rw4_rope_kv                       apply_rotary_pos_emb + StaticCache.update (device position)
     SDPA with enable_gqa              attention over the static cache, no key / value copies
     rw4_linear_residual_ws            o_proj + residual add in the GEMV epilogue
-    rw4_rmsnorm                       post_attention_layernorm
-    rw4_linear (gate|up concatenated) gate_proj, up_proj: one GEMV
+    rw4_linear_rmsnorm_ws             post_attention_layernorm, then gate_proj, up_proj as one
+                                      GEMV over the concatenated weight
     rw4_silu_mul                      act_fn(gate) * up
     rw4_linear_residual_ws            down_proj + residual add
 
@@ -34,6 +36,8 @@ expert-parallel exchange -- followed by the residual add:
     mlp (router + routed experts)     MixtralSparseMoeBlock, unchanged
     residual add                      ``residual + hidden_states``
 """
+import ctypes
+
 import torch
 
 from . import _lib, kernels
@@ -161,8 +165,13 @@ class FusedDecoder(GraphedDecoder):
             self.act = torch.empty(b, self.inter, **bf)
             shapes += [(self.hidden, 2 * self.inter), (self.inter, self.hidden)]
         self.positions = torch.arange(max_len, device=dev)
+        self.logits_buf = torch.empty(b, self.head[0].shape[0], **bf)
         self._counters = None
         wsb = max(kernels.linear_workspace_bytes(b, k, n) for k, n in shapes)
+        for k, n in shapes:   # the projections that follow a norm take it in their conversion
+            nb = ctypes.c_size_t(0)
+            _lib.call("rw4_linear_rmsnorm_workspace_size", b, k, n, ctypes.byref(nb))
+            wsb = max(wsb, nb.value)
         self.ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
 
     def _lin(self, x, w, out, residual=None):
@@ -177,6 +186,16 @@ class FusedDecoder(GraphedDecoder):
             _lib.call("rw4_linear_residual_ws", x.data_ptr(), m, k, w[0].data_ptr(),
                       w[1].data_ptr(), w[2].data_ptr(), n, 64, residual.data_ptr(),
                       out.data_ptr(), ws, wsb, stream)
+        return out
+
+    def _lin_norm(self, x, weight, eps, w, out):
+        """``out = rmsnorm(x) . W^T``: for two or more rows the norm runs inside the activation
+        conversion (one launch fewer), for one row it is rw4_rmsnorm then the one-row GEMV."""
+        m, k = x.shape
+        _lib.call("rw4_linear_rmsnorm_ws", x.data_ptr(), m, k, weight.data_ptr(), float(eps),
+                  w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(), w[0].shape[0], 64,
+                  out.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
+                  torch.cuda.current_stream(self.device).cuda_stream)
         return out
 
     def _norm(self, x, weight, eps, out):
@@ -212,7 +231,7 @@ class FusedDecoder(GraphedDecoder):
         other = self.h[1]
         for i, w in enumerate(self.layers):
             layer = self.cache.layers[i]
-            self._lin(self._norm(cur, w.ln1, w.eps1, self.xn), w.qkv, qkv)
+            self._lin_norm(cur, w.ln1, w.eps1, w.qkv, qkv)
             _lib.call("rw4_rope_kv", qkv.data_ptr(), qkv[:, nq:].data_ptr(),
                       qkv[:, nq + nk:].data_ptr(), qkv.shape[1], b, self.hq, self.hk, self.hd,
                       cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), layer.keys.shape[2],
@@ -224,21 +243,20 @@ class FusedDecoder(GraphedDecoder):
             # residual stream: each add writes the other buffer (no in-place update)
             self._lin(attn.reshape(b, nq), w.o, other, residual=cur)
             cur, other = other, cur
-            xn = self._norm(cur, w.ln2, w.eps2, self.xn)
             if w.moe is not None:
                 # the model's own sparse-MoE block (router + routed experts), then the residual
+                xn = self._norm(cur, w.ln2, w.eps2, self.xn)
                 y = w.moe(xn.view(b, 1, self.hidden)).view(b, self.hidden)
                 torch.add(cur, y, out=other)
             else:
-                self._lin(xn, w.gate_up, self.gu)
+                self._lin_norm(cur, w.ln2, w.eps2, w.gate_up, self.gu)
                 _lib.call("rw4_silu_mul", self.gu.data_ptr(), b, self.inter,
                           self.act.data_ptr(), stream)
                 self._lin(self.act, w.down, other, residual=cur)
             cur, other = other, cur
         # the static cache's own write counters, kept in step for transformers (one launch)
         torch._foreach_add_(self._counters, 1)
-        logits = kernels.linear(self._norm(cur, self.final_norm, self.final_eps, self.xn),
-                                *self.head)
+        logits = self._lin_norm(cur, self.final_norm, self.final_eps, self.head, self.logits_buf)
         self.logits = logits
         nxt_tok = logits.argmax(-1, keepdim=True)
         self.ids.copy_(nxt_tok)

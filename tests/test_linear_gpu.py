@@ -214,6 +214,33 @@ def test_linear_residual_epilogue(cuda, m, k, n):
     assert kernels.device_status() == 0
 
 
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 6144), (2, 4096, 6144), (16, 2048, 11264),
+                                   (40, 4096, 4096), (56, 4096, 12288), (3, 1600, 1024)])
+def test_linear_rmsnorm_matches_norm_then_linear(cuda, m, k, n):
+    """rw4_linear_rmsnorm_ws (a layer norm folded into the projection's activation conversion)
+    gives the bits of rw4_rmsnorm followed by the projection: the same rounding sequence and the
+    same summation order for the row's mean square.  (1600: K % 512 != 0, normalised first.)"""
+    import ctypes
+    from rocketllm_b200 import _lib
+    w = make_weight(n, k, device=cuda, seed=41)
+    x = make_activation(m, k, device=cuda, seed=42) * 3
+    nw = (1 + 0.1 * make_activation(1, k, device=cuda, seed=43)).to(torch.bfloat16).view(k)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    xn = torch.empty_like(x)
+    _lib.call("rw4_rmsnorm", x.data_ptr(), nw.data_ptr(), m, k, 1e-5, xn.data_ptr(), stream)
+    want = kernels.linear(xn, *w)
+    nb = ctypes.c_size_t(0)
+    _lib.call("rw4_linear_rmsnorm_workspace_size", m, k, n, ctypes.byref(nb))
+    ws = torch.empty(max(nb.value, 256), dtype=torch.uint8, device=cuda)
+    y = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    _lib.call("rw4_linear_rmsnorm_ws", x.data_ptr(), m, k, nw.data_ptr(), 1e-5, w[0].data_ptr(),
+              w[1].data_ptr(), w[2].data_ptr(), n, 64, y.data_ptr(), ws.data_ptr(), ws.numel(),
+              stream)
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    assert torch.equal(y, want)
+
+
 def test_linear_deterministic(cuda):
     packed, scale, zero = make_weight(4096, 14336, device=cuda, seed=5)
     x = make_activation(16, 14336, device=cuda, seed=6)
