@@ -21,8 +21,8 @@
 // shared loads within the two wavefronts 256 bytes need.  Rows past the weight's end are
 // zero-filled by the TMA unit and never stored.
 //
-// SWIGLU variant (R == 2): tile 0 holds rows [r0, r0+16) of the gate half of a stacked gate/up
-// weight and tile 1 the matching up rows [r0+I, r0+I+16); the epilogue writes
+// SWIGLU variant (R even): tiles 0 .. R/2-1 hold rows [r0, r0+8R) of the gate half of a stacked
+// gate/up weight and tiles R/2 .. R-1 the matching up rows [r0+I, r0+I+8R); the epilogue writes
 // bf16(bf16(silu(bf16(g))) * bf16(u)), the rounding sequence of the bf16 model's own
 // act_fn(gate) * up (transformers models/mixtral/modeling_mixtral.py:84-91).
 //
@@ -159,7 +159,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
                                      const __nv_bfloat16* __restrict__ res = nullptr) {
   using namespace rw4::frag;
   using L = Layout<R, S>;
-  static_assert(!SWIGLU || R == 2, "the SwiGLU epilogue pairs one gate tile with one up tile");
+  static_assert(!SWIGLU || R % 2 == 0, "the SwiGLU epilogue pairs gate tiles with up tiles");
   static_assert(!M1 || NT == 1, "one activation row fits one MMA column tile");
   static_assert(!XP || (XT && !SWIGLU), "the pre-converted activations come through the ring");
   static_assert(!XQ || (M1 && !XT && !XP && !SWIGLU), "XQ converts one activation row");
@@ -250,16 +250,17 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
           tma_load_2d(sbase + L::side_base(bm) + st * L::side_stage(bm), tm_side, 2 * x_row0, gx,
                       fb);
         if (SWIGLU) {
-          // 16-row boxes: gate tile then up tile (2048 bytes apart, swizzle phase unchanged).
+          // 8R-row boxes: gate rows then up rows (2048 R/2 bytes apart, swizzle phase unchanged).
           const int ru = r0 + up_offset;
+          constexpr int kUp = 2048 * (R / 2), kUpS = 256 * (R / 2);
           tma_load_2d_hint(cdst, tm_codes, kx, r0, fb, pol);
-          tma_load_2d_hint(cdst + 2048, tm_codes, kx, ru, fb, pol);
+          tma_load_2d_hint(cdst + kUp, tm_codes, kx, ru, fb, pol);
           tma_load_2d_hint(cdst + L::kCodeBox, tm_codes, kx + 128, r0, fb, pol);
-          tma_load_2d_hint(cdst + L::kCodeBox + 2048, tm_codes, kx + 128, ru, fb, pol);
+          tma_load_2d_hint(cdst + L::kCodeBox + kUp, tm_codes, kx + 128, ru, fb, pol);
           tma_load_2d_hint(sdst, tm_scale, gx, r0, fb, pol);
-          tma_load_2d_hint(sdst + 256, tm_scale, gx, ru, fb, pol);
+          tma_load_2d_hint(sdst + kUpS, tm_scale, gx, ru, fb, pol);
           tma_load_2d_hint(zdst, tm_zero, gx, r0, fb, pol);
-          tma_load_2d_hint(zdst + 256, tm_zero, gx, ru, fb, pol);
+          tma_load_2d_hint(zdst + kUpS, tm_zero, gx, ru, fb, pol);
         } else {
           tma_load_2d_hint(cdst, tm_codes, kx, r0, fb, pol);
           tma_load_2d_hint(cdst + L::kCodeBox, tm_codes, kx + 128, r0, fb, pol);
@@ -492,7 +493,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
   // ---- combine the consumer warps' partial sums (ring memory reused) and write bf16 -----------
   __syncthreads();
   constexpr int kCols = 16 * NT + 1;
-  constexpr int kRowsOut = SWIGLU ? 16 : L::BR;
+  constexpr int kRowsOut = SWIGLU ? L::BR / 2 : L::BR;
   constexpr int kOut = kRowsOut * (M1 ? 1 : 16 * NT);  // one row: only MMA column 0 carries data
   float* red = reinterpret_cast<float*>(smem);  // [kConsumers][BR][kCols]
   if (!aborted && warp < kConsumers) {
@@ -521,7 +522,7 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
 #pragma unroll
       for (int w = 0; w < kConsumers; ++w) {
         a0 += red[(w * L::BR + r) * kCols + m];
-        if (SWIGLU) a1 += red[(w * L::BR + 16 + r) * kCols + m];
+        if (SWIGLU) a1 += red[(w * L::BR + kRowsOut + r) * kCols + m];
       }
     }
     part[i][0] = a0;

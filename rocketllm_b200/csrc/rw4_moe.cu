@@ -109,7 +109,7 @@ __global__ void __launch_bounds__(gemv_tma::kThreads)
   if (blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x == 0 && rows > max_rows)
     atomicOr(status, RW4_DEVERR_ROWS);
   if (m0 >= rows) return;  // unrouted expert (or past its rows): no weight is read
-  constexpr int kRowsPerCta = SWIGLU ? 16 : 16 * R;
+  constexpr int kRowsPerCta = SWIGLU ? 8 * R : 16 * R;
   gemv_tma::body<NT, R, S, SWIGLU, 1, false>(&maps.codes[z], &maps.scale[z], &maps.zero[z],
                                              nullptr, nullptr, nullptr, x, beg + m0, 16,
                                              min(16, rows - m0), K,
@@ -122,9 +122,11 @@ int launch_grouped(const void* x, const int32_t* offsets, int E, int64_t max_row
                    const uint8_t* const* packed_e, const void* const* scale_e,
                    const void* const* zero_e, int K, int N, void* y, cudaStream_t stream) {
   using L = gemv_tma::Layout<R, S>;
-  const int box_rows = SWIGLU ? 16 : L::BR;
+  static_assert(L::kBars >= gemv_tma::kConsumers * L::BR * (16 * NT + 1) * 4,
+                "the epilogue's reduction buffer must fit in the ring below the barriers");
+  const int box_rows = SWIGLU ? L::BR / 2 : L::BR;
   const int n_out = SWIGLU ? N / 2 : N;
-  const int rows_per_cta = SWIGLU ? 16 : L::BR;
+  const int rows_per_cta = SWIGLU ? L::BR / 2 : L::BR;
   const int G = K / 64;
   auto kern = moe_grouped_kernel<NT, R, S, SWIGLU>;
   const int smem = L::kX + 1024;
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(gemv_tma::kThreads)
     if (threadIdx.x == 0) atomicOr(status, RW4_DEVERR_SLOT);
     return;
   }
-  constexpr int kRowsPerCta = SWIGLU ? 16 : 16 * R;
+  constexpr int kRowsPerCta = SWIGLU ? 8 * R : 16 * R;
   gemv_tma::body<NT, R, S, SWIGLU, 1, false>(
       &maps.codes[slot], &maps.scale[slot], &maps.zero[slot], nullptr, nullptr, nullptr, x,
       beg + m0, 16,
@@ -224,9 +226,11 @@ int launch_grouped_slots(const rw4_slot_maps* sm, const int32_t* slot_of, const 
                          const int32_t* offsets, int E, int64_t max_rows, void* y,
                          cudaStream_t stream) {
   using L = gemv_tma::Layout<R, S>;
+  static_assert(L::kBars >= gemv_tma::kConsumers * L::BR * (16 * NT + 1) * 4,
+                "the epilogue's reduction buffer must fit in the ring below the barriers");
   const int K = sm->K, N = sm->N;
   const int n_out = SWIGLU ? N / 2 : N;
-  const int rows_per_cta = SWIGLU ? 16 : L::BR;
+  const int rows_per_cta = SWIGLU ? L::BR / 2 : L::BR;
   auto kern = moe_grouped_slots_kernel<NT, R, S, SWIGLU>;
   const int smem = L::kX + 1024;
   static std::atomic<uint64_t> attr_set{0};
@@ -358,13 +362,13 @@ extern "C" int rw4_moe_grouped(const void* x_perm_bf16, const int32_t* offsets, 
   const bool wide = max_rows > 8;
   if (act == 1) {
     if (wide)
-      return launch_grouped<2, 2, 6, true>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,
+      return launch_grouped<2, 4, 4, true>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,
                                            zero_e, (int)K, (int)N, y_perm_bf16, s);
-    return launch_grouped<1, 2, 6, true>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,
+    return launch_grouped<1, 4, 4, true>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,
                                          zero_e, (int)K, (int)N, y_perm_bf16, s);
   }
   if (wide)
-    return launch_grouped<2, 2, 6, false>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,
+    return launch_grouped<2, 4, 4, false>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,
                                           zero_e, (int)K, (int)N, y_perm_bf16, s);
   return launch_grouped<1, 2, 6, false>(x_perm_bf16, offsets, E, max_rows, packed_e, scale_e,
                                         zero_e, (int)K, (int)N, y_perm_bf16, s);
