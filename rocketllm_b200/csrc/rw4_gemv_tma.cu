@@ -305,12 +305,14 @@ bool gemv_tma_supported(int64_t K) { return K % kStageK == 0; }
 // The K split is a function of the weight's shape alone, taken from the one-row launch: every
 // batch size then adds a row's partial sums in the same order, so a row's output has the same bits
 // at every M.  Wider CTAs amortise the per-stage work (x fragment, barrier) over more weight rows
-// and win whenever they still give about 1.5 CTAs per SM (>= 222 of the 296 two-per-SM slots):
+// and win whenever they still give about 1.3 CTAs per SM (>= 192 of the 296 two-per-SM slots;
+// measured: 4096 x 6144 at one row runs 6.5 us as 192 unsplit 32-row CTAs against 8.9 us as 384
+// CTAs with K split in two, and 11.7 against 15.3 us at 16 rows):
 // 64-row CTAs from N >= 14208, then 32-row CTAs, then 16-row CTAs, each with K split over a
 // cluster of up to 4 CTAs (keeping >= 2 stages per CTA) to reach that count.  More than 8
 // activation rows (two MMA column tiles) use at most 32-row CTAs.
 void gemv_tma_policy(int64_t M, int64_t K, int64_t N, int* row_tiles, int* ksplit) {
-  constexpr int64_t kTarget = 222;
+  constexpr int64_t kTarget = 192;
   const int64_t nst = K / kStageK;
   auto ctas = [&](int r) { return (N + 16 * r - 1) / (16 * r); };
   auto split_for = [&](int r) {
