@@ -308,7 +308,7 @@ bool gemv_tma_supported(int64_t K) { return K % kStageK == 0; }
 // and win whenever they still give about 1.3 CTAs per SM (>= 192 of the 296 two-per-SM slots;
 // measured: 4096 x 6144 at one row runs 6.5 us as 192 unsplit 32-row CTAs against 8.9 us as 384
 // CTAs with K split in two, and 11.7 against 15.3 us at 16 rows):
-// 64-row CTAs from N >= 14208, then 32-row CTAs, then 16-row CTAs, each with K split over a
+// 64-row CTAs from N >= 12288, then 32-row CTAs, then 16-row CTAs, each with K split over a
 // cluster of up to 4 CTAs (keeping >= 2 stages per CTA) to reach that count.  More than 8
 // activation rows (two MMA column tiles) use at most 32-row CTAs.
 void gemv_tma_policy(int64_t M, int64_t K, int64_t N, int* row_tiles, int* ksplit) {
