@@ -147,8 +147,9 @@ int rw4_rope_kv(const void* q, const void* k, const void* v, int64_t ld, int32_t
 int rw4_silu_mul(const void* gate_up, int64_t rows, int64_t I, void* out, void* stream);
 /* rw4_linear_rmsnorm_ws: y = x_n . W^T with x_n = rw4_rmsnorm(x, norm_weight, eps) for M <= 64
  *   (a decoder layer's input_layernorm / post_attention_layernorm followed by its first
- *   projection); for two or more rows with K % 512 == 0 the norm runs inside the activation
- *   conversion (no separate launch, the same bits as the two calls), otherwise rw4_rmsnorm first.
+ *   projection); with K % 512 == 0 the norm runs inside the activation conversion (the one-row
+ *   GEMV's prologue, or the x-prep pass of more rows: no separate launch, the same bits as the
+ *   two calls), otherwise rw4_rmsnorm first.
  *   norm_weight bf16 [K], 16-byte aligned; workspace of rw4_linear_rmsnorm_workspace_size bytes,
  *   256-byte aligned. */
 int rw4_linear_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes);

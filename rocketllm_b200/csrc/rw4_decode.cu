@@ -215,11 +215,12 @@ extern "C" int rw4_silu_mul(const void* gate_up, int64_t rows, int64_t I, void* 
 }
 
 namespace {
-// Two or more rows on the TMA path normalise inside the activation conversion; otherwise the rows
-// are normalised by rw4_rmsnorm into the workspace first.
-bool norm_folded(int64_t M, int64_t K) {
+// On the TMA path the rows are normalised inside the activation conversion (the one-row GEMV's
+// own prologue, the x-prep pass, or the decode GEMM's x-prep pass); otherwise rw4_rmsnorm writes
+// the normalised rows into the workspace first.
+bool norm_folded(int64_t K) {
   static const bool no_tma = getenv("RW4_GEMV_NO_TMA") != nullptr;
-  return M >= 2 && !no_tma && rw4::gemv_tma_supported(K);
+  return !no_tma && rw4::gemv_tma_supported(K);
 }
 }  // namespace
 
@@ -230,7 +231,7 @@ extern "C" int rw4_linear_rmsnorm_workspace_size(int64_t M, int64_t K, int64_t N
   if (M < 0 || K <= 0 || N < 0 || K % 64)
     return fail(RW4_EINVAL, "rw4_linear_rmsnorm_workspace_size: bad shape");
   const size_t lin = (M > 0 && N > 0) ? rw4::gemv_workspace(M, K, N) : 0;
-  *bytes = norm_folded(M, K) ? lin : ((lin + 255) & ~size_t(255)) + (size_t)M * K * 2;
+  *bytes = norm_folded(K) ? lin : ((lin + 255) & ~size_t(255)) + (size_t)M * K * 2;
   return RW4_OK;
 }
 
@@ -255,7 +256,7 @@ extern "C" int rw4_linear_rmsnorm_ws(const void* x_bf16, int64_t M, int64_t K,
                 need);
   cudaStream_t s = as_stream(stream);
   const XNorm norm{norm_weight, eps};
-  if (norm_folded(M, K)) {
+  if (norm_folded(K)) {
     // the norm runs inside the activation conversion that the multi-row kernels start with
     if (M >= 49 && gemm_skinny_supported(M, K, N))
       return gemm_skinny_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s,
@@ -263,7 +264,7 @@ extern "C" int rw4_linear_rmsnorm_ws(const void* x_bf16, int64_t M, int64_t K,
     return gemv_tma_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s, 0,
                            workspace, workspace_bytes, nullptr, &norm);
   }
-  // one row (its GEMV converts the row itself) or no TMA path: normalise, then the linear
+  // no TMA path (K % 512 != 0): normalise, then the linear
   const size_t lin = (gemv_workspace(M, K, N) + 255) & ~size_t(255);
   uint8_t* xn = static_cast<uint8_t*>(workspace) + lin;
   st = rw4_rmsnorm(x_bf16, norm_weight, M, K, eps, xn, stream);

@@ -164,5 +164,44 @@ __device__ __forceinline__ void exp_factors(int e, float& p1, float& p2) {
   p2 = __int_as_float((127 + e2) << 23);
 }
 
+// bf16(w * bf16(x * r)) for 8 values: RMSNorm's scaling, rounded as rw4_rmsnorm rounds it.
+__device__ __forceinline__ uint4 norm8(uint4 xv, uint4 wv, float r) {
+  const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float a = __bfloat162float(__float2bfloat16_rn(__uint_as_float(xs[j] << 16) * r));
+    const float b = __bfloat162float(__float2bfloat16_rn(__uint_as_float(xs[j] & 0xFFFF0000u) * r));
+    const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(ws[j] << 16) * a,
+                                                  __uint_as_float(ws[j] & 0xFFFF0000u) * b);
+    o[j] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  return make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+// RMSNorm's 1 / rms of one row of K values, summed in rw4_rmsnorm's order: 256 threads (tid) each
+// take elements tid, tid + 256, ... in turn, then the warp butterfly, then the 8 warps' sums in
+// order.  `part` is 8 floats of shared memory; `sync` a barrier over exactly those 256 threads.
+template <typename Sync>
+__device__ __forceinline__ float rms_scale(const __nv_bfloat16* __restrict__ xr, int K, float eps,
+                                           int tid, float* part, Sync sync) {
+  float ss = 0.f;
+  for (int i = tid; i < K; i += 256) {
+    const float v = __bfloat162float(xr[i]);
+    ss = fmaf(v, v, ss);
+  }
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 16);
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 8);
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 4);
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 2);
+  ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 1);
+  if ((tid & 31) == 0) part[tid >> 5] = ss;
+  sync();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < 8; ++w) tot += part[w];
+  return rsqrtf(tot / (float)K + eps);
+}
+
 }  // namespace frag
 }  // namespace rw4

@@ -46,21 +46,6 @@ using namespace rw4::gemv_tma;
 constexpr int kPrepThreads = 256;
 
 // One CTA per row m < Mpad; rows M..Mpad-1 only zero their side pairs and exponent.
-// bf16(w * bf16(x * r)) for 8 values (RMSNorm's scaling, as rw4_rmsnorm rounds it).
-__device__ __forceinline__ uint4 norm8(uint4 xv, uint4 wv, float r) {
-  const uint32_t xs[4] = {xv.x, xv.y, xv.z, xv.w}, ws[4] = {wv.x, wv.y, wv.z, wv.w};
-  uint32_t o[4];
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float a = __bfloat162float(__float2bfloat16_rn(__uint_as_float(xs[j] << 16) * r));
-    const float b = __bfloat162float(__float2bfloat16_rn(__uint_as_float(xs[j] & 0xFFFF0000u) * r));
-    const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(ws[j] << 16) * a,
-                                                  __uint_as_float(ws[j] & 0xFFFF0000u) * b);
-    o[j] = *reinterpret_cast<const uint32_t*>(&h);
-  }
-  return make_uint4(o[0], o[1], o[2], o[3]);
-}
-
 __global__ void __launch_bounds__(kPrepThreads)
     rw4_xprep_kernel(const __nv_bfloat16* __restrict__ x, int M, int K, int Mpad,
                      uint4* __restrict__ xf, float2* __restrict__ side, int* __restrict__ row_exp,
@@ -80,29 +65,15 @@ __global__ void __launch_bounds__(kPrepThreads)
   const __nv_bfloat16* xr = x + (int64_t)m * K;
   // 0. with a norm: the row's scale, summed in rw4_rmsnorm's order (strided per thread, the warp
   //    butterfly, the warps in order)
+  static_assert(kPrepThreads == 256, "rms_scale sums over 256 threads");
   float r = 1.f;
   if (nw) {
-    float ss = 0.f;
-    for (int i = threadIdx.x; i < K; i += kPrepThreads) {
-      const float v = __bfloat162float(xr[i]);
-      ss = fmaf(v, v, ss);
-    }
-    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 16);
-    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 8);
-    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 4);
-    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 2);
-    ss += __shfl_xor_sync(0xFFFFFFFFu, ss, 1);
     __shared__ float wss[kPrepThreads / 32];
-    if ((threadIdx.x & 31) == 0) wss[threadIdx.x >> 5] = ss;
-    __syncthreads();
-    float tot = 0.f;
-#pragma unroll
-    for (int w = 0; w < kPrepThreads / 32; ++w) tot += wss[w];
-    r = rsqrtf(tot / (float)K + eps);
+    r = frag::rms_scale(xr, K, eps, threadIdx.x, wss, [] { __syncthreads(); });
   }
   auto load8 = [&](int i) {   // 8 values of the (normalised) row starting at 8 i
     const uint4 v = ldg_u4(xr + 8 * i);
-    return nw ? norm8(v, ldg_u4(nw + 8 * i), r) : v;
+    return nw ? frag::norm8(v, ldg_u4(nw + 8 * i), r) : v;
   };
   // 1. largest magnitude
   uint32_t mx = 0;
@@ -151,7 +122,8 @@ __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
                         const __grid_constant__ CUtensorMap tm_side, const int* row_exp,
                         const __nv_bfloat16* __restrict__ x, int bm, int M, int K, int N,
                         __nv_bfloat16* __restrict__ y, unsigned int* status,
-                        const __nv_bfloat16* __restrict__ res) {
+                        const __nv_bfloat16* __restrict__ res,
+                        const __nv_bfloat16* __restrict__ nw, float eps) {
   // batch slices are the fastest grid dimension: the CTAs of all slices of one row tile run
   // together, so the slices after the first find the tile's weights in L2
   const int m0 = blockIdx.x * 16;
@@ -159,7 +131,8 @@ __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
                                               row_exp, x, m0, bm, min(16, M - m0), K,
                                               y + (int64_t)m0 * N, N,
                                               blockIdx.y * Layout<R, S>::BR, N, 0, status,
-                                              res ? res + (int64_t)m0 * N : nullptr);
+                                              res ? res + (int64_t)m0 * N : nullptr,
+                                              XQ ? nw : nullptr, eps);
 }
 
 bool pdl_enabled() {
@@ -216,7 +189,7 @@ bool one_row_in_kernel(int64_t M, int64_t K, int ks) {
 template <int NT, int R, int S, int KS = 1>
 int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, const void* zr,
                int N, void* y, const XPrepLayout& l, uint8_t* ws, cudaStream_t stream,
-               const void* res) {
+               const void* res, const XNorm* norm) {
   using L = Layout<R, S>;
   static_assert(L::kBars >= kConsumers * L::BR * (16 * NT + 1) * 4,
                 "reduction buffer must fit in the ring below the barriers");
@@ -226,6 +199,7 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   const int bm = M < 16 ? M : 16;
   if (bm > 8 * NT) return fail(RW4_EINVAL, "gemv_tma: %d activation rows for NT=%d", M, NT);
   const bool xq = NT == 1 && one_row_in_kernel(M, K, KS);
+  if (norm && !xq) return fail(RW4_EINVAL, "gemv_tma: the norm belongs to the x-prep pass here");
   int st = make_tensor_map_2d(&tc, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K / 2, K / 2, L::BR,
                               128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st == RW4_OK)
@@ -290,7 +264,10 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
                                        reinterpret_cast<const int*>(ws + l.row_exp),
                                        static_cast<const __nv_bfloat16*>(x), bm, M, K, N,
                                        static_cast<__nv_bfloat16*>(y), status,
-                                       static_cast<const __nv_bfloat16*>(res));
+                                       static_cast<const __nv_bfloat16*>(res),
+                                       norm ? static_cast<const __nv_bfloat16*>(norm->weight)
+                                            : nullptr,
+                                       norm ? norm->eps : 0.f);
   if (err != cudaSuccess) return cuda_status(err, "rw4 gemv_tma launch");
   return launch_status("rw4 gemv_tma launch");
 }
@@ -361,9 +338,10 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
   if (row_tiles == 4 && (M > 8 || ks > 1)) row_tiles = 2;
   const XPrepLayout l = xprep_layout(M, K);
   uint8_t* w = static_cast<uint8_t*>(ws);
-  if (norm && one_row_in_kernel(M, K, ks))
-    return fail(RW4_EINVAL, "gemv_tma: a normalised one-row call takes the x-prep path only");
-  if (!one_row_in_kernel(M, K, ks)) {
+  // the norm runs in the activation conversion: the GEMV's own for one row, else the x-prep pass
+  const bool xq = one_row_in_kernel(M, K, ks);
+  const XNorm* kn = xq ? norm : nullptr;
+  if (!xq) {
     if (!ws || ws_bytes < l.bytes)
       return fail(RW4_EINVAL, "rw4_linear: the GEMV needs a %zu-byte workspace (got %zu)",
                   l.bytes, ws_bytes);
@@ -373,25 +351,25 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
     if (st != RW4_OK) return st;
   }
   if (M <= 8) {
-    if (row_tiles == 4) return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+    if (row_tiles == 4) return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
     if (row_tiles == 2) {
-      if (ks == 4) return launch_tma<1, 2, 6, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
-      if (ks == 2) return launch_tma<1, 2, 6, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
-      return launch_tma<1, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+      if (ks == 4) return launch_tma<1, 2, 6, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+      if (ks == 2) return launch_tma<1, 2, 6, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+      return launch_tma<1, 2, 6>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
     }
-    if (ks == 4) return launch_tma<1, 1, 8, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
-    if (ks == 2) return launch_tma<1, 1, 8, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
-    return launch_tma<1, 1, 8>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+    if (ks == 4) return launch_tma<1, 1, 8, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+    if (ks == 2) return launch_tma<1, 1, 8, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+    return launch_tma<1, 1, 8>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
   }
   // 9..16 activation rows per slice: 16 KB of x per stage, so shallower rings keep two CTAs per SM
   if (row_tiles >= 2) {
-    if (ks == 4) return launch_tma<2, 2, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
-    if (ks == 2) return launch_tma<2, 2, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
-    return launch_tma<2, 2, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+    if (ks == 4) return launch_tma<2, 2, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+    if (ks == 2) return launch_tma<2, 2, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+    return launch_tma<2, 2, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
   }
-  if (ks == 4) return launch_tma<2, 1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
-  if (ks == 2) return launch_tma<2, 1, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
-  return launch_tma<2, 1, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res);
+  if (ks == 4) return launch_tma<2, 1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+  if (ks == 2) return launch_tma<2, 1, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+  return launch_tma<2, 1, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
 }
 
 }  // namespace rw4

@@ -142,6 +142,9 @@ __device__ __forceinline__ void x_frag_smem(uint32_t a, bool valid, uint32_t (&b
 // into fp16 fragments and (sum, -offset) pairs in shared memory -- with the same helpers, in the
 // same order, as the x-prep kernel, so the output has the same bits as the XP path's.  x is the
 // bf16 activations (row x_row0, stride K).
+// nw, eps (XQ only; nw may be null): the row is first normalised as rw4_rmsnorm does it --
+// bf16(nw * bf16(x * r)), r from the row's mean square summed in that kernel's order -- so the
+// output has the bits of rw4_rmsnorm followed by the GEMV.
 // y: output rows (stride ldy); res (XP / XQ only, may be null): rows added to the output in the
 // model's bf16 order, bf16(bf16(x . W^T) + res) -- a decoder layer's residual connection.
 // Plain: writes y[m, r0 + r] for r0 + r < n_out.  SWIGLU: writes y[m, r0 + r] for r0 + r < n_out
@@ -156,7 +159,9 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
                                      int Ml, int K,
                                      __nv_bfloat16* __restrict__ y, int64_t ldy, int r0,
                                      int n_out, int up_offset, unsigned int* status,
-                                     const __nv_bfloat16* __restrict__ res = nullptr) {
+                                     const __nv_bfloat16* __restrict__ res = nullptr,
+                                     const __nv_bfloat16* __restrict__ nw = nullptr,
+                                     float eps = 0.f) {
   using namespace rw4::frag;
   using L = Layout<R, S>;
   static_assert(!SWIGLU || R % 2 == 0, "the SwiGLU epilogue pairs gate tiles with up tiles");
@@ -302,6 +307,15 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
       const __nv_bfloat16* xr = x + (int64_t)x_row0 * K;
       const __nv_bfloat16* xk = xr + (int64_t)s_begin * kStageK;
       const int chunks = nstages * (kStageK / 16);
+      static_assert(kConsumers == 8, "rms_scale sums over 256 threads");
+      float r = 1.f;
+      if (nw) {
+        __shared__ float wss[kConsumers];
+        r = rms_scale(xr, K, eps, tid, wss, [] {
+          asm volatile("bar.sync 1, %0;" ::"n"(kConsumers * 32) : "memory");
+        });
+      }
+      const __nv_bfloat16* nwk = nw ? nw + (int64_t)s_begin * kStageK : nullptr;
       uint4 lo[kPer], hi[kPer];
       uint32_t mx = 0;
 #pragma unroll
@@ -312,13 +326,21 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
         if (c < chunks) {
           lo[i] = ldg_u4(xk + 16 * c);
           hi[i] = ldg_u4(xk + 16 * c + 8);
+          if (nw) {
+            lo[i] = norm8(lo[i], ldg_u4(nwk + 16 * c), r);
+            hi[i] = norm8(hi[i], ldg_u4(nwk + 16 * c + 8), r);
+          }
           mx = max(mx, max(absmax8(lo[i]), absmax8(hi[i])));
         }
       }
       if (KS > 1) {
         const int k0 = s_begin * kStageK, k1 = (s_begin + nstages) * kStageK;
         for (int i = tid; i < K / 8; i += kConsumers * 32)
-          if (8 * i < k0 || 8 * i >= k1) mx = max(mx, absmax8(ldg_u4(xr + 8 * i)));
+          if (8 * i < k0 || 8 * i >= k1) {
+            uint4 v = ldg_u4(xr + 8 * i);
+            if (nw) v = norm8(v, ldg_u4(nw + 8 * i), r);
+            mx = max(mx, absmax8(v));
+          }
       }
       mx = __reduce_max_sync(0xFFFFFFFFu, mx);
       __shared__ uint32_t wmax[kConsumers];

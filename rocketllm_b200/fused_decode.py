@@ -10,8 +10,8 @@ ten launches per layer (attention's two and the conversion passes included), eac
 modules' bf16 rounding sequence:
 
     rw4_linear_rmsnorm_ws             input_layernorm, then q_proj, k_proj, v_proj as one GEMV
-                                      over the concatenated weight (from two rows on, the norm
-                                      runs inside the GEMV's activation conversion)
+                                      over the concatenated weight (the norm runs inside the
+                                      GEMV's activation conversion)
     rw4_rope_kv                       apply_rotary_pos_emb + StaticCache.update (device position)
     SDPA with enable_gqa              attention over the static cache, no key / value copies
     rw4_linear_residual_ws            o_proj + residual add in the GEMV epilogue
@@ -189,8 +189,8 @@ class FusedDecoder(GraphedDecoder):
         return out
 
     def _lin_norm(self, x, weight, eps, w, out):
-        """``out = rmsnorm(x) . W^T``: for two or more rows the norm runs inside the activation
-        conversion (one launch fewer), for one row it is rw4_rmsnorm then the one-row GEMV."""
+        """``out = rmsnorm(x) . W^T``: the norm runs inside the projection's activation
+        conversion (the one-row GEMV's prologue, or the x-prep pass of a batch): one launch."""
         m, k = x.shape
         _lib.call("rw4_linear_rmsnorm_ws", x.data_ptr(), m, k, weight.data_ptr(), float(eps),
                   w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(), w[0].shape[0], 64,

@@ -214,12 +214,17 @@ def test_linear_residual_epilogue(cuda, m, k, n):
     assert kernels.device_status() == 0
 
 
-@pytest.mark.parametrize("m,k,n", [(1, 4096, 6144), (2, 4096, 6144), (16, 2048, 11264),
-                                   (40, 4096, 4096), (56, 4096, 12288), (3, 1600, 1024)])
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 6144), (1, 4096, 1024), (1, 14336, 4096),
+                                   (1, 4096, 28672), (1, 17408, 12288), (2, 4096, 6144),
+                                   (16, 2048, 11264), (40, 4096, 4096), (56, 4096, 12288),
+                                   (3, 1600, 1024), (1, 1600, 1024)])
 def test_linear_rmsnorm_matches_norm_then_linear(cuda, m, k, n):
     """rw4_linear_rmsnorm_ws (a layer norm folded into the projection's activation conversion)
     gives the bits of rw4_rmsnorm followed by the projection: the same rounding sequence and the
-    same summation order for the row's mean square.  (1600: K % 512 != 0, normalised first.)"""
+    same summation order for the row's mean square.  One row: the GEMV's own prologue normalises
+    (4096 x 1024 splits K over 4 CTAs, each normalising the whole row for its maximum); 17408 x
+    12288: 34 KB of row in one CTA, beyond the prologue's 32 KB, so through the x-prep pass.  (1600: K % 512 != 0, normalised
+    first.)"""
     import ctypes
     from rocketllm_b200 import _lib
     w = make_weight(n, k, device=cuda, seed=41)
