@@ -157,6 +157,20 @@ int rw4_linear_rmsnorm_ws(const void* x_bf16, int64_t M, int64_t K, const void* 
                           float eps, const uint8_t* packed, const void* scale_f16,
                           const void* zero_f16, int64_t N, int32_t group, void* y_bf16,
                           void* workspace, size_t workspace_bytes, void* stream);
+/* rw4_linear_rmsnorm_swiglu_ws: y[M, N/2] = act_fn(x_n . W_gate^T) * (x_n . W_up^T), x_n as in
+ *   rw4_linear_rmsnorm_ws, for a [gate; up] weight of N rows (gate rows first): a Llama MLP's
+ *   post_attention_layernorm, gate_proj, up_proj and act_fn(gate) * up (LlamaMLP.forward,
+ *   transformers models/llama/modeling_llama.py), the bits of rw4_linear_rmsnorm_ws followed by
+ *   rw4_silu_mul.  One launch where the GEMV's launch shape for the weight has no K split and the
+ *   call takes the GEMV (K % 512 == 0; M <= 48, or no decode-GEMM shape); otherwise those two
+ *   calls through the workspace (rw4_linear_rmsnorm_swiglu_workspace_size bytes, 256-byte
+ *   aligned). */
+int rw4_linear_rmsnorm_swiglu_workspace_size(int64_t M, int64_t K, int64_t N, size_t* bytes);
+int rw4_linear_rmsnorm_swiglu_ws(const void* x_bf16, int64_t M, int64_t K,
+                                 const void* norm_weight, float eps, const uint8_t* packed,
+                                 const void* scale_f16, const void* zero_f16, int64_t N,
+                                 int32_t group, void* y_bf16, void* workspace,
+                                 size_t workspace_bytes, void* stream);
 int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                            const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
                            const void* residual, void* y_bf16, void* workspace,

@@ -62,6 +62,12 @@ SIGNATURES = {
     "rw4_linear_rmsnorm_ws": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, ctypes.c_float,
                                              _c_void_p, _c_void_p, _c_void_p, _i64, _i32,
                                              _c_void_p, _c_void_p, _size, _c_void_p]),
+    "rw4_linear_rmsnorm_swiglu_workspace_size": (ctypes.c_int, [_i64, _i64, _i64,
+                                                                ctypes.POINTER(_size)]),
+    "rw4_linear_rmsnorm_swiglu_ws": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p,
+                                                    ctypes.c_float, _c_void_p, _c_void_p,
+                                                    _c_void_p, _i64, _i32, _c_void_p, _c_void_p,
+                                                    _size, _c_void_p]),
     "rw4_linear_residual_ws": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p,
                                               _c_void_p, _i64, _i32, _c_void_p, _c_void_p,
                                               _c_void_p, _size, _c_void_p]),

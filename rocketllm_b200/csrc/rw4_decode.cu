@@ -33,6 +33,10 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
                     const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
                     size_t ws_bytes, const void* res, const XNorm* norm = nullptr);
 size_t gemv_workspace(int64_t M, int64_t K, int64_t N);
+bool gemv_tma_swiglu_supported(int64_t M, int64_t K, int64_t N);
+int gemv_tma_swiglu_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq,
+                           const void* sc, const void* zr, int64_t N, void* y, cudaStream_t s,
+                           void* ws, size_t ws_bytes, const XNorm* norm);
 bool gemm_skinny_supported(int64_t M, int64_t K, int64_t N);
 int gemm_skinny_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
                        const void* zr, int64_t N, void* y, cudaStream_t s, void* ws,
@@ -271,6 +275,70 @@ extern "C" int rw4_linear_rmsnorm_ws(const void* x_bf16, int64_t M, int64_t K,
   if (st != RW4_OK) return st;
   return rw4_linear_ws(xn, M, K, packed, scale_f16, zero_f16, N, group, y_bf16, 0, workspace,
                        lin, stream);
+}
+
+// rw4_linear_rmsnorm_swiglu_ws in one launch: the TMA GEMV path (as rw4_linear_rmsnorm_ws would
+// take it) with a launch shape the SwiGLU epilogue pairs; otherwise two calls through the
+// workspace.
+namespace {
+bool swiglu_one_launch(int64_t M, int64_t K, int64_t N) {
+  using namespace rw4;
+  return norm_folded(K) && !(M >= 49 && gemm_skinny_supported(M, K, N)) &&
+         gemv_tma_swiglu_supported(M, K, N);
+}
+}  // namespace
+
+extern "C" int rw4_linear_rmsnorm_swiglu_workspace_size(int64_t M, int64_t K, int64_t N,
+                                                        size_t* bytes) {
+  if (!bytes) return fail(RW4_EINVAL, "rw4_linear_rmsnorm_swiglu_workspace_size: null output");
+  if (N % 2) return fail(RW4_EINVAL, "rw4_linear_rmsnorm_swiglu_workspace_size: odd N");
+  size_t lin = 0;
+  const int st = rw4_linear_rmsnorm_workspace_size(M, K, N, &lin);
+  if (st != RW4_OK) return st;
+  *bytes = (M == 0 || N == 0 || swiglu_one_launch(M, K, N))
+               ? lin
+               : ((lin + 255) & ~size_t(255)) + (size_t)M * N * 2;
+  return RW4_OK;
+}
+
+extern "C" int rw4_linear_rmsnorm_swiglu_ws(const void* x_bf16, int64_t M, int64_t K,
+                                            const void* norm_weight, float eps,
+                                            const uint8_t* packed, const void* scale_f16,
+                                            const void* zero_f16, int64_t N, int32_t group,
+                                            void* y_bf16, void* workspace,
+                                            size_t workspace_bytes, void* stream) {
+  using namespace rw4;
+  int st = check_linear_args("rw4_linear_rmsnorm_swiglu_ws", x_bf16, M, K, packed, scale_f16,
+                             zero_f16, N, group, y_bf16);
+  if (st != RW4_OK || M == 0 || N == 0) return st;
+  if (N % 2) return fail(RW4_EINVAL, "rw4_linear_rmsnorm_swiglu_ws: N=%lld is not [gate; up]",
+                         (long long)N);
+  if (!norm_weight || !aligned(norm_weight, 16))
+    return fail(RW4_EINVAL, "rw4_linear_rmsnorm_swiglu_ws: norm weight null or not 16-byte aligned");
+  if (M > 64)
+    return fail(RW4_EINVAL, "rw4_linear_rmsnorm_swiglu_ws: M=%lld; at most 64 rows", (long long)M);
+  size_t need = 0;
+  st = rw4_linear_rmsnorm_swiglu_workspace_size(M, K, N, &need);
+  if (st != RW4_OK) return st;
+  if (need && (!workspace || workspace_bytes < need || !aligned(workspace, 256)))
+    return fail(RW4_EINVAL,
+                "rw4_linear_rmsnorm_swiglu_ws: needs a 256-byte aligned %zu-byte workspace", need);
+  cudaStream_t s = as_stream(stream);
+  if (swiglu_one_launch(M, K, N)) {
+    const XNorm norm{norm_weight, eps};
+    return gemv_tma_swiglu_launch(x_bf16, M, K, packed, scale_f16, zero_f16, N, y_bf16, s,
+                                  workspace, workspace_bytes, &norm);
+  }
+  // two calls: [gate | up] into the workspace, then act_fn(gate) * up
+  size_t lin = 0;
+  st = rw4_linear_rmsnorm_workspace_size(M, K, N, &lin);
+  if (st != RW4_OK) return st;
+  lin = (lin + 255) & ~size_t(255);
+  uint8_t* gu = static_cast<uint8_t*>(workspace) + lin;
+  st = rw4_linear_rmsnorm_ws(x_bf16, M, K, norm_weight, eps, packed, scale_f16, zero_f16, N, group,
+                             gu, workspace, lin, stream);
+  if (st != RW4_OK) return st;
+  return rw4_silu_mul(gu, M, N / 2, y_bf16, stream);
 }
 
 extern "C" int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K,

@@ -112,8 +112,10 @@ __global__ void __launch_bounds__(kPrepThreads)
 // schedule (16 consumer warps per SM sharing the ALU pipe with the producers).  KS > 1 splits K
 // over a (1, 1, KS) thread-block cluster (grid.z = KS) reduced through distributed shared memory.
 // M1: one activation row.  XQ (with M1): the CTA converts that row itself (no x-prep launch, no
-// workspace); otherwise the x-prep output arrives through the TMA ring.
-template <int NT, int R, int S, int KS, bool M1, bool XQ>
+// workspace); otherwise the x-prep output arrives through the TMA ring.  SW: W is [gate; up] (N
+// rows, gate first) and y [M, N / 2] = act_fn(gate) * up; a CTA takes BR / 2 gate rows and the
+// matching up rows.
+template <int NT, int R, int S, int KS, bool M1, bool XQ, bool SW = false>
 __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
     rw4_gemv_tma_kernel(const __grid_constant__ CUtensorMap tm_codes,
                         const __grid_constant__ CUtensorMap tm_scale,
@@ -127,12 +129,15 @@ __global__ void __cluster_dims__(1, 1, KS) __launch_bounds__(kThreads, 2)
   // batch slices are the fastest grid dimension: the CTAs of all slices of one row tile run
   // together, so the slices after the first find the tile's weights in L2
   const int m0 = blockIdx.x * 16;
-  body<NT, R, S, false, KS, !XQ, M1, !XQ, XQ>(&tm_codes, &tm_scale, &tm_zero, &tm_x, &tm_side,
-                                              row_exp, x, m0, bm, min(16, M - m0), K,
-                                              y + (int64_t)m0 * N, N,
-                                              blockIdx.y * Layout<R, S>::BR, N, 0, status,
-                                              res ? res + (int64_t)m0 * N : nullptr,
-                                              XQ ? nw : nullptr, eps);
+  const int n_out = SW ? N / 2 : N;   // output columns (= the row stride of y)
+  body<NT, R, S, SW, KS, !XQ, M1, !XQ, XQ>(&tm_codes, &tm_scale, &tm_zero, &tm_x, &tm_side,
+                                           row_exp, x, m0, bm, min(16, M - m0), K,
+                                           y + (int64_t)m0 * n_out, n_out,
+                                           blockIdx.y * (SW ? Layout<R, S>::BR / 2
+                                                            : Layout<R, S>::BR),
+                                           n_out, SW ? N / 2 : 0, status,
+                                           res ? res + (int64_t)m0 * n_out : nullptr,
+                                           XQ ? nw : nullptr, eps);
 }
 
 bool pdl_enabled() {
@@ -186,13 +191,17 @@ bool one_row_in_kernel(int64_t M, int64_t K, int ks) {
   return M == 1 && ((K / kStageK) + ks - 1) / ks <= Layout<1, 1>::kXQMaxStages;
 }
 
-template <int NT, int R, int S, int KS = 1>
+template <int NT, int R, int S, int KS = 1, bool SW = false>
 int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, const void* zr,
                int N, void* y, const XPrepLayout& l, uint8_t* ws, cudaStream_t stream,
                const void* res, const XNorm* norm) {
   using L = Layout<R, S>;
   static_assert(L::kBars >= kConsumers * L::BR * (16 * NT + 1) * 4,
                 "reduction buffer must fit in the ring below the barriers");
+  static_assert(!SW || R % 2 == 0, "SwiGLU pairs gate and up row tiles");
+  if (SW && (N % 2 || res)) return fail(RW4_EINVAL, "gemv_tma: SwiGLU takes [gate; up], no residual");
+  // weight rows per box and per CTA: BR, or BR / 2 gate rows + BR / 2 up rows
+  const int box_rows = SW ? L::BR / 2 : L::BR;
   CUtensorMap tc, ts, tz, tx, tside;
   const int G = K / 64;
   // activation rows per slice: the whole batch for M <= 8 (NT = 1), 16-row slices above
@@ -200,14 +209,14 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   if (bm > 8 * NT) return fail(RW4_EINVAL, "gemv_tma: %d activation rows for NT=%d", M, NT);
   const bool xq = NT == 1 && one_row_in_kernel(M, K, KS);
   if (norm && !xq) return fail(RW4_EINVAL, "gemv_tma: the norm belongs to the x-prep pass here");
-  int st = make_tensor_map_2d(&tc, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K / 2, K / 2, L::BR,
-                              128, CU_TENSOR_MAP_SWIZZLE_128B);
+  int st = make_tensor_map_2d(&tc, wq, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, N, K / 2, K / 2,
+                              box_rows, 128, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st == RW4_OK)
     st = make_tensor_map_2d(&ts, sc, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, N, G, (uint64_t)G * 2,
-                            L::BR, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+                            box_rows, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st == RW4_OK)
     st = make_tensor_map_2d(&tz, zr, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, N, G, (uint64_t)G * 2,
-                            L::BR, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
+                            box_rows, 8, CU_TENSOR_MAP_SWIZZLE_NONE);
   if (st != RW4_OK) return st;
   if (xq) {
     tx = tz;  // not read by the in-kernel conversion
@@ -223,9 +232,9 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   }
   const bool m1 = NT == 1 && M == 1;
   const int variant = xq ? 2 : m1 ? 1 : 0;
-  auto kern = xq ? rw4_gemv_tma_kernel<NT, R, S, KS, NT == 1, NT == 1>
-              : m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, NT == 1, false>
-                   : rw4_gemv_tma_kernel<NT, R, S, KS, false, false>;
+  auto kern = xq ? rw4_gemv_tma_kernel<NT, R, S, KS, NT == 1, NT == 1, SW>
+              : m1 ? rw4_gemv_tma_kernel<NT, R, S, KS, NT == 1, false, SW>
+                   : rw4_gemv_tma_kernel<NT, R, S, KS, false, false, SW>;
   // The dynamic shared memory limit is a per-device function attribute: set it once per device
   // and kernel variant (this function is instantiated once per launch shape).
   static std::atomic<uint32_t> attr_set[3];
@@ -241,7 +250,7 @@ int launch_tma(const void* x, int M, int K, const uint8_t* wq, const void* sc, c
   }
   unsigned int* status = device_status_ptr();
   if (!status) return fail(RW4_ECUDA, "gemv_tma: device status word unavailable");
-  const int64_t tiles = (N + L::BR - 1) / L::BR;
+  const int64_t tiles = ((SW ? N / 2 : N) + box_rows - 1) / box_rows;
   if (tiles > 65535) return fail(RW4_EINVAL, "gemv_tma: N=%d needs more than 65535 row tiles", N);
   dim3 grid((M + 15) / 16, (unsigned)tiles, KS);
   // Programmatic dependent launch: this grid may start while the kernel before it (the x-prep pass,
@@ -320,36 +329,50 @@ size_t gemv_tma_workspace(int64_t M, int64_t K, int64_t N) {
   return one_row_in_kernel(M, K, ks) ? 0 : xprep_layout(M, K).bytes;
 }
 
-int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
-                    const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
-                    size_t ws_bytes, const void* res, const XNorm* norm) {
-  const int Mi = (int)M, Ki = (int)K, Ni = (int)N;
+// The launch shape a call takes: the measured policy, unless RW4_GEMV_ROW_TILES (row_tiles) or
+// RW4_GEMV_KSPLIT force one (measurements only: a forced K split changes the order in which a
+// row's sums are added).
+static void launch_shape(int64_t M, int64_t K, int64_t N, int row_tiles, int* rt, int* ks) {
   static const int forced_ks = [] {
     const char* e = getenv("RW4_GEMV_KSPLIT");
     return e ? atoi(e) : 0;
   }();
-  if ((M + 15) / 16 > 65535) return fail(RW4_EINVAL, "rw4_linear: M=%lld too large", (long long)M);
-  int policy_rt = 1, ks = 1;
-  gemv_tma_policy(M, K, N, &policy_rt, &ks);
-  // RW4_GEMV_ROW_TILES / RW4_GEMV_KSPLIT force a launch shape (measurements only: a forced K
-  // split changes the order in which a row's sums are added)
+  int policy_rt = 1;
+  gemv_tma_policy(M, K, N, &policy_rt, ks);
   if (row_tiles != 1 && row_tiles != 2 && row_tiles != 4) row_tiles = policy_rt;
-  if (forced_ks == 1 || forced_ks == 2 || forced_ks == 4) ks = forced_ks;
-  if (row_tiles == 4 && (M > 8 || ks > 1)) row_tiles = 2;
+  if (forced_ks == 1 || forced_ks == 2 || forced_ks == 4) *ks = forced_ks;
+  if (row_tiles == 4 && (M > 8 || *ks > 1)) row_tiles = 2;
+  *rt = row_tiles;
+}
+
+// Everything before the GEMV launch itself: the x-prep pass (with the norm) unless the one-row
+// kernel converts x itself; *kn is the norm that kernel applies.
+static int prepare_x(const void* x, int64_t M, int64_t K, int ks, void* ws, size_t ws_bytes,
+                     cudaStream_t s, const XNorm* norm, const XNorm** kn) {
+  if ((M + 15) / 16 > 65535) return fail(RW4_EINVAL, "rw4_linear: M=%lld too large", (long long)M);
+  const bool xq = one_row_in_kernel(M, K, ks);
+  *kn = xq ? norm : nullptr;
+  if (xq) return RW4_OK;
+  const XPrepLayout l = xprep_layout(M, K);
+  if (!ws || ws_bytes < l.bytes)
+    return fail(RW4_EINVAL, "rw4_linear: the GEMV needs a %zu-byte workspace (got %zu)", l.bytes,
+                ws_bytes);
+  if (!aligned(ws, 256)) return fail(RW4_EINVAL, "rw4_linear: workspace must be 256-byte aligned");
+  return launch_xprep(x, (int)M, (int)K, l, static_cast<uint8_t*>(ws), s, norm);
+}
+
+int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, const void* sc,
+                    const void* zr, int64_t N, void* y, cudaStream_t s, int row_tiles, void* ws,
+                    size_t ws_bytes, const void* res, const XNorm* norm) {
+  const int Mi = (int)M, Ki = (int)K, Ni = (int)N;
+  int ks = 1;
+  launch_shape(M, K, N, row_tiles, &row_tiles, &ks);
+  // the norm runs in the activation conversion: the GEMV's own for one row, else the x-prep pass
+  const XNorm* kn = nullptr;
+  const int pst = prepare_x(x, M, K, ks, ws, ws_bytes, s, norm, &kn);
+  if (pst != RW4_OK) return pst;
   const XPrepLayout l = xprep_layout(M, K);
   uint8_t* w = static_cast<uint8_t*>(ws);
-  // the norm runs in the activation conversion: the GEMV's own for one row, else the x-prep pass
-  const bool xq = one_row_in_kernel(M, K, ks);
-  const XNorm* kn = xq ? norm : nullptr;
-  if (!xq) {
-    if (!ws || ws_bytes < l.bytes)
-      return fail(RW4_EINVAL, "rw4_linear: the GEMV needs a %zu-byte workspace (got %zu)",
-                  l.bytes, ws_bytes);
-    if (!aligned(ws, 256))
-      return fail(RW4_EINVAL, "rw4_linear: workspace must be 256-byte aligned");
-    const int st = launch_xprep(x, Mi, Ki, l, w, s, norm);
-    if (st != RW4_OK) return st;
-  }
   if (M <= 8) {
     if (row_tiles == 4) return launch_tma<1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
     if (row_tiles == 2) {
@@ -370,6 +393,41 @@ int gemv_tma_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq, cons
   if (ks == 4) return launch_tma<2, 1, 4, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
   if (ks == 2) return launch_tma<2, 1, 4, 2>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
   return launch_tma<2, 1, 4>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, res, kn);
+}
+
+// SwiGLU form: y[M, N / 2] = act_fn(x W_gate^T) * (x W_up^T) for W = [gate; up] (N rows, gate
+// first), in one launch.  It takes the plain call's launch shape for the N-row weight, so gate
+// and up get the plain GEMV's bits, and the epilogue rounds as rw4_silu_mul does; supported where
+// that shape has no K split (the 64-row shape becomes 32 gate + 32 up rows, the 16-row one 8 + 8
+// would not pair, so 16-row shapes run as 32-row ones: a row's sums do not depend on the CTA's
+// height).
+bool gemv_tma_swiglu_supported(int64_t M, int64_t K, int64_t N) {
+  if (M < 1 || M > 64 || N < 2 || N % 2 || !gemv_tma_supported(K)) return false;
+  int rt = 1, ks = 1;
+  launch_shape(M, K, N, 0, &rt, &ks);
+  return ks == 1;
+}
+
+int gemv_tma_swiglu_launch(const void* x, int64_t M, int64_t K, const uint8_t* wq,
+                           const void* sc, const void* zr, int64_t N, void* y, cudaStream_t s,
+                           void* ws, size_t ws_bytes, const XNorm* norm) {
+  if (!gemv_tma_swiglu_supported(M, K, N))
+    return fail(RW4_EUNSUPPORTED, "gemv_tma: no one-launch SwiGLU for M=%lld K=%lld N=%lld",
+                (long long)M, (long long)K, (long long)N);
+  const int Mi = (int)M, Ki = (int)K, Ni = (int)N;
+  int rt = 1, ks = 1;
+  launch_shape(M, K, N, 0, &rt, &ks);
+  const XNorm* kn = nullptr;
+  const int pst = prepare_x(x, M, K, ks, ws, ws_bytes, s, norm, &kn);
+  if (pst != RW4_OK) return pst;
+  const XPrepLayout l = xprep_layout(M, K);
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  if (M <= 8) {
+    if (rt == 4)
+      return launch_tma<1, 4, 4, 1, true>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, nullptr, kn);
+    return launch_tma<1, 2, 6, 1, true>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, nullptr, kn);
+  }
+  return launch_tma<2, 2, 4, 1, true>(x, Mi, Ki, wq, sc, zr, Ni, y, l, w, s, nullptr, kn);
 }
 
 }  // namespace rw4

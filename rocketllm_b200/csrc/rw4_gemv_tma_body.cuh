@@ -148,7 +148,8 @@ __device__ __forceinline__ void x_frag_smem(uint32_t a, bool valid, uint32_t (&b
 // y: output rows (stride ldy); res (XP / XQ only, may be null): rows added to the output in the
 // model's bf16 order, bf16(bf16(x . W^T) + res) -- a decoder layer's residual connection.
 // Plain: writes y[m, r0 + r] for r0 + r < n_out.  SWIGLU: writes y[m, r0 + r] for r0 + r < n_out
-// (= I) from weight rows r0 + r (gate) and r0 + I + r (up).
+// (= I) from weight rows r0 + r (gate) and r0 + up_offset + r (up): bf16(bf16(silu(bf16(gate))) *
+// bf16(up)), the bits of the plain GEMV over both followed by rw4_silu_mul.
 // M1: the launch has exactly one activation row (NT == 1, M == 1).
 template <int NT, int R, int S, bool SWIGLU, int KS = 1, bool XT = true, bool M1 = false,
           bool XP = false, bool XQ = false>
@@ -166,8 +167,8 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
   using L = Layout<R, S>;
   static_assert(!SWIGLU || R % 2 == 0, "the SwiGLU epilogue pairs gate tiles with up tiles");
   static_assert(!M1 || NT == 1, "one activation row fits one MMA column tile");
-  static_assert(!XP || (XT && !SWIGLU), "the pre-converted activations come through the ring");
-  static_assert(!XQ || (M1 && !XT && !XP && !SWIGLU), "XQ converts one activation row");
+  static_assert(!XP || XT, "the pre-converted activations come through the ring");
+  static_assert(!XQ || (M1 && !XT && !XP), "XQ converts one activation row");
   if (M1) Ml = min(Ml, 1);  // a one-row launch never computes or stores a second row
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -590,8 +591,16 @@ __device__ __forceinline__ void body(const CUtensorMap* tm_codes, const CUtensor
     if (o < kOut && n < n_out && m < Ml) {
       float v;
       if (SWIGLU) {
-        const float gb = __bfloat162float(__float2bfloat16_rn(part[i][0]));
-        const float ub = __bfloat162float(__float2bfloat16_rn(part[i][SWIGLU ? 1 : 0]));
+        // gate and up as the plain GEMV rounds them (after the row's 2^-e on the fp16 paths),
+        // then act_fn(gate) * up as the model rounds it
+        float gv = part[i][0], uv = part[i][SWIGLU ? 1 : 0];
+        if (XP || XQ) {
+          const int e = XQ ? xq_e : row_exp[x_row0 + m];
+          gv = ldexpf(gv, -e);
+          uv = ldexpf(uv, -e);
+        }
+        const float gb = __bfloat162float(__float2bfloat16_rn(gv));
+        const float ub = __bfloat162float(__float2bfloat16_rn(uv));
         const float act = __bfloat162float(__float2bfloat16_rn(gb / (1.f + expf(-gb))));
         v = act * ub;
       } else if (XP || XQ) {

@@ -6,8 +6,8 @@ RMSNorm as six elementwise kernels, q / k / v as three GEMVs, the rotary embeddi
 mul / add kernels, ``index_copy_`` into the static cache, the grouped-query key / value copies
 (``repeat_kv``), attention, o_proj, the residual add, RMSNorm again, gate, up, SiLU, the product,
 down, the residual add (transformers ``models/llama/modeling_llama.py``).  The step here is about
-ten launches per layer (attention's two and the conversion passes included), each reproducing the
-modules' bf16 rounding sequence:
+seven launches per layer at batch 1 (attention's two included; from two rows on each GEMV adds
+its activation-conversion pass), each reproducing the modules' bf16 rounding sequence:
 
     rw4_linear_rmsnorm_ws             input_layernorm, then q_proj, k_proj, v_proj as one GEMV
                                       over the concatenated weight (the norm runs inside the
@@ -15,9 +15,9 @@ modules' bf16 rounding sequence:
     rw4_rope_kv                       apply_rotary_pos_emb + StaticCache.update (device position)
     SDPA with enable_gqa              attention over the static cache, no key / value copies
     rw4_linear_residual_ws            o_proj + residual add in the GEMV epilogue
-    rw4_linear_rmsnorm_ws             post_attention_layernorm, then gate_proj, up_proj as one
-                                      GEMV over the concatenated weight
-    rw4_silu_mul                      act_fn(gate) * up
+    rw4_linear_rmsnorm_swiglu_ws      post_attention_layernorm, then gate_proj, up_proj as one
+                                      GEMV over the concatenated weight, act_fn(gate) * up in
+                                      its epilogue
     rw4_linear_residual_ws            down_proj + residual add
 
 The q/k/v and gate/up weights are concatenated once at set-up and the original modules'
@@ -161,7 +161,6 @@ class FusedDecoder(GraphedDecoder):
         shapes = [(self.hidden, nqkv), (self.hq * self.hd, self.hidden),
                   (self.hidden, self.head[0].shape[0])]
         if not moe:
-            self.gu = torch.empty(b, 2 * self.inter, **bf)
             self.act = torch.empty(b, self.inter, **bf)
             shapes += [(self.hidden, 2 * self.inter), (self.inter, self.hidden)]
         self.positions = torch.arange(max_len, device=dev)
@@ -172,6 +171,9 @@ class FusedDecoder(GraphedDecoder):
             nb = ctypes.c_size_t(0)
             _lib.call("rw4_linear_rmsnorm_workspace_size", b, k, n, ctypes.byref(nb))
             wsb = max(wsb, nb.value)
+            if not moe and n == 2 * self.inter:   # gate|up with the SwiGLU epilogue
+                _lib.call("rw4_linear_rmsnorm_swiglu_workspace_size", b, k, n, ctypes.byref(nb))
+                wsb = max(wsb, nb.value)
         self.ws = torch.empty(max(wsb, 256), dtype=torch.uint8, device=dev)
 
     def _lin(self, x, w, out, residual=None):
@@ -188,11 +190,13 @@ class FusedDecoder(GraphedDecoder):
                       out.data_ptr(), ws, wsb, stream)
         return out
 
-    def _lin_norm(self, x, weight, eps, w, out):
+    def _lin_norm(self, x, weight, eps, w, out, swiglu=False):
         """``out = rmsnorm(x) . W^T``: the norm runs inside the projection's activation
-        conversion (the one-row GEMV's prologue, or the x-prep pass of a batch): one launch."""
+        conversion (the one-row GEMV's prologue, or the x-prep pass of a batch): one launch.
+        ``swiglu``: W is [gate; up] and ``out = act_fn(gate) * up``, in the same launch."""
         m, k = x.shape
-        _lib.call("rw4_linear_rmsnorm_ws", x.data_ptr(), m, k, weight.data_ptr(), float(eps),
+        fn = "rw4_linear_rmsnorm_swiglu_ws" if swiglu else "rw4_linear_rmsnorm_ws"
+        _lib.call(fn, x.data_ptr(), m, k, weight.data_ptr(), float(eps),
                   w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(), w[0].shape[0], 64,
                   out.data_ptr(), self.ws.data_ptr(), self.ws.numel(),
                   torch.cuda.current_stream(self.device).cuda_stream)
@@ -249,9 +253,7 @@ class FusedDecoder(GraphedDecoder):
                 y = w.moe(xn.view(b, 1, self.hidden)).view(b, self.hidden)
                 torch.add(cur, y, out=other)
             else:
-                self._lin_norm(cur, w.ln2, w.eps2, w.gate_up, self.gu)
-                _lib.call("rw4_silu_mul", self.gu.data_ptr(), b, self.inter,
-                          self.act.data_ptr(), stream)
+                self._lin_norm(cur, w.ln2, w.eps2, w.gate_up, self.act, swiglu=True)
                 self._lin(self.act, w.down, other, residual=cur)
             cur, other = other, cur
         # the static cache's own write counters, kept in step for transformers (one launch)

@@ -246,6 +246,46 @@ def test_linear_rmsnorm_matches_norm_then_linear(cuda, m, k, n):
     assert torch.equal(y, want)
 
 
+@pytest.mark.parametrize("m,k,n", [(1, 4096, 28672), (1, 2048, 11264), (2, 4096, 28672),
+                                   (9, 4096, 28672), (16, 2048, 11264), (40, 4096, 28672),
+                                   (56, 4096, 28672), (1, 4096, 2048), (3, 1600, 2048),
+                                   (1, 17408, 12288)])
+def test_linear_rmsnorm_swiglu_matches_three_calls(cuda, m, k, n):
+    """rw4_linear_rmsnorm_swiglu_ws over a [gate; up] weight gives the bits of
+    rw4_linear_rmsnorm_ws followed by rw4_silu_mul: one launch where the GEMV's shape pairs gate
+    and up rows (64-, 32- and 16-row shapes; one row in the GEMV's prologue, a batch through the
+    x-prep pass), the two calls otherwise (4096 x 2048 splits K; 56 rows take the decode GEMM;
+    K % 512 != 0)."""
+    import ctypes
+    from rocketllm_b200 import _lib
+    w = make_weight(n, k, device=cuda, seed=51)
+    x = make_activation(m, k, device=cuda, seed=52) * 3
+    nw = (1 + 0.1 * make_activation(1, k, device=cuda, seed=53)).to(torch.bfloat16).view(k)
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    nb = ctypes.c_size_t(0)
+    _lib.call("rw4_linear_rmsnorm_workspace_size", m, k, n, ctypes.byref(nb))
+    ws = torch.empty(max(nb.value, 256), dtype=torch.uint8, device=cuda)
+    gu = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    _lib.call("rw4_linear_rmsnorm_ws", x.data_ptr(), m, k, nw.data_ptr(), 1e-5, w[0].data_ptr(),
+              w[1].data_ptr(), w[2].data_ptr(), n, 64, gu.data_ptr(), ws.data_ptr(), ws.numel(),
+              stream)
+    want = torch.empty(m, n // 2, dtype=torch.bfloat16, device=cuda)
+    _lib.call("rw4_silu_mul", gu.data_ptr(), m, n // 2, want.data_ptr(), stream)
+    _lib.call("rw4_linear_rmsnorm_swiglu_workspace_size", m, k, n, ctypes.byref(nb))
+    ws2 = torch.empty(max(nb.value, 256), dtype=torch.uint8, device=cuda)
+    y = torch.full((m, n // 2), float("nan"), dtype=torch.bfloat16, device=cuda)
+    _lib.call("rw4_linear_rmsnorm_swiglu_ws", x.data_ptr(), m, k, nw.data_ptr(), 1e-5,
+              w[0].data_ptr(), w[1].data_ptr(), w[2].data_ptr(), n, 64, y.data_ptr(),
+              ws2.data_ptr(), ws2.numel(), stream)
+    torch.cuda.synchronize()
+    assert kernels.device_status() == 0
+    assert torch.equal(y, want)
+    # and the model's own act_fn(gate) * up over those gate / up values
+    g, u = gu[:, :n // 2].float(), gu[:, n // 2:].float()
+    ref = (torch.nn.functional.silu(g).to(torch.bfloat16).float() * u).to(torch.bfloat16)
+    assert (y.float() - ref.float()).abs().max().item() <= 1e-2 * ref.float().abs().max().item()
+
+
 def test_linear_deterministic(cuda):
     packed, scale, zero = make_weight(4096, 14336, device=cuda, seed=5)
     x = make_activation(16, 14336, device=cuda, seed=6)
