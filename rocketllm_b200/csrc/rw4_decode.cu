@@ -11,15 +11,18 @@
 //   rw4_silu_mul       act_fn(gate) * up for a concatenated [gate | up] row: silu in fp32 rounded
 //                      to bf16, the product rounded to bf16                  [:171-184]
 //   rw4_linear_rmsnorm_ws    linear(rmsnorm(x)): a projection after the layer's norm, the norm
-//                      folded into the activation conversion for two or more rows
+//                      folded into the activation conversion (the one-row GEMV's prologue or the
+//                      x-prep pass)
+//   rw4_linear_rmsnorm_swiglu_ws   act_fn(gate) * up of linear(rmsnorm(x)) over a [gate; up]
+//                      weight: the MLP's first half in the GEMV's epilogue
 //   rw4_linear_residual_ws   residual + linear(x): the GEMV with the residual added in its epilogue
 //                      (the product rounded to bf16 first, then the sum), as a decoder layer's
 //                      `hidden_states = residual + self_attn(...)` / `+ mlp(...)`.
 // All are memory-bound and tiny at decode batch sizes; their point is the launch count (about 1,600
-// small kernels per Llama-8B token through the modules, 8 per layer here).  They are launched with
-// programmatic dependent launch: each waits for the kernel before it (griddepcontrol.wait) before it
-// touches memory, then lets the next one launch, so the following GEMV streams its first weight
-// stages while they run.
+// small kernels per Llama-8B token through the modules, 5 per layer here besides attention).  They
+// are launched with programmatic dependent launch: each waits for the kernel before it
+// (griddepcontrol.wait) before it touches memory, then lets the next one launch, so the following
+// GEMV streams its first weight stages while they run.
 #include "rw4_common.cuh"
 #include "rw4_xprep.cuh"
 

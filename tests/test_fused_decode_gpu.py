@@ -1,4 +1,4 @@
-"""The fused decode step (``rocketllm_b200.fused_decode``: eight launches per Llama layer; the same
+"""The fused decode step (``rocketllm_b200.fused_decode``: seven launches per Llama layer; the same
 attention half before the model's own sparse-MoE block on a Mixtral) against the module-by-module
 step (``GraphedDecoder``: transformers' modules around the RW4 GEMVs) and against the reference's
 own CPU decode of the TinyLlama configuration.
