@@ -171,6 +171,18 @@ int rw4_linear_rmsnorm_swiglu_ws(const void* x_bf16, int64_t M, int64_t K,
                                  const void* scale_f16, const void* zero_f16, int64_t N,
                                  int32_t group, void* y_bf16, void* workspace,
                                  size_t workspace_bytes, void* stream);
+/* rw4_decode_attention: one decode step's attention over a bf16 static KV cache.  q [batch,
+ *   heads, head_dim] (the step's rotated queries), k_cache / v_cache [batch, kv_heads, cache_cap,
+ *   head_dim] (StaticCache layout, the step's own key and value already written at *pos), out
+ *   [batch, heads, head_dim] = softmax(scaling q K^T) V over positions 0 .. *pos of each sequence,
+ *   grouped-query heads (heads / kv_heads <= 8), head_dim 64 or 128, all bf16 and 16-byte aligned.
+ *   *pos is read on the device (int64), so a captured graph replays the call unchanged as the
+ *   position advances.  Stands for transformers' sdpa_attention_forward over a StaticCache with
+ *   the causal mask of a one-token step (models/llama/modeling_llama.py), within bf16 rounding. */
+int rw4_decode_attention(const void* q, int32_t batch, int32_t heads, int32_t kv_heads,
+                         int32_t head_dim, const void* k_cache, const void* v_cache,
+                         int64_t cache_cap, const int64_t* pos, float scaling, void* out,
+                         void* stream);
 int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K, const uint8_t* packed,
                            const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
                            const void* residual, void* y_bf16, void* workspace,

@@ -68,6 +68,9 @@ SIGNATURES = {
                                                     ctypes.c_float, _c_void_p, _c_void_p,
                                                     _c_void_p, _i64, _i32, _c_void_p, _c_void_p,
                                                     _size, _c_void_p]),
+    "rw4_decode_attention": (ctypes.c_int, [_c_void_p, _i32, _i32, _i32, _i32, _c_void_p,
+                                            _c_void_p, _i64, _c_void_p, ctypes.c_float,
+                                            _c_void_p, _c_void_p]),
     "rw4_linear_residual_ws": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p,
                                               _c_void_p, _i64, _i32, _c_void_p, _c_void_p,
                                               _c_void_p, _size, _c_void_p]),

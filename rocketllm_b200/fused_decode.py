@@ -6,14 +6,16 @@ RMSNorm as six elementwise kernels, q / k / v as three GEMVs, the rotary embeddi
 mul / add kernels, ``index_copy_`` into the static cache, the grouped-query key / value copies
 (``repeat_kv``), attention, o_proj, the residual add, RMSNorm again, gate, up, SiLU, the product,
 down, the residual add (transformers ``models/llama/modeling_llama.py``).  The step here is about
-seven launches per layer at batch 1 (attention's two included; from two rows on each GEMV adds
-its activation-conversion pass), each reproducing the modules' bf16 rounding sequence:
+six launches per layer at batch 1 (attention included; from two rows on each GEMV adds its
+activation-conversion pass), each reproducing the modules' bf16 rounding sequence:
 
     rw4_linear_rmsnorm_ws             input_layernorm, then q_proj, k_proj, v_proj as one GEMV
                                       over the concatenated weight (the norm runs inside the
                                       GEMV's activation conversion)
     rw4_rope_kv                       apply_rotary_pos_emb + StaticCache.update (device position)
-    SDPA with enable_gqa              attention over the static cache, no key / value copies
+    rw4_decode_attention              attention over the static cache up to the device-side
+                                      position, grouped-query heads, no key / value copies (SDPA
+                                      with enable_gqa and a mask for shapes it does not cover)
     rw4_linear_residual_ws            o_proj + residual add in the GEMV epilogue
     rw4_linear_rmsnorm_swiglu_ws      post_attention_layernorm, then gate_proj, up_proj as one
                                       GEMV over the concatenated weight, act_fn(gate) * up in
@@ -37,6 +39,7 @@ expert-parallel exchange -- followed by the residual add:
     residual add                      ``residual + hidden_states``
 """
 import ctypes
+import os
 
 import torch
 
@@ -117,9 +120,10 @@ class FusedDecoder(GraphedDecoder):
     """Greedy decode of a resident RW4 Llama or Mixtral model with the fused step (see the module
     docstring); same interface as :class:`~rocketllm_b200.decode.GraphedDecoder` (``prefill``,
     ``step``, ``generate``, ``capture``).  Raises ``ValueError`` for a model :func:`fusable`
-    rejects."""
+    rejects.  ``attention``: ``"rw4"`` (default: ``rw4_decode_attention`` where it covers the
+    shape) or ``"sdpa"`` (torch's SDPA over the static cache with a mask)."""
 
-    def __init__(self, model, batch, max_len, device="cuda", use_graph=True):
+    def __init__(self, model, batch, max_len, device="cuda", use_graph=True, attention=None):
         if not fusable(model):
             raise ValueError("the fused decode step covers resident RW4 Llama- and "
                              "Mixtral-architecture models")
@@ -158,6 +162,18 @@ class FusedDecoder(GraphedDecoder):
         self.xn = torch.empty(b, self.hidden, **bf)
         self.qkv_out = torch.empty(b, nqkv, **bf)
         self.q_rot = torch.empty(b, self.hq, 1, self.hd, **bf)
+        # attention: rw4_decode_attention (device-side length, programmatic launch) where it
+        # covers the shape, else SDPA over the whole static cache with a mask.  A Mixtral keeps
+        # SDPA, the module path's own kernel: its top-k routing is discontinuous, and attention
+        # that differs within bf16 rounding flips near-tied expert choices, so the fused step
+        # keeps the modules' attention bits there.
+        if attention is None:   # RW4_FUSED_ATTENTION=sdpa selects SDPA (for measurements)
+            attention = os.environ.get("RW4_FUSED_ATTENTION", "rw4")
+        if attention not in ("rw4", "sdpa"):
+            raise ValueError(f"attention must be 'rw4' or 'sdpa', not {attention!r}")
+        self.own_attention = (attention == "rw4" and not moe and self.hq % self.hk == 0
+                              and self.hq // self.hk <= 8 and self.hd in (64, 128))
+        self.attn_out = torch.empty(b, self.hq, 1, self.hd, **bf)
         shapes = [(self.hidden, nqkv), (self.hq * self.hd, self.hidden),
                   (self.hidden, self.head[0].shape[0])]
         if not moe:
@@ -227,9 +243,11 @@ class FusedDecoder(GraphedDecoder):
         cos, sin = inner.rotary_emb(cur.view(b, 1, self.hidden), pos.view(1, 1).expand(b, 1))
         cos = cos.reshape(b, self.hd).to(torch.bfloat16).contiguous()
         sin = sin.reshape(b, self.hd).to(torch.bfloat16).contiguous()
-        # one additive mask per step for every layer (0 up to the position, -inf after)
-        mask = torch.where(self.positions <= pos, 0.0, float("-inf")).to(torch.bfloat16)
-        mask = mask.view(1, 1, 1, -1)
+        mask = None
+        if not self.own_attention:
+            # one additive mask per step for every layer (0 up to the position, -inf after)
+            mask = torch.where(self.positions <= pos, 0.0, float("-inf")).to(torch.bfloat16)
+            mask = mask.view(1, 1, 1, -1)
         nq, nk = self.hq * self.hd, self.hk * self.hd
         qkv = self.qkv_out
         other = self.h[1]
@@ -241,9 +259,16 @@ class FusedDecoder(GraphedDecoder):
                       cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), layer.keys.shape[2],
                       self.q_rot.data_ptr(), layer.keys.data_ptr(), layer.values.data_ptr(),
                       stream)
-            attn = torch.nn.functional.scaled_dot_product_attention(
-                self.q_rot, layer.keys, layer.values, attn_mask=mask,
-                scale=self.hd ** -0.5, enable_gqa=True)
+            if self.own_attention:
+                attn = self.attn_out
+                _lib.call("rw4_decode_attention", self.q_rot.data_ptr(), b, self.hq, self.hk,
+                          self.hd, layer.keys.data_ptr(), layer.values.data_ptr(),
+                          layer.keys.shape[2], pos.data_ptr(), self.hd ** -0.5,
+                          attn.data_ptr(), stream)
+            else:
+                attn = torch.nn.functional.scaled_dot_product_attention(
+                    self.q_rot, layer.keys, layer.values, attn_mask=mask,
+                    scale=self.hd ** -0.5, enable_gqa=True)
             # residual stream: each add writes the other buffer (no in-place update)
             self._lin(attn.reshape(b, nq), w.o, other, residual=cur)
             cur, other = other, cur

@@ -1,12 +1,12 @@
-"""The fused decode step (``rocketllm_b200.fused_decode``: seven launches per Llama layer; the same
+"""The fused decode step (``rocketllm_b200.fused_decode``: six launches per Llama layer; the same
 attention half before the model's own sparse-MoE block on a Mixtral) against the module-by-module
 step (``GraphedDecoder``: transformers' modules around the RW4 GEMVs) and against the reference's
 own CPU decode of the TinyLlama configuration.
 
 Both steps run the same arithmetic in the same bf16 rounding sequence, but not bit for bit: the
 concatenated q|k|v and gate|up weights may split K differently from the separate projections, and
-attention reads the static cache through SDPA's grouped-query path instead of copied keys and
-values.  So, with the module path's tokens fed back to both (teacher forcing), every step's logits
+attention reads the static cache through rw4_decode_attention (or SDPA's grouped-query path)
+instead of copied keys and values.  So, with the module path's tokens fed back to both (teacher forcing), every step's logits
 must agree within the linear tests' bf16 tolerance scaled to the logits, and the greedy choice must
 agree wherever the module path's top-1 margin is at least 4e-2.
 """
@@ -50,8 +50,8 @@ def forced_steps(dec, prompt, tokens):
     return torch.stack(out)
 
 
-@pytest.mark.parametrize("batch", [1, 3])
-def test_fused_step_matches_module_step(checkpoint, batch):
+@pytest.mark.parametrize("batch,attention", [(1, "rw4"), (3, "rw4"), (3, "sdpa")])
+def test_fused_step_matches_module_step(checkpoint, batch, attention):
     model = AutoModel.from_pretrained(checkpoint).model
     assert fusable(model)
     g = torch.Generator().manual_seed(batch)
@@ -59,7 +59,9 @@ def test_fused_step_matches_module_step(checkpoint, batch):
     ref_dec = GraphedDecoder(model, batch, 37 + 24 + 8)
     want = ref_dec.generate(prompt, 24)                      # module path, greedy
     ref = forced_steps(GraphedDecoder(model, batch, 37 + 24 + 8), prompt, want.T)
-    fused = forced_steps(FusedDecoder(model, batch, 37 + 24 + 8), prompt, want.T)
+    fdec = FusedDecoder(model, batch, 37 + 24 + 8, attention=attention)
+    assert fdec.own_attention == (attention == "rw4")
+    fused = forced_steps(fdec, prompt, want.T)
     assert kernels.device_status() == 0
     scale = float(ref.abs().max())
     err = float((fused - ref).abs().max())
@@ -69,7 +71,7 @@ def test_fused_step_matches_module_step(checkpoint, batch):
     clear = (top2[..., 0] - top2[..., 1]) >= 4e-2
     assert torch.equal(fused.argmax(-1)[clear], ref.argmax(-1)[clear])
     # free-running: the fused decoder's greedy tokens equal the module path's up to a near-tie
-    got = FusedDecoder(model, batch, 37 + 24 + 8).generate(prompt, 24)
+    got = FusedDecoder(model, batch, 37 + 24 + 8, attention=attention).generate(prompt, 24)
     for b in range(batch):
         diff = (got[b] != want[b]).nonzero()
         if diff.numel():
