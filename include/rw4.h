@@ -187,6 +187,14 @@ int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K, const uint8
                            const void* scale_f16, const void* zero_f16, int64_t N, int32_t group,
                            const void* residual, void* y_bf16, void* workspace,
                            size_t workspace_bytes, void* stream);
+/* rw4_argmax_rows: the greedy token choice of a decode step, out[r] (int64) = the index of the
+ *   largest of row r's V bf16 scores (row stride ld elements), the first index among equal maxima,
+ *   a NaN counting as larger than every number -- torch.argmax(scores, dim=-1), which the
+ *   reference's generate() reaches through the model's own greedy search (rocketllm/base.py:
+ *   2014-2044 -> transformers generation/utils.py, the greedy branch of _sample).  rows <= 65535,
+ *   V < 2^31.  One launch, one cluster of CTAs per row, no scratch. */
+int rw4_argmax_rows(const void* scores_bf16, int64_t rows, int64_t V, int64_t ld, int64_t* out,
+                    void* stream);
 
 /* rw4_linear_noalloc: rw4_linear for M <= 64 (the GEMV) that allocates nothing.  No counterpart in
  * the reference.  For callers that cannot allocate device memory per call: a host that plans every

@@ -74,6 +74,7 @@ SIGNATURES = {
     "rw4_linear_residual_ws": (ctypes.c_int, [_c_void_p, _i64, _i64, _c_void_p, _c_void_p,
                                               _c_void_p, _i64, _i32, _c_void_p, _c_void_p,
                                               _c_void_p, _size, _c_void_p]),
+    "rw4_argmax_rows": (ctypes.c_int, [_c_void_p, _i64, _i64, _i64, _c_void_p, _c_void_p]),
     "rw4_device_status": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), _i32, _c_void_p]),
     "rw4_wait_selftest": (ctypes.c_int, [_i32, _c_void_p]),
     "rw4_moe_permute": (ctypes.c_int, [_c_void_p, _i64, _i32, _i32, _c_void_p, _c_void_p,

@@ -18,11 +18,17 @@
 //   rw4_linear_residual_ws   residual + linear(x): the GEMV with the residual added in its epilogue
 //                      (the product rounded to bf16 first, then the sum), as a decoder layer's
 //                      `hidden_states = residual + self_attn(...)` / `+ mlp(...)`.
+//   rw4_argmax_rows    the greedy choice over the vocabulary, torch.argmax(scores, dim=-1)
+//                      (transformers generation/utils.py, the greedy branch of _sample)
 // All are memory-bound and tiny at decode batch sizes; their point is the launch count (about 1,600
 // small kernels per Llama-8B token through the modules, 5 per layer here besides attention).  They
 // are launched with programmatic dependent launch: each waits for the kernel before it
 // (griddepcontrol.wait) before it touches memory, then lets the next one launch, so the following
 // GEMV streams its first weight stages while they run.
+#include <cooperative_groups.h>
+
+#include <climits>
+
 #include "rw4_common.cuh"
 #include "rw4_xprep.cuh"
 
@@ -174,9 +180,135 @@ __global__ void add_kernel(__nv_bfloat16* __restrict__ y, const __nv_bfloat16* _
   if (i < n) y[i] = __float2bfloat16_rn(__bfloat162float(y[i]) + __bfloat162float(r[i]));
 }
 
+// ---- greedy token choice -----------------------------------------------------------------------
+// out[r] = the index of row r's largest bf16 score: the first index among equal maxima, and a NaN
+// counts as larger than every number (torch.argmax's rule on CUDA).  One thread-block cluster of
+// kArgmaxCluster CTAs per row, each CTA a contiguous share of the row; the CTAs' winners meet in
+// CTA 0 through distributed shared memory, so one launch reads the row once with no global
+// scratch.  (At 128,256 scores torch's reduction runs one CTA per row.)
+constexpr int kArgmaxCluster = 8;
+constexpr int kArgmaxThreads = 256;
+
+// (a, ia) wins over (b, ib)
+__device__ __forceinline__ bool argmax_better(float a, int ia, float b, int ib) {
+  const bool na = a != a, nb = b != b;
+  if (na != nb) return na;
+  if (!na && a != b) return a > b;
+  return ia < ib;
+}
+
+__global__ void __launch_bounds__(kArgmaxThreads)
+    argmax_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld, int V, bool vec,
+                  int64_t* __restrict__ out) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  __shared__ float wv[kArgmaxThreads / 32];
+  __shared__ int wi[kArgmaxThreads / 32];
+  __shared__ float cta_v;
+  __shared__ int cta_i;
+  pdl_enter();
+  const int c = (int)cluster.block_rank();
+  const __nv_bfloat16* xr = x + (int64_t)blockIdx.y * ld;
+  // this CTA's share, a multiple of 8 scores
+  const int per = ((V + kArgmaxCluster - 1) / kArgmaxCluster + 7) & ~7;
+  const int beg = min(V, c * per), end = min(V, beg + per);
+  float bv = -INFINITY;
+  int bi = INT_MAX;
+  if (vec) {
+    // each thread walks its 8-score vectors in increasing order, so a strict win keeps the first
+    for (int i = beg + 8 * (int)threadIdx.x; i < end; i += 8 * kArgmaxThreads) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xr + i);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v = __bfloat162float(e[j]);
+        if (argmax_better(v, i + j, bv, bi)) {
+          bv = v;
+          bi = i + j;
+        }
+      }
+    }
+  } else {
+    for (int i = beg + (int)threadIdx.x; i < end; i += kArgmaxThreads) {
+      const float v = __bfloat162float(xr[i]);
+      if (argmax_better(v, i, bv, bi)) {
+        bv = v;
+        bi = i;
+      }
+    }
+  }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, off);
+    const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, off);
+    if (argmax_better(ov, oi, bv, bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) {
+    wv[warp] = bv;
+    wi[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kArgmaxThreads / 32; ++w)
+      if (argmax_better(wv[w], wi[w], bv, bi)) {
+        bv = wv[w];
+        bi = wi[w];
+      }
+    cta_v = bv;
+    cta_i = bi;
+  }
+  cluster.sync();   // every CTA's winner is in its shared memory
+  if (c == 0 && threadIdx.x == 0) {
+    for (int q = 1; q < kArgmaxCluster; ++q) {
+      const float qv = *cluster.map_shared_rank(&cta_v, q);
+      const int qi = *cluster.map_shared_rank(&cta_i, q);
+      if (argmax_better(qv, qi, bv, bi)) {
+        bv = qv;
+        bi = qi;
+      }
+    }
+    out[blockIdx.y] = bi;
+  }
+  cluster.sync();   // no CTA leaves while CTA 0 still reads its shared memory
+}
+
 unsigned blocks(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
 
 }  // namespace
+
+extern "C" int rw4_argmax_rows(const void* scores_bf16, int64_t rows, int64_t V, int64_t ld,
+                               int64_t* out, void* stream) {
+  if (rows < 0 || V <= 0 || V > INT_MAX - 8 || ld < V)
+    return fail(RW4_EINVAL, "rw4_argmax_rows: bad shape (rows %lld, V %lld, ld %lld)",
+                (long long)rows, (long long)V, (long long)ld);
+  if (rows == 0) return RW4_OK;
+  if (!scores_bf16 || !out) return fail(RW4_EINVAL, "rw4_argmax_rows: null pointer");
+  if (rows > 65535) return fail(RW4_EINVAL, "rw4_argmax_rows: more than 65535 rows");
+  // 16-byte loads when every row starts aligned and holds whole vectors (no load past V)
+  const bool vec = rw4::aligned(scores_bf16, 16) && ld % 8 == 0 && V % 8 == 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kArgmaxCluster, (unsigned)rows);
+  cfg.blockDim = dim3(kArgmaxThreads);
+  cfg.stream = rw4::as_stream(stream);
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kArgmaxCluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = pdl_on() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t err =
+      cudaLaunchKernelEx(&cfg, argmax_kernel, static_cast<const __nv_bfloat16*>(scores_bf16), ld,
+                         (int)V, vec, out);
+  if (err != cudaSuccess) return rw4::cuda_status(err, "rw4_argmax_rows launch");
+  return rw4::launch_status("rw4_argmax_rows launch");
+}
 
 extern "C" int rw4_rmsnorm(const void* x, const void* weight, int64_t rows, int64_t H, float eps,
                            void* y, void* stream) {

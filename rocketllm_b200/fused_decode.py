@@ -285,7 +285,7 @@ class FusedDecoder(GraphedDecoder):
         torch._foreach_add_(self._counters, 1)
         logits = self._lin_norm(cur, self.final_norm, self.final_eps, self.head, self.logits_buf)
         self.logits = logits
-        nxt_tok = logits.argmax(-1, keepdim=True)
-        self.ids.copy_(nxt_tok)
+        # the greedy choice straight into the next step's token (logits.argmax's bits)
+        kernels.argmax_rows(logits, out=self.ids)
         self.pos.add_(1)
-        return nxt_tok
+        return self.ids

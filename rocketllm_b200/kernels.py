@@ -143,6 +143,22 @@ def device_status(clear=True):
 
 # ---- routed experts ------------------------------------------------------------------------------
 
+def argmax_rows(scores, out=None):
+    """Greedy choice per row of bf16 ``scores [R, V]`` (``rw4_argmax_rows``): int64 ``[R, 1]``, the
+    first index among equal maxima, NaN above every number -- ``scores.argmax(-1, keepdim=True)``.
+    Rows may be a strided view (unit stride along V)."""
+    if not scores.is_cuda:
+        raise ValueError(f"RW4 kernels take CUDA tensors only; got a {scores.device} tensor")
+    if scores.dtype != torch.bfloat16 or scores.dim() != 2 or scores.stride(1) != 1:
+        raise TypeError("scores must be a 2-D bf16 tensor with unit stride along V")
+    r, v = scores.shape
+    if out is None:
+        out = torch.empty(r, 1, dtype=torch.int64, device=scores.device)
+    _lib.call("rw4_argmax_rows", scores.data_ptr(), r, v, scores.stride(0), out.data_ptr(),
+              _stream())
+    return out
+
+
 def moe_permute(topk_idx, num_experts):
     """``(perm, inv, offsets)`` int32 for ``topk_idx`` int64 ``[T, k]`` (stable, by expert)."""
     _require_cuda(topk_idx)
