@@ -116,18 +116,13 @@ class _LayerWeights:
     __slots__ = ("ln1", "ln2", "qkv", "o", "gate_up", "down", "eps1", "eps2", "moe")
 
 
-class FusedDecoder(GraphedDecoder):
-    """Greedy decode of a resident RW4 Llama or Mixtral model with the fused step (see the module
-    docstring); same interface as :class:`~rocketllm_b200.decode.GraphedDecoder` (``prefill``,
-    ``step``, ``generate``, ``capture``).  Raises ``ValueError`` for a model :func:`fusable`
-    rejects.  ``attention``: ``"rw4"`` (default: ``rw4_decode_attention`` where it covers the
-    shape) or ``"sdpa"`` (torch's SDPA over the static cache with a mask)."""
+class _FusedOps:
+    """The fused per-layer decode ops over a list of decoder layers of a resident RW4 Llama or
+    Mixtral model: their weights (q|k|v and gate|up concatenated), the step's static buffers and
+    workspace, and the layer loop.  :class:`FusedDecoder` runs it over every layer; a pipeline
+    stage (:class:`~rocketllm_b200.pipeline.GraphedPipelineDecoder`) over the layers it owns."""
 
-    def __init__(self, model, batch, max_len, device="cuda", use_graph=True, attention=None):
-        if not fusable(model):
-            raise ValueError("the fused decode step covers resident RW4 Llama- and "
-                             "Mixtral-architecture models")
-        super().__init__(model, batch, max_len, device=device, use_graph=use_graph)
+    def _setup(self, model, batch, layer_ids, max_len, with_head, attention):
         cfg = model.config
         self.hq = cfg.num_attention_heads
         self.hk = cfg.num_key_value_heads
@@ -135,8 +130,10 @@ class FusedDecoder(GraphedDecoder):
         self.hidden = cfg.hidden_size
         self.inter = cfg.intermediate_size
         moe = cfg.model_type == "mixtral"
+        self.layer_ids = list(layer_ids)
         self.layers = []
-        for layer in model.model.layers:
+        for i in self.layer_ids:
+            layer = model.model.layers[i]
             a, m = layer.self_attn, layer.mlp
             w = _LayerWeights()
             w.ln1, w.eps1 = layer.input_layernorm.weight, layer.input_layernorm.variance_epsilon
@@ -150,10 +147,12 @@ class FusedDecoder(GraphedDecoder):
                 w.down = (m.down_proj.weight_packed, m.down_proj.weight_scale,
                           m.down_proj.weight_zero_point)
             self.layers.append(w)
-        norm = model.model.norm
-        self.final_norm, self.final_eps = norm.weight, norm.variance_epsilon
-        head = model.lm_head
-        self.head = (head.weight_packed, head.weight_scale, head.weight_zero_point)
+        self.head = None
+        if with_head:
+            norm = model.model.norm
+            self.final_norm, self.final_eps = norm.weight, norm.variance_epsilon
+            head = model.lm_head
+            self.head = (head.weight_packed, head.weight_scale, head.weight_zero_point)
         dev, b = self.device, batch
         bf = dict(dtype=torch.bfloat16, device=dev)
         nqkv = (self.hq + 2 * self.hk) * self.hd
@@ -174,13 +173,14 @@ class FusedDecoder(GraphedDecoder):
         self.own_attention = (attention == "rw4" and not moe and self.hq % self.hk == 0
                               and self.hq // self.hk <= 8 and self.hd in (64, 128))
         self.attn_out = torch.empty(b, self.hq, 1, self.hd, **bf)
-        shapes = [(self.hidden, nqkv), (self.hq * self.hd, self.hidden),
-                  (self.hidden, self.head[0].shape[0])]
+        shapes = [(self.hidden, nqkv), (self.hq * self.hd, self.hidden)]
+        if with_head:
+            shapes.append((self.hidden, self.head[0].shape[0]))
         if not moe:
             self.act = torch.empty(b, self.inter, **bf)
             shapes += [(self.hidden, 2 * self.inter), (self.inter, self.hidden)]
         self.positions = torch.arange(max_len, device=dev)
-        self.logits_buf = torch.empty(b, self.head[0].shape[0], **bf)
+        self.logits_buf = torch.empty(b, self.head[0].shape[0], **bf) if with_head else None
         self._counters = None
         wsb = max(kernels.linear_workspace_bytes(b, k, n) for k, n in shapes)
         for k, n in shapes:   # the projections that follow a norm take it in their conversion
@@ -223,36 +223,16 @@ class FusedDecoder(GraphedDecoder):
                   float(eps), out.data_ptr(), torch.cuda.current_stream(self.device).cuda_stream)
         return out
 
-    @torch.no_grad()
-    def prefill(self, input_ids):
-        nxt = super().prefill(input_ids)
-        self._counters = [layer.cumulative_length for layer in self.cache.layers]
-        return nxt
-
-    @torch.no_grad()
-    def _step(self):
-        model, b = self.model, self.batch
-        stream = torch.cuda.current_stream(self.device).cuda_stream
-        inner = model.model
-        h = inner.embed_tokens(self.ids).view(b, self.hidden)
-        if h.dtype != torch.bfloat16:
-            h = h.to(torch.bfloat16)
-        cur = self.h[0]
-        cur.copy_(h)
-        pos = self.pos
-        cos, sin = inner.rotary_emb(cur.view(b, 1, self.hidden), pos.view(1, 1).expand(b, 1))
-        cos = cos.reshape(b, self.hd).to(torch.bfloat16).contiguous()
-        sin = sin.reshape(b, self.hd).to(torch.bfloat16).contiguous()
-        mask = None
-        if not self.own_attention:
-            # one additive mask per step for every layer (0 up to the position, -inf after)
-            mask = torch.where(self.positions <= pos, 0.0, float("-inf")).to(torch.bfloat16)
-            mask = mask.view(1, 1, 1, -1)
+    def _run_layers(self, cur, pos, cos, sin, mask, cache, stream):
+        """The fused ops of every layer in ``layer_ids`` on the residual stream ``cur`` (one of
+        ``self.h``; the other is the step's second buffer), the layers' keys and values in
+        ``cache.layers[i]``; returns the buffer holding the result."""
+        b = self.batch
         nq, nk = self.hq * self.hd, self.hk * self.hd
         qkv = self.qkv_out
-        other = self.h[1]
-        for i, w in enumerate(self.layers):
-            layer = self.cache.layers[i]
+        other = self.h[1] if cur is self.h[0] else self.h[0]
+        for i, w in zip(self.layer_ids, self.layers):
+            layer = cache.layers[i]
             self._lin_norm(cur, w.ln1, w.eps1, w.qkv, qkv)
             _lib.call("rw4_rope_kv", qkv.data_ptr(), qkv[:, nq:].data_ptr(),
                       qkv[:, nq + nk:].data_ptr(), qkv.shape[1], b, self.hq, self.hk, self.hd,
@@ -281,6 +261,57 @@ class FusedDecoder(GraphedDecoder):
                 self._lin_norm(cur, w.ln2, w.eps2, w.gate_up, self.act, swiglu=True)
                 self._lin(self.act, w.down, other, residual=cur)
             cur, other = other, cur
+        return cur
+
+    def _rotary(self, rotary_emb, h, pos):
+        """bf16 cos / sin [batch, head_dim] of the step's position (the model's rotary module)."""
+        b = self.batch
+        cos, sin = rotary_emb(h.view(b, 1, self.hidden), pos.view(1, 1).expand(b, 1))
+        return (cos.reshape(b, self.hd).to(torch.bfloat16).contiguous(),
+                sin.reshape(b, self.hd).to(torch.bfloat16).contiguous())
+
+    def _step_mask(self, pos):
+        """The additive mask SDPA needs (0 up to the position, -inf after), or None."""
+        if self.own_attention:
+            return None
+        mask = torch.where(self.positions <= pos, 0.0, float("-inf")).to(torch.bfloat16)
+        return mask.view(1, 1, 1, -1)
+
+
+class FusedDecoder(_FusedOps, GraphedDecoder):
+    """Greedy decode of a resident RW4 Llama or Mixtral model with the fused step (see the module
+    docstring); same interface as :class:`~rocketllm_b200.decode.GraphedDecoder` (``prefill``,
+    ``step``, ``generate``, ``capture``).  Raises ``ValueError`` for a model :func:`fusable`
+    rejects.  ``attention``: ``"rw4"`` (default: ``rw4_decode_attention`` where it covers the
+    shape) or ``"sdpa"`` (torch's SDPA over the static cache with a mask)."""
+
+    def __init__(self, model, batch, max_len, device="cuda", use_graph=True, attention=None):
+        if not fusable(model):
+            raise ValueError("the fused decode step covers resident RW4 Llama- and "
+                             "Mixtral-architecture models")
+        GraphedDecoder.__init__(self, model, batch, max_len, device=device, use_graph=use_graph)
+        self._setup(model, batch, range(len(model.model.layers)), max_len, True, attention)
+
+    @torch.no_grad()
+    def prefill(self, input_ids):
+        nxt = super().prefill(input_ids)
+        self._counters = [layer.cumulative_length for layer in self.cache.layers]
+        return nxt
+
+    @torch.no_grad()
+    def _step(self):
+        model, b = self.model, self.batch
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        inner = model.model
+        h = inner.embed_tokens(self.ids).view(b, self.hidden)
+        if h.dtype != torch.bfloat16:
+            h = h.to(torch.bfloat16)
+        cur = self.h[0]
+        cur.copy_(h)
+        pos = self.pos
+        cos, sin = self._rotary(inner.rotary_emb, cur, pos)
+        mask = self._step_mask(pos)
+        cur = self._run_layers(cur, pos, cos, sin, mask, self.cache, stream)
         # the static cache's own write counters, kept in step for transformers (one launch)
         torch._foreach_add_(self._counters, 1)
         logits = self._lin_norm(cur, self.final_norm, self.final_eps, self.head, self.logits_buf)
@@ -289,3 +320,51 @@ class FusedDecoder(GraphedDecoder):
         kernels.argmax_rows(logits, out=self.ids)
         self.pos.add_(1)
         return self.ids
+
+
+class FusedLayerRange(_FusedOps):
+    """The fused decode ops of the decoder layers ``layer_ids`` of a resident RW4 Llama model (the
+    layers a pipeline stage owns): ``run(cur, pos, cos, sin, mask, cache, stream)`` on one token
+    per sequence, ``head(cur)`` for the stage that holds the final norm and ``lm_head``."""
+
+    def __init__(self, model, batch, layer_ids, max_len, with_head, device="cuda",
+                 attention=None):
+        self.device = torch.device(device)
+        self.batch = batch
+        self._setup(model, batch, layer_ids, max_len, with_head, attention)
+
+    def run(self, cur, pos, cos, sin, mask, cache, stream):
+        return self._run_layers(cur, pos, cos, sin, mask, cache, stream)
+
+    def head_logits(self, cur):
+        return self._lin_norm(cur, self.final_norm, self.final_eps, self.head, self.logits_buf)
+
+
+def fusable_layers(model, layer_ids, with_head):
+    """Whether :class:`FusedLayerRange` covers these layers of ``model``: a Llama architecture,
+    the layers' projections (and ``lm_head`` when ``with_head``) ``RW4Linear`` without bias, no
+    hooks, SiLU, all on a CUDA device."""
+    cfg = model.config
+    if getattr(cfg, "model_type", None) != "llama" or getattr(cfg, "sliding_window", None):
+        return False
+    if cfg.hidden_act not in ("silu", "swish"):
+        return False
+    inner = getattr(model, "model", None)
+    if inner is None:
+        return False
+    if with_head and (not isinstance(getattr(model, "lm_head", None), RW4Linear)
+                      or getattr(inner, "norm", None) is None):
+        return False
+    for i in layer_ids:
+        layer = inner.layers[i]
+        a, m = getattr(layer, "self_attn", None), getattr(layer, "mlp", None)
+        if a is None or m is None:
+            return False
+        if not _rw4((a.q_proj, a.k_proj, a.v_proj, a.o_proj, m.gate_proj, m.up_proj,
+                     m.down_proj)):
+            return False
+        if layer._forward_pre_hooks or layer._forward_hooks:
+            return False
+        if not all(p.is_cuda for p in layer.parameters()):
+            return False
+    return True

@@ -118,10 +118,23 @@ class GraphedPipelineDecoder(PipelineDecoder):
     mask of the positions written so far."""
 
     def __init__(self, model, batch, max_len, group=None, device="cuda", drop_remote=True,
-                 local=False, use_graph=True):
+                 local=False, use_graph=True, fused=None):
         super().__init__(model, group, device, drop_remote, local)
         from transformers import StaticCache
+
+        from .fused_decode import FusedLayerRange, fusable_layers
         self.cache = StaticCache(config=model.config, max_cache_len=max_len)
+        # The stage's decode step: the fused decode ops over its layers (resident RW4 Llama
+        # layers; default where they apply) or the transformers modules.
+        own = range(self.start, self.stop)
+        can_fuse = self.device.type == "cuda" and fusable_layers(model, own, self.last)
+        if fused is None:
+            fused = can_fuse
+        elif fused and not can_fuse:
+            raise ValueError("the fused stage covers resident RW4 Llama layers on a CUDA device")
+        self.fl = (FusedLayerRange(model, batch, own, max_len, self.last, device=self.device)
+                   if fused else None)
+        self._counters = None
         self.batch, self.max_len = batch, max_len
         h = self.hidden_size
         self.ids = torch.zeros(batch, 1, dtype=torch.long, device=self.device)
@@ -176,9 +189,36 @@ class GraphedPipelineDecoder(PipelineDecoder):
             dist.broadcast(self.ids, src=self._last_rank(), group=self.group)
         self.pos.fill_(t)
         self.host_pos = t
+        # the static cache's write counters of this stage's layers, advanced by the fused step
+        counters = (getattr(self.cache.layers[i], "cumulative_length", None)
+                    for i in range(self.start, self.stop))
+        self._counters = [c for c in counters if torch.is_tensor(c)]
         return self.ids.clone()
 
+    def _fused_stage(self):
+        """The stage's decode step through the fused ops (``FusedLayerRange``): embedding on the
+        first rank, the rank's layers, then the final norm + lm_head and the greedy choice on the
+        last rank -- the launches :class:`~rocketllm_b200.fused_decode.FusedDecoder` makes for
+        the same layers."""
+        fl, b = self.fl, self.batch
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        h = self.embed(self.ids) if self.first else self.h_in
+        cur = fl.h[0]
+        cur.copy_(h.view(b, self.hidden_size))
+        cos, sin = fl._rotary(self.rotary, cur, self.pos)
+        cur = fl.run(cur, self.pos, cos, sin, fl._step_mask(self.pos), self.cache, stream)
+        if self._counters:
+            torch._foreach_add_(self._counters, 1)
+        if self.last:
+            from . import kernels
+            kernels.argmax_rows(fl.head_logits(cur), out=self.ids)
+        else:
+            self.h_out.view(b, self.hidden_size).copy_(cur)
+        self.pos.add_(1)
+
     def _stage(self):
+        if self.fl is not None:
+            return self._fused_stage()
         h = self.embed(self.ids) if self.first else self.h_in
         h = self._run_layers(h, self.pos, masked=True)
         if self.last:

@@ -175,3 +175,24 @@ def test_generate_takes_the_fused_path_and_matches_transformers(checkpoint):
                           logits_processor=LogitsProcessorList([]), eos_token_id=None,
                           pad_token_id=0)
     assert out.shape == (2, 26)
+
+
+@pytest.mark.parametrize("batch", [1, 3])
+def test_fused_pipeline_stage_equals_fused_decoder(checkpoint, batch):
+    """A pipeline stage owning every layer (one rank) runs the fused ops over its layer range
+    (``FusedLayerRange``): the same launches as the fused decoder, so the same tokens and logits
+    bit for bit; with ``fused=False`` the stage runs the modules."""
+    from rocketllm_b200.pipeline import GraphedPipelineDecoder
+    model = AutoModel.from_pretrained(checkpoint).model
+    g = torch.Generator().manual_seed(10 + batch)
+    prompt = torch.randint(0, 2048, (batch, 29), generator=g).cuda()
+    want = FusedDecoder(model, batch, 29 + 20 + 8).generate(prompt, 20)
+    stage = GraphedPipelineDecoder(model, batch, 29 + 20 + 8, local=True)
+    assert stage.fl is not None
+    got = stage.generate(prompt, 20)
+    assert kernels.device_status() == 0
+    assert torch.equal(got, want)
+    mods = GraphedPipelineDecoder(model, batch, 29 + 20 + 8, local=True, fused=False)
+    assert mods.fl is None
+    ref = mods.generate(prompt, 20)
+    assert ref.shape == want.shape and torch.equal(ref[:, :1], want[:, :1])   # one prefill
