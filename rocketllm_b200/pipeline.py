@@ -7,8 +7,10 @@ norm and ``lm_head``.  One forward (prefill or one decode step): rank 0 embeds, 
 layers on the hidden states it received from the previous rank (``dist.recv``) and sends the
 result on (``dist.send``; NCCL point-to-point over NVLink), the last rank computes the logits and
 the greedy token, and the token is broadcast to every rank for the next step.  Each rank keeps the
-KV cache of its own layers.  The layers themselves are transformers' modules (RW4Linear inside);
-only the hand-off is new.
+KV cache of its own layers.  ``PipelineDecoder`` runs the layers as transformers' modules
+(RW4Linear inside); ``GraphedPipelineDecoder`` runs a decode step of resident RW4 Llama layers
+through the fused decode ops over the rank's own layer range
+(:class:`~rocketllm_b200.fused_decode.FusedLayerRange`), the prefill through the modules.
 """
 import torch
 import torch.distributed as dist
@@ -115,7 +117,10 @@ class GraphedPipelineDecoder(PipelineDecoder):
 
     The prefill runs the prompt through an empty cache with causal attention (no mask: queries
     never reach the unwritten cache slots); decode steps attend over the whole static cache under a
-    mask of the positions written so far."""
+    mask of the positions written so far.  ``fused`` (default: where it applies, i.e. resident RW4
+    Llama layers on a CUDA device) runs each decode step through the fused decode ops over this
+    rank's layers instead of the modules; ``fused=True`` where it does not apply raises
+    ``ValueError``."""
 
     def __init__(self, model, batch, max_len, group=None, device="cuda", drop_remote=True,
                  local=False, use_graph=True, fused=None):

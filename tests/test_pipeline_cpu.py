@@ -136,3 +136,19 @@ def test_pipeline_with_the_int4_kv_cache_matches_single_rank():
         out = mgr.dict()
         mp.spawn(_int4_worker, args=(2, 29731, out), nprocs=2, join=True)
         assert all(out[r] for r in range(2)), dict(out)
+
+
+def test_fused_stage_only_where_it_applies():
+    """The graphed stage takes the fused decode ops only for resident RW4 Llama layers on a CUDA
+    device: a plain fp32 model on the CPU runs the modules by default, and asking for the fused
+    stage there is an error, not a silent fallback."""
+    from rocketllm_b200.fused_decode import fusable_layers
+    from rocketllm_b200.pipeline import GraphedPipelineDecoder
+    model = tiny_model()
+    assert not fusable_layers(model, range(5), True)
+    dec = GraphedPipelineDecoder(model, batch=1, max_len=8, device="cpu", local=True,
+                                 use_graph=False)
+    assert dec.fl is None
+    with pytest.raises(ValueError):
+        GraphedPipelineDecoder(tiny_model(), batch=1, max_len=8, device="cpu", local=True,
+                               fused=True)
