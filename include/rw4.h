@@ -192,7 +192,7 @@ int rw4_linear_residual_ws(const void* x_bf16, int64_t M, int64_t K, const uint8
  *   a NaN counting as larger than every number -- torch.argmax(scores, dim=-1), which the
  *   reference's generate() reaches through the model's own greedy search (rocketllm/base.py:
  *   2014-2044 -> transformers generation/utils.py, the greedy branch of _sample).  rows <= 65535,
- *   V < 2^31.  One launch, one cluster of CTAs per row, no scratch. */
+ *   V <= 2^31 - 2049.  One launch, one cluster of CTAs per row, no scratch. */
 int rw4_argmax_rows(const void* scores_bf16, int64_t rows, int64_t V, int64_t ld, int64_t* out,
                     void* stream);
 

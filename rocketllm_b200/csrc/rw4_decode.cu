@@ -282,7 +282,7 @@ unsigned blocks(int64_t n, int t) { return (unsigned)((n + t - 1) / t); }
 
 extern "C" int rw4_argmax_rows(const void* scores_bf16, int64_t rows, int64_t V, int64_t ld,
                                int64_t* out, void* stream) {
-  if (rows < 0 || V <= 0 || V > INT_MAX - 8 || ld < V)
+  if (rows < 0 || V <= 0 || V > INT_MAX - 8 * kArgmaxThreads || ld < V)   // int indices
     return fail(RW4_EINVAL, "rw4_argmax_rows: bad shape (rows %lld, V %lld, ld %lld)",
                 (long long)rows, (long long)V, (long long)ld);
   if (rows == 0) return RW4_OK;
