@@ -120,7 +120,8 @@ class _FusedOps:
     """The fused per-layer decode ops over a list of decoder layers of a resident RW4 Llama or
     Mixtral model: their weights (q|k|v and gate|up concatenated), the step's static buffers and
     workspace, and the layer loop.  :class:`FusedDecoder` runs it over every layer; a pipeline
-    stage (:class:`~rocketllm_b200.pipeline.GraphedPipelineDecoder`) over the layers it owns."""
+    stage (:class:`~rocketllm_b200.pipeline.GraphedPipelineDecoder`) over the layers it owns.
+    The user sets ``device`` and ``batch`` before calling ``_setup``."""
 
     def _setup(self, model, batch, layer_ids, max_len, with_head, attention):
         cfg = model.config
